@@ -1,0 +1,234 @@
+/*
+ * pi05_b200 — C ABI of the B200 (sm_100a) kernels behind pi0.5 sample_actions.
+ *
+ * Conventions
+ *  - Every pointer is a device pointer unless named host_*; tensors are dense
+ *    row-major; bf16 tensors are passed as void*, fp32 as float*.
+ *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *  - Nothing here allocates or frees device memory.  Ops that need scratch take a
+ *    caller-owned `workspace` of pi05_workspace_bytes() bytes, 256-byte aligned,
+ *    zero-filled once before first use.  Its first 16 KiB (status word and
+ *    split-K barrier counters) must not be modified by the caller; every op
+ *    leaves the counters at zero.  The rest is scratch.  Ops that share one
+ *    workspace must be ordered on one stream.
+ *  - Return value: 0 on success, else a PI05_ERR_* code (pi05_status.h);
+ *    pi05_last_error() gives a one-line reason.  No C++ exception crosses the ABI.
+ *  - Kernels give up any internal wait after 2 s and OR a PI05_DEV_* bit into the
+ *    workspace status word instead of hanging; pi05_read_device_status() reads it.
+ *
+ * Each entry point names the reference interface it replaces (paths inside the
+ * chenchaoxu7575/pi05-infer tree).
+ */
+#ifndef PI05_B200_H
+#define PI05_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- library ----------------------------------------------------------- */
+
+/* ABI version (bumped on any signature change). */
+int pi05_abi_version(void);
+
+/* Text of the last error on this host thread ("" if none). */
+const char* pi05_last_error(void);
+
+/* Workspace bytes needed by the ops below for up to `max_tokens` activation rows
+ * (tokens x batch) and attention over up to `max_kv` keys. */
+size_t pi05_workspace_bytes(int max_tokens, int max_kv);
+
+/* Synchronise `stream`, copy the workspace status word to *host_status and clear
+ * it.  Returns PI05_ERR_DEVICE if the word was non-zero. */
+int pi05_read_device_status(void* workspace, int* host_status, void* stream);
+
+/* Number of kernel launches this library has issued in this process (a CUDA-graph
+ * capture counts the launches it records). */
+long long pi05_launch_count(void);
+
+/* Test hook for the split-K path: force the split count of the skinny GEMMs
+ * (0 = automatic).  Process-wide. */
+void pi05_debug_set_splits(int splits);
+
+/* ---- fused denoise ops (swap-AB tcgen05 GEMM + fused epilogue) ---------- */
+
+/* out[m, n] = gelu_tanh(bf16(x @ wg^T)) * (x @ wu^T), bf16.
+ * Replaces torch.ops.pi05_infer.gate_up_geglu
+ * (pi05_infer/gemma/rlinf_fused_denoise.py:350-389).
+ * x [m, k], wg/wu [n, k]; k % 64 == 0, n % 64 == 0. */
+int pi05_gate_up_geglu(const void* x, const void* wg, const void* wu, void* out, int m, int n, int k,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* Fused q|k|v projection + RoPE + static-KV tail write.
+ * Replaces torch.ops.pi05_infer.qkv_rope_kv (rlinf_fused_denoise.py:392-467).
+ * x [m, k]; w [(hq + 2*hkv) * d, k] = cat(q_proj, k_proj, v_proj) rows;
+ * cos/sin [m, d] bf16; q_out [m, hq, d]; k_cache/v_cache [hkv, kv_rows, d]
+ * receive rows krow0 .. krow0+m-1.  d % 128 == 0, k % 64 == 0. */
+int pi05_qkv_rope_kv(const void* x, const void* w, const void* cos, const void* sin, void* q_out, void* k_cache,
+                     void* v_cache, int m, int k, int krow0, int kv_rows, int n_q_heads, int n_kv_heads,
+                     int head_dim, void* workspace, size_t workspace_bytes, void* stream);
+
+/* out[m, n] = bf16(resid[m, n] + bf16(x @ w^T) * bf16(gate[n])); gate NULL -> plain residual.
+ * Replaces o_proj / down_proj + _gated_residual
+ * (pi05_infer/gemma/modeling_gemma.py:455-456, 138-148, 231-249).
+ * out may alias resid.  n % 128 == 0, k % 64 == 0. */
+int pi05_linear_gated_residual(const void* x, const void* w, const void* resid, const float* gate, void* out,
+                               int m, int n, int k, void* workspace, size_t workspace_bytes, void* stream);
+
+/* out[m, n] = bf16(x @ w^T) (nn.Linear without bias, bf16).  n % 128 == 0, k % 64 == 0. */
+int pi05_linear(const void* x, const void* w, void* out, int m, int n, int k, void* workspace,
+                size_t workspace_bytes, void* stream);
+
+
+/* ---- normalisation, attention, glue ------------------------------------- */
+
+/* adaRMSNorm (mod != NULL, mod = [scale | shift | gate] fp32 [3*d]) or Gemma RMSNorm
+ * (mod == NULL, weight fp32 [d], scale (1 + weight)); fp32 statistics, bf16 out.
+ * Replaces GemmaRMSNorm.forward (pi05_infer/gemma/modeling_gemma.py:65-116).
+ * x, out [rows, d] with row pitches ldx / ldo (elements); d % 8 == 0. */
+int pi05_rms_norm(const void* x, int ldx, const float* mod, const float* weight, void* out, int ldo, int rows, int d,
+                  float eps, void* stream);
+
+/* Multi-query attention, one KV head shared by all query heads.
+ * Replaces eager_attention_forward + repeat_kv (modeling_gemma.py:219-228, 252-275).
+ * q [rows, head_dim] (row = token * n_heads + head), k/v [kv_len, head_dim],
+ * key_valid [kv_len] bytes (0 = masked key), out [rows, head_dim].
+ * head_dim == 256.  splits <= 0 picks the split-KV factor automatically. */
+int pi05_attention(const void* q, const void* k, const void* v, const uint8_t* key_valid, void* out, int rows,
+                   int kv_len, int head_dim, float scale, int splits, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
+/* h[rows, dout] = bf16(x @ w^T + b), fp32 math.  Replaces action_in_proj
+ * (pi05_infer/openpi_patched/pi0_pytorch.py:303-323). */
+int pi05_action_in(const float* x, const float* w, const float* b, void* h, int rows, int din, int dout,
+                   void* stream);
+
+/* Final adaRMSNorm -> fp32 -> action_out_proj -> flow_ode Euler update of x_t in
+ * place (modeling_gemma.py:782-783; engine.py:664-675, 754-767).  v_out (may be
+ * NULL) receives the velocity.  dout <= 64. */
+int pi05_final_euler(const void* h, const float* mod, const float* w, const float* b, float* x_t, float* v_out,
+                     int rows, int d, int dout, float eps, float t, float delta, void* stream);
+
+/* RoPE cos/sin tables [rows, d] bf16 from a key-validity mask (GemmaRotaryEmbedding,
+ * modeling_gemma.py:151-182).  mode 0: prefix rows, position = cumsum(valid) - 1
+ * (engine.py:778); mode 1: suffix rows, position = sum(valid[0:n_prefix]) + row
+ * (engine.py:476-477).  inv_freq [d/2] fp32.  n_prefix <= 4096. */
+int pi05_rope_table(const uint8_t* valid, int n_prefix, int mode, int rows, const float* inv_freq, int d, void* cos,
+                    void* sin, void* stream);
+
+/* adaRMS modulation table for every denoise step (engine.py:556-599):
+ * table[s] = stack_i(dense_i(silu(time_mlp_out(silu(time_mlp_in(sinusoid(t_s))))))),
+ * all fp32.  timesteps [n_steps] device fp32; w_dense [n_norm*3*width, width] and
+ * b_dense [n_norm*3*width] are the norms' dense layers stacked in forward order;
+ * table [n_steps, n_norm*3*width].  n_steps <= 16. */
+int pi05_adarms_table(const float* timesteps, int n_steps, int width, const float* w_tin, const float* b_tin,
+                      const float* w_tout, const float* b_tout, const float* w_dense, const float* b_dense,
+                      int n_norm, float* table, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- whole denoise loop --------------------------------------------------- */
+
+/* Per-layer device pointers of the action expert (bf16 weights, reference layout). */
+typedef struct Pi05ExpertLayer {
+  const void* w_qkv;   /* [(hq + 2*hkv) * d, width]: cat(q_proj, k_proj, v_proj) */
+  const void* w_o;     /* [width, hq * d] */
+  const void* w_gate;  /* [mlp, width] */
+  const void* w_up;    /* [mlp, width] */
+  const void* w_down;  /* [width, mlp] */
+  void* k_cache;       /* [hkv, kv_rows, d]; rows [0, prefix_len) hold the prefix keys */
+  void* v_cache;
+} Pi05ExpertLayer;
+
+/* Everything one denoise step touches.  Host memory owned by the caller. */
+typedef struct Pi05ExpertPlan {
+  int depth, width, mlp_dim, n_q_heads, n_kv_heads, head_dim;
+  int tokens;              /* action horizon (50) */
+  int action_dim;          /* 32 */
+  int prefix_len;          /* rows of the KV cache holding prefix keys (P) */
+  int kv_rows;             /* >= prefix_len + tokens */
+  float eps;
+  const Pi05ExpertLayer* layers;  /* host array [depth] */
+  int num_steps;
+  const float* host_timesteps;    /* host [num_steps + 1]: 1, ..., 1/N, 0 */
+  const float* mod_table;         /* [num_steps, 2*depth+1, 3*width] fp32 */
+  const float* w_in;              /* action_in_proj [width, action_dim] fp32 */
+  const float* b_in;
+  const float* w_out;             /* action_out_proj [action_dim, width] fp32 */
+  const float* b_out;
+  const void* rope_cos;           /* [tokens, d] bf16 */
+  const void* rope_sin;
+  const uint8_t* key_valid;       /* [prefix_len + tokens] */
+  float* x_t;                     /* [tokens, action_dim] fp32: noise in, actions out */
+  float* v_t;                     /* [tokens, action_dim] fp32: last velocity (may be NULL) */
+  void* h;                        /* [tokens, width] bf16 residual stream */
+  void* xn;                       /* [tokens, width] bf16 normalised input */
+  void* q;                        /* [tokens, hq, d] bf16 */
+  void* attn;                     /* [tokens, hq * d] bf16 */
+  void* act;                      /* [tokens, mlp] bf16 */
+  void* workspace;
+  size_t workspace_bytes;
+  int attn_splits;                /* <= 0: automatic */
+} Pi05ExpertPlan;
+
+/* One Euler step `step` (0-based) of the denoise loop: action_in_proj, 18 expert
+ * layers, final norm, action_out_proj, Euler update of plan->x_t.
+ * Replaces one replay of the reference's captured step (engine.py:629-676, 908-1001). */
+int pi05_denoise_step(const Pi05ExpertPlan* plan, int step, void* stream);
+
+/* All plan->num_steps steps (engine.py:390-405). */
+int pi05_denoise_loop(const Pi05ExpertPlan* plan, void* stream);
+
+
+/* ---- prefix (PaliGemma Gemma-2B over image + language tokens) ------------- */
+
+/* out[i, :] = bf16(bf16(table[ids[i], :]) * scale): embed_tokens(ids) * sqrt(width)
+ * (pi05_infer/openpi_patched/pi0_pytorch.py:225-228).  ids int32, table bf16 [vocab, d],
+ * out row pitch ldo; d % 8 == 0.  Out-of-range ids produce a zero row and set
+ * PI05_DEV_BAD_INDEX in the workspace status word. */
+int pi05_embed_tokens(const void* table, int vocab, const int32_t* ids, int n, int d, float scale, void* out,
+                      int ldo, void* workspace, size_t workspace_bytes, void* stream);
+
+typedef struct Pi05PrefixLayer {
+  const void* w_qkv;    /* [(hq + 2*hkv) * d, width] = cat(q_proj, k_proj, v_proj) (prefix_qkv_fused.py:132-139) */
+  const void* w_o;      /* [width, hq * d] */
+  const void* w_gate;   /* [mlp, width] */
+  const void* w_up;
+  const void* w_down;   /* [width, mlp] */
+  const float* ln1_w;   /* input_layernorm weight fp32 [width] (scale 1 + w) */
+  const float* ln2_w;   /* post_attention_layernorm weight fp32 [width] */
+  void* k_cache;        /* [hkv, kv_rows, d]: rows [0, tokens) receive this layer's prefix K */
+  void* v_cache;
+} Pi05PrefixLayer;
+
+typedef struct Pi05PrefixPlan {
+  int depth, width, mlp_dim, n_q_heads, n_kv_heads, head_dim;
+  int tokens;                    /* prefix length P (<= 4096) */
+  int kv_rows;                   /* >= tokens */
+  float eps;
+  const Pi05PrefixLayer* layers; /* host array [depth] */
+  const uint8_t* key_valid;      /* [tokens] pad mask (1 = real token) */
+  const float* inv_freq;         /* [d/2] fp32 */
+  void* rope_cos;                /* [tokens, d] bf16 scratch */
+  void* rope_sin;
+  void* h;                       /* [tokens, width] bf16: prefix embeddings in; residual stream */
+  void* xn;                      /* [tokens, width] bf16 */
+  void* q;                       /* [tokens, hq, d] bf16 */
+  void* attn;                    /* [tokens, hq * d] bf16 */
+  void* act;                     /* [tokens, mlp] bf16 */
+  void* workspace;
+  size_t workspace_bytes;
+  int kv_only_last_layer;        /* 1: the last layer stops after K/V (prefix_last_layer.py:46-112) */
+} Pi05PrefixPlan;
+
+/* Prefix LM forward with use_cache=True: fills every layer's K/V cache rows
+ * [0, tokens).  Replaces PaliGemmaWithExpertModel.forward(inputs_embeds=[prefix, None])
+ * (gemma_pytorch.py:131-142) as called by _build_prefix_cache (engine.py:770-794). */
+int pi05_prefix_forward(const Pi05PrefixPlan* plan, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PI05_B200_H */

@@ -1,0 +1,344 @@
+// Multi-query flash attention with split-KV, for the denoise step (50 suffix
+// tokens x 8 heads against P+50 cached keys) and the prefix LM (P tokens x 8
+// heads against P keys).
+//
+// All query heads share the single KV head, so the query rows (token, head) are
+// one [R, D] matrix and every CTA of a key range reads its K/V chunk once for 16 x
+// WARPS query rows.  The key mask depends only on the key (suffix tokens see every
+// valid prefix key and all suffix keys; valid prefix tokens see every valid prefix
+// key), so it is a byte per key.
+//
+// Numerics follow eager_attention_forward (pi05_infer/gemma/modeling_gemma.py:
+// 252-275): the score is the bf16-rounded Q.K^T times the scale (rounded again
+// to bf16), masked keys are excluded, softmax in fp32 with a running max, the
+// probabilities enter P.V as bf16, accumulation in fp32.
+//
+// mma.sync m16n8k16 (bf16 -> fp32) fragments, ldmatrix from XOR-swizzled shared
+// memory, cp.async double-buffered K/V chunks of 64 keys.
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "host_util.h"
+#include "attention.h"
+
+namespace pi05 {
+namespace {
+
+constexpr int kD = 256;           // head dim
+constexpr int kChunk = 64;        // keys per chunk
+constexpr int kRowBytes = kD * 2; // 512 B per K/V/Q row
+
+// 16-byte chunk c of row r lives at chunk (c ^ (r & 7)) -> conflict-free ldmatrix.
+__device__ __forceinline__ uint32_t swz(int r, int c) { return r * kRowBytes + ((c ^ (r & 7)) << 4); }
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  const int n = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& a, uint32_t& b, uint32_t& c, uint32_t& d) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(a), "=r"(b), "=r"(c), "=r"(d)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& a, uint32_t& b, uint32_t& c, uint32_t& d) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(a), "=r"(b), "=r"(c), "=r"(d)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void mma_bf16(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ float bfr(float x) { return __bfloat162float(__float2bfloat16(x)); }
+
+template <int WARPS>
+__global__ void __launch_bounds__(WARPS * 32, 1)
+    mqa_flash_kernel(const AttnParams p) {
+  constexpr int kRows = 16 * WARPS;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* sQ = smem;                                  // kRows x 512 B
+  uint8_t* sK = smem + kRows * kRowBytes;              // 2 x 64 x 512 B
+  uint8_t* sV = sK + 2 * kChunk * kRowBytes;           // 2 x 64 x 512 B
+  uint8_t* sValid = sV + 2 * kChunk * kRowBytes;       // 2 x 64 bytes
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int row0 = blockIdx.x * kRows;
+  const int split = blockIdx.y;
+  const int n_chunks_total = (p.kv_len + kChunk - 1) / kChunk;
+  const int c_begin = (split * n_chunks_total) / p.splits;
+  const int c_end = ((split + 1) * n_chunks_total) / p.splits;
+
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
+  // Q rows (zero-fill beyond R).
+  for (int i = tid; i < kRows * 32; i += WARPS * 32) {
+    const int r = i >> 5, c = i & 31;
+    const int gr = row0 + r;
+    const bool ok = gr < p.rows;
+    cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(sQ)) + swz(r, c),
+               p.q + (size_t)(ok ? gr : 0) * p.q_stride + c * 8, ok);
+  }
+  auto load_chunk = [&](int ci, int buf) {
+    const int key0 = ci * kChunk;
+    const uint32_t kb = static_cast<uint32_t>(__cvta_generic_to_shared(sK + buf * kChunk * kRowBytes));
+    const uint32_t vb = static_cast<uint32_t>(__cvta_generic_to_shared(sV + buf * kChunk * kRowBytes));
+    for (int i = tid; i < kChunk * 32; i += WARPS * 32) {
+      const int r = i >> 5, c = i & 31;
+      const int key = key0 + r;
+      const bool ok = key < p.kv_len;
+      const size_t off = (size_t)(ok ? key : 0) * p.kv_stride + c * 8;
+      cp_async16(kb + swz(r, c), p.k + off, ok);
+      cp_async16(vb + swz(r, c), p.v + off, ok);
+    }
+    for (int r = tid; r < kChunk; r += WARPS * 32) {
+      const int key = key0 + r;
+      sValid[buf * kChunk + r] = (key < p.kv_len && p.key_valid[key]) ? 1 : 0;
+    }
+  };
+
+  float o[32][4];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY};
+  float l_run[2] = {0.f, 0.f};
+
+  if (c_begin < c_end) load_chunk(c_begin, 0);
+  cp_commit();
+
+  const uint32_t sQa = static_cast<uint32_t>(__cvta_generic_to_shared(sQ));
+  const int g = lane >> 2, t4 = lane & 3;
+  const float scale = p.scale;
+
+  for (int ci = c_begin; ci < c_end; ++ci) {
+    const int buf = (ci - c_begin) & 1;
+    if (ci + 1 < c_end) load_chunk(ci + 1, buf ^ 1);
+    cp_commit();
+    cp_wait<1>();
+    __syncthreads();
+
+    const uint32_t sKa = static_cast<uint32_t>(__cvta_generic_to_shared(sK + buf * kChunk * kRowBytes));
+    const uint32_t sVa = static_cast<uint32_t>(__cvta_generic_to_shared(sV + buf * kChunk * kRowBytes));
+
+    // S = Q_w (16 x 256) . K_chunk^T (256 x 64)
+    float s[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < kD / 16; ++kk) {
+      uint32_t a0, a1, a2, a3;
+      {
+        const int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = kk * 2 + (lane >> 4);
+        ldsm_x4(sQa + swz(r, c), a0, a1, a2, a3);
+      }
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {  // two n-tiles of 8 keys per ldmatrix.x4
+        uint32_t b0, b1, b2, b3;
+        const int mi = lane >> 3;
+        const int r = jj * 16 + (mi >> 1) * 8 + (lane & 7);
+        const int c = kk * 2 + (mi & 1);
+        ldsm_x4(sKa + swz(r, c), b0, b1, b2, b3);
+        mma_bf16(s[2 * jj], a0, a1, a2, a3, b0, b1);
+        mma_bf16(s[2 * jj + 1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+    // scale, mask, online softmax (rows g and g+8 of this warp's 16)
+    const uint8_t* valid = sValid + buf * kChunk;
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = j * 8 + 2 * t4 + (e & 1);
+        float v = bfr(bfr(s[j][e]) * scale);
+        v = valid[key] ? v : -INFINITY;
+        s[j][e] = v;
+        mx[e >> 1] = fmaxf(mx[e >> 1], v);
+      }
+    }
+    float corr[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffff, mx[h], 1));
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffff, mx[h], 2));
+      const float m_new = fmaxf(m_run[h], mx[h]);
+      corr[h] = (m_new == -INFINITY) ? 1.f : __expf(m_run[h] - m_new);
+      m_run[h] = m_new;
+    }
+    float ls[2] = {0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int h = e >> 1;
+        const float pv = (s[j][e] == -INFINITY) ? 0.f : __expf(s[j][e] - m_run[h]);
+        s[j][e] = pv;
+        ls[h] += pv;
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      ls[h] += __shfl_xor_sync(0xffffffff, ls[h], 1);
+      ls[h] += __shfl_xor_sync(0xffffffff, ls[h], 2);
+      l_run[h] = l_run[h] * corr[h] + ls[h];
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      o[j][0] *= corr[0];
+      o[j][1] *= corr[0];
+      o[j][2] *= corr[1];
+      o[j][3] *= corr[1];
+    }
+    // O += P (16 x 64, bf16) . V_chunk (64 x 256)
+#pragma unroll
+    for (int kk = 0; kk < kChunk / 16; ++kk) {
+      const uint32_t a0 = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
+      const uint32_t a1 = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
+      const uint32_t a2 = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      const uint32_t a3 = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) {  // two 8-wide d tiles per ldmatrix.x4.trans
+        uint32_t b0, b1, b2, b3;
+        const int mi = lane >> 3;
+        const int r = kk * 16 + (mi & 1) * 8 + (lane & 7);
+        const int c = jj * 2 + (mi >> 1);
+        ldsm_x4_t(sVa + swz(r, c), b0, b1, b2, b3);
+        mma_bf16(o[2 * jj], a0, a1, a2, a3, b0, b1);
+        mma_bf16(o[2 * jj + 1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+    __syncthreads();
+  }
+  cp_wait<0>();
+
+  // Output: rows (warp*16 + g) and (+8), columns j*8 + 2*t4 .. +1.
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int r = row0 + warp * 16 + g + h * 8;
+    if (r >= p.rows) continue;
+    if (p.splits == 1) {
+      const float inv = l_run[h] > 0.f ? 1.f / l_run[h] : 0.f;
+      __nv_bfloat16* dst = p.out + (size_t)r * p.out_stride;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        *reinterpret_cast<__nv_bfloat162*>(dst + j * 8 + 2 * t4) =
+            __floats2bfloat162_rn(o[j][2 * h] * inv, o[j][2 * h + 1] * inv);
+      }
+    } else {
+      float* dst = p.part_o + ((size_t)split * p.rows + r) * kD;
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        *reinterpret_cast<float2*>(dst + j * 8 + 2 * t4) = make_float2(o[j][2 * h], o[j][2 * h + 1]);
+      if (t4 == 0) {
+        p.part_ml[((size_t)split * p.rows + r) * 2] = m_run[h];
+        p.part_ml[((size_t)split * p.rows + r) * 2 + 1] = l_run[h];
+      }
+    }
+  }
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// One warp per row: merge the split partials (O unnormalised, running max m, sum l).
+__global__ void __launch_bounds__(256) mqa_combine_kernel(const AttnParams p) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= p.rows) return;
+  const int r = warp;
+  float mmax = -INFINITY;
+  for (int s = 0; s < p.splits; ++s) mmax = fmaxf(mmax, p.part_ml[((size_t)s * p.rows + r) * 2]);
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  float l = 0.f;
+  for (int s = 0; s < p.splits; ++s) {
+    const float ms = p.part_ml[((size_t)s * p.rows + r) * 2];
+    const float ls = p.part_ml[((size_t)s * p.rows + r) * 2 + 1];
+    const float w = (ms == -INFINITY) ? 0.f : __expf(ms - mmax);
+    l += ls * w;
+    const float4* src = reinterpret_cast<const float4*>(p.part_o + ((size_t)s * p.rows + r) * kD + lane * 8);
+    const float4 a = src[0], b = src[1];
+    acc[0] += a.x * w; acc[1] += a.y * w; acc[2] += a.z * w; acc[3] += a.w * w;
+    acc[4] += b.x * w; acc[5] += b.y * w; acc[6] += b.z * w; acc[7] += b.w * w;
+  }
+  const float inv = l > 0.f ? 1.f / l : 0.f;
+  __nv_bfloat16* dst = p.out + (size_t)r * p.out_stride + lane * 8;
+  uint4 pk;
+  pk.x = pack_bf16(acc[0] * inv, acc[1] * inv);
+  pk.y = pack_bf16(acc[2] * inv, acc[3] * inv);
+  pk.z = pack_bf16(acc[4] * inv, acc[5] * inv);
+  pk.w = pack_bf16(acc[6] * inv, acc[7] * inv);
+  *reinterpret_cast<uint4*>(dst) = pk;
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+}  // namespace
+
+int mqa_attention_run(AttnParams p, float* part, size_t part_bytes, int splits, void* stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (p.head_dim != kD) {
+    set_last_error("attention: head_dim %d unsupported (256 only)", p.head_dim);
+    return PI05_ERR_SHAPE;
+  }
+  if (p.rows <= 0 || p.kv_len <= 0) {
+    set_last_error("attention: empty rows/keys");
+    return PI05_ERR_SHAPE;
+  }
+  constexpr int W = 4;
+  constexpr int kRows = 16 * W;
+  const int row_blocks = (p.rows + kRows - 1) / kRows;
+  const int n_chunks = (p.kv_len + kChunk - 1) / kChunk;
+  if (splits <= 0) {
+    // Enough CTAs to cover the SMs, at least two chunks per split when possible.
+    int sms = 148;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    splits = 1;
+    while (row_blocks * splits * 2 <= sms && splits * 2 <= n_chunks) splits *= 2;
+  }
+  splits = splits > n_chunks ? n_chunks : splits;
+  p.splits = splits;
+  if (splits > 1) {
+    const size_t need_o = (size_t)splits * p.rows * kD * sizeof(float);
+    const size_t need = need_o + (size_t)splits * p.rows * 2 * sizeof(float);
+    if (part == nullptr || need > part_bytes) {
+      set_last_error("attention: workspace too small (%zu needed)", need);
+      return PI05_ERR_WORKSPACE;
+    }
+    p.part_o = part;
+    p.part_ml = part + (size_t)splits * p.rows * kD;
+  }
+  const size_t smem = (size_t)kRows * kRowBytes + 4 * kChunk * kRowBytes + 2 * kChunk;
+  auto kern = mqa_flash_kernel<W>;
+  static bool attr_done[16] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 16 && !attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) {
+      set_last_error("attention smem attr: %s", cudaGetErrorString(e));
+      return PI05_ERR_LAUNCH;
+    }
+    attr_done[dev] = true;
+  }
+  int rc = launch_pdl(kern, dim3(row_blocks, splits), dim3(W * 32), smem, st, pdl_enabled(), p);
+  if (rc || splits == 1) return rc;
+  return launch_pdl(mqa_combine_kernel, dim3((p.rows + 7) / 8), dim3(256), 0, st, pdl_enabled(), p);
+}
+
+}  // namespace pi05

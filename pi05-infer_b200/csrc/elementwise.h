@@ -1,0 +1,21 @@
+// Internal interface of the small kernels (see elementwise.cu).
+#pragma once
+
+#include <stdint.h>
+
+namespace pi05 {
+
+// mod != null: adaRMS with mod = [scale | shift | gate] (fp32, 3*d); else plain RMSNorm with weight w (fp32, d).
+int rms_norm_run(const void* x, int ldx, const float* mod, const float* w, void* out, int ldo, int rows, int d,
+                 float eps, void* stream);
+int action_in_run(const float* x, const float* w, const float* b, void* h, int rows, int din, int dout,
+                  void* stream);
+int final_euler_run(const void* h, const float* mod, const float* w, const float* b, float* x_t, float* v_out,
+                    int rows, int d, int dout, float eps, float t, float delta, void* stream);
+int rope_table_run(const uint8_t* valid, int n_prefix, int mode, int rows, const float* inv_freq, int d, void* cos,
+                   void* sin, void* stream);
+int sinusoid_run(const float* ts, int n_t, int dim, double min_p, double max_p, float* out, void* stream);
+int linear_f32_rows_run(const float* in, int n_rows, int k, const float* w, const float* b, float* out, int n,
+                        int act, void* stream);
+
+}  // namespace pi05

@@ -1,0 +1,477 @@
+// Swap-AB tcgen05 GEMM for the denoise step's small-token projections.
+//
+//   Y[t, n] = sum_k X[t, k] * W[n, k]       (X: tokens x K activations, W: N x K weights)
+//
+// is computed as Y^T = W * X^T so that the weights fill the 128-row UMMA M
+// dimension and the (<= 64 .. 256) tokens form the UMMA N dimension.  Weights
+// stream from HBM by TMA (128-byte swizzle, evict-first) into a STAGES-deep ring;
+// one elected thread issues tcgen05.mma into a TMEM accumulator; four epilogue
+// warps read TMEM back and apply the fused epilogue.
+//
+// A 128-row A tile is assembled from two 64-row TMA boxes, which lets one tile pair
+// rows that the epilogue must combine without re-packing the reference's weights:
+//   * GEGLU     : 64 rows of W_gate + the same 64 rows of W_up       (gelu_tanh(g)*u)
+//   * QKV_ROPE  : rows d..d+63 and d+D/2..d+D/2+63 of one head        (RoPE pairs)
+//   * STORE / GATED_RESID : 128 consecutive rows.
+//
+// Split-K: when N has too few 128-row tiles to cover the SMs, the K range is split
+// across CTAs.  Each split stores its fp32 partial in the workspace, the splits of
+// a tile meet at a bounded counter barrier, and each then reduces 1/splits of the
+// tile in fixed split order and applies the epilogue to that slice, so results
+// do not depend on CTA timing.
+//
+// Reference ops replaced (pi05_infer/gemma/rlinf_fused_denoise.py):
+//   gate_up_geglu  (:350-389, kernel :116-180)
+//   qkv_rope_kv    (:392-467, kernel :182-332)
+// and the o_proj / down_proj GEMMs with _gated_residual
+// (pi05_infer/gemma/modeling_gemma.py:231-249, :455-456, :138-148, :503).
+#include <algorithm>
+
+#include "host_util.h"
+#include "ptx.cuh"
+#include "skinny_gemm.h"
+
+namespace pi05 {
+
+namespace {
+
+constexpr int kBK = 64;           // K elements per stage (one 128-byte swizzle row)
+constexpr int kBM = 128;          // UMMA M: weight rows per tile
+constexpr int kABytes = kBM * 128;
+constexpr int kThreads = 192;     // warp0 TMA, warp1 MMA/TMEM, warps2-5 epilogue
+constexpr int kEpiThreads = 128;
+
+__device__ __forceinline__ float gelu_tanh_f(float x) {
+  // Same op order as the reference's fused epilogue (rlinf_fused_denoise.py:166-172).
+  const float t3 = x * 0.5f;
+  const float t5 = (x * x) * x;
+  const float t8 = x + t5 * 0.044715f;
+  const float t11 = tanhf(t8 * 0.7978845608028654f);
+  return t3 * (t11 + 1.0f);
+}
+
+struct TileRows {
+  int row0;  // first row of the low 64-row box (map 0)
+  int row1;  // first row of the high 64-row box (map 1)
+};
+
+template <int EPI>
+__device__ __forceinline__ TileRows tile_rows(const SkinnyParams& p, int tile) {
+  TileRows r;
+  if (EPI == SK_EPI_GEGLU) {
+    r.row0 = tile * 64;
+    r.row1 = tile * 64;
+  } else if (EPI == SK_EPI_QKV_ROPE) {
+    const int half = p.head_dim / 2;
+    const int tph = half / 64;  // tiles per rotary head
+    const int n_rot_tiles = (p.n_q_heads + p.n_kv_heads) * tph;
+    if (tile < n_rot_tiles) {
+      const int h = tile / tph, part = tile % tph;
+      r.row0 = h * p.head_dim + part * 64;
+      r.row1 = r.row0 + half;
+    } else {
+      r.row0 = (p.n_q_heads + p.n_kv_heads) * p.head_dim + (tile - n_rot_tiles) * kBM;
+      r.row1 = r.row0 + 64;
+    }
+  } else {
+    r.row0 = tile * kBM;
+    r.row1 = r.row0 + 64;
+  }
+  return r;
+}
+
+// Finished fp32 tile values: either the CTA's own staging tile (no split) or the
+// fixed-order sum of every split's partial (split-K), val(t, r) for token t and
+// tile row r (rows 0..63 from box 0, 64..127 from box 1).
+struct TileSrc {
+  const float* st;    // staging tile [TOK][128] (splits == 1)
+  const float* part;  // partials [splits][TOK][128] of this tile (splits > 1)
+  int splits;
+  int tok_stride;     // TOK * 128
+  __device__ __forceinline__ float operator()(int t, int r) const {
+    if (splits == 1) return st[t * 128 + r];
+    float a = 0.f;
+    const float* q = part + t * 128 + r;
+    for (int s = 0; s < splits; ++s) a += __ldcg(q + (size_t)s * tok_stride);
+    return a;
+  }
+};
+
+// Number of epilogue items of a tile: (token, row) pairs, or (token, row-pair)
+// for the epilogues that combine rows r and r + 64.
+template <int EPI>
+__device__ __forceinline__ int epi_items(const SkinnyParams& p, int tile, int mt) {
+  if (EPI == SK_EPI_GEGLU) return mt * 64;
+  if (EPI == SK_EPI_QKV_ROPE) {
+    const int n_rot_tiles = (p.n_q_heads + p.n_kv_heads) * (p.head_dim / 128);
+    return tile < n_rot_tiles ? mt * 64 : mt * kBM;
+  }
+  return mt * kBM;
+}
+
+// Apply the epilogue to items [i0, i1) (item = t * width + r, r fastest).
+template <int EPI>
+__device__ __forceinline__ void apply_epilogue(const SkinnyParams& p, const TileSrc& val, int tile, int tok0, int i0,
+                                               int i1, int et) {
+  if (EPI == SK_EPI_STORE || EPI == SK_EPI_GATED_RESID) {
+    const int n0 = tile * kBM;
+    for (int idx = i0 + et; idx < i1; idx += kEpiThreads) {
+      const int t = idx >> 7, r = idx & 127, n = n0 + r, tok = tok0 + t;
+      float y = bf16_round(val(t, r));
+      if (EPI == SK_EPI_GATED_RESID) {
+        const float res = __bfloat162float(p.resid[(size_t)tok * p.ldr + n]);
+        if (p.gate != nullptr) y = res + y * bf16_round(p.gate[n]);
+        else y = res + y;
+      }
+      p.out[(size_t)tok * p.ldo + n] = __float2bfloat16(y);
+    }
+  } else if (EPI == SK_EPI_GEGLU) {
+    const int n0 = tile * 64;
+    for (int idx = i0 + et; idx < i1; idx += kEpiThreads) {
+      const int t = idx >> 6, r = idx & 63, tok = tok0 + t;
+      const float g = bf16_round(val(t, r));
+      const float u = val(t, 64 + r);
+      p.out[(size_t)tok * p.ldo + n0 + r] = __float2bfloat16(gelu_tanh_f(g) * u);
+    }
+  } else {  // SK_EPI_QKV_ROPE
+    const int hd = p.head_dim, half = hd / 2, tph = half / 64;
+    const int n_rot_tiles = (p.n_q_heads + p.n_kv_heads) * tph;
+    if (tile < n_rot_tiles) {
+      const int h = tile / tph, part = tile % tph;
+      for (int idx = i0 + et; idx < i1; idx += kEpiThreads) {
+        const int t = idx >> 6, r = idx & 63, tok = tok0 + t;
+        const int dl = part * 64 + r, dh = dl + half;
+        const float xlo = bf16_round(val(t, r));
+        const float xhi = bf16_round(val(t, 64 + r));
+        const float cl = __bfloat162float(p.cos[(size_t)tok * hd + dl]);
+        const float sl = __bfloat162float(p.sin[(size_t)tok * hd + dl]);
+        const float ch = __bfloat162float(p.cos[(size_t)tok * hd + dh]);
+        const float sh = __bfloat162float(p.sin[(size_t)tok * hd + dh]);
+        const float olo = xlo * cl - xhi * sl;
+        const float ohi = xhi * ch + xlo * sh;
+        __nv_bfloat16* dst;
+        if (h < p.n_q_heads) {
+          dst = p.q_out + ((size_t)tok * p.n_q_heads + h) * hd;
+        } else {
+          dst = p.k_cache + (size_t)(h - p.n_q_heads) * p.kv_head_stride + (size_t)(p.krow0 + tok) * hd;
+        }
+        dst[dl] = __float2bfloat16(olo);
+        dst[dh] = __float2bfloat16(ohi);
+      }
+    } else {
+      const int vcol0 = (tile - n_rot_tiles) * kBM;  // column within the packed v heads
+      for (int idx = i0 + et; idx < i1; idx += kEpiThreads) {
+        const int t = idx >> 7, r = idx & 127, tok = tok0 + t;
+        const int c = vcol0 + r, vh = c / hd, d = c % hd;
+        p.v_cache[(size_t)vh * p.kv_head_stride + (size_t)(p.krow0 + tok) * hd + d] =
+            __float2bfloat16(val(t, r));
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+template <int EPI, int TOK, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    skinny_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
+                       const __grid_constant__ CUtensorMap tm_x, const SkinnyParams p) {
+  constexpr int kBBytes = TOK * 128;
+  constexpr int kStageBytes = kABytes + kBBytes;
+  constexpr uint32_t kTmemCols = TOK < 32 ? 32 : TOK;
+  constexpr uint32_t kIdesc = umma_idesc_bf16(kBM, TOK);
+  static_assert(TOK % 16 == 0 && TOK >= 16 && TOK <= 256, "UMMA N for M=128");
+  static_assert(TOK * kBM * 4 <= STAGES * kStageBytes, "epilogue staging must fit in the ring");
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accum = empty + STAGES;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(accum + 1);
+  int* s_flag = reinterpret_cast<int*>(s_tmem + 1);  // [0] abort, [1] ticket
+  float* stage_tile = reinterpret_cast<float*>(smem);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x / p.splits, split = blockIdx.x % p.splits;
+  const int tok0 = blockIdx.y * TOK;
+  const int mt = min(TOK, p.m_tok - tok0);
+  const int kb0 = (split * p.kb_total) / p.splits;
+  const int kb1 = ((split + 1) * p.kb_total) / p.splits;
+  const int nk = kb1 - kb0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    s_flag[0] = 0;
+    s_flag[1] = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tm_w0);
+    prefetch_tmap(&tm_w1);
+    prefetch_tmap(&tm_x);
+  }
+  if (warp == 1) {
+    tmem_alloc(s_tmem, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_acc = *s_tmem;
+  // Let the next kernel in the stream start its prologue / weight prefetch.
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol_w = l2_policy_evict_first();
+      const uint64_t pol_x = l2_policy_evict_last();
+      const TileRows tr = tile_rows<EPI>(p, tile);
+      const int pre = min(STAGES, nk);
+      // Weights do not depend on the previous kernel: issue them before the grid-dependency wait.
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], kStageBytes);
+        const int kx = (kb0 + i) * kBK;
+        tma_load_2d(sA + i * kABytes, &tm_w0, &full[i], kx, tr.row0, pol_w);
+        tma_load_2d(sA + i * kABytes + kABytes / 2, &tm_w1, &full[i], kx, tr.row1, pol_w);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i)
+        tma_load_2d(sB + i * kBBytes, &tm_x, &full[i], (kb0 + i) * kBK, tok0, pol_x);
+      for (int i = pre; i < nk; ++i) {
+        const int s = i % STAGES;
+        if (!mbar_wait(&empty[s], ((i / STAGES) & 1) ^ 1)) {
+          report_status(p.status, PI05_DEV_TIMEOUT_PRODUCER);
+          s_flag[0] = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[s], kStageBytes);
+        const int kx = (kb0 + i) * kBK;
+        tma_load_2d(sA + s * kABytes, &tm_w0, &full[s], kx, tr.row0, pol_w);
+        tma_load_2d(sA + s * kABytes + kABytes / 2, &tm_w1, &full[s], kx, tr.row1, pol_w);
+        tma_load_2d(sB + s * kBBytes, &tm_x, &full[s], kx, tok0, pol_x);
+      }
+    }
+  } else if (warp == 1) {
+    pdl_wait();
+    if (lane == 0) {
+      bool ok = true;
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % STAGES;
+        if (!mbar_wait(&full[s], (i / STAGES) & 1)) {
+          report_status(p.status, PI05_DEV_TIMEOUT_MMA);
+          s_flag[0] = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(sA + s * kABytes);
+        const uint32_t b0 = smem_u32(sB + s * kBBytes);
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk) {
+          umma_bf16(tmem_acc, umma_sdesc_sw128(a0 + kk * 32), umma_sdesc_sw128(b0 + kk * 32), kIdesc,
+                    (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);
+      }
+      if (ok) umma_commit(accum);
+    }
+  } else {
+    // Epilogue warps 2..5: TMEM lane quarter = warp % 4.
+    pdl_wait();
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const int et = threadIdx.x - 64;
+    const bool ok = mbar_wait(accum, 0);
+    if (!ok) report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
+    tc_fence_after();
+    if (ok) {
+#pragma unroll 1
+      for (int c = 0; c < TOK / 32; ++c) {
+        float v[32];
+        tmem_ld32(tmem_acc + ((uint32_t)(q * 32) << 16) + c * 32, v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) stage_tile[(c * 32 + j) * kBM + row] = v[j];
+      }
+    }
+    named_bar_sync(1, kEpiThreads);
+    const int items = epi_items<EPI>(p, tile, mt);
+    if (ok && p.splits == 1) {
+      TileSrc src{stage_tile, nullptr, 1, TOK * kBM};
+      apply_epilogue<EPI>(p, src, tile, tok0, 0, items, et);
+    } else if (ok) {
+      // Deterministic split-K: publish this split's partial, wait (bounded) until
+      // every split of the tile has published, then reduce a 1/splits slice of the
+      // tile in fixed split order and apply the epilogue to it.  All CTAs of the
+      // grid are co-resident (the launcher keeps split grids within one wave).
+      const size_t tile_id = (size_t)blockIdx.y * p.n_tiles + tile;
+      float* part = p.accum + tile_id * p.splits * TOK * kBM;
+      float* mine = part + (size_t)split * TOK * kBM;
+      for (int idx = et * 4; idx < mt * kBM; idx += kEpiThreads * 4)
+        __stcg(reinterpret_cast<float4*>(mine + idx),
+               make_float4(stage_tile[idx], stage_tile[idx + 1], stage_tile[idx + 2], stage_tile[idx + 3]));
+      __threadfence();
+      named_bar_sync(1, kEpiThreads);
+      int* arrive = p.counters + 2 * tile_id;
+      int* depart = arrive + 1;
+      if (et == 0) {
+        atomicAdd(arrive, 1);
+        int seen = ld_acquire(arrive);
+        if (seen < p.splits) {
+          const uint64_t t0 = globaltimer_ns();
+          while ((seen = ld_acquire(arrive)) < p.splits) {
+            if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+              report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
+              break;
+            }
+          }
+        }
+        s_flag[1] = (seen >= p.splits) ? 1 : 0;
+      }
+      named_bar_sync(1, kEpiThreads);
+      if (s_flag[1]) {
+        __threadfence();
+        TileSrc src{nullptr, part, p.splits, TOK * kBM};
+        const int i0 = (int)(((long)split * items) / p.splits);
+        const int i1 = (int)(((long)(split + 1) * items) / p.splits);
+        apply_epilogue<EPI>(p, src, tile, tok0, i0, i1, et);
+      }
+      named_bar_sync(1, kEpiThreads);
+      if (et == 0 && atomicAdd(depart, 1) == p.splits - 1) {
+        // Last one out: re-arm the tile's counters for the next launch.
+        atomicExch(arrive, 0);
+        atomicExch(depart, 0);
+      }
+    }
+  }
+
+  // Teardown.  If the producer bailed out, the ring may still have copies in
+  // flight: wait (bounded) for every armed stage before releasing shared memory.
+  __syncthreads();
+  if (s_flag[0] != 0 && warp == 0 && lane == 0) {
+    for (int s = 0; s < STAGES && s < nk; ++s) {
+      // Phase parity of the last arming of stage s.
+      const int uses = (nk - s + STAGES - 1) / STAGES;
+      if (!mbar_wait(&full[s], (uses - 1) & 1)) report_status(p.status, PI05_DEV_TIMEOUT_DRAIN);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_acc, kTmemCols);
+  }
+}
+
+template <int EPI, int TOK, int STAGES>
+int launch_one(const SkinnyParams& p, const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x,
+               int tok_tiles, cudaStream_t stream) {
+  constexpr int kSmem = 1024 + STAGES * (kABytes + TOK * 128) + (2 * STAGES + 1) * 8 + 16;
+  auto kern = skinny_gemm_kernel<EPI, TOK, STAGES>;
+  static bool attr_done[16] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 16 && !attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e != cudaSuccess) {
+      set_last_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      return PI05_ERR_LAUNCH;
+    }
+    attr_done[dev] = true;
+  }
+  return launch_pdl(kern, dim3(p.n_tiles * p.splits, tok_tiles), dim3(kThreads), kSmem, stream, pdl_enabled(), w0,
+                    w1, x, p);
+}
+
+int num_sms() {
+  static int cached[16] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 16 && cached[dev]) return cached[dev];
+  int n = 148;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (dev < 16) cached[dev] = n;
+  return n;
+}
+
+}  // namespace
+
+int skinny_choose_splits(int n_tiles, int kb_total, int tok_tiles, int sms) {
+  // Minimise (waves x k-blocks per CTA) plus a small per-split reduction cost.
+  int best = 1;
+  double best_cost = 1e30;
+  const int max_s = std::min(kb_total, 32);
+  for (int s = 1; s <= max_s; ++s) {
+    const long units = (long)n_tiles * s * tok_tiles;
+    if (s > 1 && units > sms) break;  // split grids must fit in one wave (tile barrier)
+    const long waves = (units + sms - 1) / sms;
+    const int kb_per = (kb_total + s - 1) / s;
+    const double cost = (double)waves * (kb_per + 1.5) + (s > 1 ? 0.75 : 0.0);
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = s;
+    }
+  }
+  return best;
+}
+
+int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int w_rows0, int w_rows1,
+                    const void* x, int ldx, int splits_override, void* stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (p.m_tok <= 0 || p.k <= 0 || p.k % kBK != 0 || p.n_tiles <= 0) {
+    set_last_error("skinny_gemm: bad shape m=%d k=%d tiles=%d", p.m_tok, p.k, p.n_tiles);
+    return PI05_ERR_SHAPE;
+  }
+  const int tok = p.m_tok <= 64 ? 64 : (p.m_tok <= 128 ? 128 : 256);
+  const int tok_tiles = (p.m_tok + tok - 1) / tok;
+  p.kb_total = p.k / kBK;
+  p.splits = splits_override > 0 ? std::min(splits_override, p.kb_total)
+                                 : skinny_choose_splits(p.n_tiles, p.kb_total, tok_tiles, num_sms());
+  if (p.splits > 1) {
+    const size_t need = (size_t)tok_tiles * p.n_tiles * p.splits * tok * kBM * sizeof(float);
+    if ((long)tok_tiles * p.n_tiles * p.splits > num_sms()) {
+      set_last_error("skinny_gemm: split grid (%d CTAs) exceeds one wave", tok_tiles * p.n_tiles * p.splits);
+      return PI05_ERR_SHAPE;
+    }
+    if (p.accum == nullptr || p.counters == nullptr || need > p.accum_bytes ||
+        2 * tok_tiles * p.n_tiles > kWsMaxCounters) {
+      set_last_error("skinny_gemm: workspace too small (%zu needed)", need);
+      return PI05_ERR_WORKSPACE;
+    }
+  }
+  CUtensorMap tw0, tw1, tx;
+  int rc = make_tmap_bf16_2d(&tw0, w0, w_rows0, p.k, p.k, 64, 64, true);
+  if (rc) return rc;
+  rc = make_tmap_bf16_2d(&tw1, w1, w_rows1, p.k, p.k, 64, 64, true);
+  if (rc) return rc;
+  rc = make_tmap_bf16_2d(&tx, x, p.m_tok, p.k, ldx, tok, 64, true);
+  if (rc) return rc;
+  constexpr int S = 4;
+  switch (epi) {
+#define PI05_SK_CASE(E)                                                                 \
+  case E:                                                                               \
+    if (tok == 64) return launch_one<E, 64, S>(p, tw0, tw1, tx, tok_tiles, st);         \
+    if (tok == 128) return launch_one<E, 128, S>(p, tw0, tw1, tx, tok_tiles, st);       \
+    return launch_one<E, 256, 3>(p, tw0, tw1, tx, tok_tiles, st);
+    PI05_SK_CASE(SK_EPI_STORE)
+    PI05_SK_CASE(SK_EPI_GATED_RESID)
+    PI05_SK_CASE(SK_EPI_GEGLU)
+    PI05_SK_CASE(SK_EPI_QKV_ROPE)
+#undef PI05_SK_CASE
+    default:
+      set_last_error("skinny_gemm: unknown epilogue %d", epi);
+      return PI05_ERR_INVALID_ARG;
+  }
+}
+
+}  // namespace pi05

@@ -1,0 +1,53 @@
+// Internal interface of the swap-AB tcgen05 GEMM (see skinny_gemm.cu).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <stddef.h>
+
+namespace pi05 {
+
+enum SkinnyEpi : int {
+  SK_EPI_STORE = 0,        // out[t, n] = bf16(y)
+  SK_EPI_GATED_RESID = 1,  // out[t, n] = bf16(resid[t, n] + bf16(y) * bf16(gate[n]))   (gate may be null)
+  SK_EPI_GEGLU = 2,        // out[t, n] = bf16(gelu_tanh(bf16(y_gate)) * y_up)
+  SK_EPI_QKV_ROPE = 3,     // RoPE(q) -> q_out, RoPE(k) / v -> KV cache rows krow0 + t
+};
+
+struct SkinnyParams {
+  int m_tok = 0;     // valid tokens
+  int k = 0;         // reduction length (multiple of 64)
+  int n_tiles = 0;   // 128-row weight tiles
+  int kb_total = 0;  // set by the launcher
+  int splits = 1;    // set by the launcher
+  // STORE / GATED_RESID / GEGLU
+  __nv_bfloat16* out = nullptr;
+  int ldo = 0;
+  const __nv_bfloat16* resid = nullptr;
+  int ldr = 0;
+  const float* gate = nullptr;
+  // QKV_ROPE
+  const __nv_bfloat16* cos = nullptr;  // [m_tok, head_dim]
+  const __nv_bfloat16* sin = nullptr;
+  __nv_bfloat16* q_out = nullptr;      // [m_tok, n_q_heads, head_dim]
+  __nv_bfloat16* k_cache = nullptr;    // [n_kv_heads][kv_rows][head_dim]
+  __nv_bfloat16* v_cache = nullptr;
+  size_t kv_head_stride = 0;           // elements between KV heads
+  int krow0 = 0;
+  int n_q_heads = 0;
+  int n_kv_heads = 0;
+  int head_dim = 0;
+  // workspace
+  float* accum = nullptr;   // fp32 split-K accumulator (zero on entry, left zero on exit)
+  size_t accum_bytes = 0;
+  int* counters = nullptr;  // split-K tickets (zero on entry, left zero on exit)
+  int* status = nullptr;    // device status word
+};
+
+int skinny_choose_splits(int n_tiles, int kb_total, int tok_tiles, int sms);
+
+// w0/w1: weight matrices for the two 64-row boxes of each tile (the same matrix
+// except for GEGLU, where w0 = gate and w1 = up).  w_rows*: their row counts.
+int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int w_rows0, int w_rows1,
+                    const void* x, int ldx, int splits_override, void* stream);
+
+}  // namespace pi05

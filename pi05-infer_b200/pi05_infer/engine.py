@@ -1,0 +1,338 @@
+"""``OpenPi0Inference`` (alias ``Engine``): the reference's engine API on B200 kernels.
+
+Mirrors ``pi05_infer/engine.py`` of the reference:
+
+* ``sample_actions(observation, noise=None) -> {"actions": [B, 50, 32] fp32}``
+  (``engine.py:344-406``): prefix (SigLIP + language embedding + Gemma-2B prefix
+  LM filling the static KV cache) then ``num_steps`` Euler steps of the action
+  expert, all enqueued through the C ABI and replayed as CUDA graphs.
+* ``predict_action_batch(env_obs)`` (``engine.py:321-342``) for dict observations.
+* ``enable_torch_compile(mode)`` (``engine.py:1003``): accepted for API
+  compatibility; the kernels are compiled ahead of time, so it does nothing.
+* ``capture_cuda_graph(train_bs, eval_bs)`` (``engine.py:831``): enables graph
+  replay (on by default).
+* ``invalidate_weight_derived_caches()`` (``engine.py:526-554``): after an
+  in-place weight update, re-packs every derived device buffer in place (fused
+  QKV, stacked adaRMS dense, modulation table) so captured graphs stay valid.
+
+There is no CPU or eager fallback: without the built library every call raises.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import math
+from typing import Any, Dict, Optional
+
+import torch
+
+from . import _lib, abi, ops, synthetic
+from .config import ACTION_DIM, ACTION_HORIZON, GEMMA_2B, GEMMA_300M, SIGLIP_SO400M, EngineConfig
+from .expert import DenoiseRunner, ExpertWeights
+from .prefix import PrefixRunner, PrefixWeights, embed_tokens
+
+
+@dataclasses.dataclass
+class Observation:
+    """openpi ``Observation`` fields used by ``sample_actions`` (openpi is not a dependency)."""
+
+    images: Dict[str, torch.Tensor]          # name -> [B, 3, 224, 224] float in [-1, 1]
+    image_masks: Dict[str, torch.Tensor]     # name -> [B] bool
+    tokenized_prompt: torch.Tensor           # [B, L] int
+    tokenized_prompt_mask: torch.Tensor      # [B, L] bool
+    state: torch.Tensor                      # [B, 32]
+
+    @classmethod
+    def from_dict(cls, d: Dict[str, Any]) -> "Observation":
+        return cls(images=d["image"], image_masks=d["image_mask"], tokenized_prompt=d["tokenized_prompt"],
+                   tokenized_prompt_mask=d["tokenized_prompt_mask"], state=d["state"])
+
+
+class OpenPi0Inference:
+    """bs=1 pi0.5 inference engine (one observation per call; one engine per GPU for replicas)."""
+
+    def __init__(self, config: Optional[EngineConfig] = None, state_dict: Optional[Dict[str, torch.Tensor]] = None,
+                 device="cuda", prefix_len: int = 968, num_views: int = 3, prompt_len: int = 200):
+        if not torch.cuda.is_available():
+            raise RuntimeError("pi05_infer needs a CUDA device (sm_100a); there is no CPU path")
+        self.config = config or EngineConfig()
+        self.device = torch.device(device)
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        _lib.lib()
+        self.num_views = num_views
+        self.prompt_len = prompt_len
+        self.prefix_len = prefix_len
+        self.state_dict = state_dict
+        self.use_cuda_graph = True
+        self.expert = None
+        self.prefix_w = None
+        self.vision = None
+        self.embed_table = None
+        self._denoise = None
+        self._prefix = None
+        self._graphs = {}
+        if state_dict is not None:
+            self.load_state_dict(state_dict)
+
+    # ------------------------------------------------------------------ weights
+    @classmethod
+    def synthetic(cls, device="cuda", seed: int = 0, with_vision: bool = False, with_prefix: bool = True,
+                  config: Optional[EngineConfig] = None) -> "OpenPi0Inference":
+        """Random-init weights (N(0, 0.02)) drawn on the device (benchmarks, smoke tests)."""
+        dev = torch.device(device)
+        sd = {}
+        sd.update(synthetic.make_expert_weights(seed, GEMMA_300M, device=dev))
+        if with_prefix:
+            sd.update(synthetic.make_prefix_lm_weights(seed + 10, GEMMA_2B, device=dev, with_embedding=with_vision))
+        if with_vision:
+            sd.update(synthetic.make_siglip_weights(seed + 20, device=dev))
+        eng = cls(config, sd, device=dev)
+        return eng
+
+    def load_state_dict(self, sd: Dict[str, torch.Tensor]) -> None:
+        self.state_dict = sd
+        if self.expert is None:
+            self.expert = ExpertWeights(sd, self.config.expert, self.device)
+        else:
+            self.expert.load(sd)
+        lm_key = synthetic.LM_PREFIX + "layers.0.self_attn.q_proj.weight"
+        if lm_key in sd:
+            if self.prefix_w is None:
+                self.prefix_w = PrefixWeights(sd, self.config.prefix_lm, self.device)
+            else:
+                self.prefix_w.load(sd)
+        if synthetic.EMBED_KEY in sd:
+            t = sd[synthetic.EMBED_KEY]
+            if self.embed_table is None:
+                self.embed_table = t.to(device=self.device, dtype=torch.bfloat16).contiguous()
+            else:
+                self.embed_table.copy_(t)
+        vkey = synthetic.VISION_PREFIX + "embeddings.patch_embedding.weight"
+        if vkey in sd:
+            from .vision import SiglipWeights
+
+            if self.vision is None:
+                self.vision = SiglipWeights(sd, self.config.siglip, self.device)
+            else:
+                self.vision.load(sd)
+
+    def invalidate_weight_derived_caches(self) -> None:
+        """Re-pack every derived buffer from ``self.state_dict`` in place (engine.py:526-554)."""
+        if self.state_dict is None:
+            return
+        self.load_state_dict(self.state_dict)
+        if self._denoise is not None:
+            self._denoise.build_table()
+
+    # ------------------------------------------------------------ compat knobs
+    def enable_torch_compile(self, mode: str = "max-autotune") -> None:  # noqa: ARG002
+        """Kernels are compiled ahead of time; kept for API compatibility."""
+        return None
+
+    def capture_cuda_graph(self, train_bs: Optional[int] = None, eval_bs: Optional[int] = None) -> None:  # noqa: ARG002
+        self.use_cuda_graph = True
+
+    def is_cuda_graph_enabled(self) -> bool:
+        return self.use_cuda_graph
+
+    # ------------------------------------------------------------- components
+    def _runners(self):
+        if self._denoise is None:
+            self._denoise = DenoiseRunner(self.expert, prefix_len=self.prefix_len, num_steps=self.config.num_steps,
+                                          horizon=self.config.action_horizon, action_dim=self.config.action_dim)
+        if self._prefix is None and self.prefix_w is not None:
+            self._prefix = PrefixRunner(self.prefix_w, self.prefix_len, self._denoise.k_cache, self._denoise.v_cache)
+        return self._prefix, self._denoise
+
+    def prefill_from_embeddings(self, embs: torch.Tensor, valid: Optional[torch.Tensor] = None) -> None:
+        """Run the prefix LM over given prefix embeddings ``[P, 2048]`` (config 2)."""
+        prefix, den = self._runners()
+        if prefix is None:
+            raise RuntimeError("engine has no prefix-LM weights")
+        if valid is None:
+            valid = torch.ones(self.prefix_len, dtype=torch.bool, device=self.device)
+        prefix.run(embs.to(self.device, torch.bfloat16), valid.to(self.device))
+        den.key_valid[: self.prefix_len].copy_(valid.reshape(-1).to(torch.uint8))
+        den.key_valid[self.prefix_len:].fill_(1)
+
+    def set_prefix_kv(self, kv, valid: torch.Tensor) -> None:
+        """Use a precomputed prefix cache ``[(K, V)]`` (config 1)."""
+        _, den = self._runners()
+        den.set_prefix(kv, valid.to(self.device))
+
+    def _embed_prefix(self, obs: Observation) -> torch.Tensor:
+        """SigLIP image tokens + scaled language embeddings -> prefix buffer (pi0_pytorch.py:190-253)."""
+        prefix, den = self._runners()
+        if self.vision is None or self.embed_table is None:
+            raise RuntimeError("engine has no SigLIP / embedding weights")
+        from .vision import SiglipRunner
+
+        if not hasattr(self, "_siglip"):
+            self._siglip = SiglipRunner(self.vision, self.num_views)
+        names = list(obs.images.keys())
+        imgs = torch.cat([obs.images[n].to(self.device, torch.float32) for n in names], 0)
+        npatch = self.config.siglip.num_patches
+        self._siglip.run(imgs, out=prefix.h[: len(names) * npatch])
+        ids = obs.tokenized_prompt.reshape(-1).to(self.device, torch.int32)
+        if not hasattr(self, "_ids"):
+            self._ids = torch.zeros(self.prompt_len, dtype=torch.int32, device=self.device)
+        self._ids.copy_(ids)
+        base = len(names) * npatch
+        embed_tokens(self.embed_table, self._ids, prefix.h[base: base + self.prompt_len],
+                     math.sqrt(self.embed_table.shape[1]), ops.workspace(self.device), abi.stream_of(self.device))
+        valid = torch.cat([obs.image_masks[n].to(self.device).reshape(-1, 1).expand(-1, npatch).reshape(-1)
+                           for n in names] + [obs.tokenized_prompt_mask.reshape(-1).to(self.device)])
+        return valid
+
+    # ------------------------------------------------------------ public API
+    @torch.no_grad()
+    def sample_actions(self, observation: Observation, noise: Optional[torch.Tensor] = None) -> dict:
+        """Full inference: prefix cache + ``num_steps`` flow_ode Euler steps (engine.py:344-406)."""
+        prefix, den = self._runners()
+        if noise is None:
+            noise = torch.randn((1, self.config.action_horizon, self.config.action_dim), dtype=torch.float32,
+                                device=self.device)
+        valid = self._embed_prefix(observation)
+        prefix.key_valid.copy_(valid.to(torch.uint8))
+        prefix.enqueue(abi.stream_of(self.device))
+        den.key_valid[: self.prefix_len].copy_(valid.to(torch.uint8))
+        den.key_valid[self.prefix_len:].fill_(1)
+        actions = den.run(noise.to(self.device, non_blocking=True).float(), use_graph=self.use_cuda_graph)
+        return {"actions": actions.clone().reshape(1, self.config.action_horizon, self.config.action_dim)}
+
+    @torch.no_grad()
+    def denoise(self, noise: Optional[torch.Tensor] = None) -> dict:
+        """The Euler loop over the current prefix cache (config 2): noise -> actions."""
+        _, den = self._runners()
+        if noise is None:
+            noise = torch.randn((self.config.action_horizon, self.config.action_dim), device=self.device)
+        actions = den.run(noise.to(self.device, non_blocking=True).float(), use_graph=self.use_cuda_graph)
+        return {"actions": actions.clone().reshape(1, self.config.action_horizon, self.config.action_dim)}
+
+    def predict_action_batch(self, env_obs: Dict[str, Any]) -> torch.Tensor:
+        """``engine.py:321-342`` without openpi's input/output transforms: a dict with
+        openpi ``Observation`` keys in, ``[B, action_chunk, 32]`` actions out."""
+        obs = Observation.from_dict(env_obs)
+        out = self.sample_actions(obs)["actions"]
+        return out[:, : self.config.action_chunk]
+
+    # ------------------------------------------------------------ bench hooks
+    def synthetic_observation(self, seed: int = 100) -> Observation:
+        g = torch.Generator().manual_seed(seed)
+        imgs = {f"cam{i}": (torch.rand((1, 3, 224, 224), generator=g) * 2 - 1) for i in range(self.num_views)}
+        masks = {k: torch.ones(1, dtype=torch.bool) for k in imgs}
+        toks = torch.randint(0, synthetic.VOCAB_SIZE, (1, self.prompt_len), generator=g)
+        return Observation(imgs, masks, toks, torch.ones(1, self.prompt_len, dtype=torch.bool),
+                           torch.randn(1, ACTION_DIM, generator=g))
+
+    def observation_host_bytes(self, obs: Observation) -> int:
+        n = sum(t.numel() * t.element_size() for t in obs.images.values())
+        n += obs.tokenized_prompt.numel() * 4 + obs.tokenized_prompt_mask.numel()
+        return n
+
+    def prepare(self, obs: Observation, embed_seed: int = 3) -> None:
+        """Fill the prefix cache once: from SigLIP + tokens when vision weights are
+        loaded (config 3), else from N(0,1) prefix embeddings (config 2)."""
+        prefix, den = self._runners()
+        if self.vision is not None and self.embed_table is not None:
+            valid = self._embed_prefix(obs)
+            prefix.key_valid.copy_(valid.to(torch.uint8))
+            prefix.enqueue(abi.stream_of(self.device))
+            den.key_valid[: self.prefix_len].copy_(valid.to(torch.uint8))
+        else:
+            g = torch.Generator(device=self.device).manual_seed(embed_seed)
+            embs = torch.randn((self.prefix_len, self.config.prefix_lm.width), generator=g, device=self.device)
+            self.prefill_from_embeddings(embs)
+        torch.cuda.synchronize(self.device)
+
+    def capture_denoise(self, noise: torch.Tensor):
+        """Capture the Euler loop as one CUDA graph; returns a zero-arg replay callable."""
+        _, den = self._runners()
+        den.x_t.copy_(noise.reshape(den.horizon, den.action_dim))
+        den.capture()
+        g = den.graph
+
+        def step():
+            den.x_t.copy_(noise.reshape(den.horizon, den.action_dim))
+            g.replay()
+
+        return step
+
+    def capture_full(self, obs: Observation, noise: torch.Tensor):
+        """Capture prefix + loop (device-resident inputs) as one CUDA graph."""
+        prefix, den = self._runners()
+        self._embed_prefix(obs)
+        stream = torch.cuda.Stream(self.device)
+        imgs = torch.cat([obs.images[n].to(self.device, torch.float32) for n in obs.images], 0)
+        self._static_imgs = imgs
+        den.x_t.copy_(noise.reshape(den.horizon, den.action_dim))
+
+        def enqueue(st):
+            self._siglip.enqueue(self._static_imgs, prefix.h, st)
+            embed_tokens(self.embed_table, self._ids, prefix.h[self.num_views * 256: self.num_views * 256 + self.prompt_len],
+                         math.sqrt(self.embed_table.shape[1]), ops.workspace(self.device), st)
+            prefix.enqueue(st)
+            den._enqueue(st)
+
+        enqueue(abi.stream_of(self.device))
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            enqueue(torch.cuda.current_stream(self.device).cuda_stream)
+        self._graphs["full"] = g
+
+        def step():
+            den.x_t.copy_(noise.reshape(den.horizon, den.action_dim))
+            g.replay()
+
+        return step
+
+    def time_geglu_kernel(self, reps: int = 20) -> dict:
+        """Time the gate/up+GeGLU GEMM alone over the 18 layers' weights (302 MB > L2)."""
+        _, den = self._runners()
+        s = self.expert.shape
+        x = den.xn
+        out = den.act
+        for L in self.expert.layers:
+            ops.geglu(x, L["w_gate"], L["w_up"], out=out)
+        torch.cuda.synchronize(self.device)
+        st = torch.cuda.current_stream(self.device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(reps):
+            for L in self.expert.layers:
+                ops.geglu(x, L["w_gate"], L["w_up"], out=out)
+        e1.record(st)
+        torch.cuda.synchronize(self.device)
+        n = reps * len(self.expert.layers)
+        us = e0.elapsed_time(e1) * 1e3 / n
+        m = self.config.action_horizon
+        nbytes = 2 * s.mlp_dim * s.width * 2 + m * s.width * 2 + m * s.mlp_dim * 2
+        return {"us": us, "bytes": nbytes, "launches": n}
+
+    def denoise_step_bytes(self) -> int:
+        """Algorithmic HBM bytes of one Euler step: expert weights + KV read + KV tail
+        write + the step's adaRMS rows + action in/out projections."""
+        s = self.expert.shape
+        kv_len = self.prefix_len + self.config.action_horizon
+        w = self.expert.nbytes_streamed_per_step()
+        kv_read = s.depth * 2 * kv_len * s.head_dim * 2
+        kv_write = s.depth * 2 * self.config.action_horizon * s.head_dim * 2
+        mods = self.expert.n_norm * 3 * s.width * 4
+        io = 2 * s.width * ACTION_DIM * 4
+        return w + kv_read + kv_write + mods + io
+
+    def last_denoise_step_us(self, loop_ms: Optional[float]) -> Optional[float]:
+        if loop_ms is None:
+            return None
+        return loop_ms * 1e3 / self.config.num_steps
+
+    def release_graphs(self) -> None:
+        self._graphs.clear()
+        if self._denoise is not None:
+            self._denoise.graph = None
+
+
+Engine = OpenPi0Inference
+EngineConfig = EngineConfig

@@ -1,0 +1,126 @@
+"""GPU parity of the denoise loop (configs 1/2) against the CPU oracle.
+
+Same seeded weights (config-1 recipe: N(0, 0.02) everywhere, seed 0), prefix KV
+N(0, 1) (seed 1), noise (seed 2).  Tolerance: per-step
+velocity cosine >= 0.9999 and final action max-abs error <= 2e-2 against the
+oracle's bf16 policy (the reference's dtype policy).
+"""
+
+import pytest
+import torch
+
+from conftest import load_oracle
+
+from pi05_infer import abi, ops, synthetic
+from pi05_infer.config import GEMMA_300M
+from pi05_infer.expert import DenoiseRunner, ExpertWeights
+
+pytestmark = pytest.mark.gpu
+
+oracle = load_oracle()
+
+
+def _cos(a, b):
+    a = a.flatten().double()
+    b = b.flatten().double()
+    return float(a @ b / (a.norm() * b.norm()))
+
+
+@pytest.fixture(scope="module")
+def setup():
+    sd = synthetic.make_expert_weights(0)
+    kv = synthetic.make_prefix_kv(1, 18, 968)
+    kv = [(k[0, 0].bfloat16().float(), v[0, 0].bfloat16().float()) for k, v in kv]
+    noise = synthetic.make_noise(2)[0]
+    w = ExpertWeights(sd, GEMMA_300M, "cuda")
+    return sd, kv, noise, w
+
+
+@pytest.mark.parametrize("ragged", [False, True], ids=["full", "ragged"])
+def test_denoise_loop_parity(setup, ragged):
+    sd, kv, noise, w = setup
+    pad = torch.ones(968, dtype=torch.bool)
+    if ragged:
+        pad[-37:] = False
+    r = DenoiseRunner(w, prefix_len=968, num_steps=10)
+    r.set_prefix([(k.cuda(), v.cuda()) for k, v in kv], pad.cuda())
+    # step by step (no graph) to collect velocities
+    r.x_t.copy_(noise.cuda())
+    abi.rope_table(r.key_valid, 968, 1, 50, r.inv_freq, 256, r.rope_cos, r.rope_sin)
+    vel_gpu = []
+    for s in range(10):
+        abi.denoise_step(r.plan, s, abi.stream_of(r.device))
+        vel_gpu.append(r.v_t.clone().cpu())
+    act_steps = r.x_t.clone().cpu()
+    assert ops.read_device_status() == 0
+
+    vel_ref = []
+    act_ref = oracle.denoise_loop(sd, noise, kv, pad, 18, 10, "bf16", velocities=vel_ref)
+    for s in range(10):
+        c = _cos(vel_gpu[s], vel_ref[s])
+        assert c >= 0.9999, (s, c)
+    err = (act_steps - act_ref).abs().max().item()
+    assert err <= 2e-2, err
+
+    # the captured graph gives the same actions
+    act_graph = r.run(noise.cuda(), use_graph=True).clone().cpu()
+    assert (act_graph - act_steps).abs().max().item() <= 2e-3
+    # and replays are stable
+    act_graph2 = r.run(noise.cuda(), use_graph=True).clone().cpu()
+    assert (act_graph2 - act_graph).abs().max().item() <= 2e-3
+    assert ops.read_device_status() == 0
+
+
+def test_adarms_table(setup):
+    sd, kv, noise, w = setup
+    r = DenoiseRunner(w, prefix_len=968, num_steps=10)
+    ref = oracle.adarms_table(sd, 18, 10, synthetic.EXPERT_PREFIX).reshape(10, -1)
+    got = r.table.cpu()
+    assert (got - ref).abs().max().item() < 1e-4
+
+
+def test_attention_op():
+    g = torch.Generator(device="cuda").manual_seed(5)
+    t, h, d, s = 50, 8, 256, 1018
+    q = (torch.randn(t * h, d, device="cuda", generator=g) * 0.6).bfloat16()
+    k = torch.randn(s, d, device="cuda", generator=g).bfloat16()
+    v = torch.randn(s, d, device="cuda", generator=g).bfloat16()
+    valid = torch.ones(s, dtype=torch.uint8, device="cuda")
+    valid[900:968] = 0
+    ws = ops.workspace(q.device)
+    for splits in (1, 4, 0):
+        out = torch.empty_like(q)
+        abi.attention(q, k, v, valid, out, 1 / 16, splits, ws)
+        mask = torch.where(valid.bool().cpu(), 0.0, oracle.MASK_NEG)[None].expand(t, s)
+        ref = oracle.attention(q.float().cpu().view(t, h, d), k.float().cpu(), v.float().cpu(), mask, 1 / 16, "bf16")
+        err = (out.float().cpu().view(t, h * d) - ref).abs().max().item()
+        assert err < 3e-2, (splits, err)
+        assert _cos(out.float().cpu(), ref) > 0.9999
+
+
+def test_rms_norm_ops():
+    g = torch.Generator(device="cuda").manual_seed(6)
+    x = torch.randn(50, 1024, device="cuda", generator=g).bfloat16()
+    mod = torch.randn(3 * 1024, device="cuda", generator=g) * 0.1
+    out = torch.empty_like(x)
+    abi.rms_norm(x, mod, None, out, 1e-6)
+    ref, _ = oracle.ada_rms_norm(x.float().cpu(), mod.cpu(), 1e-6, "bf16")
+    assert (out.float().cpu() - ref).abs().max().item() < 2e-2
+    wt = torch.randn(1024, device="cuda", generator=g) * 0.1
+    abi.rms_norm(x, None, wt, out, 1e-6)
+    ref = oracle.rms_norm(x.float().cpu(), wt.cpu(), 1e-6, "bf16")
+    assert (out.float().cpu() - ref).abs().max().item() < 2e-2
+
+
+def test_rope_table_prefix_mode():
+    valid = torch.ones(968, dtype=torch.uint8, device="cuda")
+    valid[100:110] = 0
+    inv = torch.tensor((1.0 / (10000 ** (torch.arange(0, 256, 2, dtype=torch.int64).float() / 256))).tolist(),
+                       device="cuda")
+    cos = torch.empty(968, 256, dtype=torch.bfloat16, device="cuda")
+    sin = torch.empty_like(cos)
+    abi.rope_table(valid, 968, 0, 968, inv, 256, cos, sin)
+    pos = torch.cumsum(valid.cpu().long(), 0) - 1
+    rc, rs = oracle.rope_cos_sin(pos, 256, 10000.0, "bf16")
+    assert (cos.float().cpu() - rc).abs().max().item() <= 8e-3
+    assert (sin.float().cpu() - rs).abs().max().item() <= 8e-3
