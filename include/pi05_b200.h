@@ -227,6 +227,65 @@ typedef struct Pi05PrefixPlan {
  * (gemma_pytorch.py:131-142) as called by _build_prefix_cache (engine.py:770-794). */
 int pi05_prefix_forward(const Pi05PrefixPlan* plan, void* stream);
 
+
+/* ---- SigLIP So400m/14 vision tower + projector ---------------------------- */
+
+/* LayerNorm (fp32 statistics, fp32 weight/bias), bf16 in/out; x row pitch d.
+ * Replaces the SigLIP layer_norm1 / layer_norm2 / post_layernorm modules. */
+int pi05_layer_norm(const void* x, const float* w, const float* b, void* out, int ldo, int rows, int d, float eps,
+                    void* stream);
+
+/* Per-head attention of the SigLIP encoder: qkv [views*seq, 3*width] (q | k | v,
+ * head h at columns h*head_dim of each), out [views*seq, width]; no mask,
+ * scale head_dim^-0.5.  head_dim == 72, seq == 256. */
+int pi05_siglip_attention(const void* qkv, int views, int seq, int width, int heads, int head_dim, void* out,
+                          void* stream);
+
+typedef struct Pi05SiglipLayer {
+  const void* w_qkv;   /* [3*width, width] bf16 = cat(q_proj, k_proj, v_proj) */
+  const float* b_qkv;  /* [3*width] */
+  const void* w_o;     /* out_proj [width, width] */
+  const float* b_o;
+  const void* w_fc1;   /* [mlp, width] */
+  const float* b_fc1;
+  const void* w_fc2;   /* [width, mlp] */
+  const float* b_fc2;
+  const float* ln1_w;
+  const float* ln1_b;
+  const float* ln2_w;
+  const float* ln2_b;
+} Pi05SiglipLayer;
+
+typedef struct Pi05SiglipPlan {
+  int depth, width, mlp_dim, n_heads, head_dim, patch, image_size, num_views, proj_dim;
+  float eps;
+  const Pi05SiglipLayer* layers;  /* host array [depth] */
+  const void* w_patch;            /* [width, k_pad] bf16: conv weight flattened (c, ky, kx), zero-padded */
+  const float* b_patch;           /* [width] */
+  const float* pos_emb;           /* [patches, width] fp32 */
+  int k_pad;                      /* >= 3*patch*patch, multiple of 64 */
+  const float* post_ln_w;
+  const float* post_ln_b;
+  const void* w_proj;             /* multi_modal_projector [proj_dim, width] bf16 */
+  const float* b_proj;
+  const float* images;            /* [views, 3, image_size, image_size] fp32 in [-1, 1] */
+  void* cols;                     /* [views*patches, k_pad] bf16 scratch */
+  void* h;                        /* [views*patches, width] bf16 */
+  void* xn;                       /* [views*patches, width] bf16 */
+  void* qkv;                      /* [views*patches, 3*width] bf16 */
+  void* attn;                     /* [views*patches, width] bf16 */
+  void* act;                      /* [views*patches, mlp] bf16 */
+  void* out;                      /* [views*patches, proj_dim] bf16 (rows of the prefix buffer) */
+  int ldo;
+  void* workspace;
+  size_t workspace_bytes;
+} Pi05SiglipPlan;
+
+/* All views through SigLIP and the projector into `out`.  Replaces embed_image /
+ * PaliGemma get_image_features (gemma_pytorch.py:106-107) over cat(images)
+ * (pi0_pytorch.py:203-217). */
+int pi05_siglip_forward(const Pi05SiglipPlan* plan, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -43,8 +43,10 @@ def _r(x: Tensor, policy: str) -> Tensor:
 
 
 def _mm(a: Tensor, w: Tensor, policy: str) -> Tensor:
-    """``a @ w.T`` with fp32 accumulation; output rounded like a bf16 GEMM under bf16."""
-    return _r(a.float() @ w.float().t(), policy)
+    """``a @ w.T`` with fp32 accumulation.  Under bf16 the weight is the bf16 copy the
+    reference holds (``gemma_pytorch.py:84-104``) and the output is rounded like a
+    bf16 GEMM's."""
+    return _r(a.float() @ _r(w.float(), policy).t(), policy)
 
 
 def gelu_tanh(x: Tensor) -> Tensor:
@@ -227,7 +229,7 @@ def expert_forward(
         resid = h
         hn, gate2 = ada_rms_norm(h, mods[2 * i + 1], eps, policy)
         g = _mm(hn, w[p + "mlp.gate_proj.weight"], policy)
-        u = hn.float() @ w[p + "mlp.up_proj.weight"].float().t()
+        u = hn.float() @ _r(w[p + "mlp.up_proj.weight"].float(), policy).t()
         act = _r(gelu_tanh(g) * u, policy)
         dn = _mm(act, w[p + "mlp.down_proj.weight"], policy)
         h = _r(resid + dn * gate2, policy)
@@ -340,7 +342,7 @@ def prefix_lm_kv(
         h = _r(h + _mm(a, w[p + "self_attn.o_proj.weight"], policy), policy)
         hn = rms_norm(h, w[p + "post_attention_layernorm.weight"], eps, policy)
         g = _mm(hn, w[p + "mlp.gate_proj.weight"], policy)
-        u = hn.float() @ w[p + "mlp.up_proj.weight"].float().t()
+        u = hn.float() @ _r(w[p + "mlp.up_proj.weight"].float(), policy).t()
         act = _r(gelu_tanh(g) * u, policy)
         h = _r(h + _mm(act, w[p + "mlp.down_proj.weight"], policy), policy)
     return kv
@@ -352,7 +354,8 @@ def prefix_lm_kv(
 
 
 def layer_norm(x: Tensor, w: Tensor, b: Tensor, eps: float, policy: str) -> Tensor:
-    y = torch.nn.functional.layer_norm(x.float(), (x.shape[-1],), w.float(), b.float(), eps)
+    """LayerNorm with fp32 statistics; bf16 parameters under the bf16 policy."""
+    y = torch.nn.functional.layer_norm(x.float(), (x.shape[-1],), _r(w.float(), policy), _r(b.float(), policy), eps)
     return _r(y, policy)
 
 
@@ -389,11 +392,12 @@ def siglip_image_features(
         p = f"{prefix}encoder.layers.{i}."
         xn = layer_norm(h, w[p + "layer_norm1.weight"], w[p + "layer_norm1.bias"], eps, policy)
         def lin(name, a):
-            return _r(a.float() @ w[p + name + ".weight"].float().t() + w[p + name + ".bias"].float(), policy)
+            wt = _r(w[p + name + ".weight"].float(), policy)
+            return _r(a.float() @ wt.t() + _r(w[p + name + ".bias"].float(), policy), policy)
         q = lin("self_attn.q_proj", xn).view(v_, -1, num_heads, hd)
         k = lin("self_attn.k_proj", xn).view(v_, -1, num_heads, hd)
         vv = lin("self_attn.v_proj", xn).view(v_, -1, num_heads, hd)
-        s = torch.einsum("bqhd,bkhd->bhqk", q, k) * hd ** -0.5
+        s = _r(_r(torch.einsum("bqhd,bkhd->bhqk", q, k), policy) * hd ** -0.5, policy)
         pr = _r(torch.softmax(s.float(), dim=-1), policy)
         a = _r(torch.einsum("bhqk,bkhd->bqhd", pr, vv), policy).reshape(v_, -1, width)
         h = _r(h + lin("self_attn.out_proj", a), policy)
@@ -401,7 +405,8 @@ def siglip_image_features(
         f = _r(gelu_tanh(lin("mlp.fc1", xn)), policy)
         h = _r(h + lin("mlp.fc2", f), policy)
     h = layer_norm(h, w[prefix + "post_layernorm.weight"], w[prefix + "post_layernorm.bias"], eps, policy)
-    return _r(h.float() @ w[proj_prefix + "weight"].float().t() + w[proj_prefix + "bias"].float(), policy)
+    wp = _r(w[proj_prefix + "weight"].float(), policy)
+    return _r(h.float() @ wp.t() + _r(w[proj_prefix + "bias"].float(), policy), policy)
 
 
 def embed_language(embed_table: Tensor, tokens: Tensor, policy: str) -> Tensor:

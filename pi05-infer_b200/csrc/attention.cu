@@ -255,25 +255,46 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-// One warp per row: merge the split partials (O unnormalised, running max m, sum l).
+// One warp per row: merge the split partials (O unnormalised, running max m,
+// sum l).  Lane s holds split s's (m, l); the O loads of four splits are issued
+// together per pass.
 __global__ void __launch_bounds__(256) mqa_combine_kernel(const AttnParams p) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= p.rows) return;
   const int r = warp;
-  float mmax = -INFINITY;
-  for (int s = 0; s < p.splits; ++s) mmax = fmaxf(mmax, p.part_ml[((size_t)s * p.rows + r) * 2]);
+  float ms = -INFINITY, ls = 0.f;
+  if (lane < p.splits) {
+    ms = p.part_ml[((size_t)lane * p.rows + r) * 2];
+    ls = p.part_ml[((size_t)lane * p.rows + r) * 2 + 1];
+  }
+  float mmax = ms;
+  for (int o = 16; o > 0; o >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffff, mmax, o));
+  const float w = (lane < p.splits && ms != -INFINITY) ? __expf(ms - mmax) : 0.f;
+  float l = ls * w;
+  for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffff, l, o);
   float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  float l = 0.f;
-  for (int s = 0; s < p.splits; ++s) {
-    const float ms = p.part_ml[((size_t)s * p.rows + r) * 2];
-    const float ls = p.part_ml[((size_t)s * p.rows + r) * 2 + 1];
-    const float w = (ms == -INFINITY) ? 0.f : __expf(ms - mmax);
-    l += ls * w;
-    const float4* src = reinterpret_cast<const float4*>(p.part_o + ((size_t)s * p.rows + r) * kD + lane * 8);
-    const float4 a = src[0], b = src[1];
-    acc[0] += a.x * w; acc[1] += a.y * w; acc[2] += a.z * w; acc[3] += a.w * w;
-    acc[4] += b.x * w; acc[5] += b.y * w; acc[6] += b.z * w; acc[7] += b.w * w;
+  for (int s0 = 0; s0 < p.splits; s0 += 4) {
+    float4 a[4], b[4];
+    float ws[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int sj = s0 + j;
+      ws[j] = __shfl_sync(0xffffffff, w, sj & 31);
+      if (sj < p.splits) {
+        const float4* src = reinterpret_cast<const float4*>(p.part_o + ((size_t)sj * p.rows + r) * kD + lane * 8);
+        a[j] = __ldcg(src);
+        b[j] = __ldcg(src + 1);
+      } else {
+        ws[j] = 0.f;
+        a[j] = b[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      acc[0] += a[j].x * ws[j]; acc[1] += a[j].y * ws[j]; acc[2] += a[j].z * ws[j]; acc[3] += a[j].w * ws[j];
+      acc[4] += b[j].x * ws[j]; acc[5] += b[j].y * ws[j]; acc[6] += b[j].z * ws[j]; acc[7] += b[j].w * ws[j];
+    }
   }
   const float inv = l > 0.f ? 1.f / l : 0.f;
   __nv_bfloat16* dst = p.out + (size_t)r * p.out_stride + lane * 8;
@@ -312,6 +333,7 @@ int mqa_attention_run(AttnParams p, float* part, size_t part_bytes, int splits, 
     while (row_blocks * splits * 2 <= sms && splits * 2 <= n_chunks) splits *= 2;
   }
   splits = splits > n_chunks ? n_chunks : splits;
+  splits = splits > 32 ? 32 : splits;
   p.splits = splits;
   if (splits > 1) {
     const size_t need_o = (size_t)splits * p.rows * kD * sizeof(float);

@@ -113,8 +113,9 @@ int pi05_qkv_rope_kv(const void* x, const void* w, const void* cos, const void* 
     set_last_error("qkv_rope_kv: bad shape m=%d k=%d d=%d krow0=%d kv_rows=%d", m, k, head_dim, krow0, kv_rows);
     return PI05_ERR_SHAPE;
   }
-  if (!aligned16(x) || !aligned16(w)) {
-    set_last_error("qkv_rope_kv: x/w must be 16-byte aligned");
+  if (!aligned16(x) || !aligned16(w) || !aligned16(cos) || !aligned16(sin) || !aligned16(q_out) ||
+      !aligned16(k_cache) || !aligned16(v_cache)) {
+    set_last_error("qkv_rope_kv: all tensors must be 16-byte aligned");
     return PI05_ERR_ALIGN;
   }
   SkinnyParams p;
@@ -147,8 +148,8 @@ int pi05_linear_gated_residual(const void* x, const void* w, const void* resid, 
     set_last_error("linear_gated_residual: need n %% 128 == 0, k %% 64 == 0 (n=%d k=%d)", n, k);
     return PI05_ERR_SHAPE;
   }
-  if (!aligned16(x) || !aligned16(w)) {
-    set_last_error("linear_gated_residual: x/w must be 16-byte aligned");
+  if (!aligned16(x) || !aligned16(w) || !aligned16(resid) || !aligned16(out) || (gate && !aligned16(gate))) {
+    set_last_error("linear_gated_residual: all tensors must be 16-byte aligned");
     return PI05_ERR_ALIGN;
   }
   SkinnyParams p;
@@ -175,8 +176,8 @@ int pi05_linear(const void* x, const void* w, void* out, int m, int n, int k, vo
     set_last_error("linear: need n %% 128 == 0, k %% 64 == 0 (n=%d k=%d)", n, k);
     return PI05_ERR_SHAPE;
   }
-  if (!aligned16(x) || !aligned16(w)) {
-    set_last_error("linear: x/w must be 16-byte aligned");
+  if (!aligned16(x) || !aligned16(w) || !aligned16(out)) {
+    set_last_error("linear: all tensors must be 16-byte aligned");
     return PI05_ERR_ALIGN;
   }
   SkinnyParams p;

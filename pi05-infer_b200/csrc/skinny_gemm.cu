@@ -81,90 +81,200 @@ __device__ __forceinline__ TileRows tile_rows(const SkinnyParams& p, int tile) {
 }
 
 // Finished fp32 tile values: either the CTA's own staging tile (no split) or the
-// fixed-order sum of every split's partial (split-K), val(t, r) for token t and
-// tile row r (rows 0..63 from box 0, 64..127 from box 1).
+// fixed-order sum of every split's partial (split-K).  get8(t, r, v) fills v with
+// rows r..r+7 (r % 8 == 0) of token t; tile rows 0..63 come from box 0 and
+// 64..127 from box 1.
 struct TileSrc {
   const float* st;    // staging tile [TOK][128] (splits == 1)
   const float* part;  // partials [splits][TOK][128] of this tile (splits > 1)
   int splits;
   int tok_stride;     // TOK * 128
-  __device__ __forceinline__ float operator()(int t, int r) const {
-    if (splits == 1) return st[t * 128 + r];
-    float a = 0.f;
+  __device__ __forceinline__ void get8(int t, int r, float* v) const {
+    if (splits == 1) {
+      const float4 a = *reinterpret_cast<const float4*>(st + t * 128 + r);
+      const float4 b = *reinterpret_cast<const float4*>(st + t * 128 + r + 4);
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      return;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = 0.f;
     const float* q = part + t * 128 + r;
-    for (int s = 0; s < splits; ++s) a += __ldcg(q + (size_t)s * tok_stride);
-    return a;
+    for (int s = 0; s < splits; ++s) {
+      const float4 a = __ldcg(reinterpret_cast<const float4*>(q + (size_t)s * tok_stride));
+      const float4 b = __ldcg(reinterpret_cast<const float4*>(q + (size_t)s * tok_stride + 4));
+      v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w; v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+    }
   }
 };
 
-// Number of epilogue items of a tile: (token, row) pairs, or (token, row-pair)
-// for the epilogues that combine rows r and r + 64.
+// Epilogue items are groups of 8 consecutive tile rows of one token: mt * 16
+// groups, or mt * 8 for the epilogues that pair row r with row r + 64.
 template <int EPI>
 __device__ __forceinline__ int epi_items(const SkinnyParams& p, int tile, int mt) {
-  if (EPI == SK_EPI_GEGLU) return mt * 64;
+  if (EPI == SK_EPI_GEGLU) return mt * 8;
   if (EPI == SK_EPI_QKV_ROPE) {
     const int n_rot_tiles = (p.n_q_heads + p.n_kv_heads) * (p.head_dim / 128);
-    return tile < n_rot_tiles ? mt * 64 : mt * kBM;
+    return tile < n_rot_tiles ? mt * 8 : mt * 16;
   }
-  return mt * kBM;
+  return mt * 16;
 }
 
-// Apply the epilogue to items [i0, i1) (item = t * width + r, r fastest).
+__device__ __forceinline__ void unpack8(const uint4& u, float* f) {
+  const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) f[j] = __bfloat162float(b[j]);
+}
+
+__device__ __forceinline__ void load8f(const float* src, float* f) {
+  const float4 a = *reinterpret_cast<const float4*>(src);
+  const float4 b = *reinterpret_cast<const float4*>(src + 4);
+  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+
+__device__ __forceinline__ uint4 pack8(const float* f) {
+  uint4 u;
+  __nv_bfloat16* b = reinterpret_cast<__nv_bfloat16*>(&u);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) b[j] = __float2bfloat16(f[j]);
+  return u;
+}
+
+// Apply the epilogue to item groups [i0, i1).  Each thread handles kBatch
+// groups per pass and issues every load of the pass before any store, so the
+// global-memory latency of a pass is paid once (outputs may alias inputs, e.g.
+// the in-place residual, which rules out compiler reordering across passes).
 template <int EPI>
-__device__ __forceinline__ void apply_epilogue(const SkinnyParams& p, const TileSrc& val, int tile, int tok0, int i0,
+__device__ __forceinline__ void apply_epilogue(const SkinnyParams& p, const TileSrc& src, int tile, int tok0, int i0,
                                                int i1, int et) {
+  constexpr int kBatch = 4;
   if (EPI == SK_EPI_STORE || EPI == SK_EPI_GATED_RESID) {
+    constexpr int kBatch = 2;  // five 8-float operands per group
     const int n0 = tile * kBM;
-    for (int idx = i0 + et; idx < i1; idx += kEpiThreads) {
-      const int t = idx >> 7, r = idx & 127, n = n0 + r, tok = tok0 + t;
-      float y = bf16_round(val(t, r));
-      if (EPI == SK_EPI_GATED_RESID) {
-        const float res = __bfloat162float(p.resid[(size_t)tok * p.ldr + n]);
-        if (p.gate != nullptr) y = res + y * bf16_round(p.gate[n]);
-        else y = res + y;
+    const int n_valid = p.n_valid > 0 ? p.n_valid : 1 << 30;
+    for (int base = i0 + et; base < i1; base += kBatch * kEpiThreads) {
+      float y[kBatch][8], res[kBatch][8], g[kBatch][8], bi[kBatch][8], ps[kBatch][8];
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        const int idx = base + b * kEpiThreads;
+        const int t = idx >> 4, r = (idx & 15) * 8, n = n0 + r, tok = tok0 + t;
+        if (idx < i1 && n < n_valid) {
+          src.get8(t, r, y[b]);
+          if (p.bias != nullptr) load8f(p.bias + n, bi[b]);
+          if (EPI == SK_EPI_STORE && p.pos != nullptr) load8f(p.pos + (size_t)(tok % p.pos_rows) * p.ldo + n, ps[b]);
+          if (EPI == SK_EPI_GATED_RESID) {
+            unpack8(*reinterpret_cast<const uint4*>(p.resid + (size_t)tok * p.ldr + n), res[b]);
+            if (p.gate != nullptr) load8f(p.gate + n, g[b]);
+          }
+        }
       }
-      p.out[(size_t)tok * p.ldo + n] = __float2bfloat16(y);
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        const int idx = base + b * kEpiThreads;
+        const int t = idx >> 4, r = (idx & 15) * 8, n = n0 + r, tok = tok0 + t;
+        if (idx < i1 && n < n_valid) {
+          float o[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float v = y[b][j];
+            if (p.bias != nullptr) v += bi[b][j];
+            if (EPI == SK_EPI_STORE && p.pos != nullptr) v += ps[b][j];
+            v = bf16_round(v);
+            if (EPI == SK_EPI_STORE && p.act == 1) v = gelu_tanh_f(v);
+            if (EPI == SK_EPI_GATED_RESID) v = (p.gate != nullptr) ? res[b][j] + v * bf16_round(g[b][j]) : res[b][j] + v;
+            o[j] = v;
+          }
+          *reinterpret_cast<uint4*>(p.out + (size_t)tok * p.ldo + n) = pack8(o);
+        }
+      }
     }
   } else if (EPI == SK_EPI_GEGLU) {
     const int n0 = tile * 64;
-    for (int idx = i0 + et; idx < i1; idx += kEpiThreads) {
-      const int t = idx >> 6, r = idx & 63, tok = tok0 + t;
-      const float g = bf16_round(val(t, r));
-      const float u = val(t, 64 + r);
-      p.out[(size_t)tok * p.ldo + n0 + r] = __float2bfloat16(gelu_tanh_f(g) * u);
+    for (int base = i0 + et; base < i1; base += kBatch * kEpiThreads) {
+      float gv[kBatch][8], uv[kBatch][8];
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        const int idx = base + b * kEpiThreads;
+        if (idx < i1) {
+          const int t = idx >> 3, r = (idx & 7) * 8;
+          src.get8(t, r, gv[b]);
+          src.get8(t, 64 + r, uv[b]);
+        }
+      }
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        const int idx = base + b * kEpiThreads;
+        if (idx < i1) {
+          const int t = idx >> 3, r = (idx & 7) * 8, tok = tok0 + t;
+          float o[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = gelu_tanh_f(bf16_round(gv[b][j])) * uv[b][j];
+          *reinterpret_cast<uint4*>(p.out + (size_t)tok * p.ldo + n0 + r) = pack8(o);
+        }
+      }
     }
   } else {  // SK_EPI_QKV_ROPE
     const int hd = p.head_dim, half = hd / 2, tph = half / 64;
     const int n_rot_tiles = (p.n_q_heads + p.n_kv_heads) * tph;
     if (tile < n_rot_tiles) {
       const int h = tile / tph, part = tile % tph;
-      for (int idx = i0 + et; idx < i1; idx += kEpiThreads) {
-        const int t = idx >> 6, r = idx & 63, tok = tok0 + t;
-        const int dl = part * 64 + r, dh = dl + half;
-        const float xlo = bf16_round(val(t, r));
-        const float xhi = bf16_round(val(t, 64 + r));
-        const float cl = __bfloat162float(p.cos[(size_t)tok * hd + dl]);
-        const float sl = __bfloat162float(p.sin[(size_t)tok * hd + dl]);
-        const float ch = __bfloat162float(p.cos[(size_t)tok * hd + dh]);
-        const float sh = __bfloat162float(p.sin[(size_t)tok * hd + dh]);
-        const float olo = xlo * cl - xhi * sl;
-        const float ohi = xhi * ch + xlo * sh;
-        __nv_bfloat16* dst;
-        if (h < p.n_q_heads) {
-          dst = p.q_out + ((size_t)tok * p.n_q_heads + h) * hd;
-        } else {
-          dst = p.k_cache + (size_t)(h - p.n_q_heads) * p.kv_head_stride + (size_t)(p.krow0 + tok) * hd;
+      constexpr int kRB = 2;  // six 8-float operands per group: two groups per pass fit in registers
+      for (int base = i0 + et; base < i1; base += kRB * kEpiThreads) {
+        float lo[kRB][8], hi[kRB][8], cl[kRB][8], sl[kRB][8], ch[kRB][8], sh[kRB][8];
+#pragma unroll
+        for (int b = 0; b < kRB; ++b) {
+          const int idx = base + b * kEpiThreads;
+          if (idx < i1) {
+            const int t = idx >> 3, r = (idx & 7) * 8, tok = tok0 + t;
+            const int dl = part * 64 + r, dh = dl + half;
+            src.get8(t, r, lo[b]);
+            src.get8(t, 64 + r, hi[b]);
+            unpack8(*reinterpret_cast<const uint4*>(p.cos + (size_t)tok * hd + dl), cl[b]);
+            unpack8(*reinterpret_cast<const uint4*>(p.sin + (size_t)tok * hd + dl), sl[b]);
+            unpack8(*reinterpret_cast<const uint4*>(p.cos + (size_t)tok * hd + dh), ch[b]);
+            unpack8(*reinterpret_cast<const uint4*>(p.sin + (size_t)tok * hd + dh), sh[b]);
+          }
         }
-        dst[dl] = __float2bfloat16(olo);
-        dst[dh] = __float2bfloat16(ohi);
+#pragma unroll
+        for (int b = 0; b < kRB; ++b) {
+          const int idx = base + b * kEpiThreads;
+          if (idx < i1) {
+            const int t = idx >> 3, r = (idx & 7) * 8, tok = tok0 + t;
+            const int dl = part * 64 + r, dh = dl + half;
+            float olo[8], ohi[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float xl = bf16_round(lo[b][j]), xh = bf16_round(hi[b][j]);
+              olo[j] = xl * cl[b][j] - xh * sl[b][j];
+              ohi[j] = xh * ch[b][j] + xl * sh[b][j];
+            }
+            __nv_bfloat16* dst = (h < p.n_q_heads)
+                                     ? p.q_out + ((size_t)tok * p.n_q_heads + h) * hd
+                                     : p.k_cache + (size_t)(h - p.n_q_heads) * p.kv_head_stride +
+                                           (size_t)(p.krow0 + tok) * hd;
+            *reinterpret_cast<uint4*>(dst + dl) = pack8(olo);
+            *reinterpret_cast<uint4*>(dst + dh) = pack8(ohi);
+          }
+        }
       }
     } else {
       const int vcol0 = (tile - n_rot_tiles) * kBM;  // column within the packed v heads
-      for (int idx = i0 + et; idx < i1; idx += kEpiThreads) {
-        const int t = idx >> 7, r = idx & 127, tok = tok0 + t;
-        const int c = vcol0 + r, vh = c / hd, d = c % hd;
-        p.v_cache[(size_t)vh * p.kv_head_stride + (size_t)(p.krow0 + tok) * hd + d] =
-            __float2bfloat16(val(t, r));
+      for (int base = i0 + et; base < i1; base += kBatch * kEpiThreads) {
+        float v[kBatch][8];
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) {
+          const int idx = base + b * kEpiThreads;
+          if (idx < i1) src.get8(idx >> 4, (idx & 15) * 8, v[b]);
+        }
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) {
+          const int idx = base + b * kEpiThreads;
+          if (idx < i1) {
+            const int t = idx >> 4, r = (idx & 15) * 8, tok = tok0 + t;
+            const int c = vcol0 + r, vh = c / hd, d = c % hd;
+            *reinterpret_cast<uint4*>(p.v_cache + (size_t)vh * p.kv_head_stride + (size_t)(p.krow0 + tok) * hd + d) =
+                pack8(v[b]);
+          }
+        }
       }
     }
   }
@@ -176,8 +286,13 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
   return v;
 }
 
+// Small-token variants are limited to 170 registers so that two CTAs fit per SM:
+// with PDL the next kernel's CTAs then become resident (and start their weight
+// prefetch) while this kernel's CTAs are still finishing.  (The QKV+RoPE variant
+// is followed by attention, which needs a whole SM's shared memory, so it keeps
+// the registers its epilogue wants.)
 template <int EPI, int TOK, int STAGES>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROPE ? 2 : 1))
     skinny_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
                        const __grid_constant__ CUtensorMap tm_x, const SkinnyParams p) {
   constexpr int kBBytes = TOK * 128;
@@ -428,13 +543,13 @@ int skinny_choose_splits(int n_tiles, int kb_total, int tok_tiles, int sms) {
 int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int w_rows0, int w_rows1,
                     const void* x, int ldx, int splits_override, void* stream) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (p.m_tok <= 0 || p.k <= 0 || p.k % kBK != 0 || p.n_tiles <= 0) {
+  if (p.m_tok <= 0 || p.k <= 0 || p.k % 8 != 0 || p.n_tiles <= 0 || (p.n_valid % 8) != 0) {
     set_last_error("skinny_gemm: bad shape m=%d k=%d tiles=%d", p.m_tok, p.k, p.n_tiles);
     return PI05_ERR_SHAPE;
   }
   const int tok = p.m_tok <= 64 ? 64 : (p.m_tok <= 128 ? 128 : 256);
   const int tok_tiles = (p.m_tok + tok - 1) / tok;
-  p.kb_total = p.k / kBK;
+  p.kb_total = (p.k + kBK - 1) / kBK;
   p.splits = splits_override > 0 ? std::min(splits_override, p.kb_total)
                                  : skinny_choose_splits(p.n_tiles, p.kb_total, tok_tiles, num_sms());
   if (p.splits > 1) {

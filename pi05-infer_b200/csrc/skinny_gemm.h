@@ -7,15 +7,15 @@
 namespace pi05 {
 
 enum SkinnyEpi : int {
-  SK_EPI_STORE = 0,        // out[t, n] = bf16(y)
-  SK_EPI_GATED_RESID = 1,  // out[t, n] = bf16(resid[t, n] + bf16(y) * bf16(gate[n]))   (gate may be null)
+  SK_EPI_STORE = 0,        // out[t, n] = act(bf16(y + bias[n] + pos[t % pos_rows, n]))   (bias, pos, act optional)
+  SK_EPI_GATED_RESID = 1,  // out[t, n] = bf16(resid[t, n] + bf16(y + bias[n]) * bf16(gate[n]))   (bias, gate optional)
   SK_EPI_GEGLU = 2,        // out[t, n] = bf16(gelu_tanh(bf16(y_gate)) * y_up)
   SK_EPI_QKV_ROPE = 3,     // RoPE(q) -> q_out, RoPE(k) / v -> KV cache rows krow0 + t
 };
 
 struct SkinnyParams {
   int m_tok = 0;     // valid tokens
-  int k = 0;         // reduction length (multiple of 64)
+  int k = 0;         // reduction length (multiple of 8; a ragged last 64-block is zero-filled)
   int n_tiles = 0;   // 128-row weight tiles
   int kb_total = 0;  // set by the launcher
   int splits = 1;    // set by the launcher
@@ -25,6 +25,11 @@ struct SkinnyParams {
   const __nv_bfloat16* resid = nullptr;
   int ldr = 0;
   const float* gate = nullptr;
+  const float* bias = nullptr;   // fp32 [n]
+  const float* pos = nullptr;    // fp32 [pos_rows, n] added before rounding (patch embedding)
+  int pos_rows = 0;
+  int act = 0;                   // 0 none, 1 gelu_tanh on the bf16-rounded value
+  int n_valid = 0;               // output columns (multiple of 8); 0 = n_tiles * 128
   // QKV_ROPE
   const __nv_bfloat16* cos = nullptr;  // [m_tok, head_dim]
   const __nv_bfloat16* sin = nullptr;

@@ -289,24 +289,33 @@ class OpenPi0Inference:
         return step
 
     def time_geglu_kernel(self, reps: int = 20) -> dict:
-        """Time the gate/up+GeGLU GEMM alone over the 18 layers' weights (302 MB > L2)."""
+        """Time the gate/up+GeGLU GEMM alone: one launch per expert layer (302 MB of
+        weights > L2) captured in a CUDA graph, replayed ``reps`` times, CUDA events
+        on the replay stream."""
         _, den = self._runners()
         s = self.expert.shape
         x = den.xn
         out = den.act
+        st = torch.cuda.current_stream(self.device)
         for L in self.expert.layers:
             ops.geglu(x, L["w_gate"], L["w_up"], out=out)
         torch.cuda.synchronize(self.device)
-        st = torch.cuda.current_stream(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for L in self.expert.layers:
+                ops.geglu(x, L["w_gate"], L["w_up"], out=out)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize(self.device)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(st)
         for _ in range(reps):
-            for L in self.expert.layers:
-                ops.geglu(x, L["w_gate"], L["w_up"], out=out)
+            g.replay()
         e1.record(st)
         torch.cuda.synchronize(self.device)
         n = reps * len(self.expert.layers)
         us = e0.elapsed_time(e1) * 1e3 / n
+        del g
         m = self.config.action_horizon
         nbytes = 2 * s.mlp_dim * s.width * 2 + m * s.width * 2 + m * s.mlp_dim * 2
         return {"us": us, "bytes": nbytes, "launches": n}
