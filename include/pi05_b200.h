@@ -71,6 +71,18 @@ int pi05_qkv_rope_kv(const void* x, const void* w, const void* cos, const void* 
                      void* v_cache, int m, int k, int krow0, int kv_rows, int n_q_heads, int n_kv_heads,
                      int head_dim, void* workspace, size_t workspace_bytes, void* stream);
 
+/* pi05_gate_up_geglu for callers that cannot allocate device memory -- no
+ * counterpart in the reference.  Same math and arguments minus the workspace:
+ * the split-K scratch is a fixed 4 MiB (+4 KiB) device array inside this library,
+ * held by every GPU that loads it until the process exits.  Limits: m <= 64,
+ * n <= 16384, k <= 16384 (n % 64 == 0, k % 64 == 0); larger shapes return
+ * PI05_ERR_SHAPE.  The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress), so make that call before any stream capture.  All calls
+ * share the one array: calls that can overlap on the GPU (different streams,
+ * different host threads on one device) race and must be serialised by the caller. */
+int pi05_gate_up_geglu_noalloc(const void* x, const void* wg, const void* wu, void* out, int m, int n, int k,
+                               void* stream);
+
 /* out[m, n] = bf16(resid[m, n] + bf16(x @ w^T) * bf16(gate[n])); gate NULL -> plain residual.
  * Replaces o_proj / down_proj + _gated_residual
  * (pi05_infer/gemma/modeling_gemma.py:455-456, 138-148, 231-249).
