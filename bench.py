@@ -117,46 +117,114 @@ def _dist():
     return ws, rank, local
 
 
-def run_reference(args):
-    """CPU reference arm: the oracle port of the reference path on host cores."""
-    ws, rank, _ = _dist()
-    if rank != 0:
-        return 0
+def _load_oracle():
     import importlib.util
 
-    import torch
-
-    torch.set_num_threads(os.cpu_count() or 1)
     spec = importlib.util.spec_from_file_location("pi05_oracle", os.path.join(HERE, "oracle", "pi05_oracle.py"))
     oracle = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(oracle)
-    from pi05_infer import synthetic
+    return oracle
 
-    sd = synthetic.make_expert_weights(0)
-    kv = [(k[0, 0], v[0, 0]) for k, v in synthetic.make_prefix_kv(1, 18, PREFIX_LEN)]
-    noise = synthetic.make_noise(2)[0]
-    pad = torch.ones(PREFIX_LEN, dtype=torch.bool)
-    table = oracle.adarms_table(sd, 18, 10, synthetic.EXPERT_PREFIX)
-    # One sample = one velocity evaluation (1 of the loop's 10 Euler steps), fp32.
-    x = noise
-    for _ in range(args.warmup):
-        oracle.velocity(sd, x, kv, table[0], pad, 18, "fp32")
-    times = []
-    for i in range(args.steps):
+
+class CpuSampler:
+    """Bounded CPU samples of the reference path (oracle port, fp32, all host threads).
+
+    One sample times one component of sample_actions on the host CPU: a SigLIP
+    encoder layer over the 3 views (768 tokens), a Gemma-2B prefix layer over 968
+    tokens, or one velocity evaluation of the 18-layer action expert (one Euler
+    step).  The whole call is estimated as 27 x SigLIP layer + 18 x prefix layer +
+    10 x velocity (config 3), or 10 x velocity (config 2).
+    """
+
+    def __init__(self, workload: str):
+        import torch
+
+        from pi05_infer import synthetic
+        from pi05_infer.config import GemmaShape, SiglipShape
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        self.torch = torch
+        self.oracle = _load_oracle()
+        self.workload = workload
+        self.sd = synthetic.make_expert_weights(0)
+        self.kv = [(k[0, 0], v[0, 0]) for k, v in synthetic.make_prefix_kv(1, 18, PREFIX_LEN)]
+        self.noise = synthetic.make_noise(2)[0]
+        self.pad = torch.ones(PREFIX_LEN, dtype=torch.bool)
+        self.table = self.oracle.adarms_table(self.sd, 18, 10, synthetic.EXPERT_PREFIX)
+        self.components = ["velocity"]
+        if workload == "e2e":
+            lm1 = GemmaShape(width=2048, depth=1, mlp_dim=16384, num_heads=8, num_kv_heads=1, head_dim=256)
+            self.sd_lm = synthetic.make_prefix_lm_weights(10, lm1)
+            self.embs = synthetic.make_prefix_embeddings(3, PREFIX_LEN, 2048)[0]
+            self.sd_vis = synthetic.make_siglip_weights(20, SiglipShape(depth=1))
+            self.imgs = synthetic.make_images(4, 3, 224)
+            self.components = ["siglip_layer", "prefix_layer", "velocity"]
+        self.times = {c: [] for c in self.components}
+
+    def run(self, comp: str, record: bool = True) -> float:
+        o = self.oracle
         t0 = time.perf_counter()
-        v = oracle.velocity(sd, x, kv, table[i % 10], pad, 18, "fp32")
-        times.append(time.perf_counter() - t0)
-    ms_loop = statistics.mean(times) * 1e3 * 10
-    cores = torch.get_num_threads()
+        if comp == "velocity":
+            o.velocity(self.sd, self.noise, self.kv, self.table[0], self.pad, 18, "fp32")
+        elif comp == "prefix_layer":
+            self._prefix_layer()
+        else:
+            o.siglip_image_features(self.sd_vis, self.imgs, 1, "fp32")
+        dt = time.perf_counter() - t0
+        if record:
+            self.times[comp].append(dt)
+        return dt
+
+    def _prefix_layer(self):
+        """One full Gemma-2B decoder layer over the prefix (oracle math, fp32)."""
+        o = self.oracle
+        w, p = self.sd_lm, "paligemma_with_expert.paligemma.model.language_model.layers.0."
+        h = self.embs
+        xn = o.rms_norm(h, w[p + "input_layernorm.weight"], 1e-6, "fp32")
+        q = (xn @ w[p + "self_attn.q_proj.weight"].t()).view(-1, 8, 256)
+        k = xn @ w[p + "self_attn.k_proj.weight"].t()
+        v = xn @ w[p + "self_attn.v_proj.weight"].t()
+        a = o.attention(q, k, v, o.prefix_mask(self.pad), 1 / 16, "fp32")
+        h = h + a @ w[p + "self_attn.o_proj.weight"].t()
+        hn = o.rms_norm(h, w[p + "post_attention_layernorm.weight"], 1e-6, "fp32")
+        act = o.gelu_tanh(hn @ w[p + "mlp.gate_proj.weight"].t()) * (hn @ w[p + "mlp.up_proj.weight"].t())
+        return h + act @ w[p + "mlp.down_proj.weight"].t()
+
+    def estimate_ms(self) -> float:
+        mean = {c: statistics.mean(v) for c, v in self.times.items() if v}
+        ms = 10 * mean["velocity"]
+        if self.workload == "e2e":
+            ms += 27 * mean["siglip_layer"] + 18 * mean["prefix_layer"]
+        return ms * 1e3
+
+    def describe(self) -> str:
+        n = {c: len(v) for c, v in self.times.items()}
+        if self.workload == "e2e":
+            return (f"{n} timed component samples (fp32 torch CPU restatement of the reference path); "
+                    "sample_actions estimated as 27 x SigLIP layer + 18 x Gemma-2B prefix layer + 10 x expert velocity")
+        return f"{n['velocity']} expert velocity evaluations (fp32); loop = 10 x velocity"
+
+
+def run_reference(args):
+    """CPU reference arm: the oracle port of the reference path on the host cores."""
+    ws, rank, _ = _dist()
+    if rank != 0:
+        return 0
+    cs = CpuSampler(args.workload)
+    for i in range(min(args.warmup, len(cs.components))):
+        cs.run(cs.components[i % len(cs.components)], record=False)
+    n = max(len(cs.components), min(args.steps, 60))
+    for i in range(n):
+        cs.run(cs.components[i % len(cs.components)])
+    ms = cs.estimate_ms()
     line = {
-        "impl": "reference", "metric": METRIC, "value": ms_loop, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_loop, "higher_is_better": False, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,0.02) weights, N(0,1) KV and noise)",
+        "impl": "reference", "metric": METRIC, "value": ms, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,0.02) weights, N(0,1) inputs)",
         "config": _config(args, ws),
-        "cpu_baseline": {"value": ms_loop, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": f"{args.steps} velocity evaluations (1 Euler step each) of the config-2 loop, "
-                                   "fp32 torch CPU restatement of the reference expert; value = mean x 10 steps"},
-        "e2e": {"value": ms_loop, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "cpu_baseline": {"value": ms, "unit": UNIT, "cores": cs.torch.get_num_threads(), "kind": "port",
+                         "sample": cs.describe() + f" (timed samples capped at 60 of --steps {args.steps})"},
+        "e2e": {"value": ms, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -170,34 +238,6 @@ def _config(args, ws):
     return {"workload": "config2: 10-step Euler denoise loop, Gemma-300M expert, bs=1, 968-token prefix KV from a random Gemma-2B prefix",
             "global_batch": ws, "seq_len": PREFIX_LEN + 50, "parallelism": f"replicas{ws}",
             "l2": "inputs larger than L2: 623 MB of bf16 expert weights streamed per Euler step (5x L2)"}
-
-
-def cpu_baseline_sample(sd_seed=0):
-    """Bounded CPU sample (rank 0, N=1): oracle velocity evaluations, fp32, all host threads."""
-    import importlib.util
-
-    import torch
-
-    from pi05_infer import synthetic
-
-    torch.set_num_threads(os.cpu_count() or 1)
-    spec = importlib.util.spec_from_file_location("pi05_oracle", os.path.join(HERE, "oracle", "pi05_oracle.py"))
-    oracle = importlib.util.module_from_spec(spec)
-    spec.loader.exec_module(oracle)
-    sd = synthetic.make_expert_weights(sd_seed)
-    kv = [(k[0, 0], v[0, 0]) for k, v in synthetic.make_prefix_kv(1, 18, PREFIX_LEN)]
-    noise = synthetic.make_noise(2)[0]
-    pad = torch.ones(PREFIX_LEN, dtype=torch.bool)
-    table = oracle.adarms_table(sd, 18, 10, synthetic.EXPERT_PREFIX)
-    oracle.velocity(sd, noise, kv, table[0], pad, 18, "fp32")
-    n = 6
-    t0 = time.perf_counter()
-    for i in range(n):
-        oracle.velocity(sd, noise, kv, table[i], pad, 18, "fp32")
-    dt = (time.perf_counter() - t0) / n
-    return {"value": dt * 1e3 * 10, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{n} velocity evaluations (Euler steps) of the config-2 loop in fp32 on the host CPU "
-                      "(torch restatement of the reference expert), scaled x10 to one sample_actions loop"}
 
 
 def run_ours(args):
@@ -259,6 +299,26 @@ def run_ours(args):
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         ms = float(t.item())
 
+    # Denoise-step sub-metric: the config-2 loop (10 Euler steps over the prefix
+    # cache just filled) replayed alone as its own CUDA graph.
+    den_fn = step_fn if args.workload == "denoise" else engine.capture_denoise(noise)
+    den_ms = ms
+    if args.workload != "denoise":
+        for _ in range(3):
+            den_fn()
+        torch.cuda.synchronize(dev)
+        e0.record(stream)
+        n_den = max(10, args.steps // 2)
+        for _ in range(n_den):
+            den_fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        den_ms = e0.elapsed_time(e1) / n_den
+        if pg is not None:
+            t = torch.tensor([den_ms], device=dev)
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+            den_ms = float(t.item())
+
     # End to end through the public API: host noise (pinned) in, host actions out.
     noise_host = synthetic.make_noise(2 + rank).pin_memory()
     torch.cuda.synchronize(dev)
@@ -283,7 +343,7 @@ def run_ours(args):
     roof = engine.time_geglu_kernel(reps=20)
     achieved = roof["bytes"] / (roof["us"] * 1e-6) / 1e9
     traffic = _traffic_from_profiles("skinny_gemm_geglu")
-    denoise_us = engine.last_denoise_step_us(ms if args.workload == "denoise" else None)
+    denoise_us = engine.last_denoise_step_us(den_ms)
 
     line = {
         "metric": METRIC, "value": ms, "unit": UNIT, "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
@@ -304,7 +364,14 @@ def run_ours(args):
         "clocks": clk.summary(),
     }
     if ws == 1 and rank == 0 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline_sample()
+        cs = CpuSampler(args.workload)
+        for c in cs.components:
+            cs.run(c, record=False)
+        for _ in range(3):
+            for c in cs.components:
+                cs.run(c)
+        line["cpu_baseline"] = {"value": cs.estimate_ms(), "unit": UNIT, "cores": cs.torch.get_num_threads(),
+                                "kind": "port", "sample": cs.describe()}
     if rank == 0:
         print(json.dumps(line), flush=True)
     engine.release_graphs()
@@ -317,10 +384,10 @@ def run_ours(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["denoise", "e2e"], default="denoise")
+    ap.add_argument("--workload", choices=["denoise", "e2e"], default="e2e")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -182,15 +182,29 @@ typedef struct Pi05ExpertPlan {
   void* workspace;
   size_t workspace_bytes;
   int attn_splits;                /* <= 0: automatic */
+  unsigned long long* trace;      /* optional device buffer for the persistent kernel's phase timestamps
+                                     ([SMs][pi05_trace_slots()] ns), NULL = off */
 } Pi05ExpertPlan;
+
+/* Timestamp slots per CTA that pi05_denoise_loop_persistent writes when plan->trace is set. */
+int pi05_trace_slots(void);
 
 /* One Euler step `step` (0-based) of the denoise loop: action_in_proj, 18 expert
  * layers, final norm, action_out_proj, Euler update of plan->x_t.
  * Replaces one replay of the reference's captured step (engine.py:629-676, 908-1001). */
 int pi05_denoise_step(const Pi05ExpertPlan* plan, int step, void* stream);
 
-/* All plan->num_steps steps (engine.py:390-405). */
+/* All plan->num_steps steps (engine.py:390-405), one launch per kernel phase. */
 int pi05_denoise_loop(const Pi05ExpertPlan* plan, void* stream);
+
+/* All plan->num_steps steps in ONE persistent cooperative launch (one CTA per SM,
+ * warp-specialised: weight TMA / MMA / activation TMA / worker warps, phases
+ * ordered by completion counters).  Same math as pi05_denoise_loop.  Needs
+ * width 1024, head_dim 256, one KV head, tokens <= 64, <= 18 layers, <= 16 steps
+ * and at least 144 SMs; otherwise returns PI05_ERR_SHAPE.  Uses the workspace
+ * scratch for a second normalised-activation buffer and the attention partials
+ * (plan->xn is the first). */
+int pi05_denoise_loop_persistent(const Pi05ExpertPlan* plan, void* stream);
 
 
 /* ---- prefix (PaliGemma Gemma-2B over image + language tokens) ------------- */

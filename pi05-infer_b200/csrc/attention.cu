@@ -86,6 +86,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   const int c_end = ((split + 1) * n_chunks_total) / p.splits;
 
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   // Q rows (zero-fill beyond R).
   for (int i = tid; i < kRows * 32; i += WARPS * 32) {
@@ -252,7 +253,6 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       }
     }
   }
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // One warp per row: merge the split partials (O unnormalised, running max m,
@@ -260,6 +260,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 // together per pass.
 __global__ void __launch_bounds__(256) mqa_combine_kernel(const AttnParams p) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= p.rows) return;
   const int r = warp;
@@ -304,7 +305,6 @@ __global__ void __launch_bounds__(256) mqa_combine_kernel(const AttnParams p) {
   pk.z = pack_bf16(acc[4] * inv, acc[5] * inv);
   pk.w = pack_bf16(acc[6] * inv, acc[7] * inv);
   *reinterpret_cast<uint4*>(dst) = pk;
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 }  // namespace

@@ -30,6 +30,7 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const __nv_bfloat16* __re
                                                        __nv_bfloat16* __restrict__ out, int ldo, int d, float eps) {
   __shared__ float red[32];
   pdl_wait();
+  pdl_launch_dependents();  // let the next kernel's CTAs start their prologue / weight prefetch
   const int row = blockIdx.x;
   const __nv_bfloat16* xr = x + (size_t)row * ldx;
   float ss = 0.f;
@@ -58,7 +59,6 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const __nv_bfloat16* __re
     }
     *reinterpret_cast<uint4*>(out + (size_t)row * ldo + i) = *reinterpret_cast<const uint4*>(o);
   }
-  pdl_launch_dependents();
 }
 
 // action_in_proj (pi0_pytorch.py:303-323): h[t, n] = bf16(sum_k x[t, k] w[n, k] + b[n]), fp32 math.
@@ -67,6 +67,7 @@ __global__ void __launch_bounds__(256) action_in_kernel(const float* __restrict_
                                                         int din, int dout) {
   extern __shared__ float xs[];
   pdl_wait();
+  pdl_launch_dependents();  // let the next kernel's CTAs start their prologue / weight prefetch
   const int t = blockIdx.x;
   for (int k = threadIdx.x; k < din; k += blockDim.x) xs[k] = x[(size_t)t * din + k];
   __syncthreads();
@@ -76,7 +77,6 @@ __global__ void __launch_bounds__(256) action_in_kernel(const float* __restrict_
     for (int k = 0; k < din; ++k) acc = fmaf(xs[k], wr[k], acc);
     h[(size_t)t * dout + n] = __float2bfloat16(acc);
   }
-  pdl_launch_dependents();
 }
 
 // Final adaRMS norm -> fp32 -> action_out_proj -> flow_ode Euler step
@@ -91,6 +91,7 @@ __global__ void __launch_bounds__(256) final_euler_kernel(const __nv_bfloat16* _
   __shared__ float red[32];
   __shared__ float vs[64];
   pdl_wait();
+  pdl_launch_dependents();  // let the next kernel's CTAs start their prologue / weight prefetch
   const int row = blockIdx.x;
   const __nv_bfloat16* hr = h + (size_t)row * d;
   float ss = 0.f;
@@ -122,7 +123,6 @@ __global__ void __launch_bounds__(256) final_euler_kernel(const __nv_bfloat16* _
     x_t[(size_t)row * dout + j] = x0 * (1.0f - (t - delta)) + x1 * (t - delta);
     if (v_out != nullptr) v_out[(size_t)row * dout + j] = v;
   }
-  pdl_launch_dependents();
 }
 
 // RoPE table (GemmaRotaryEmbedding, modeling_gemma.py:151-182) for rows whose
@@ -136,6 +136,7 @@ __global__ void __launch_bounds__(1024) rope_table_kernel(const uint8_t* __restr
   __shared__ int cnt[4096];
   __shared__ int wsum[32];
   pdl_wait();
+  pdl_launch_dependents();  // let the next kernel's CTAs start their prologue / weight prefetch
   const int n = n_prefix;
   // inclusive scan of valid[0:n] (n <= 4096), 4 elements per thread
   const int per = 4;
@@ -179,7 +180,6 @@ __global__ void __launch_bounds__(1024) rope_table_kernel(const uint8_t* __restr
     cos_out[idx] = __float2bfloat16(cosf(f));
     sin_out[idx] = __float2bfloat16(sinf(f));
   }
-  pdl_launch_dependents();
 }
 
 // torch.linspace(start, end, steps) element, float64 (torch's two-sided formula).

@@ -28,6 +28,7 @@ __global__ void __launch_bounds__(256) embed_tokens_kernel(const __nv_bfloat16* 
                                                            const int32_t* __restrict__ ids, int n, int d, float scale,
                                                            __nv_bfloat16* __restrict__ out, int ldo, int* status) {
   pdl_wait();
+  pdl_launch_dependents();  // let the next kernel's CTAs start their prologue / weight prefetch
   const int row = blockIdx.x;
   const int id = ids[row];
   const bool ok = id >= 0 && id < vocab;
@@ -45,7 +46,6 @@ __global__ void __launch_bounds__(256) embed_tokens_kernel(const __nv_bfloat16* 
     }
     *reinterpret_cast<uint4*>(out + (size_t)row * ldo + c) = *reinterpret_cast<const uint4*>(o);
   }
-  pdl_launch_dependents();
 }
 
 inline bool nz(const void* p) { return p != nullptr; }

@@ -29,6 +29,7 @@ __global__ void __launch_bounds__(128) layer_norm_kernel(const __nv_bfloat16* __
                                                          __nv_bfloat16* __restrict__ out, int ldo, int d, float eps) {
   __shared__ float red[4];
   pdl_wait();
+  pdl_launch_dependents();  // let the next kernel's CTAs start their prologue / weight prefetch
   const int row = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const __nv_bfloat16* xr = x + (size_t)row * d;
   float s = 0.f;
@@ -65,7 +66,6 @@ __global__ void __launch_bounds__(128) layer_norm_kernel(const __nv_bfloat16* __
     for (int j = 0; j < 8; ++j) o8[j] = __float2bfloat16((__bfloat162float(v[j]) - mean) * rstd * w[i + j] + b[i + j]);
     *reinterpret_cast<uint4*>(out + (size_t)row * ldo + i) = *reinterpret_cast<const uint4*>(o8);
   }
-  pdl_launch_dependents();
 }
 
 // im2col for the 14x14/14 patch conv: cols[v*gp*gp + py*gp + px, c*P*P + ky*P + kx] =
@@ -73,6 +73,7 @@ __global__ void __launch_bounds__(128) layer_norm_kernel(const __nv_bfloat16* __
 __global__ void __launch_bounds__(256) im2col_kernel(const float* __restrict__ img, int views, int hw, int patch,
                                                      int k_pad, __nv_bfloat16* __restrict__ cols) {
   pdl_wait();
+  pdl_launch_dependents();  // let the next kernel's CTAs start their prologue / weight prefetch
   const int gp = hw / patch;
   const int kk = 3 * patch * patch;
   const size_t total = (size_t)views * gp * gp * k_pad;
@@ -89,7 +90,6 @@ __global__ void __launch_bounds__(256) im2col_kernel(const float* __restrict__ i
     }
     cols[idx] = __float2bfloat16(val);
   }
-  pdl_launch_dependents();
 }
 
 // ---- per-head flash attention, head dim 72 (padded to 80), mma.sync --------
@@ -132,6 +132,7 @@ __global__ void __launch_bounds__(128) mha72_kernel(const __nv_bfloat16* __restr
   __nv_bfloat16* sK = sQ + 64 * kRowE;                          // SEQ x 88
   __nv_bfloat16* sV = sK + SEQ * kRowE;                         // SEQ x 88
   pdl_wait();
+  pdl_launch_dependents();  // let the next kernel's CTAs start their prologue / weight prefetch
   const int vh = blockIdx.x, view = vh / heads, h = vh % heads;
   const int q0 = blockIdx.y * 64;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -252,7 +253,6 @@ __global__ void __launch_bounds__(128) mha72_kernel(const __nv_bfloat16* __restr
     for (int j = 0; j < 9; ++j)
       *reinterpret_cast<uint32_t*>(dst + j * 8 + 2 * t4) = pack2(o[j][2 * hh] * inv, o[j][2 * hh + 1] * inv);
   }
-  pdl_launch_dependents();
 }
 
 inline bool nz(const void* p) { return p != nullptr; }

@@ -27,6 +27,7 @@
 // (pi05_infer/gemma/modeling_gemma.py:231-249, :455-456, :138-148, :503).
 #include <algorithm>
 
+#include "gemm_epilogue.cuh"
 #include "host_util.h"
 #include "ptx.cuh"
 #include "skinny_gemm.h"
@@ -35,256 +36,8 @@ namespace pi05 {
 
 namespace {
 
-constexpr int kBK = 64;           // K elements per stage (one 128-byte swizzle row)
-constexpr int kBM = 128;          // UMMA M: weight rows per tile
-constexpr int kABytes = kBM * 128;
+using namespace gemm;
 constexpr int kThreads = 192;     // warp0 TMA, warp1 MMA/TMEM, warps2-5 epilogue
-constexpr int kEpiThreads = 128;
-
-__device__ __forceinline__ float gelu_tanh_f(float x) {
-  // Same op order as the reference's fused epilogue (rlinf_fused_denoise.py:166-172).
-  const float t3 = x * 0.5f;
-  const float t5 = (x * x) * x;
-  const float t8 = x + t5 * 0.044715f;
-  const float t11 = tanhf(t8 * 0.7978845608028654f);
-  return t3 * (t11 + 1.0f);
-}
-
-struct TileRows {
-  int row0;  // first row of the low 64-row box (map 0)
-  int row1;  // first row of the high 64-row box (map 1)
-};
-
-template <int EPI>
-__device__ __forceinline__ TileRows tile_rows(const SkinnyParams& p, int tile) {
-  TileRows r;
-  if (EPI == SK_EPI_GEGLU) {
-    r.row0 = tile * 64;
-    r.row1 = tile * 64;
-  } else if (EPI == SK_EPI_QKV_ROPE) {
-    const int half = p.head_dim / 2;
-    const int tph = half / 64;  // tiles per rotary head
-    const int n_rot_tiles = (p.n_q_heads + p.n_kv_heads) * tph;
-    if (tile < n_rot_tiles) {
-      const int h = tile / tph, part = tile % tph;
-      r.row0 = h * p.head_dim + part * 64;
-      r.row1 = r.row0 + half;
-    } else {
-      r.row0 = (p.n_q_heads + p.n_kv_heads) * p.head_dim + (tile - n_rot_tiles) * kBM;
-      r.row1 = r.row0 + 64;
-    }
-  } else {
-    r.row0 = tile * kBM;
-    r.row1 = r.row0 + 64;
-  }
-  return r;
-}
-
-// Finished fp32 tile values: either the CTA's own staging tile (no split) or the
-// fixed-order sum of every split's partial (split-K).  get8(t, r, v) fills v with
-// rows r..r+7 (r % 8 == 0) of token t; tile rows 0..63 come from box 0 and
-// 64..127 from box 1.
-struct TileSrc {
-  const float* st;    // staging tile [TOK][128] (splits == 1)
-  const float* part;  // partials [splits][TOK][128] of this tile (splits > 1)
-  int splits;
-  int tok_stride;     // TOK * 128
-  __device__ __forceinline__ void get8(int t, int r, float* v) const {
-    if (splits == 1) {
-      const float4 a = *reinterpret_cast<const float4*>(st + t * 128 + r);
-      const float4 b = *reinterpret_cast<const float4*>(st + t * 128 + r + 4);
-      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-      return;
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = 0.f;
-    const float* q = part + t * 128 + r;
-    for (int s = 0; s < splits; ++s) {
-      const float4 a = __ldcg(reinterpret_cast<const float4*>(q + (size_t)s * tok_stride));
-      const float4 b = __ldcg(reinterpret_cast<const float4*>(q + (size_t)s * tok_stride + 4));
-      v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w; v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
-    }
-  }
-};
-
-// Epilogue items are groups of 8 consecutive tile rows of one token: mt * 16
-// groups, or mt * 8 for the epilogues that pair row r with row r + 64.
-template <int EPI>
-__device__ __forceinline__ int epi_items(const SkinnyParams& p, int tile, int mt) {
-  if (EPI == SK_EPI_GEGLU) return mt * 8;
-  if (EPI == SK_EPI_QKV_ROPE) {
-    const int n_rot_tiles = (p.n_q_heads + p.n_kv_heads) * (p.head_dim / 128);
-    return tile < n_rot_tiles ? mt * 8 : mt * 16;
-  }
-  return mt * 16;
-}
-
-__device__ __forceinline__ void unpack8(const uint4& u, float* f) {
-  const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
-#pragma unroll
-  for (int j = 0; j < 8; ++j) f[j] = __bfloat162float(b[j]);
-}
-
-__device__ __forceinline__ void load8f(const float* src, float* f) {
-  const float4 a = *reinterpret_cast<const float4*>(src);
-  const float4 b = *reinterpret_cast<const float4*>(src + 4);
-  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
-}
-
-__device__ __forceinline__ uint4 pack8(const float* f) {
-  uint4 u;
-  __nv_bfloat16* b = reinterpret_cast<__nv_bfloat16*>(&u);
-#pragma unroll
-  for (int j = 0; j < 8; ++j) b[j] = __float2bfloat16(f[j]);
-  return u;
-}
-
-// Apply the epilogue to item groups [i0, i1).  Each thread handles kBatch
-// groups per pass and issues every load of the pass before any store, so the
-// global-memory latency of a pass is paid once (outputs may alias inputs, e.g.
-// the in-place residual, which rules out compiler reordering across passes).
-template <int EPI>
-__device__ __forceinline__ void apply_epilogue(const SkinnyParams& p, const TileSrc& src, int tile, int tok0, int i0,
-                                               int i1, int et) {
-  constexpr int kBatch = 4;
-  if (EPI == SK_EPI_STORE || EPI == SK_EPI_GATED_RESID) {
-    constexpr int kBatch = 2;  // five 8-float operands per group
-    const int n0 = tile * kBM;
-    const int n_valid = p.n_valid > 0 ? p.n_valid : 1 << 30;
-    for (int base = i0 + et; base < i1; base += kBatch * kEpiThreads) {
-      float y[kBatch][8], res[kBatch][8], g[kBatch][8], bi[kBatch][8], ps[kBatch][8];
-#pragma unroll
-      for (int b = 0; b < kBatch; ++b) {
-        const int idx = base + b * kEpiThreads;
-        const int t = idx >> 4, r = (idx & 15) * 8, n = n0 + r, tok = tok0 + t;
-        if (idx < i1 && n < n_valid) {
-          src.get8(t, r, y[b]);
-          if (p.bias != nullptr) load8f(p.bias + n, bi[b]);
-          if (EPI == SK_EPI_STORE && p.pos != nullptr) load8f(p.pos + (size_t)(tok % p.pos_rows) * p.ldo + n, ps[b]);
-          if (EPI == SK_EPI_GATED_RESID) {
-            unpack8(*reinterpret_cast<const uint4*>(p.resid + (size_t)tok * p.ldr + n), res[b]);
-            if (p.gate != nullptr) load8f(p.gate + n, g[b]);
-          }
-        }
-      }
-#pragma unroll
-      for (int b = 0; b < kBatch; ++b) {
-        const int idx = base + b * kEpiThreads;
-        const int t = idx >> 4, r = (idx & 15) * 8, n = n0 + r, tok = tok0 + t;
-        if (idx < i1 && n < n_valid) {
-          float o[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float v = y[b][j];
-            if (p.bias != nullptr) v += bi[b][j];
-            if (EPI == SK_EPI_STORE && p.pos != nullptr) v += ps[b][j];
-            v = bf16_round(v);
-            if (EPI == SK_EPI_STORE && p.act == 1) v = gelu_tanh_f(v);
-            if (EPI == SK_EPI_GATED_RESID) v = (p.gate != nullptr) ? res[b][j] + v * bf16_round(g[b][j]) : res[b][j] + v;
-            o[j] = v;
-          }
-          *reinterpret_cast<uint4*>(p.out + (size_t)tok * p.ldo + n) = pack8(o);
-        }
-      }
-    }
-  } else if (EPI == SK_EPI_GEGLU) {
-    const int n0 = tile * 64;
-    for (int base = i0 + et; base < i1; base += kBatch * kEpiThreads) {
-      float gv[kBatch][8], uv[kBatch][8];
-#pragma unroll
-      for (int b = 0; b < kBatch; ++b) {
-        const int idx = base + b * kEpiThreads;
-        if (idx < i1) {
-          const int t = idx >> 3, r = (idx & 7) * 8;
-          src.get8(t, r, gv[b]);
-          src.get8(t, 64 + r, uv[b]);
-        }
-      }
-#pragma unroll
-      for (int b = 0; b < kBatch; ++b) {
-        const int idx = base + b * kEpiThreads;
-        if (idx < i1) {
-          const int t = idx >> 3, r = (idx & 7) * 8, tok = tok0 + t;
-          float o[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) o[j] = gelu_tanh_f(bf16_round(gv[b][j])) * uv[b][j];
-          *reinterpret_cast<uint4*>(p.out + (size_t)tok * p.ldo + n0 + r) = pack8(o);
-        }
-      }
-    }
-  } else {  // SK_EPI_QKV_ROPE
-    const int hd = p.head_dim, half = hd / 2, tph = half / 64;
-    const int n_rot_tiles = (p.n_q_heads + p.n_kv_heads) * tph;
-    if (tile < n_rot_tiles) {
-      const int h = tile / tph, part = tile % tph;
-      constexpr int kRB = 2;  // six 8-float operands per group: two groups per pass fit in registers
-      for (int base = i0 + et; base < i1; base += kRB * kEpiThreads) {
-        float lo[kRB][8], hi[kRB][8], cl[kRB][8], sl[kRB][8], ch[kRB][8], sh[kRB][8];
-#pragma unroll
-        for (int b = 0; b < kRB; ++b) {
-          const int idx = base + b * kEpiThreads;
-          if (idx < i1) {
-            const int t = idx >> 3, r = (idx & 7) * 8, tok = tok0 + t;
-            const int dl = part * 64 + r, dh = dl + half;
-            src.get8(t, r, lo[b]);
-            src.get8(t, 64 + r, hi[b]);
-            unpack8(*reinterpret_cast<const uint4*>(p.cos + (size_t)tok * hd + dl), cl[b]);
-            unpack8(*reinterpret_cast<const uint4*>(p.sin + (size_t)tok * hd + dl), sl[b]);
-            unpack8(*reinterpret_cast<const uint4*>(p.cos + (size_t)tok * hd + dh), ch[b]);
-            unpack8(*reinterpret_cast<const uint4*>(p.sin + (size_t)tok * hd + dh), sh[b]);
-          }
-        }
-#pragma unroll
-        for (int b = 0; b < kRB; ++b) {
-          const int idx = base + b * kEpiThreads;
-          if (idx < i1) {
-            const int t = idx >> 3, r = (idx & 7) * 8, tok = tok0 + t;
-            const int dl = part * 64 + r, dh = dl + half;
-            float olo[8], ohi[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float xl = bf16_round(lo[b][j]), xh = bf16_round(hi[b][j]);
-              olo[j] = xl * cl[b][j] - xh * sl[b][j];
-              ohi[j] = xh * ch[b][j] + xl * sh[b][j];
-            }
-            __nv_bfloat16* dst = (h < p.n_q_heads)
-                                     ? p.q_out + ((size_t)tok * p.n_q_heads + h) * hd
-                                     : p.k_cache + (size_t)(h - p.n_q_heads) * p.kv_head_stride +
-                                           (size_t)(p.krow0 + tok) * hd;
-            *reinterpret_cast<uint4*>(dst + dl) = pack8(olo);
-            *reinterpret_cast<uint4*>(dst + dh) = pack8(ohi);
-          }
-        }
-      }
-    } else {
-      const int vcol0 = (tile - n_rot_tiles) * kBM;  // column within the packed v heads
-      for (int base = i0 + et; base < i1; base += kBatch * kEpiThreads) {
-        float v[kBatch][8];
-#pragma unroll
-        for (int b = 0; b < kBatch; ++b) {
-          const int idx = base + b * kEpiThreads;
-          if (idx < i1) src.get8(idx >> 4, (idx & 15) * 8, v[b]);
-        }
-#pragma unroll
-        for (int b = 0; b < kBatch; ++b) {
-          const int idx = base + b * kEpiThreads;
-          if (idx < i1) {
-            const int t = idx >> 4, r = (idx & 15) * 8, tok = tok0 + t;
-            const int c = vcol0 + r, vh = c / hd, d = c % hd;
-            *reinterpret_cast<uint4*>(p.v_cache + (size_t)vh * p.kv_head_stride + (size_t)(p.krow0 + tok) * hd + d) =
-                pack8(v[b]);
-          }
-        }
-      }
-    }
-  }
-}
-
-__device__ __forceinline__ int ld_acquire(const int* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
 
 // Small-token variants are limited to 170 registers so that two CTAs fit per SM:
 // with PDL the next kernel's CTAs then become resident (and start their weight
@@ -423,7 +176,7 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
     const int items = epi_items<EPI>(p, tile, mt);
     if (ok && p.splits == 1) {
       TileSrc src{stage_tile, nullptr, 1, TOK * kBM};
-      apply_epilogue<EPI>(p, src, tile, tok0, 0, items, et);
+      apply_epilogue<EPI, 4>(p, src, tile, tok0, 0, items, et);
     } else if (ok) {
       // Deterministic split-K: publish this split's partial, wait (bounded) until
       // every split of the tile has published, then reduce a 1/splits slice of the
@@ -459,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
         TileSrc src{nullptr, part, p.splits, TOK * kBM};
         const int i0 = (int)(((long)split * items) / p.splits);
         const int i1 = (int)(((long)(split + 1) * items) / p.splits);
-        apply_epilogue<EPI>(p, src, tile, tok0, i0, i1, et);
+        apply_epilogue<EPI, 1>(p, src, tile, tok0, i0, i1, et);
       }
       named_bar_sync(1, kEpiThreads);
       if (et == 0 && atomicAdd(depart, 1) == p.splits - 1) {

@@ -31,7 +31,7 @@ class Pi05ExpertPlan(ctypes.Structure):
         ("w_in", _P), ("b_in", _P), ("w_out", _P), ("b_out", _P),
         ("rope_cos", _P), ("rope_sin", _P), ("key_valid", _P),
         ("x_t", _P), ("v_t", _P), ("h", _P), ("xn", _P), ("q", _P), ("attn", _P), ("act", _P),
-        ("workspace", _P), ("workspace_bytes", _Z), ("attn_splits", _I),
+        ("workspace", _P), ("workspace_bytes", _Z), ("attn_splits", _I), ("trace", _P),
     ]
 
 
@@ -44,6 +44,8 @@ _EXTRA = {
     "pi05_adarms_table": (_I, [_P, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _Z, _P]),
     "pi05_denoise_step": (_I, [ctypes.POINTER(Pi05ExpertPlan), _I, _P]),
     "pi05_denoise_loop": (_I, [ctypes.POINTER(Pi05ExpertPlan), _P]),
+    "pi05_denoise_loop_persistent": (_I, [ctypes.POINTER(Pi05ExpertPlan), _P]),
+    "pi05_trace_slots": (_I, []),
 }
 _lib.SIGNATURES.update(_EXTRA)
 
@@ -99,6 +101,11 @@ def adarms_table(timesteps, width, w_tin, b_tin, w_tout, b_tout, w_dense, b_dens
 def denoise_loop(plan: Pi05ExpertPlan, stream: int):
     _bind()
     _lib.call("pi05_denoise_loop", ctypes.byref(plan), stream)
+
+
+def denoise_loop_persistent(plan: Pi05ExpertPlan, stream: int):
+    _bind()
+    _lib.call("pi05_denoise_loop_persistent", ctypes.byref(plan), stream)
 
 
 def denoise_step(plan: Pi05ExpertPlan, step: int, stream: int):

@@ -33,7 +33,8 @@ def test_library_exports_every_declared_symbol():
     missing = [n for n in names if not hasattr(L, n)]
     assert not missing, missing
     # and every declared function has a ctypes signature on the Python side
-    import pi05_infer.prefix  # noqa: F401  (registers its signatures)
+    import pi05_infer.prefix  # noqa: F401  (these modules register their signatures)
+    import pi05_infer.vision  # noqa: F401
     assert not [n for n in names if n not in _lib.SIGNATURES], [n for n in names if n not in _lib.SIGNATURES]
 
 
@@ -66,7 +67,7 @@ int main(void) {
   P(Pi05ExpertPlan, depth) P(Pi05ExpertPlan, eps) P(Pi05ExpertPlan, layers) P(Pi05ExpertPlan, num_steps)
   P(Pi05ExpertPlan, host_timesteps) P(Pi05ExpertPlan, mod_table) P(Pi05ExpertPlan, key_valid)
   P(Pi05ExpertPlan, x_t) P(Pi05ExpertPlan, act) P(Pi05ExpertPlan, workspace) P(Pi05ExpertPlan, workspace_bytes)
-  P(Pi05ExpertPlan, attn_splits)
+  P(Pi05ExpertPlan, attn_splits) P(Pi05ExpertPlan, trace)
   P(Pi05PrefixLayer, ln1_w) P(Pi05PrefixLayer, v_cache)
   P(Pi05PrefixPlan, tokens) P(Pi05PrefixPlan, eps) P(Pi05PrefixPlan, layers) P(Pi05PrefixPlan, key_valid)
   P(Pi05PrefixPlan, act) P(Pi05PrefixPlan, workspace_bytes) P(Pi05PrefixPlan, kv_only_last_layer)
