@@ -155,6 +155,9 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
   int rc = action_in_run(P->x_t, P->w_in, P->b_in, h, T, P->action_dim, W, stream);
   for (int l = 0; l < P->depth && rc == PI05_OK; ++l) {
     const Pi05ExpertLayer& L = P->layers[l];
+    // The same op of the next layer (layer 0 again for the next Euler step) is
+    // prefetched into L2 by each GEMM while it runs.
+    const Pi05ExpertLayer& N = P->layers[(l + 1) % P->depth];
     const float* mod1 = mods + (size_t)(2 * l) * 3 * W;
     const float* mod2 = mods + (size_t)(2 * l + 1) * 3 * W;
     // input_layernorm (adaRMS)
@@ -163,6 +166,7 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
     // q|k|v + RoPE -> q, KV-cache tail rows [prefix_len, prefix_len + T)
     {
       SkinnyParams sp;
+      sp.trace = P->trace;
       sp.status = ws.status;
       sp.counters = ws.counters;
       sp.accum = ws.accum;
@@ -181,6 +185,9 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.n_kv_heads = HKV;
       sp.head_dim = D;
       const int rows = (HQ + 2 * HKV) * D;
+      sp.pf0 = N.w_qkv;
+      sp.pf0_bytes = (size_t)rows * W * 2;
+      sp.trace_tag = (step * P->depth + l) * 8 + 0;
       rc = skinny_gemm_run(SK_EPI_QKV_ROPE, sp, L.w_qkv, L.w_qkv, rows, rows, xn, W, split_override, stream);
       if (rc) break;
     }
@@ -205,6 +212,7 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
     // o_proj + gated residual (gate = third chunk of mod1)
     {
       SkinnyParams sp;
+      sp.trace = P->trace;
       sp.status = ws.status;
       sp.counters = ws.counters;
       sp.accum = ws.accum;
@@ -217,6 +225,9 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.resid = h;
       sp.ldr = W;
       sp.gate = mod1 + 2 * W;
+      sp.pf0 = N.w_o;
+      sp.pf0_bytes = (size_t)W * HQ * D * 2;
+      sp.trace_tag = (step * P->depth + l) * 8 + 1;
       rc = skinny_gemm_run(SK_EPI_GATED_RESID, sp, L.w_o, L.w_o, W, W, attn, HQ * D, split_override, stream);
       if (rc) break;
     }
@@ -226,6 +237,7 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
     // gate/up + GeGLU
     {
       SkinnyParams sp;
+      sp.trace = P->trace;
       sp.status = ws.status;
       sp.counters = ws.counters;
       sp.accum = ws.accum;
@@ -235,12 +247,18 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.n_tiles = F / 64;
       sp.out = act;
       sp.ldo = F;
+      sp.pf0 = N.w_gate;
+      sp.pf0_bytes = (size_t)F * W * 2;
+      sp.pf1 = N.w_up;
+      sp.pf1_bytes = (size_t)F * W * 2;
+      sp.trace_tag = (step * P->depth + l) * 8 + 2;
       rc = skinny_gemm_run(SK_EPI_GEGLU, sp, L.w_gate, L.w_up, F, F, xn, W, split_override, stream);
       if (rc) break;
     }
     // down + gated residual (gate = third chunk of mod2)
     {
       SkinnyParams sp;
+      sp.trace = P->trace;
       sp.status = ws.status;
       sp.counters = ws.counters;
       sp.accum = ws.accum;
@@ -253,6 +271,9 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.resid = h;
       sp.ldr = W;
       sp.gate = mod2 + 2 * W;
+      sp.pf0 = N.w_down;
+      sp.pf0_bytes = (size_t)W * F * 2;
+      sp.trace_tag = (step * P->depth + l) * 8 + 3;
       rc = skinny_gemm_run(SK_EPI_GATED_RESID, sp, L.w_down, L.w_down, W, W, act, F, split_override, stream);
       if (rc) break;
     }

@@ -98,6 +98,37 @@ struct TileSrc {
   }
 };
 
+// Split-K through distributed shared memory: every split CTA of the cluster holds
+// its partial tile in its own staging tile (same smem offset in every CTA); the sum
+// is taken in increasing cluster-rank order.
+struct ClusterSrc {
+  uint32_t st;  // shared::cta address of this CTA's staging tile [TOK][128] fp32
+  int splits;
+  __device__ __forceinline__ void get8(int t, int r, float* v) const {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = 0.f;
+    const uint32_t off = st + (uint32_t)(t * 128 + r) * 4u;
+    for (int s0 = 0; s0 < splits; s0 += 8) {
+      float4 a[8], b[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (s0 + j < splits) {
+          const uint32_t ra = mapa_shared(off, (uint32_t)(s0 + j));
+          a[j] = ld_dsmem_f4(ra);
+          b[j] = ld_dsmem_f4(ra + 16);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (s0 + j < splits) {
+          v[0] += a[j].x; v[1] += a[j].y; v[2] += a[j].z; v[3] += a[j].w;
+          v[4] += b[j].x; v[5] += b[j].y; v[6] += b[j].z; v[7] += b[j].w;
+        }
+      }
+    }
+  }
+};
+
 // Epilogue items are groups of 8 consecutive tile rows of one token: mt * 16
 // groups, or mt * 8 for the epilogues that pair row r with row r + 64.
 template <int EPI>
@@ -136,8 +167,8 @@ __device__ __forceinline__ uint4 pack8(const float* f) {
 // the in-place residual, which rules out compiler reordering across passes).
 // KB: groups per pass for a CTA's own staging tile; with split partials each
 // group already keeps eight splits' loads in flight, so callers pass KB = 1.
-template <int EPI, int KB>
-__device__ __forceinline__ void apply_epilogue(const SkinnyParams& p, const TileSrc& src, int tile, int tok0, int i0,
+template <int EPI, int KB, class Src>
+__device__ __forceinline__ void apply_epilogue(const SkinnyParams& p, const Src& src, int tile, int tok0, int i0,
                                                int i1, int et) {
   constexpr int kBatch = KB;
   if (EPI == SK_EPI_STORE || EPI == SK_EPI_GATED_RESID) {

@@ -26,6 +26,8 @@
 // and the o_proj / down_proj GEMMs with _gated_residual
 // (pi05_infer/gemma/modeling_gemma.py:231-249, :455-456, :138-148, :503).
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 
 #include "gemm_epilogue.cuh"
 #include "host_util.h"
@@ -38,6 +40,10 @@ namespace {
 
 using namespace gemm;
 constexpr int kThreads = 192;     // warp0 TMA, warp1 MMA/TMEM, warps2-5 epilogue
+template <int TOK, int STAGES>
+constexpr int smem_bytes() {
+  return 1024 + STAGES * (kABytes + TOK * 128) + 512;
+}
 
 // Small-token variants are limited to 170 registers so that two CTAs fit per SM:
 // with PDL the next kernel's CTAs then become resident (and start their weight
@@ -62,10 +68,12 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* accum = empty + STAGES;
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(accum + 1);
+  unsigned long long* s_stamp = reinterpret_cast<unsigned long long*>(accum + 1);  // 8-byte aligned
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(accum + 2);
   int* s_flag = reinterpret_cast<int*>(s_tmem + 1);  // [0] abort, [1] ticket
   float* stage_tile = reinterpret_cast<float*>(smem);
 
+  const uint64_t t_entry = (p.trace != nullptr) ? globaltimer_ns() : 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x / p.splits, split = blockIdx.x % p.splits;
   const int tok0 = blockIdx.y * TOK;
@@ -97,6 +105,8 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_acc = *s_tmem;
+  const uint64_t t_start = (p.trace != nullptr) ? globaltimer_ns() : 0;
+  uint64_t t_pdl = 0, t_acc = 0, t_pub = 0, t_red = 0;
   // Let the next kernel in the stream start its prologue / weight prefetch.
   pdl_launch_dependents();
 
@@ -107,6 +117,7 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
       const TileRows tr = tile_rows<EPI>(p, tile);
       const int pre = min(STAGES, nk);
       // Weights do not depend on the previous kernel: issue them before the grid-dependency wait.
+      if (p.trace != nullptr) s_stamp[0] = globaltimer_ns();
       for (int i = 0; i < pre; ++i) {
         mbar_arrive_expect_tx(&full[i], kStageBytes);
         const int kx = (kb0 + i) * kBK;
@@ -155,13 +166,30 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
       if (ok) umma_commit(accum);
     }
   } else {
-    // Epilogue warps 2..5: TMEM lane quarter = warp % 4.
+    // Epilogue warps 2..5: TMEM lane quarter = warp % 4.  While the mainloop runs,
+    // one lane spreads this CTA's share of the L2 prefetch ranges.
+    if (warp == 2 && lane == 0) {
+      const int nct = gridDim.x * gridDim.y, id = blockIdx.y * gridDim.x + blockIdx.x;
+      const void* pfs[2] = {p.pf0, p.pf1};
+      const size_t pfb[2] = {p.pf0_bytes, p.pf1_bytes};
+      for (int r = 0; r < 2; ++r) {
+        if (pfs[r] == nullptr || pfb[r] == 0) continue;
+        const size_t share = ((pfb[r] / nct) + 255) & ~size_t(255);
+        const size_t b0 = (size_t)id * share;
+        for (size_t off = b0; off < pfb[r] && off < b0 + share; off += 65536) {
+          const size_t n = min(min(share - (off - b0), pfb[r] - off), (size_t)65536);
+          if (n >= 16) prefetch_l2_bulk(static_cast<const char*>(pfs[r]) + off, (uint32_t)(n & ~size_t(15)));
+        }
+      }
+    }
     pdl_wait();
     const int q = warp & 3;
     const int row = q * 32 + lane;
     const int et = threadIdx.x - 64;
+    if (p.trace != nullptr) t_pdl = globaltimer_ns();
     const bool ok = mbar_wait(accum, 0);
     if (!ok) report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
+    if (p.trace != nullptr) t_acc = globaltimer_ns();
     tc_fence_after();
     if (ok) {
 #pragma unroll 1
@@ -177,7 +205,7 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
     if (ok && p.splits == 1) {
       TileSrc src{stage_tile, nullptr, 1, TOK * kBM};
       apply_epilogue<EPI, 4>(p, src, tile, tok0, 0, items, et);
-    } else if (ok) {
+    } else if (ok && !p.cluster) {
       // Deterministic split-K: publish this split's partial, wait (bounded) until
       // every split of the tile has published, then reduce a 1/splits slice of the
       // tile in fixed split order and apply the epilogue to it.  All CTAs of the
@@ -190,6 +218,7 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
                make_float4(stage_tile[idx], stage_tile[idx + 1], stage_tile[idx + 2], stage_tile[idx + 3]));
       __threadfence();
       named_bar_sync(1, kEpiThreads);
+      if (p.trace != nullptr) t_pub = globaltimer_ns();
       int* arrive = p.counters + 2 * tile_id;
       int* depart = arrive + 1;
       if (et == 0) {
@@ -223,6 +252,44 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
     }
   }
 
+  // Cluster split-K: every split CTA of the tile has its partial in its staging
+  // tile; after the cluster barrier each reduces its 1/splits slice by reading all
+  // peers' tiles (fixed rank order), applies the epilogue, and a second barrier
+  // keeps every staging tile alive until all peers are done reading.
+  if (p.cluster) {
+    __syncwarp();
+    cluster_sync_all();
+    if (p.trace != nullptr) t_pub = globaltimer_ns();  // (cluster path: after the first barrier)
+    if (warp >= 2) {
+      const int et = threadIdx.x - 64;
+      const int items = epi_items<EPI>(p, tile, mt);
+      const int rank = (int)cluster_ctarank();
+      ClusterSrc src{smem_u32(stage_tile), p.splits};
+      const int i0 = (int)(((long)rank * items) / p.splits);
+      const int i1 = (int)(((long)(rank + 1) * items) / p.splits);
+      apply_epilogue<EPI, 1>(p, src, tile, tok0, i0, i1, et);
+    }
+    if (p.trace != nullptr) t_red = globaltimer_ns();
+    __syncwarp();
+    cluster_sync_all();
+  }
+
+  if (p.trace != nullptr && threadIdx.x == 64) {
+    const unsigned long long slot = atomicAdd(p.trace, 1ull);
+    const unsigned long long cap = p.trace[1];  // records the buffer holds
+    if (slot < cap) {
+      unsigned long long* w = p.trace + 8 + slot * 8;
+      w[0] = ((unsigned long long)p.trace_tag << 32) | (blockIdx.y * gridDim.x + blockIdx.x);
+      w[1] = t_entry;
+      w[2] = t_start;
+      w[3] = t_pdl;
+      w[4] = t_acc;
+      w[5] = t_pub;
+      w[6] = t_red != 0 ? t_red : globaltimer_ns();
+      w[7] = s_stamp[0];
+    }
+  }
+
   // Teardown.  If the producer bailed out, the ring may still have copies in
   // flight: wait (bounded) for every armed stage before releasing shared memory.
   __syncthreads();
@@ -244,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
 template <int EPI, int TOK, int STAGES>
 int launch_one(const SkinnyParams& p, const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x,
                int tok_tiles, cudaStream_t stream) {
-  constexpr int kSmem = 1024 + STAGES * (kABytes + TOK * 128) + (2 * STAGES + 1) * 8 + 16;
+  constexpr int kSmem = smem_bytes<TOK, STAGES>();
   auto kern = skinny_gemm_kernel<EPI, TOK, STAGES>;
   static bool attr_done[16] = {false};
   int dev = 0;
@@ -257,8 +324,65 @@ int launch_one(const SkinnyParams& p, const CUtensorMap& w0, const CUtensorMap& 
     }
     attr_done[dev] = true;
   }
-  return launch_pdl(kern, dim3(p.n_tiles * p.splits, tok_tiles), dim3(kThreads), kSmem, stream, pdl_enabled(), w0,
-                    w1, x, p);
+  if (!p.cluster)
+    return launch_pdl(kern, dim3(p.n_tiles * p.splits, tok_tiles), dim3(kThreads), kSmem, stream, pdl_enabled(),
+                      w0, w1, x, p);
+  cudaLaunchConfig_t cfg;
+  std::memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(p.n_tiles * p.splits, tok_tiles);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = p.splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, w0, w1, x, p);
+  count_launch();
+  if (e != cudaSuccess) {
+    set_last_error("cluster launch failed (splits %d): %s", p.splits, cudaGetErrorString(e));
+    return PI05_ERR_LAUNCH;
+  }
+  return PI05_OK;
+}
+
+// Largest cluster size usable for this kernel instantiation on the current device
+// (queried once per device: clusters of `s` CTAs with this kernel's resources).
+template <int EPI, int TOK, int STAGES>
+int max_cluster_size() {
+  constexpr int kSmem = smem_bytes<TOK, STAGES>();
+  static int cached[16] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 16 && cached[dev]) return cached[dev];
+  auto kern = skinny_gemm_kernel<EPI, TOK, STAGES>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  int best = 1;
+  for (int s = 2; s <= 16; ++s) {
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(s * 8, 1);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = s;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0) best = s;
+    else cudaGetLastError();
+  }
+  if (dev < 16) cached[dev] = best;
+  return best;
 }
 
 int num_sms() {
@@ -293,6 +417,33 @@ int skinny_choose_splits(int n_tiles, int kb_total, int tok_tiles, int sms) {
   return best;
 }
 
+int skinny_choose_splits_cluster(int n_tiles, int kb_total, int tok_tiles, int sms, int max_cluster) {
+  // Splits reduce inside a cluster, so any number of waves is legal; minimise
+  // (waves x k-blocks per CTA) with a small cost per extra split.
+  int best = 1;
+  double best_cost = 1e30;
+  const int max_s = std::min(kb_total, max_cluster);
+  for (int s = 1; s <= max_s; ++s) {
+    const long units = (long)n_tiles * s * tok_tiles;
+    const long waves = (units + sms - 1) / sms;
+    const int kb_per = (kb_total + s - 1) / s;
+    const double cost = (double)waves * (kb_per + 1.5) + 0.15 * (s - 1);
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = s;
+    }
+  }
+  return best;
+}
+
+bool cluster_disabled() {
+  static int v = [] {
+    const char* e = getenv("PI05_CLUSTER");
+    return (e != nullptr && e[0] == '0') ? 1 : 0;
+  }();
+  return v != 0;
+}
+
 int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int w_rows0, int w_rows1,
                     const void* x, int ldx, int splits_override, void* stream) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -303,9 +454,36 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
   const int tok = p.m_tok <= 64 ? 64 : (p.m_tok <= 128 ? 128 : 256);
   const int tok_tiles = (p.m_tok + tok - 1) / tok;
   p.kb_total = (p.k + kBK - 1) / kBK;
-  p.splits = splits_override > 0 ? std::min(splits_override, p.kb_total)
-                                 : skinny_choose_splits(p.n_tiles, p.kb_total, tok_tiles, num_sms());
-  if (p.splits > 1) {
+  int max_cl = 1;
+  {
+    constexpr int S = 4;
+    switch (epi) {
+#define PI05_SK_MAXCL(E)                                                      \
+  case E:                                                                     \
+    max_cl = tok == 64    ? max_cluster_size<E, 64, 4>()                      \
+             : tok == 128 ? max_cluster_size<E, 128, S>()                     \
+                          : max_cluster_size<E, 256, 3>();                    \
+    break;
+      PI05_SK_MAXCL(SK_EPI_STORE)
+      PI05_SK_MAXCL(SK_EPI_GATED_RESID)
+      PI05_SK_MAXCL(SK_EPI_GEGLU)
+      PI05_SK_MAXCL(SK_EPI_QKV_ROPE)
+#undef PI05_SK_MAXCL
+      default:
+        break;
+    }
+  }
+  if (splits_override > 0) {
+    p.splits = std::min(splits_override, p.kb_total);
+    p.cluster = (p.splits > 1 && p.splits <= max_cl && p.accum == nullptr) ? 1 : 0;
+  } else if (max_cl > 1 && !cluster_disabled()) {
+    p.splits = skinny_choose_splits_cluster(p.n_tiles, p.kb_total, tok_tiles, num_sms(), max_cl);
+    p.cluster = p.splits > 1 ? 1 : 0;
+  } else {
+    p.splits = skinny_choose_splits(p.n_tiles, p.kb_total, tok_tiles, num_sms());
+    p.cluster = 0;
+  }
+  if (p.splits > 1 && !p.cluster) {
     const size_t need = (size_t)tok_tiles * p.n_tiles * p.splits * tok * kBM * sizeof(float);
     if ((long)tok_tiles * p.n_tiles * p.splits > num_sms()) {
       set_last_error("skinny_gemm: split grid (%d CTAs) exceeds one wave", tok_tiles * p.n_tiles * p.splits);
@@ -328,7 +506,7 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
   switch (epi) {
 #define PI05_SK_CASE(E)                                                                 \
   case E:                                                                               \
-    if (tok == 64) return launch_one<E, 64, S>(p, tw0, tw1, tx, tok_tiles, st);         \
+    if (tok == 64) return launch_one<E, 64, 4>(p, tw0, tw1, tx, tok_tiles, st);         \
     if (tok == 128) return launch_one<E, 128, S>(p, tw0, tw1, tx, tok_tiles, st);       \
     return launch_one<E, 256, 3>(p, tw0, tw1, tx, tok_tiles, st);
     PI05_SK_CASE(SK_EPI_STORE)

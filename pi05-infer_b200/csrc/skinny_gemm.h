@@ -19,6 +19,7 @@ struct SkinnyParams {
   int n_tiles = 0;   // 128-row weight tiles
   int kb_total = 0;  // set by the launcher
   int splits = 1;    // set by the launcher
+  int cluster = 0;   // set by the launcher: 1 = the splits of a tile form a cluster and reduce through DSMEM
   // STORE / GATED_RESID / GEGLU
   __nv_bfloat16* out = nullptr;
   int ldo = 0;
@@ -41,6 +42,19 @@ struct SkinnyParams {
   int n_q_heads = 0;
   int n_kv_heads = 0;
   int head_dim = 0;
+  // L2 prefetch issued by every CTA for its share of these ranges (e.g. the same
+  // op's weights of the next layer), so later launches read them from L2.
+  const void* pf0 = nullptr;
+  size_t pf0_bytes = 0;
+  const void* pf1 = nullptr;
+  size_t pf1_bytes = 0;
+  // Optional timing trace: word 0 is a slot counter, word 1 the capacity in
+  // records (records beyond it are dropped); each CTA appends 8 words at 8 + 8*slot
+  // {tag << 32 | cta, entry, after prologue, after grid-dependency wait,
+  //  accumulator ready, partial published (global split-K), epilogue done,
+  //  first weight TMA issued}.
+  unsigned long long* trace = nullptr;
+  int trace_tag = 0;
   // workspace
   float* accum = nullptr;   // fp32 split-K accumulator (zero on entry, left zero on exit)
   size_t accum_bytes = 0;
@@ -49,6 +63,9 @@ struct SkinnyParams {
 };
 
 int skinny_choose_splits(int n_tiles, int kb_total, int tok_tiles, int sms);
+int skinny_choose_splits_cluster(int n_tiles, int kb_total, int tok_tiles, int sms, int max_cluster);
+// PI05_CLUSTER=0 in the environment selects the global-memory split-K path.
+bool cluster_disabled();
 
 // w0/w1: weight matrices for the two 64-row boxes of each tile (the same matrix
 // except for GEGLU, where w0 = gate and w1 = up).  w_rows*: their row counts.
