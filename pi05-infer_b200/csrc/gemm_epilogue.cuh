@@ -98,36 +98,257 @@ struct TileSrc {
   }
 };
 
-// Split-K through distributed shared memory: every split CTA of the cluster holds
-// its partial tile in its own staging tile (same smem offset in every CTA); the sum
-// is taken in increasing cluster-rank order.
-struct ClusterSrc {
-  uint32_t st;  // shared::cta address of this CTA's staging tile [TOK][128] fp32
-  int splits;
-  __device__ __forceinline__ void get8(int t, int r, float* v) const {
+// ---------------------------------------------------------------------------
+// Split-K through distributed shared memory.  Every split CTA of a tile's cluster
+// holds its fp32 partial in its own staging tile (same shared-memory offset in
+// every CTA).  After the first cluster barrier, rank r reduces the r-th slice of
+// the tile's work units by reading all peers' partials (summed from 0.f in
+// increasing rank order, the same order as the global-memory split path) and
+// applies the epilogue.  A work unit is 4 consecutive tile rows of one token
+// (paired with the same 4 rows + 64 for GEGLU and rotary tiles), so a warp reads
+// 512 contiguous bytes of a peer's tile and writes 256 contiguous output bytes.
+// The epilogue's global operands for the first pass (residual, gate, bias,
+// position rows, cos/sin) are loaded before the barrier, and every split's DSMEM
+// load of a pass is issued before the first is consumed: one round trip per pass.
+enum ClusterKind { CK_ROWS = 0, CK_GEGLU = 1, CK_ROT = 2, CK_V = 3 };
+
+struct UnitOps {
+  float a[4], b[4], c[4], d[4];  // rows: resid/gate/bias/pos; rotary: cos_lo/sin_lo/cos_hi/sin_hi
+};
+
+__device__ __forceinline__ void load4bf(const __nv_bfloat16* src, float* f) {
+  const uint2 u = *reinterpret_cast<const uint2*>(src);
+  const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = 0.f;
-    const uint32_t off = st + (uint32_t)(t * 128 + r) * 4u;
-    for (int s0 = 0; s0 < splits; s0 += 8) {
-      float4 a[8], b[8];
+  for (int j = 0; j < 4; ++j) f[j] = __bfloat162float(b[j]);
+}
+
+__device__ __forceinline__ void load4f(const float* src, float* f) {
+  const float4 a = *reinterpret_cast<const float4*>(src);
+  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+}
+
+__device__ __forceinline__ uint2 pack4(const float* f) {
+  uint2 u;
+  __nv_bfloat16* b = reinterpret_cast<__nv_bfloat16*>(&u);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (s0 + j < splits) {
-          const uint32_t ra = mapa_shared(off, (uint32_t)(s0 + j));
-          a[j] = ld_dsmem_f4(ra);
-          b[j] = ld_dsmem_f4(ra + 16);
+  for (int j = 0; j < 4; ++j) b[j] = __float2bfloat16(f[j]);
+  return u;
+}
+
+// Unit geometry: token t and first tile row r of unit idx (tile-relative).
+template <int KIND>
+__device__ __forceinline__ void unit_pos(int idx, int& t, int& r) {
+  if (KIND == CK_GEGLU || KIND == CK_ROT) {
+    t = idx >> 4;
+    r = (idx & 15) * 4;
+  } else {
+    t = idx >> 5;
+    r = (idx & 31) * 4;
+  }
+}
+
+template <int EPI, int KIND>
+__device__ __forceinline__ bool unit_valid(const SkinnyParams& p, int tile, int idx, int u1) {
+  if (idx >= u1) return false;
+  if (KIND == CK_ROWS && p.n_valid > 0) {
+    int t, r;
+    unit_pos<KIND>(idx, t, r);
+    return tile * kBM + r < p.n_valid;
+  }
+  return true;
+}
+
+template <int EPI, int KIND>
+__device__ __forceinline__ void unit_load_ops(const SkinnyParams& p, int tile, int tok0, int idx, UnitOps& o) {
+  int t, r;
+  unit_pos<KIND>(idx, t, r);
+  const int tok = tok0 + t;
+  if (KIND == CK_ROWS) {
+    const int n = tile * kBM + r;
+    if (p.bias != nullptr) load4f(p.bias + n, o.c);
+    if (EPI == SK_EPI_STORE && p.pos != nullptr) load4f(p.pos + (size_t)(tok % p.pos_rows) * p.ldo + n, o.d);
+    if (EPI == SK_EPI_GATED_RESID) {
+      load4bf(p.resid + (size_t)tok * p.ldr + n, o.a);
+      if (p.gate != nullptr) load4f(p.gate + n, o.b);
+    }
+  } else if (KIND == CK_ROT) {
+    const int hd = p.head_dim, half = hd / 2, tph = half / 64;
+    const int dl = (tile % tph) * 64 + r, dh = dl + half;
+    load4bf(p.cos + (size_t)tok * hd + dl, o.a);
+    load4bf(p.sin + (size_t)tok * hd + dl, o.b);
+    load4bf(p.cos + (size_t)tok * hd + dh, o.c);
+    load4bf(p.sin + (size_t)tok * hd + dh, o.d);
+  }
+}
+
+// y[h][j]: the reduced tile values of rows r + 64h + j.  Same arithmetic as
+// apply_epilogue for the corresponding epilogue.
+template <int EPI, int KIND>
+__device__ __forceinline__ void unit_finish(const SkinnyParams& p, int tile, int tok0, int idx, const UnitOps& o,
+                                            const float (&y)[2][4]) {
+  int t, r;
+  unit_pos<KIND>(idx, t, r);
+  const int tok = tok0 + t;
+  if (KIND == CK_ROWS) {
+    const int n = tile * kBM + r;
+    float out[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float v = y[0][j];
+      if (p.bias != nullptr) v += o.c[j];
+      if (EPI == SK_EPI_STORE && p.pos != nullptr) v += o.d[j];
+      v = bf16_round(v);
+      if (EPI == SK_EPI_STORE && p.act == 1) v = gelu_tanh_f(v);
+      if (EPI == SK_EPI_GATED_RESID) v = (p.gate != nullptr) ? o.a[j] + v * bf16_round(o.b[j]) : o.a[j] + v;
+      out[j] = v;
+    }
+    *reinterpret_cast<uint2*>(p.out + (size_t)tok * p.ldo + n) = pack4(out);
+  } else if (KIND == CK_GEGLU) {
+    float out[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) out[j] = gelu_tanh_f(bf16_round(y[0][j])) * y[1][j];
+    *reinterpret_cast<uint2*>(p.out + (size_t)tok * p.ldo + tile * 64 + r) = pack4(out);
+  } else if (KIND == CK_ROT) {
+    const int hd = p.head_dim, half = hd / 2, tph = half / 64;
+    const int h = tile / tph, dl = (tile % tph) * 64 + r, dh = dl + half;
+    float olo[4], ohi[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float xl = bf16_round(y[0][j]), xh = bf16_round(y[1][j]);
+      olo[j] = xl * o.a[j] - xh * o.b[j];
+      ohi[j] = xh * o.c[j] + xl * o.d[j];
+    }
+    __nv_bfloat16* dst = (h < p.n_q_heads) ? p.q_out + ((size_t)tok * p.n_q_heads + h) * hd
+                                           : p.k_cache + (size_t)(h - p.n_q_heads) * p.kv_head_stride +
+                                                 (size_t)(p.krow0 + tok) * hd;
+    *reinterpret_cast<uint2*>(dst + dl) = pack4(olo);
+    *reinterpret_cast<uint2*>(dst + dh) = pack4(ohi);
+  } else {  // CK_V
+    const int hd = p.head_dim;
+    const int n_rot_tiles = (p.n_q_heads + p.n_kv_heads) * (hd / 128);
+    const int c = (tile - n_rot_tiles) * kBM + r, vh = c / hd, d = c % hd;
+    *reinterpret_cast<uint2*>(p.v_cache + (size_t)vh * p.kv_head_stride + (size_t)(p.krow0 + tok) * hd + d) =
+        pack4(y[0]);
+  }
+}
+
+// Body of the cluster epilogue for one unit kind and U units per thread per pass.
+// Called by all threads of the CTA (it holds the first cluster barrier); `epi`
+// selects the 128 epilogue threads, `et` is their index.
+template <int EPI, int KIND, int U>
+__device__ __forceinline__ void cluster_epilogue_body(const SkinnyParams& p, uint32_t st, int tile, int tok0,
+                                                      int u0, int u1, int et, bool epi) {
+  constexpr int H = (KIND == CK_GEGLU || KIND == CK_ROT) ? 2 : 1;
+  constexpr int KS = 16 / (U * H) > 0 ? 16 / (U * H) : 1;  // splits per batch of DSMEM loads
+  const int splits = p.splits;
+  UnitOps ops[U];
+  if (epi) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int idx = u0 + u * kEpiThreads + et;
+      if (unit_valid<EPI, KIND>(p, tile, idx, u1)) unit_load_ops<EPI, KIND>(p, tile, tok0, idx, ops[u]);
+    }
+  }
+  __syncwarp();
+  cluster_sync_all();
+  if (!epi) return;
+  for (int base = u0 + et, pass = 0; base < u1; base += U * kEpiThreads, ++pass) {
+    bool ok[U];
+    uint32_t off[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int idx = base + u * kEpiThreads;
+      ok[u] = unit_valid<EPI, KIND>(p, tile, idx, u1);
+      int t, r;
+      unit_pos<KIND>(idx, t, r);
+      off[u] = (uint32_t)(t * kBM + r) * 4u;
+      if (pass > 0 && ok[u]) unit_load_ops<EPI, KIND>(p, tile, tok0, idx, ops[u]);
+    }
+    float acc[U][H][4];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+      for (int h = 0; h < H; ++h)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[u][h][j] = 0.f;
+    for (int s0 = 0; s0 < splits; s0 += KS) {
+      float4 v[KS][U][H];
+#pragma unroll
+      for (int k = 0; k < KS; ++k) {
+        if (s0 + k < splits) {
+          const uint32_t peer = mapa_shared(st, (uint32_t)(s0 + k));
+#pragma unroll
+          for (int u = 0; u < U; ++u)
+            if (ok[u])
+#pragma unroll
+              for (int h = 0; h < H; ++h) v[k][u][h] = ld_dsmem_f4(peer + off[u] + h * 256u);
         }
       }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (s0 + j < splits) {
-          v[0] += a[j].x; v[1] += a[j].y; v[2] += a[j].z; v[3] += a[j].w;
-          v[4] += b[j].x; v[5] += b[j].y; v[6] += b[j].z; v[7] += b[j].w;
+      for (int k = 0; k < KS; ++k) {
+        if (s0 + k < splits) {
+#pragma unroll
+          for (int u = 0; u < U; ++u)
+#pragma unroll
+            for (int h = 0; h < H; ++h) {
+              acc[u][h][0] += v[k][u][h].x;
+              acc[u][h][1] += v[k][u][h].y;
+              acc[u][h][2] += v[k][u][h].z;
+              acc[u][h][3] += v[k][u][h].w;
+            }
         }
       }
     }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (!ok[u]) continue;
+      float y[2][4];
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) y[h][j] = acc[u][h < H ? h : 0][j];
+      unit_finish<EPI, KIND>(p, tile, tok0, base + u * kEpiThreads, ops[u], y);
+    }
   }
-};
+}
+
+template <int EPI, int KIND>
+__device__ __forceinline__ void cluster_epilogue_kind(const SkinnyParams& p, uint32_t st, int tile, int tok0, int mt,
+                                                      int rank, int et, bool epi) {
+  constexpr int H = (KIND == CK_GEGLU || KIND == CK_ROT) ? 2 : 1;
+  const int units = mt * (H == 2 ? 16 : 32);
+  const int u0 = (int)(((long)rank * units) / p.splits);
+  const int u1 = (int)(((long)(rank + 1) * units) / p.splits);
+  const int per_thread = (u1 - u0 + kEpiThreads - 1) / kEpiThreads;
+  if (per_thread >= 4 && p.splits * H * 4 <= 16)
+    cluster_epilogue_body<EPI, KIND, 4>(p, st, tile, tok0, u0, u1, et, epi);
+  else if (per_thread >= 2 && p.splits * H * 2 <= 16)
+    cluster_epilogue_body<EPI, KIND, 2>(p, st, tile, tok0, u0, u1, et, epi);
+  else
+    cluster_epilogue_body<EPI, KIND, 1>(p, st, tile, tok0, u0, u1, et, epi);
+}
+
+// Whole cluster split-K epilogue (both cluster barriers included); every thread of
+// the CTA calls it.  The second barrier keeps each staging tile alive until all
+// peers have finished reading it.
+template <int EPI>
+__device__ __forceinline__ void cluster_epilogue(const SkinnyParams& p, uint32_t st, int tile, int tok0, int mt,
+                                                 int rank, int et, bool epi) {
+  if (EPI == SK_EPI_GEGLU) {
+    cluster_epilogue_kind<EPI, CK_GEGLU>(p, st, tile, tok0, mt, rank, et, epi);
+  } else if (EPI == SK_EPI_QKV_ROPE) {
+    const int n_rot_tiles = (p.n_q_heads + p.n_kv_heads) * (p.head_dim / 128);
+    if (tile < n_rot_tiles)
+      cluster_epilogue_kind<EPI, CK_ROT>(p, st, tile, tok0, mt, rank, et, epi);
+    else
+      cluster_epilogue_kind<EPI, CK_V>(p, st, tile, tok0, mt, rank, et, epi);
+  } else {
+    cluster_epilogue_kind<EPI, CK_ROWS>(p, st, tile, tok0, mt, rank, et, epi);
+  }
+  __syncwarp();
+  cluster_sync_all();
+}
 
 // Epilogue items are groups of 8 consecutive tile rows of one token: mt * 16
 // groups, or mt * 8 for the epilogues that pair row r with row r + 64.

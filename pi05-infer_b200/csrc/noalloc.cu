@@ -107,6 +107,7 @@ extern "C" int pi05_gate_up_geglu_noalloc(const void* x, const void* wg, const v
   p.n_tiles = n / 64;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.ldo = n;
+  p.allow_cluster = 0;  // partials go through the built-in scratch
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

@@ -253,25 +253,13 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
   }
 
   // Cluster split-K: every split CTA of the tile has its partial in its staging
-  // tile; after the cluster barrier each reduces its 1/splits slice by reading all
-  // peers' tiles (fixed rank order), applies the epilogue, and a second barrier
-  // keeps every staging tile alive until all peers are done reading.
+  // tile; cluster_epilogue reduces this rank's slice through DSMEM and applies the
+  // epilogue between its two cluster barriers.
   if (p.cluster) {
     __syncwarp();
-    cluster_sync_all();
-    if (p.trace != nullptr) t_pub = globaltimer_ns();  // (cluster path: after the first barrier)
-    if (warp >= 2) {
-      const int et = threadIdx.x - 64;
-      const int items = epi_items<EPI>(p, tile, mt);
-      const int rank = (int)cluster_ctarank();
-      ClusterSrc src{smem_u32(stage_tile), p.splits};
-      const int i0 = (int)(((long)rank * items) / p.splits);
-      const int i1 = (int)(((long)(rank + 1) * items) / p.splits);
-      apply_epilogue<EPI, 1>(p, src, tile, tok0, i0, i1, et);
-    }
+    cluster_epilogue<EPI>(p, smem_u32(stage_tile), tile, tok0, mt, (int)cluster_ctarank(), (int)threadIdx.x - 64,
+                          warp >= 2);
     if (p.trace != nullptr) t_red = globaltimer_ns();
-    __syncwarp();
-    cluster_sync_all();
   }
 
   if (p.trace != nullptr && threadIdx.x == 64) {
@@ -473,10 +461,11 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
         break;
     }
   }
+  const bool use_cluster = p.allow_cluster != 0 && max_cl > 1 && !cluster_disabled();
   if (splits_override > 0) {
     p.splits = std::min(splits_override, p.kb_total);
-    p.cluster = (p.splits > 1 && p.splits <= max_cl && p.accum == nullptr) ? 1 : 0;
-  } else if (max_cl > 1 && !cluster_disabled()) {
+    p.cluster = (use_cluster && p.splits > 1 && p.splits <= max_cl) ? 1 : 0;
+  } else if (use_cluster) {
     p.splits = skinny_choose_splits_cluster(p.n_tiles, p.kb_total, tok_tiles, num_sms(), max_cl);
     p.cluster = p.splits > 1 ? 1 : 0;
   } else {

@@ -20,6 +20,7 @@ struct SkinnyParams {
   int kb_total = 0;  // set by the launcher
   int splits = 1;    // set by the launcher
   int cluster = 0;   // set by the launcher: 1 = the splits of a tile form a cluster and reduce through DSMEM
+  int allow_cluster = 1;  // 0 = split-K only through the global accumulator
   // STORE / GATED_RESID / GEGLU
   __nv_bfloat16* out = nullptr;
   int ldo = 0;
