@@ -53,6 +53,11 @@ long long pi05_launch_count(void);
  * (0 = automatic).  Process-wide. */
 void pi05_debug_set_splits(int splits);
 
+/* Profiling hook: device buffer that the GEMM ops called through this header
+ * append per-CTA timestamp records to (word 0: record counter, word 1: capacity
+ * in records; record i at words 8 + 8 i).  NULL disables.  Process-wide. */
+void pi05_debug_set_trace(unsigned long long* buf);
+
 /* ---- fused denoise ops (swap-AB tcgen05 GEMM + fused epilogue) ---------- */
 
 /* out[m, n] = gelu_tanh(bf16(x @ wg^T)) * (x @ wu^T), bf16.

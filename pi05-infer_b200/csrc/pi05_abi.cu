@@ -12,6 +12,7 @@ using namespace pi05;
 namespace {
 
 std::atomic<int> g_split_override{0};
+std::atomic<unsigned long long*> g_trace{nullptr};
 
 inline bool nz(const void* p) { return p != nullptr; }
 
@@ -26,6 +27,7 @@ int ws_for_skinny(void* ws, size_t bytes, SkinnyParams* p) {
   p->counters = w.counters;
   p->accum = w.accum;
   p->accum_bytes = w.accum_bytes;
+  p->trace = g_trace.load();
   return PI05_OK;
 }
 
@@ -75,6 +77,8 @@ int pi05_read_device_status(void* workspace, int* host_status, void* stream) {
 long long pi05_launch_count(void) { return launch_count(); }
 
 void pi05_debug_set_splits(int splits) { g_split_override.store(std::max(0, splits)); }
+
+void pi05_debug_set_trace(unsigned long long* buf) { g_trace.store(buf); }
 
 int pi05_gate_up_geglu(const void* x, const void* wg, const void* wu, void* out, int m, int n, int k,
                        void* workspace, size_t workspace_bytes, void* stream) {

@@ -33,6 +33,7 @@
 #include "host_util.h"
 #include "ptx.cuh"
 #include "skinny_gemm.h"
+#include "wide_gemm.h"
 
 namespace pi05 {
 
@@ -438,6 +439,17 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
   if (p.m_tok <= 0 || p.k <= 0 || p.k % 8 != 0 || p.n_tiles <= 0 || (p.n_valid % 8) != 0) {
     set_last_error("skinny_gemm: bad shape m=%d k=%d tiles=%d", p.m_tok, p.k, p.n_tiles);
     return PI05_ERR_SHAPE;
+  }
+  if (p.m_tok >= kWideMinTokens && !wide_disabled()) {
+    int n_cols = 0;
+    if (epi == SK_EPI_GEGLU)
+      n_cols = p.n_tiles * 64;
+    else if (epi == SK_EPI_QKV_ROPE)
+      n_cols = (p.n_q_heads + 2 * p.n_kv_heads) * p.head_dim;
+    else
+      n_cols = p.n_valid > 0 ? p.n_valid : p.n_tiles * kBM;
+    if (epi != SK_EPI_QKV_ROPE || p.head_dim == 256)
+      return wide_gemm_run(epi, p, w0, w1, w_rows0, w_rows1, n_cols, x, ldx, stream);
   }
   const int tok = p.m_tok <= 64 ? 64 : (p.m_tok <= 128 ? 128 : 256);
   const int tok_tiles = (p.m_tok + tok - 1) / tok;

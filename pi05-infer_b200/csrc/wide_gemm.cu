@@ -1,0 +1,700 @@
+// Persistent tcgen05 GEMM for the many-token projections (prefix LM: 968 tokens,
+// SigLIP: 256 patches per view, batched denoise at M > 128).
+//
+//   Y[t, n] = sum_k X[t, k] * W[n, k]
+//
+// Tokens fill the UMMA M dimension (128 rows per tile) and BN weight rows the N
+// dimension (BN = 128 or 256), so TMEM lane r holds token r's BN outputs.
+//
+// One CTA per SM loops over output tiles (m fastest, so the CTAs resident at a
+// time share weight tiles in L2):
+//   warp 0      TMA producer: X box 128x64 + two W boxes (BN/2)x64 per k-block
+//               into a STAGES-deep ring (128-byte swizzle);
+//   warp 1      TMEM owner + MMA issuer: 4 x tcgen05.mma (128 x BN x 16) per
+//               k-block into one of two TMEM accumulators (2 x BN columns);
+//   warps 2..5  epilogue on the accumulator the MMA warp has finished, while it
+//               fills the other one.
+//
+// Epilogue: each epilogue warp owns 32 token rows (its TMEM lane quarter) and
+// works in 64-column slabs (32 rows x 128 B).  A thread reads its row from TMEM,
+// applies the fused epilogue and writes the bf16 result into a 128B-swizzled
+// slab in shared memory; one lane then stores the slab with a TMA tensor store.
+// Row-wise operands (the residual, the RoPE cos/sin rows) arrive the same way,
+// by TMA loads into the slab, the first one issued while the mainloop still
+// runs.  Every global access of the epilogue is therefore a whole 32x64 box
+// instead of 16-byte pieces of 32 different rows, and rows past the token
+// count are clipped by the tensor maps.
+//
+// The two W boxes of a tile are what lets one tile carry the rows an epilogue
+// combines (the same pairing as the small-token kernel):
+//   GEGLU     : 128 rows of W_gate + the same 128 rows of W_up (BN = 256)
+//   QKV_ROPE  : one 256-dim head; columns d and d + 128 are RoPE pairs
+//   STORE / GATED_RESID : BN consecutive rows.
+//
+// Reference ops replaced: the prefix-LM projections of
+// pi05_infer/gemma/modeling_gemma.py (GemmaAttention / GemmaMLP forward, :231-249,
+// :455-456, :138-148) with the fused QKV+RoPE of prefix_qkv_fused.py:220-246, and
+// the SigLIP encoder projections (pi05_infer/siglip/modeling_siglip.py: patch
+// embedding, attention in/out projections, MLP fc1/fc2).
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+
+#include "gemm_epilogue.cuh"
+#include "host_util.h"
+#include "ptx.cuh"
+#include "skinny_gemm.h"
+#include "wide_gemm.h"
+
+namespace pi05 {
+
+namespace {
+
+using namespace gemm;
+constexpr int kWThreads = 192;
+constexpr int kWBM = 128;         // tokens per tile
+constexpr int kSlabBytes = 4096;  // 32 rows x 64 bf16, 128B swizzle
+
+// Epilogue slabs per warp: QKV keeps cos/sin lo/hi of one 64-column chunk
+// (4 slabs); the others double-buffer one slab.
+template <int EPI>
+constexpr int epi_slabs() {
+  return EPI == SK_EPI_QKV_ROPE ? 4 : 2;
+}
+
+template <int EPI, int BN, int STAGES>
+constexpr int wide_smem_bytes() {
+  return 1024 + STAGES * (kABytes + BN * 128) + 4 * epi_slabs<EPI>() * kSlabBytes + 256;
+}
+
+struct WideSched {
+  int m_tiles;
+  int n_tiles;
+  int kb_total;
+};
+
+// Tensor maps of one launch.  out: STORE / GATED_RESID / GEGLU output, or q_out
+// for QKV_ROPE.  in0 / in1: residual (GATED_RESID) or cos / sin (QKV_ROPE).
+// kc / vc: the K and V cache rows [0, krow0 + m_tok) (QKV_ROPE).  All epilogue
+// maps use 32 x 64 boxes with the 128-byte swizzle.
+struct WideMaps {
+  CUtensorMap x, w0, w1;
+  CUtensorMap out, in0, in1, kc, vc;
+};
+
+// First weight row of each of the tile's two (BN/2)-row boxes.
+template <int EPI, int BN>
+__device__ __forceinline__ void wide_rows(int n_tile, int& row0, int& row1) {
+  if (EPI == SK_EPI_GEGLU) {
+    row0 = n_tile * (BN / 2);
+    row1 = row0;
+  } else {
+    row0 = n_tile * BN;
+    row1 = row0 + BN / 2;
+  }
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_normal() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// Byte offset of 16-byte chunk g (8 bf16 columns) of row r in a 128B-swizzled slab.
+__device__ __forceinline__ uint32_t slab_off(int r, int g) { return (uint32_t)(r * 128 + ((g ^ (r & 7)) << 4)); }
+
+__device__ __forceinline__ uint4 lds16(const uint8_t* slab, int r, int g) {
+  return *reinterpret_cast<const uint4*>(slab + slab_off(r, g));
+}
+
+__device__ __forceinline__ void sts16(uint8_t* slab, int r, int g, uint4 v) {
+  *reinterpret_cast<uint4*>(slab + slab_off(r, g)) = v;
+}
+
+// One warp's epilogue state: its 32-row quarter, slabs, slab barriers and the
+// phase of each slab barrier (warp-uniform).
+struct EpiWarp {
+  int q;          // TMEM lane quarter: rows q*32 .. q*32+31 of the tile
+  int lane;
+  uint8_t* slab;  // epi_slabs<EPI>() consecutive slabs
+  uint64_t* bar;  // one barrier per double-buffered slab (QKV uses [0] only)
+  uint32_t phase; // bit i: parity of the next completion of bar[i]
+};
+
+__device__ __forceinline__ uint8_t* slab_at(const EpiWarp& e, int i) { return e.slab + i * kSlabBytes; }
+
+// Issue (lane 0) the loads of the row operands the tile needs before its
+// accumulator is read: residual slab 0, or RoPE cos/sin lo/hi of chunk 0.
+template <int EPI, int BN>
+__device__ __forceinline__ void wide_epi_prefetch(const SkinnyParams& p, const WideMaps& mp, EpiWarp& e, int n_tile,
+                                                  int m0) {
+  if (e.lane != 0) return;
+  if (EPI == SK_EPI_GATED_RESID) {
+    bulk_wait_group_read<0>();
+    mbar_arrive_expect_tx(&e.bar[0], kSlabBytes);
+    tma_load_2d(slab_at(e, 0), &mp.in0, &e.bar[0], n_tile * BN, m0 + e.q * 32, l2_policy_evict_normal());
+  } else if (EPI == SK_EPI_QKV_ROPE) {
+    if (n_tile < p.n_q_heads + p.n_kv_heads) {
+      const uint64_t pol = l2_policy_evict_last();
+      bulk_wait_group_read<0>();
+      mbar_arrive_expect_tx(&e.bar[0], 4 * kSlabBytes);
+      const int y = m0 + e.q * 32;
+      tma_load_2d(slab_at(e, 0), &mp.in0, &e.bar[0], 0, y, pol);
+      tma_load_2d(slab_at(e, 1), &mp.in1, &e.bar[0], 0, y, pol);
+      tma_load_2d(slab_at(e, 2), &mp.in0, &e.bar[0], 128, y, pol);
+      tma_load_2d(slab_at(e, 3), &mp.in1, &e.bar[0], 128, y, pol);
+    }
+  }
+}
+
+__device__ __forceinline__ bool slab_wait(EpiWarp& e, int i, int* status) {
+  const bool ok = mbar_wait(&e.bar[i], (e.phase >> i) & 1u);
+  e.phase ^= 1u << i;
+  if (!ok) report_status(status, PI05_DEV_TIMEOUT_EPILOGUE);
+  return ok;
+}
+
+// Finish the slab: make the smem writes visible to TMA, store it, commit.
+__device__ __forceinline__ void slab_store(const EpiWarp& e, const CUtensorMap* tm, const uint8_t* slab, int x,
+                                           int y) {
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (e.lane == 0) {
+    tma_store_2d(tm, slab, x, y);
+    bulk_commit_group();
+  }
+}
+
+// STORE / GATED_RESID (same arithmetic as apply_epilogue).
+template <int EPI, int BN>
+__device__ __forceinline__ bool wide_epi_rows(const SkinnyParams& p, const WideMaps& mp, EpiWarp& e, uint32_t taddr,
+                                              int n_tile, int m0) {
+  constexpr int NS = BN / 64;
+  const int r = e.lane;
+  const int tok = m0 + e.q * 32 + r;
+  const int n_valid = p.n_valid > 0 ? p.n_valid : 1 << 30;
+  bool ok = true;
+#pragma unroll 1
+  for (int j = 0; j < NS; ++j) {
+    const int b = j & 1;
+    uint8_t* slab = slab_at(e, b);
+    if (EPI == SK_EPI_GATED_RESID) {
+      if (j + 1 < NS && e.lane == 0) {  // next residual slab into the other buffer
+        bulk_wait_group_read<0>();
+        mbar_arrive_expect_tx(&e.bar[b ^ 1], kSlabBytes);
+        tma_load_2d(slab_at(e, b ^ 1), &mp.in0, &e.bar[b ^ 1], n_tile * BN + (j + 1) * 64, m0 + e.q * 32,
+                    l2_policy_evict_normal());
+      }
+    } else {
+      if (e.lane == 0) bulk_wait_group_read<1>();  // this buffer's previous store has read it
+      __syncwarp();
+    }
+#pragma unroll 1
+    for (int h = 0; h < 2; ++h) {
+      float v[32];
+      tmem_ld32(taddr + j * 64 + h * 32, v);
+      if (EPI == SK_EPI_GATED_RESID && h == 0) ok = slab_wait(e, b, p.status) && ok;
+#pragma unroll
+      for (int g4 = 0; g4 < 4; ++g4) {
+        const int g = h * 4 + g4;
+        const int n = n_tile * BN + j * 64 + g * 8;
+        const bool in = n < n_valid;
+        float bi[8], ps[8], gt[8], rs[8];
+        if (p.bias != nullptr && in) load8f(p.bias + n, bi);
+        if (EPI == SK_EPI_STORE && p.pos != nullptr && in) load8f(p.pos + (size_t)(tok % p.pos_rows) * p.ldo + n, ps);
+        if (EPI == SK_EPI_GATED_RESID) {
+          unpack8(lds16(slab, r, g), rs);
+          if (p.gate != nullptr && in) load8f(p.gate + n, gt);
+        }
+        float o[8];
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          float y = v[g4 * 8 + jj];
+          if (p.bias != nullptr && in) y += bi[jj];
+          if (EPI == SK_EPI_STORE && p.pos != nullptr && in) y += ps[jj];
+          y = bf16_round(y);
+          if (EPI == SK_EPI_STORE && p.act == 1) y = gelu_tanh_f(y);
+          if (EPI == SK_EPI_GATED_RESID) y = (p.gate != nullptr && in) ? rs[jj] + y * bf16_round(gt[jj]) : rs[jj] + y;
+          o[jj] = y;
+        }
+        sts16(slab, r, g, pack8(o));
+      }
+    }
+    slab_store(e, &mp.out, slab, n_tile * BN + j * 64, m0 + e.q * 32);
+  }
+  return ok;
+}
+
+// GEGLU: TMEM columns [0, 128) are gate rows, [128, 256) the matching up rows.
+__device__ __forceinline__ void wide_epi_geglu(const WideMaps& mp, EpiWarp& e, uint32_t taddr, int n_tile, int m0) {
+  const int r = e.lane;
+#pragma unroll 1
+  for (int j = 0; j < 2; ++j) {
+    uint8_t* slab = slab_at(e, j);
+    if (e.lane == 0) bulk_wait_group_read<1>();
+    __syncwarp();
+#pragma unroll 1
+    for (int h = 0; h < 2; ++h) {
+      float g[32], u[32];
+      tmem_ld32(taddr + j * 64 + h * 32, g);
+      tmem_ld32(taddr + 128 + j * 64 + h * 32, u);
+#pragma unroll
+      for (int g4 = 0; g4 < 4; ++g4) {
+        float o[8];
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) o[jj] = gelu_tanh_f(bf16_round(g[g4 * 8 + jj])) * u[g4 * 8 + jj];
+        sts16(slab, r, h * 4 + g4, pack8(o));
+      }
+    }
+    slab_store(e, &mp.out, slab, n_tile * 128 + j * 64, m0 + e.q * 32);
+  }
+}
+
+// QKV_ROPE, one 256-dim head per tile (n_kv_heads == 1): q / k heads are rotated
+// (pairs d, d + 128) into q_out / the K cache; the v head is copied to the V cache.
+__device__ __forceinline__ bool wide_epi_qkv(const SkinnyParams& p, const WideMaps& mp, EpiWarp& e, uint32_t taddr,
+                                             int head, int m0) {
+  const int r = e.lane;
+  const int y_q = m0 + e.q * 32;
+  const int y_kv = p.krow0 + m0 + e.q * 32;
+  bool ok = true;
+  if (head < p.n_q_heads + p.n_kv_heads) {
+    const bool is_q = head < p.n_q_heads;
+    const CUtensorMap* dst = is_q ? &mp.out : &mp.kc;
+    const int x0 = is_q ? head * 256 : 0;
+    const int y = is_q ? y_q : y_kv;
+    uint8_t* s_cl = slab_at(e, 0);
+    uint8_t* s_sl = slab_at(e, 1);
+    uint8_t* s_ch = slab_at(e, 2);
+    uint8_t* s_sh = slab_at(e, 3);
+#pragma unroll 1
+    for (int c = 0; c < 2; ++c) {
+      if (c == 1 && e.lane == 0) {  // chunk 1's cos/sin once chunk 0's stores have read the slabs
+        const uint64_t pol = l2_policy_evict_last();
+        bulk_wait_group_read<0>();
+        mbar_arrive_expect_tx(&e.bar[0], 4 * kSlabBytes);
+        tma_load_2d(s_cl, &mp.in0, &e.bar[0], 64, y_q, pol);
+        tma_load_2d(s_sl, &mp.in1, &e.bar[0], 64, y_q, pol);
+        tma_load_2d(s_ch, &mp.in0, &e.bar[0], 192, y_q, pol);
+        tma_load_2d(s_sh, &mp.in1, &e.bar[0], 192, y_q, pol);
+      }
+      ok = slab_wait(e, 0, p.status) && ok;
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        float lo[32], hi[32];
+        tmem_ld32(taddr + c * 64 + h * 32, lo);
+        tmem_ld32(taddr + 128 + c * 64 + h * 32, hi);
+#pragma unroll
+        for (int g4 = 0; g4 < 4; ++g4) {
+          const int g = h * 4 + g4;
+          float cl[8], sl[8], ch[8], sh[8], olo[8], ohi[8];
+          unpack8(lds16(s_cl, r, g), cl);
+          unpack8(lds16(s_sl, r, g), sl);
+          unpack8(lds16(s_ch, r, g), ch);
+          unpack8(lds16(s_sh, r, g), sh);
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) {
+            const float xl = bf16_round(lo[g4 * 8 + jj]), xh = bf16_round(hi[g4 * 8 + jj]);
+            olo[jj] = xl * cl[jj] - xh * sl[jj];
+            ohi[jj] = xh * ch[jj] + xl * sh[jj];
+          }
+          // Each thread overwrites only its own row's chunks, which it has just read.
+          sts16(s_cl, r, g, pack8(olo));
+          sts16(s_ch, r, g, pack8(ohi));
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (e.lane == 0) {
+        tma_store_2d(dst, s_cl, x0 + c * 64, y);
+        tma_store_2d(dst, s_ch, x0 + 128 + c * 64, y);
+        bulk_commit_group();
+      }
+    }
+  } else {
+    if (e.lane == 0) bulk_wait_group_read<0>();
+    __syncwarp();
+#pragma unroll 1
+    for (int j = 0; j < 4; ++j) {
+      uint8_t* slab = slab_at(e, j & 1);
+      if (j > 1) {
+        if (e.lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+      }
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        float v[32];
+        tmem_ld32(taddr + j * 64 + h * 32, v);
+#pragma unroll
+        for (int g4 = 0; g4 < 4; ++g4) sts16(slab, r, h * 4 + g4, pack8(v + g4 * 8));
+      }
+      slab_store(e, &mp.vc, slab, j * 64, y_kv);
+    }
+  }
+  return ok;
+}
+
+template <int EPI, int BN, int STAGES>
+__global__ void __launch_bounds__(kWThreads, 1)
+    wide_gemm_kernel(const __grid_constant__ WideMaps mp, const SkinnyParams p, const WideSched ws) {
+  constexpr int kBBytes = BN * 128;
+  constexpr int kStageBytes = kABytes + kBBytes;
+  constexpr uint32_t kTmemCols = 2 * BN;
+  constexpr uint32_t kIdesc = umma_idesc_bf16(kWBM, BN);
+  constexpr int kSlabs = epi_slabs<EPI>();
+  static_assert(BN == 128 || BN == 256, "tile width");
+  static_assert((EPI != SK_EPI_GEGLU && EPI != SK_EPI_QKV_ROPE) || BN == 256, "paired epilogues use BN = 256");
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * kABytes;
+  uint8_t* sEpi = smem + STAGES * kStageBytes;  // 4 warps x kSlabs slabs, 1024-aligned
+  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + 4 * kSlabs * kSlabBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accf = empty + STAGES;  // [2] accumulator ready (MMA commit)
+  uint64_t* acce = accf + 2;        // [2] accumulator drained (128 epilogue arrivals)
+  uint64_t* mdone = acce + 2;       // all MMAs of this CTA complete
+  uint64_t* sbar = mdone + 1;       // [4 warps][2] epilogue slab loads
+  unsigned long long* s_stamp = reinterpret_cast<unsigned long long*>(sbar + 8);  // [2] trace
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(s_stamp + 2);
+  int* s_flag = reinterpret_cast<int*>(s_tmem + 1);  // [0] abort, [2] k-blocks armed
+
+  const uint64_t t_entry = (p.trace != nullptr) ? globaltimer_ns() : 0;
+  uint64_t t_setup = 0, t_acc = 0, t_epi = 0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int total = ws.m_tiles * ws.n_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], kEpiThreads);
+    }
+    mbar_init(mdone, 1);
+    for (int i = 0; i < 8; ++i) mbar_init(&sbar[i], 1);
+    s_flag[0] = 0;
+    s_flag[2] = 0;
+    s_stamp[0] = 0;
+    s_stamp[1] = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&mp.x);
+    prefetch_tmap(&mp.w0);
+    prefetch_tmap(&mp.w1);
+  }
+  if (warp == 2 && lane == 0) {
+    prefetch_tmap(&mp.out);
+    if (EPI == SK_EPI_GATED_RESID || EPI == SK_EPI_QKV_ROPE) prefetch_tmap(&mp.in0);
+    if (EPI == SK_EPI_QKV_ROPE) {
+      prefetch_tmap(&mp.in1);
+      prefetch_tmap(&mp.kc);
+      prefetch_tmap(&mp.vc);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(s_tmem, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+  if (p.trace != nullptr) t_setup = globaltimer_ns();
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol_w = l2_policy_evict_normal();
+      const uint64_t pol_x = l2_policy_evict_last();
+      int it = 0;
+      bool waited = false;
+      for (int t = blockIdx.x; t < total; t += gridDim.x) {
+        const int m = t % ws.m_tiles, n = t / ws.m_tiles;
+        int row0, row1;
+        wide_rows<EPI, BN>(n, row0, row1);
+        // First tile: weights do not depend on the previous kernel, so the first
+        // ring's worth of W boxes is issued before the grid-dependency wait.
+        int kb = 0;
+        if (!waited) {
+          const int pre = min(STAGES, ws.kb_total);
+          for (int i = 0; i < pre; ++i) {
+            mbar_arrive_expect_tx(&full[i], kStageBytes);
+            tma_load_2d(sB + i * kBBytes, &mp.w0, &full[i], i * kBK, row0, pol_w);
+            tma_load_2d(sB + i * kBBytes + kBBytes / 2, &mp.w1, &full[i], i * kBK, row1, pol_w);
+          }
+          pdl_wait();
+          waited = true;
+          if (p.trace != nullptr) s_stamp[0] = globaltimer_ns();
+          for (int i = 0; i < pre; ++i) tma_load_2d(sA + i * kABytes, &mp.x, &full[i], i * kBK, m * kWBM, pol_x);
+          kb = pre;
+          it = pre;
+        }
+        for (; kb < ws.kb_total; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1)) {
+            report_status(p.status, PI05_DEV_TIMEOUT_PRODUCER);
+            s_flag[0] = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], kStageBytes);
+          tma_load_2d(sB + s * kBBytes, &mp.w0, &full[s], kb * kBK, row0, pol_w);
+          tma_load_2d(sB + s * kBBytes + kBBytes / 2, &mp.w1, &full[s], kb * kBK, row1, pol_w);
+          tma_load_2d(sA + s * kABytes, &mp.x, &full[s], kb * kBK, m * kWBM, pol_x);
+        }
+        if (s_flag[0] != 0) break;
+      }
+      if (!waited) pdl_wait();
+      s_flag[2] = it;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int it = 0, lt = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++lt) {
+        const int buf = lt & 1;
+        if (!mbar_wait(&acce[buf], ((lt >> 1) & 1) ^ 1)) {
+          report_status(p.status, PI05_DEV_TIMEOUT_MMA);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (p.trace != nullptr && lt == 0) s_stamp[1] = globaltimer_ns();
+        const uint32_t d = tmem + (uint32_t)(buf * BN);
+        for (int kb = 0; kb < ws.kb_total; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(&full[s], (it / STAGES) & 1)) {
+            report_status(p.status, PI05_DEV_TIMEOUT_MMA);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + s * kABytes);
+          const uint32_t b0 = smem_u32(sB + s * kBBytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            umma_bf16(d, umma_sdesc_sw128(a0 + kk * 32), umma_sdesc_sw128(b0 + kk * 32), kIdesc,
+                      (kb > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(&accf[buf]);
+      }
+      if (!ok) s_flag[0] = 1;
+      // Every MMA issued by this thread has completed once mdone fires.
+      umma_commit(mdone);
+      if (!mbar_wait(mdone, 0)) report_status(p.status, PI05_DEV_TIMEOUT_DRAIN);
+    }
+  } else {
+    // Epilogue warps 2..5: TMEM lane quarter = warp % 4, one token row per thread.
+    pdl_wait();
+    EpiWarp e;
+    e.q = warp & 3;
+    e.lane = lane;
+    e.slab = sEpi + (warp - 2) * kSlabs * kSlabBytes;
+    e.bar = sbar + (warp - 2) * 2;
+    e.phase = 0;
+    int lt = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++lt) {
+      const int m = t % ws.m_tiles, n = t / ws.m_tiles;
+      const int buf = lt & 1;
+      wide_epi_prefetch<EPI, BN>(p, mp, e, n, m * kWBM);
+      if (!mbar_wait(&accf[buf], (lt >> 1) & 1)) {
+        report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
+        break;
+      }
+      tc_fence_after();
+      if (p.trace != nullptr && lt == 0) t_acc = globaltimer_ns();
+      const uint32_t taddr = tmem + ((uint32_t)(e.q * 32) << 16) + (uint32_t)(buf * BN);
+      bool ok = true;
+      if (EPI == SK_EPI_GEGLU)
+        wide_epi_geglu(mp, e, taddr, n, m * kWBM);
+      else if (EPI == SK_EPI_QKV_ROPE)
+        ok = wide_epi_qkv(p, mp, e, taddr, n, m * kWBM);
+      else
+        ok = wide_epi_rows<EPI, BN>(p, mp, e, taddr, n, m * kWBM);
+      tc_fence_before();
+      mbar_arrive(&acce[buf]);
+      if (!ok) break;
+    }
+    // All of this warp's tensor stores complete (and stop reading shared memory)
+    // before the CTA exits.
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+    if (p.trace != nullptr) t_epi = globaltimer_ns();
+  }
+
+  // Teardown.  If the producer stopped early, wait (bounded) for the copies it
+  // armed before shared memory is released.
+  __syncthreads();
+  if (s_flag[0] != 0 && warp == 0 && lane == 0) {
+    const int armed = s_flag[2];
+    for (int s = 0; s < STAGES && s < armed; ++s) {
+      const int uses = (armed - s + STAGES - 1) / STAGES;  // armings of stage s
+      if (!mbar_wait(&full[s], (uses - 1) & 1)) report_status(p.status, PI05_DEV_TIMEOUT_DRAIN);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+  // Trace record {tag << 32 | cta, entry, setup done, first X TMA after the grid
+  // dependency wait, MMA passed the first accumulator-free wait, first
+  // accumulator ready, epilogue done (stores complete), exit}.
+  if (p.trace != nullptr && threadIdx.x == 64) {
+    const unsigned long long slot = atomicAdd(p.trace, 1ull);
+    if (slot < p.trace[1]) {
+      unsigned long long* w = p.trace + 8 + slot * 8;
+      w[0] = ((unsigned long long)p.trace_tag << 32) | blockIdx.x;
+      w[1] = t_entry;
+      w[2] = t_setup;
+      w[3] = s_stamp[0];
+      w[4] = s_stamp[1];
+      w[5] = t_acc;
+      w[6] = t_epi;
+      w[7] = globaltimer_ns();
+    }
+  }
+}
+
+int wide_sms() {
+  static int cached[16] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 16 && cached[dev]) return cached[dev];
+  int n = 148;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (dev < 16) cached[dev] = n;
+  return n;
+}
+
+template <int EPI, int BN, int STAGES>
+int wide_launch(const SkinnyParams& p, const WideSched& ws, const WideMaps& mp, cudaStream_t stream) {
+  constexpr int kSmem = wide_smem_bytes<EPI, BN, STAGES>();
+  static_assert(kSmem <= 232448, "shared memory per block");
+  auto kern = wide_gemm_kernel<EPI, BN, STAGES>;
+  static bool attr_done[16] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 16 && !attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e != cudaSuccess) {
+      set_last_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      return PI05_ERR_LAUNCH;
+    }
+    attr_done[dev] = true;
+  }
+  const int total = ws.m_tiles * ws.n_tiles;
+  const int grid = std::min(total, wide_sms());
+  return launch_pdl(kern, dim3(grid), dim3(kWThreads), kSmem, stream, pdl_enabled(), mp, p, ws);
+}
+
+// Debug override read once: PI05_WIDE_BN (128 / 256) for STORE / GATED_RESID.
+int env_int(const char* name) {
+  const char* e = getenv(name);
+  return e != nullptr ? atoi(e) : 0;
+}
+
+}  // namespace
+
+int wide_choose(int epi, int m_tiles, int n_cols, int kb_total, int sms, int* bn) {
+  static const int force_bn = env_int("PI05_WIDE_BN");
+  if (epi == SK_EPI_GEGLU || epi == SK_EPI_QKV_ROPE) {
+    *bn = 256;
+    return 0;
+  }
+  // Minimise waves x (per-tile MMA time + fixed per-tile cost).  A 128-wide tile
+  // streams as many operand bytes per MMA cycle as it computes, a 256-wide tile
+  // two thirds of that, so narrow tiles only win when they fill more SMs.
+  double best_cost = 1e30;
+  for (int b : {256, 128}) {
+    const int nt = (n_cols + b - 1) / b;
+    const long tiles = (long)m_tiles * nt;
+    const long waves = (tiles + sms - 1) / sms;
+    const double per_tile = (double)kb_total * (b == 256 ? 1.0 : 0.667) + 4.0;
+    const double cost = (double)waves * per_tile;
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      *bn = b;
+    }
+  }
+  if (force_bn == 128 || force_bn == 256) *bn = force_bn;
+  return 0;
+}
+
+bool wide_disabled() {
+  static int v = [] {
+    const char* e = getenv("PI05_WIDE");
+    return (e != nullptr && e[0] == '0') ? 1 : 0;
+  }();
+  return v != 0;
+}
+
+int wide_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int w_rows0, int w_rows1, int n_cols,
+                  const void* x, int ldx, void* stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (p.m_tok <= 0 || p.k <= 0 || p.k % 8 != 0 || n_cols <= 0 || n_cols % 8 != 0) {
+    set_last_error("wide_gemm: bad shape m=%d k=%d n=%d", p.m_tok, p.k, n_cols);
+    return PI05_ERR_SHAPE;
+  }
+  if (epi == SK_EPI_QKV_ROPE && (p.head_dim != 256 || p.n_kv_heads != 1)) {
+    set_last_error("wide_gemm: QKV+RoPE needs head_dim 256 and one KV head");
+    return PI05_ERR_SHAPE;
+  }
+  WideSched ws;
+  ws.m_tiles = (p.m_tok + kWBM - 1) / kWBM;
+  ws.kb_total = (p.k + kBK - 1) / kBK;
+  int bn = 256;
+  wide_choose(epi, ws.m_tiles, n_cols, ws.kb_total, wide_sms(), &bn);
+  if (epi == SK_EPI_GEGLU)
+    ws.n_tiles = (n_cols + 127) / 128;
+  else if (epi == SK_EPI_QKV_ROPE)
+    ws.n_tiles = p.n_q_heads + 2 * p.n_kv_heads;
+  else
+    ws.n_tiles = (n_cols + bn - 1) / bn;
+  p.splits = 1;
+  p.n_valid = n_cols;
+  WideMaps mp;
+  std::memset(&mp, 0, sizeof(mp));
+  int rc = make_tmap_bf16_2d(&mp.x, x, p.m_tok, p.k, ldx, kWBM, 64, true);
+  if (!rc) rc = make_tmap_bf16_2d(&mp.w0, w0, w_rows0, p.k, p.k, bn / 2, 64, true);
+  if (!rc) rc = make_tmap_bf16_2d(&mp.w1, w1, w_rows1, p.k, p.k, bn / 2, 64, true);
+  if (rc) return rc;
+  if (epi == SK_EPI_QKV_ROPE) {
+    const int hd = 256;
+    const uint64_t kv_rows = (uint64_t)p.krow0 + p.m_tok;
+    rc = make_tmap_bf16_2d(&mp.out, p.q_out, p.m_tok, (uint64_t)p.n_q_heads * hd, (uint64_t)p.n_q_heads * hd, 32,
+                           64, true);
+    if (!rc) rc = make_tmap_bf16_2d(&mp.in0, p.cos, p.m_tok, hd, hd, 32, 64, true);
+    if (!rc) rc = make_tmap_bf16_2d(&mp.in1, p.sin, p.m_tok, hd, hd, 32, 64, true);
+    if (!rc) rc = make_tmap_bf16_2d(&mp.kc, p.k_cache, kv_rows, hd, hd, 32, 64, true);
+    if (!rc) rc = make_tmap_bf16_2d(&mp.vc, p.v_cache, kv_rows, hd, hd, 32, 64, true);
+  } else {
+    rc = make_tmap_bf16_2d(&mp.out, p.out, p.m_tok, n_cols, p.ldo, 32, 64, true);
+    if (!rc && epi == SK_EPI_GATED_RESID)
+      rc = make_tmap_bf16_2d(&mp.in0, p.resid, p.m_tok, n_cols, p.ldr, 32, 64, true);
+  }
+  if (rc) return rc;
+  switch (epi) {
+    case SK_EPI_STORE:
+      return bn == 256 ? wide_launch<SK_EPI_STORE, 256, 4>(p, ws, mp, st)
+                       : wide_launch<SK_EPI_STORE, 128, 6>(p, ws, mp, st);
+    case SK_EPI_GATED_RESID:
+      return bn == 256 ? wide_launch<SK_EPI_GATED_RESID, 256, 4>(p, ws, mp, st)
+                       : wide_launch<SK_EPI_GATED_RESID, 128, 6>(p, ws, mp, st);
+    case SK_EPI_GEGLU:
+      return wide_launch<SK_EPI_GEGLU, 256, 4>(p, ws, mp, st);
+    case SK_EPI_QKV_ROPE:
+      return wide_launch<SK_EPI_QKV_ROPE, 256, 3>(p, ws, mp, st);
+    default:
+      set_last_error("wide_gemm: unknown epilogue %d", epi);
+      return PI05_ERR_INVALID_ARG;
+  }
+}
+
+}  // namespace pi05

@@ -37,6 +37,7 @@ SIGNATURES = {
     "pi05_workspace_bytes": (_Z, [_I, _I]),
     "pi05_read_device_status": (_I, [_P, ctypes.POINTER(_I), _P]),
     "pi05_debug_set_splits": (None, [_I]),
+    "pi05_debug_set_trace": (None, [_P]),
     "pi05_launch_count": (ctypes.c_longlong, []),
     "pi05_gate_up_geglu": (_I, [_P, _P, _P, _P, _I, _I, _I, _P, _Z, _P]),
     "pi05_gate_up_geglu_noalloc": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),
