@@ -288,22 +288,17 @@ class OpenPi0Inference:
 
         return step
 
-    def time_geglu_kernel(self, reps: int = 20) -> dict:
-        """Time the gate/up+GeGLU GEMM alone: one launch per expert layer (302 MB of
-        weights > L2) captured in a CUDA graph, replayed ``reps`` times, CUDA events
-        on the replay stream."""
-        _, den = self._runners()
-        s = self.expert.shape
-        x = den.xn
-        out = den.act
+    def _time_per_layer(self, launch, reps: int) -> float:
+        """Mean µs of ``launch(layer)`` over all expert layers, captured once in a
+        CUDA graph and replayed ``reps`` times (CUDA events on the replay stream)."""
         st = torch.cuda.current_stream(self.device)
         for L in self.expert.layers:
-            ops.geglu(x, L["w_gate"], L["w_up"], out=out)
+            launch(L)
         torch.cuda.synchronize(self.device)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
             for L in self.expert.layers:
-                ops.geglu(x, L["w_gate"], L["w_up"], out=out)
+                launch(L)
         for _ in range(3):
             g.replay()
         torch.cuda.synchronize(self.device)
@@ -313,12 +308,30 @@ class OpenPi0Inference:
             g.replay()
         e1.record(st)
         torch.cuda.synchronize(self.device)
-        n = reps * len(self.expert.layers)
-        us = e0.elapsed_time(e1) * 1e3 / n
         del g
+        return e0.elapsed_time(e1) * 1e3 / (reps * len(self.expert.layers))
+
+    def time_geglu_kernel(self, reps: int = 20) -> dict:
+        """The gate/up+GeGLU GEMM alone: one launch per expert layer (302 MB of
+        weights > L2)."""
+        _, den = self._runners()
+        s = self.expert.shape
+        us = self._time_per_layer(lambda L: ops.geglu(den.xn, L["w_gate"], L["w_up"], out=den.act), reps)
         m = self.config.action_horizon
         nbytes = 2 * s.mlp_dim * s.width * 2 + m * s.width * 2 + m * s.mlp_dim * 2
-        return {"us": us, "bytes": nbytes, "launches": n}
+        return {"us": us, "bytes": nbytes, "launches": reps * len(self.expert.layers)}
+
+    def time_down_kernel(self, reps: int = 20) -> dict:
+        """The down projection + gated residual GEMM alone: one launch per expert
+        layer (151 MB of weights > L2 between replays of the same layer)."""
+        _, den = self._runners()
+        s = self.expert.shape
+        gate = torch.ones(s.width, dtype=torch.float32, device=self.device)
+        us = self._time_per_layer(
+            lambda L: ops.linear_gated_residual(den.act, L["w_down"], den.h, gate, out=den.h), reps)
+        m = self.config.action_horizon
+        nbytes = s.width * s.mlp_dim * 2 + m * s.mlp_dim * 2 + 2 * m * s.width * 2 + s.width * 4
+        return {"us": us, "bytes": nbytes, "launches": reps * len(self.expert.layers)}
 
     def denoise_step_bytes(self) -> int:
         """Algorithmic HBM bytes of one Euler step: expert weights + KV read + KV tail

@@ -65,9 +65,10 @@ def test_denoise_loop_parity(setup, ragged):
     # the captured graph gives the same actions
     act_graph = r.run(noise.cuda(), use_graph=True).clone().cpu()
     assert (act_graph - act_steps).abs().max().item() <= 2e-3
-    # and replays are stable
+    # and replays are bit-identical (split-K and split-KV partials are summed in a
+    # fixed order, no atomics on the data path)
     act_graph2 = r.run(noise.cuda(), use_graph=True).clone().cpu()
-    assert (act_graph2 - act_graph).abs().max().item() <= 2e-3
+    assert torch.equal(act_graph2, act_graph)
     assert ops.read_device_status() == 0
 
 

@@ -137,3 +137,56 @@ def test_replicas_gloo_two_ranks():
     for rank, outs, t in res:
         assert outs == [float(i) for i in range(8)]
         assert t == 2.0
+
+
+def _failing_replica_worker(rank, world, port, q):
+    """Rank 1's engine raises on its first observation (a replica failure made on
+    the host); the survivors must see an error from the next collective within the
+    process-group timeout instead of waiting for ever."""
+    import datetime
+    import time
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=15))
+
+    def run_one(i):
+        if rank == 1:
+            raise RuntimeError("replica 1 failed")
+        return torch.full((2,), float(i))
+
+    t0 = time.monotonic()
+    try:
+        serve(8, run_one, dist)
+        q.put((rank, "completed", time.monotonic() - t0))
+    except Exception as e:  # noqa: BLE001 - any backend error is the detection
+        q.put((rank, type(e).__name__, time.monotonic() - t0))
+    # no destroy_process_group: the peer is gone
+
+
+def test_replica_failure_detected_gloo():
+    import socket
+
+    import torch.multiprocessing as mp
+
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_failing_replica_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in procs:
+        rank, what, dt = q.get(timeout=120)
+        res[rank] = (what, dt)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert res[1][0] == "RuntimeError"  # the failing replica saw its own error
+    assert res[0][0] != "completed"  # the survivor did not return a partial result
+    assert res[0][1] < 60.0  # and learned of the failure within the bound
