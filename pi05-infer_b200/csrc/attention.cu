@@ -14,12 +14,21 @@
 // probabilities enter P.V as bf16, accumulation in fp32.
 //
 // mma.sync m16n8k16 (bf16 -> fp32) fragments, ldmatrix from XOR-swizzled shared
-// memory, cp.async double-buffered K/V chunks of 64 keys.
+// memory, cp.async K/V chunks of 64 keys (double-buffered when a split owns more
+// than one chunk).  Chunks of the static part of the cache (the prefix rows, written
+// long before) are fetched before the grid-dependency wait, so their latency hides
+// behind the previous kernel.
+//
+// Split-KV partials (unnormalised O, running max, sum) go through global memory
+// and a second kernel merges them in split order.
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <cstring>
+
 #include "host_util.h"
 #include "attention.h"
+#include "ptx.cuh"
 
 namespace pi05 {
 namespace {
@@ -68,34 +77,33 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 
 __device__ __forceinline__ float bfr(float x) { return __bfloat162float(__float2bfloat16(x)); }
 
+// Shared memory of one CTA: Q rows, nbuf K and V chunk buffers, the chunk key masks.
+template <int WARPS>
+__host__ __device__ constexpr size_t attn_smem_bytes(int nbuf) {
+  return (size_t)16 * WARPS * kRowBytes + (size_t)nbuf * 2 * kChunk * kRowBytes + (size_t)nbuf * kChunk;
+}
+
 template <int WARPS>
 __global__ void __launch_bounds__(WARPS * 32, 1)
     mqa_flash_kernel(const AttnParams p) {
   constexpr int kRows = 16 * WARPS;
   extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* sQ = smem;                                  // kRows x 512 B
-  uint8_t* sK = smem + kRows * kRowBytes;              // 2 x 64 x 512 B
-  uint8_t* sV = sK + 2 * kChunk * kRowBytes;           // 2 x 64 x 512 B
-  uint8_t* sValid = sV + 2 * kChunk * kRowBytes;       // 2 x 64 bytes
+  const int nbuf = p.nbuf;
+  uint8_t* sQ = smem;                                     // kRows x 512 B
+  uint8_t* sK = smem + kRows * kRowBytes;                 // nbuf x 64 x 512 B
+  uint8_t* sV = sK + nbuf * kChunk * kRowBytes;           // nbuf x 64 x 512 B
+  uint8_t* sValid = sV + nbuf * kChunk * kRowBytes;       // nbuf x 64 bytes
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int row0 = blockIdx.x * kRows;
   const int split = blockIdx.y;
+  const bool tr = p.trace != nullptr && tid == 0;
+  const uint64_t t_entry = tr ? globaltimer_ns() : 0;
+  uint64_t t_wait = 0, t_data = 0, t_loop = 0;
   const int n_chunks_total = (p.kv_len + kChunk - 1) / kChunk;
   const int c_begin = (split * n_chunks_total) / p.splits;
   const int c_end = ((split + 1) * n_chunks_total) / p.splits;
 
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-
-  // Q rows (zero-fill beyond R).
-  for (int i = tid; i < kRows * 32; i += WARPS * 32) {
-    const int r = i >> 5, c = i & 31;
-    const int gr = row0 + r;
-    const bool ok = gr < p.rows;
-    cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(sQ)) + swz(r, c),
-               p.q + (size_t)(ok ? gr : 0) * p.q_stride + c * 8, ok);
-  }
   auto load_chunk = [&](int ci, int buf) {
     const int key0 = ci * kChunk;
     const uint32_t kb = static_cast<uint32_t>(__cvta_generic_to_shared(sK + buf * kChunk * kRowBytes));
@@ -114,13 +122,30 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     }
   };
 
+  // The first chunk's K, V and mask come from the static rows when the whole chunk
+  // lies below static_rows: fetch them before waiting on the previous kernel.
+  const bool first_static = c_begin < c_end && (c_begin + 1) * kChunk <= p.static_rows;
+  if (first_static) load_chunk(c_begin, 0);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (tr) t_wait = globaltimer_ns();
+
+  // Q rows (zero-fill beyond R).
+  for (int i = tid; i < kRows * 32; i += WARPS * 32) {
+    const int r = i >> 5, c = i & 31;
+    const int gr = row0 + r;
+    const bool ok = gr < p.rows;
+    cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(sQ)) + swz(r, c),
+               p.q + (size_t)(ok ? gr : 0) * p.q_stride + c * 8, ok);
+  }
+
   float o[32][4];
 #pragma unroll
   for (int j = 0; j < 32; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
   float m_run[2] = {-INFINITY, -INFINITY};
   float l_run[2] = {0.f, 0.f};
 
-  if (c_begin < c_end) load_chunk(c_begin, 0);
+  if (c_begin < c_end && !first_static) load_chunk(c_begin, 0);
   cp_commit();
 
   const uint32_t sQa = static_cast<uint32_t>(__cvta_generic_to_shared(sQ));
@@ -128,11 +153,12 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   const float scale = p.scale;
 
   for (int ci = c_begin; ci < c_end; ++ci) {
-    const int buf = (ci - c_begin) & 1;
-    if (ci + 1 < c_end) load_chunk(ci + 1, buf ^ 1);
+    const int buf = (ci - c_begin) % nbuf;
+    if (ci + 1 < c_end) load_chunk(ci + 1, (buf + 1) % nbuf);
     cp_commit();
     cp_wait<1>();
     __syncthreads();
+    if (tr && t_data == 0) t_data = globaltimer_ns();
 
     const uint32_t sKa = static_cast<uint32_t>(__cvta_generic_to_shared(sK + buf * kChunk * kRowBytes));
     const uint32_t sVa = static_cast<uint32_t>(__cvta_generic_to_shared(sV + buf * kChunk * kRowBytes));
@@ -228,6 +254,24 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     __syncthreads();
   }
   cp_wait<0>();
+  if (tr) t_loop = globaltimer_ns();
+  // Trace record {tag << 32 | cta, entry, grid-dependency wait done, first chunk
+  // ready, key loop done, output / partial written, 0, 0}.
+  auto trace_out = [&]() {
+    if (!tr) return;
+    const unsigned long long slot = atomicAdd(p.trace, 1ull);
+    if (slot < p.trace[1]) {
+      unsigned long long* w = p.trace + 8 + slot * 8;
+      w[0] = ((unsigned long long)p.trace_tag << 32) | (blockIdx.y * gridDim.x + blockIdx.x);
+      w[1] = t_entry;
+      w[2] = t_wait;
+      w[3] = t_data;
+      w[4] = t_loop;
+      w[5] = globaltimer_ns();
+      w[6] = 0;
+      w[7] = 0;
+    }
+  };
 
   // Output: rows (warp*16 + g) and (+8), columns j*8 + 2*t4 .. +1.
 #pragma unroll
@@ -253,15 +297,30 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       }
     }
   }
+  trace_out();
 }
 
 // One warp per row: merge the split partials (O unnormalised, running max m,
-// sum l).  Lane s holds split s's (m, l); the O loads of four splits are issued
+// sum l).  Lane s holds split s's (m, l); the O loads of eight splits are issued
 // together per pass.
 __global__ void __launch_bounds__(256) mqa_combine_kernel(const AttnParams p) {
+  const bool tr = p.trace != nullptr && threadIdx.x == 0;
+  const uint64_t t_entry = tr ? globaltimer_ns() : 0;
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const uint64_t t_wait = tr ? globaltimer_ns() : 0;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (tr) {
+    // Trace record {(tag + 1) << 32 | cta, entry, grid-dependency wait done, 0, 0, 0, 0, 0}.
+    const unsigned long long slot = atomicAdd(p.trace, 1ull);
+    if (slot < p.trace[1]) {
+      unsigned long long* w = p.trace + 8 + slot * 8;
+      w[0] = ((unsigned long long)(p.trace_tag + 1) << 32) | blockIdx.x;
+      w[1] = t_entry;
+      w[2] = t_wait;
+      w[3] = w[4] = w[5] = w[6] = w[7] = 0;
+    }
+  }
   if (warp >= p.rows) return;
   const int r = warp;
   float ms = -INFINITY, ls = 0.f;
@@ -275,11 +334,11 @@ __global__ void __launch_bounds__(256) mqa_combine_kernel(const AttnParams p) {
   float l = ls * w;
   for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffff, l, o);
   float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  for (int s0 = 0; s0 < p.splits; s0 += 4) {
-    float4 a[4], b[4];
-    float ws[4];
+  for (int s0 = 0; s0 < p.splits; s0 += 8) {
+    float4 a[8], b[8];
+    float ws[8];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < 8; ++j) {
       const int sj = s0 + j;
       ws[j] = __shfl_sync(0xffffffff, w, sj & 31);
       if (sj < p.splits) {
@@ -292,7 +351,7 @@ __global__ void __launch_bounds__(256) mqa_combine_kernel(const AttnParams p) {
       }
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < 8; ++j) {
       acc[0] += a[j].x * ws[j]; acc[1] += a[j].y * ws[j]; acc[2] += a[j].z * ws[j]; acc[3] += a[j].w * ws[j];
       acc[4] += b[j].x * ws[j]; acc[5] += b[j].y * ws[j]; acc[6] += b[j].z * ws[j]; acc[7] += b[j].w * ws[j];
     }
@@ -309,6 +368,32 @@ __global__ void __launch_bounds__(256) mqa_combine_kernel(const AttnParams p) {
 
 }  // namespace
 
+namespace {
+
+template <int W>
+int set_attn_smem() {
+  static bool done[16] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 16 && done[dev]) return PI05_OK;
+  const cudaError_t e =
+      cudaFuncSetAttribute(mqa_flash_kernel<W>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem_bytes<W>(2));
+  if (e != cudaSuccess) {
+    set_last_error("attention smem attr: %s", cudaGetErrorString(e));
+    return PI05_ERR_LAUNCH;
+  }
+  if (dev < 16) done[dev] = true;
+  return PI05_OK;
+}
+
+}  // namespace
+
+constexpr int kTcMinRows = 1024;  // query rows above which the tcgen05 kernel is used
+
+int launch_combine(const AttnParams& p, cudaStream_t st) {
+  return launch_pdl(mqa_combine_kernel, dim3((p.rows + 7) / 8), dim3(256), 0, st, pdl_enabled(), p);
+}
+
 int mqa_attention_run(AttnParams p, float* part, size_t part_bytes, int splits, void* stream) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (p.head_dim != kD) {
@@ -319,6 +404,10 @@ int mqa_attention_run(AttnParams p, float* part, size_t part_bytes, int splits, 
     set_last_error("attention: empty rows/keys");
     return PI05_ERR_SHAPE;
   }
+  // tcgen05 for many query rows (prefix LM: 968 x 8); the mma.sync kernel below is
+  // faster for the denoise suffix (50 x 8 rows), where each CTA owns one key chunk.
+  if (tc_attention_enabled() && p.rows > kTcMinRows)
+    return mqa_tc_attention_run(p, part, part_bytes, splits, st, launch_combine);
   constexpr int W = 4;
   constexpr int kRows = 16 * W;
   const int row_blocks = (p.rows + kRows - 1) / kRows;
@@ -335,6 +424,8 @@ int mqa_attention_run(AttnParams p, float* part, size_t part_bytes, int splits, 
   splits = splits > n_chunks ? n_chunks : splits;
   splits = splits > 32 ? 32 : splits;
   p.splits = splits;
+  p.nbuf = (n_chunks + splits - 1) / splits > 1 ? 2 : 1;
+  const size_t smem = attn_smem_bytes<W>(p.nbuf);
   if (splits > 1) {
     const size_t need_o = (size_t)splits * p.rows * kD * sizeof(float);
     const size_t need = need_o + (size_t)splits * p.rows * 2 * sizeof(float);
@@ -345,22 +436,11 @@ int mqa_attention_run(AttnParams p, float* part, size_t part_bytes, int splits, 
     p.part_o = part;
     p.part_ml = part + (size_t)splits * p.rows * kD;
   }
-  const size_t smem = (size_t)kRows * kRowBytes + 4 * kChunk * kRowBytes + 2 * kChunk;
-  auto kern = mqa_flash_kernel<W>;
-  static bool attr_done[16] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 16 && !attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) {
-      set_last_error("attention smem attr: %s", cudaGetErrorString(e));
-      return PI05_ERR_LAUNCH;
-    }
-    attr_done[dev] = true;
-  }
-  int rc = launch_pdl(kern, dim3(row_blocks, splits), dim3(W * 32), smem, st, pdl_enabled(), p);
+  int rc = set_attn_smem<W>();
+  if (rc) return rc;
+  rc = launch_pdl(mqa_flash_kernel<W>, dim3(row_blocks, splits), dim3(W * 32), smem, st, pdl_enabled(), p);
   if (rc || splits == 1) return rc;
-  return launch_pdl(mqa_combine_kernel, dim3((p.rows + 7) / 8), dim3(256), 0, st, pdl_enabled(), p);
+  return launch_combine(p, st);
 }
 
 }  // namespace pi05

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
 
@@ -20,12 +21,24 @@ struct AttnParams {
   int kv_len = 0;
   int head_dim = 0;
   float scale = 0.f;
+  int static_rows = 0;                 // keys [0, static_rows) (K, V and mask) do not depend on the
+                                       // previous kernel: prefetched before the grid-dependency wait
   int splits = 1;                      // set by the launcher
+  int nbuf = 2;                        // set by the launcher: K/V chunk buffers (1 when a split has one chunk)
+  int* status = nullptr;               // device status word (bounded-wait timeouts)
+  unsigned long long* trace = nullptr; // optional per-CTA timestamps (same format as the GEMMs)
+  int trace_tag = 0;
   float* part_o = nullptr;             // [splits, rows, head_dim]
   float* part_ml = nullptr;            // [splits, rows, 2]
 };
 
-// splits <= 0 picks a split count that covers the SMs.
+// splits <= 0 picks a split count that covers the SMs.  head_dim 256 runs on the
+// tcgen05 kernel (attention_tc.cu) unless PI05_ATTN_TC=0 selects the mma.sync one.
 int mqa_attention_run(AttnParams p, float* part, size_t part_bytes, int splits, void* stream);
+
+// tcgen05 kernel; `combine` launches the split-KV merge when splits > 1.
+int mqa_tc_attention_run(AttnParams p, float* part, size_t part_bytes, int splits, cudaStream_t stream,
+                         int (*combine)(const AttnParams&, cudaStream_t));
+bool tc_attention_enabled();
 
 }  // namespace pi05

@@ -1,0 +1,399 @@
+// Multi-query flash attention on the 5th-generation tensor cores (tcgen05).
+//
+// All query heads share the single KV head, so the query rows (token, head) form
+// one [R, 256] matrix; a CTA owns 128 query rows and a contiguous range of
+// 64-key chunks (split-KV across CTAs when the row blocks alone do not fill the
+// GPU).  Per chunk j:
+//
+//   S_j  = Q . K_j^T          tcgen05.mma M=128 N=64  K=256 -> TMEM (two S buffers)
+//   P_j  = exp(S_j - m)       one thread per query row reads its S row from TMEM,
+//                             updates the running max / sum, rescales its O row in
+//                             TMEM when the max moved, writes P_j (bf16) to shared
+//                             memory in the 128B-swizzled K-major layout
+//   O   += P_j . V_j          tcgen05.mma M=128 N=256 K=64, V read MN-major straight
+//                             from the cache layout [key][256]
+//
+// Warp roles: warp 0 TMA (Q once, K/V chunks through a 1- or 2-stage ring),
+// warp 1 TMEM owner + MMA issuer (S_{j+1} is issued before P_j is ready, so the
+// tensor core works on the next scores while the softmax runs), warps 2-5
+// softmax and the output.  Chunks of the static part of the cache (the prefix
+// rows) are loaded before the grid-dependency wait.
+//
+// Numerics follow eager_attention_forward (pi05_infer/gemma/modeling_gemma.py:
+// 252-275) the same way as the mma.sync kernel in attention.cu: the score is the
+// bf16-rounded Q.K^T times the scale rounded again to bf16, masked keys are
+// excluded, softmax in fp32 with a running max, probabilities enter P.V as bf16,
+// fp32 accumulation.  Split-KV partials use that kernel's layout and combine.
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+
+#include "attention.h"
+#include "host_util.h"
+#include "ptx.cuh"
+
+namespace pi05 {
+namespace {
+
+constexpr int kD = 256;
+constexpr int kBR = 128;                     // query rows per CTA (UMMA M)
+constexpr int kBC = 64;                      // keys per chunk
+constexpr int kQBytes = kBR * kD * 2;        // 4 boxes of [128 rows x 64 dims]
+constexpr int kKVBytes = kBC * kD * 2;       // 4 boxes of [64 keys x 64 dims]
+constexpr int kPBytes = kBR * kBC * 2;       // [128 rows x 64 keys]
+constexpr int kThreads = 192;
+constexpr int kSoftThreads = 128;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColO = 128;              // S buffers at columns 0 and 64, O at 128..383
+constexpr uint32_t kIdescS = umma_idesc_bf16(kBR, kBC);
+constexpr uint32_t kIdescPV = umma_idesc_bf16(kBR, kD) | (1u << 16);  // B (V) MN-major
+
+struct TcMaps {
+  CUtensorMap q, k, v;
+};
+
+size_t tc_smem_bytes(int nst) { return 1024 + kQBytes + (size_t)nst * 2 * kKVBytes + kPBytes + 256; }
+
+__device__ __forceinline__ uint32_t p_off(int r, int g) { return (uint32_t)(r * 128 + ((g ^ (r & 7)) << 4)); }
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_constant__ TcMaps mp, const AttnParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int nst = p.nbuf;
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + kQBytes;
+  uint8_t* sV = sK + nst * kKVBytes;
+  uint8_t* sP = sV + nst * kKVBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kPBytes);
+  uint64_t* q_full = bars;        // Q landed
+  uint64_t* kv_full = bars + 1;   // [2] K/V chunk landed
+  uint64_t* kv_empty = bars + 3;  // [2] P.V of the chunk done
+  uint64_t* s_full = bars + 5;    // [2] S buffer written
+  uint64_t* s_empty = bars + 7;   // [2] S buffer read (128 arrivals)
+  uint64_t* p_full = bars + 9;    // P written, O rescaled (128 arrivals)
+  uint64_t* p_empty = bars + 10;  // P.V done (P free, O stable)
+  uint64_t* mdone = bars + 11;    // every MMA of the CTA complete
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 12);
+  int* s_flag = reinterpret_cast<int*>(s_tmem + 1);  // [0] abort, [1] K/V chunks armed
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = blockIdx.x * kBR;
+  const int split = blockIdx.y;
+  const int n_chunks_total = (p.kv_len + kBC - 1) / kBC;
+  const int c_begin = (split * n_chunks_total) / p.splits;
+  const int c_end = ((split + 1) * n_chunks_total) / p.splits;
+  const int nc = c_end - c_begin;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], kSoftThreads);
+    }
+    mbar_init(p_full, kSoftThreads);
+    mbar_init(p_empty, 1);
+    mbar_init(mdone, 1);
+    s_flag[0] = 0;
+    s_flag[1] = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&mp.q);
+    prefetch_tmap(&mp.k);
+    prefetch_tmap(&mp.v);
+  }
+  if (warp == 1) {
+    tmem_alloc(s_tmem, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol_kv = l2_policy_evict_last();
+      int armed = 0;
+      auto load_kv = [&](int j) -> bool {
+        const int st = j % nst;
+        if (j >= nst && !mbar_wait(&kv_empty[st], ((j / nst) - 1) & 1)) {
+          report_status(p.status, PI05_DEV_TIMEOUT_PRODUCER);
+          s_flag[0] = 1;
+          return false;
+        }
+        mbar_arrive_expect_tx(&kv_full[st], 2 * kKVBytes);
+        const int key0 = (c_begin + j) * kBC;
+        for (int b = 0; b < 4; ++b) {
+          tma_load_2d(sK + st * kKVBytes + b * 8192, &mp.k, &kv_full[st], b * 64, key0, pol_kv);
+          tma_load_2d(sV + st * kKVBytes + b * 8192, &mp.v, &kv_full[st], b * 64, key0, pol_kv);
+        }
+        ++armed;
+        return true;
+      };
+      // Chunk 0 from the static rows does not depend on the previous kernel.
+      const bool first_static = nc > 0 && (c_begin + 1) * kBC <= p.static_rows;
+      if (first_static) load_kv(0);
+      pdl_wait();
+      mbar_arrive_expect_tx(q_full, kQBytes);
+      for (int b = 0; b < 4; ++b) tma_load_2d(sQ + b * 16384, &mp.q, q_full, b * 64, row0, l2_policy_evict_first());
+      bool ok = true;
+      if (!first_static && nc > 0) ok = load_kv(0);
+      for (int j = 1; j < nc && ok; ++j) ok = load_kv(j);
+      s_flag[1] = armed;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = mbar_wait(q_full, 0);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j % nst, sb = j & 1;
+        if (!mbar_wait(&kv_full[st], (j / nst) & 1)) return false;
+        if (j >= 2 && !mbar_wait(&s_empty[sb], ((j >> 1) - 1) & 1)) return false;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(sb * kBC);
+        const uint32_t a0 = smem_u32(sQ), b0 = smem_u32(sK + st * kKVBytes);
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16(d, umma_sdesc_sw128(a0 + b * 16384 + kk * 32), umma_sdesc_sw128(b0 + b * 8192 + kk * 32),
+                      kIdescS, (b | kk) ? 1u : 0u);
+        umma_commit(&s_full[sb]);
+        return true;
+      };
+      if (ok && nc > 0) ok = issue_s(0);
+      for (int j = 0; j < nc && ok; ++j) {
+        if (j + 1 < nc) ok = issue_s(j + 1);
+        if (!ok || !mbar_wait(p_full, j & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int st = j % nst;
+        const uint32_t a0 = smem_u32(sP), b0 = smem_u32(sV + st * kKVBytes);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_bf16(tmem + kColO, umma_sdesc_sw128(a0 + kk * 32), umma_sdesc_mn_sw128(b0 + kk * 2048, 8192, 1024),
+                    kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(p_empty);
+        umma_commit(&kv_empty[st]);
+      }
+      if (!ok) {
+        report_status(p.status, PI05_DEV_TIMEOUT_MMA);
+        s_flag[0] = 1;
+      }
+      umma_commit(mdone);
+      if (!mbar_wait(mdone, 0)) report_status(p.status, PI05_DEV_TIMEOUT_DRAIN);
+    }
+  } else {
+    // Softmax warps: TMEM lane quarter = warp % 4, one query row per thread.
+    pdl_wait();
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const int grow = row0 + r;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nc; ++j) {
+      const int sb = j & 1;
+      if (!mbar_wait(&s_full[sb], (j >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[64];
+      tmem_ld32(tmem + lane_base + sb * kBC, s);
+      tmem_ld32(tmem + lane_base + sb * kBC + 32, s + 32);
+      tc_fence_before();
+      mbar_arrive(&s_empty[sb]);
+      const int key0 = (c_begin + j) * kBC;
+      uint8_t vk[64];
+      if (key0 + kBC <= p.kv_len && (reinterpret_cast<uintptr_t>(p.key_valid) & 15) == 0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          *reinterpret_cast<uint4*>(vk + i * 16) = *reinterpret_cast<const uint4*>(p.key_valid + key0 + i * 16);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) vk[i] = (key0 + i < p.kv_len) ? p.key_valid[key0 + i] : 0;
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        float v = bf16_round(bf16_round(s[i]) * p.scale);
+        v = vk[i] ? v : -INFINITY;
+        s[i] = v;
+        mx = fmaxf(mx, v);
+      }
+      const float m_new = fmaxf(m, mx);
+      const float corr = (m_new == -INFINITY || m == m_new) ? 1.f : __expf(m - m_new);
+      m = m_new;
+      float ls = 0.f;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const float pv = (s[i] == -INFINITY) ? 0.f : __expf(s[i] - m);
+        s[i] = pv;
+        ls += pv;
+      }
+      l = l * corr + ls;
+      if (j > 0) {
+        // P.V of the previous chunk must be done: P is single-buffered and O may
+        // need rescaling.
+        if (!mbar_wait(p_empty, (j - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // tcgen05.ld/st are warp-collective: rescale when any row of the warp moved
+        // (rows whose max did not move multiply by 1).
+        if (__any_sync(0xffffffff, corr != 1.f)) {
+#pragma unroll 1
+          for (int c = 0; c < kD / 32; ++c) {
+            float o[32];
+            tmem_ld32(tmem + lane_base + kColO + c * 32, o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= corr;
+            tmem_st32(tmem + lane_base + kColO + c * 32, o);
+          }
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < 8; ++g) {
+        uint4 u;
+        u.x = pack_bf16x2(s[g * 8 + 0], s[g * 8 + 1]);
+        u.y = pack_bf16x2(s[g * 8 + 2], s[g * 8 + 3]);
+        u.z = pack_bf16x2(s[g * 8 + 4], s[g * 8 + 5]);
+        u.w = pack_bf16x2(s[g * 8 + 6], s[g * 8 + 7]);
+        *reinterpret_cast<uint4*>(sP + p_off(r, g)) = u;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (!ok) report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
+    if (ok && nc > 0 && mbar_wait(p_empty, (nc - 1) & 1)) {
+      tc_fence_after();
+      // Every lane runs the (warp-collective) TMEM loads; rows past R store nothing.
+      const bool live = grow < p.rows;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < kD / 32; ++c) {
+        float o[32];
+        tmem_ld32(tmem + lane_base + kColO + c * 32, o);
+        if (!live) continue;
+        if (p.splits == 1) {
+          __nv_bfloat16* dst = p.out + (size_t)grow * p.out_stride + c * 32;
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            uint4 u;
+            u.x = pack_bf16x2(o[g * 8 + 0] * inv, o[g * 8 + 1] * inv);
+            u.y = pack_bf16x2(o[g * 8 + 2] * inv, o[g * 8 + 3] * inv);
+            u.z = pack_bf16x2(o[g * 8 + 4] * inv, o[g * 8 + 5] * inv);
+            u.w = pack_bf16x2(o[g * 8 + 6] * inv, o[g * 8 + 7] * inv);
+            *reinterpret_cast<uint4*>(dst + g * 8) = u;
+          }
+        } else {
+          float* dst = p.part_o + ((size_t)split * p.rows + grow) * kD + c * 32;
+#pragma unroll
+          for (int g = 0; g < 8; ++g)
+            *reinterpret_cast<float4*>(dst + g * 4) = make_float4(o[g * 4], o[g * 4 + 1], o[g * 4 + 2], o[g * 4 + 3]);
+        }
+      }
+      if (live && p.splits > 1) {
+        p.part_ml[((size_t)split * p.rows + grow) * 2] = m;
+        p.part_ml[((size_t)split * p.rows + grow) * 2 + 1] = l;
+      }
+    } else if (ok && nc > 0) {
+      report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
+    }
+  }
+
+  // Teardown: if the producer stopped early, wait (bounded) for the copies it armed.
+  __syncthreads();
+  if (s_flag[0] != 0 && warp == 0 && lane == 0) {
+    const int armed = s_flag[1];
+    for (int st = 0; st < nst && st < armed; ++st) {
+      const int uses = (armed - st + nst - 1) / nst;
+      if (!mbar_wait(&kv_full[st], (uses - 1) & 1)) report_status(p.status, PI05_DEV_TIMEOUT_DRAIN);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace
+
+bool tc_attention_enabled() {
+  static int v = [] {
+    const char* e = getenv("PI05_ATTN_TC");
+    return (e != nullptr && e[0] == '0') ? 0 : 1;
+  }();
+  return v != 0;
+}
+
+int mqa_tc_attention_run(AttnParams p, float* part, size_t part_bytes, int splits, cudaStream_t stream,
+                         int (*combine)(const AttnParams&, cudaStream_t)) {
+  const int row_blocks = (p.rows + kBR - 1) / kBR;
+  const int n_chunks = (p.kv_len + kBC - 1) / kBC;
+  int sms = 148;
+  {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  if (splits <= 0) {
+    // Fill about one wave; fewer splits keep the partial round trip small.
+    splits = std::max(1, std::min(n_chunks, sms / std::max(1, row_blocks)));
+    splits = std::min(splits, 16);
+  }
+  splits = std::min(splits, n_chunks);
+  splits = std::min(splits, 32);
+  p.splits = splits;
+  p.nbuf = (n_chunks + splits - 1) / splits > 1 ? 2 : 1;
+  if (splits > 1) {
+    const size_t need = (size_t)splits * p.rows * kD * sizeof(float) + (size_t)splits * p.rows * 2 * sizeof(float);
+    if (part == nullptr || need > part_bytes) {
+      set_last_error("attention: workspace too small (%zu needed)", need);
+      return PI05_ERR_WORKSPACE;
+    }
+    p.part_o = part;
+    p.part_ml = part + (size_t)splits * p.rows * kD;
+  }
+  TcMaps mp;
+  std::memset(&mp, 0, sizeof(mp));
+  int rc = make_tmap_bf16_2d(&mp.q, p.q, p.rows, kD, p.q_stride, kBR, 64, true);
+  if (!rc) rc = make_tmap_bf16_2d(&mp.k, p.k, p.kv_len, kD, p.kv_stride, kBC, 64, true);
+  if (!rc) rc = make_tmap_bf16_2d(&mp.v, p.v, p.kv_len, kD, p.kv_stride, kBC, 64, true);
+  if (rc) return rc;
+  const size_t smem = tc_smem_bytes(p.nbuf);
+  static bool attr_done[16] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 16 && !attr_done[dev]) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(mqa_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc_smem_bytes(2));
+    if (e != cudaSuccess) {
+      set_last_error("attention smem attr: %s", cudaGetErrorString(e));
+      return PI05_ERR_LAUNCH;
+    }
+    attr_done[dev] = true;
+  }
+  rc = launch_pdl(mqa_tc_kernel, dim3(row_blocks, splits), dim3(kThreads), smem, stream, pdl_enabled(), mp, p);
+  if (rc || splits == 1) return rc;
+  return combine(p, stream);
+}
+
+}  // namespace pi05

@@ -9,6 +9,8 @@
 // loop in one CUDA graph.
 #include <algorithm>
 #include <cmath>
+#include <cstdio>
+#include <cstdlib>
 
 #include "../../include/pi05_b200.h"
 #include "attention.h"
@@ -21,6 +23,19 @@ using namespace pi05;
 namespace {
 
 inline bool nz(const void* p) { return p != nullptr; }
+
+// PI05_SPLITS="q,o,g,d" in the environment forces the split-K count of the four
+// denoise GEMMs (tuning only; 0 or absent = automatic).
+const int* debug_split_overrides() {
+  static int v[4] = {0, 0, 0, 0};
+  static bool init = [] {
+    const char* e = getenv("PI05_SPLITS");
+    if (e != nullptr) sscanf(e, "%d,%d,%d,%d", &v[0], &v[1], &v[2], &v[3]);
+    return true;
+  }();
+  (void)init;
+  return v;
+}
 
 }  // namespace
 
@@ -63,6 +78,7 @@ int pi05_attention(const void* q, const void* k, const void* v, const uint8_t* k
   p.rows = rows;
   p.kv_len = kv_len;
   p.head_dim = head_dim;
+  p.status = w.status;
   p.scale = scale;
   return mqa_attention_run(p, w.scratch, w.scratch_bytes, splits, stream);
 }
@@ -143,7 +159,7 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
   }
   const int n_norm = 2 * P->depth + 1;
   const float* mods = P->mod_table + (size_t)step * n_norm * 3 * W;
-  const int split_override = 0;
+  const int* so = debug_split_overrides();  // per GEMM (qkv, o, gate/up, down); 0 = automatic
   auto* h = static_cast<__nv_bfloat16*>(P->h);
   auto* xn = static_cast<__nv_bfloat16*>(P->xn);
   auto* q = static_cast<__nv_bfloat16*>(P->q);
@@ -188,7 +204,7 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.pf0 = N.w_qkv;
       sp.pf0_bytes = (size_t)rows * W * 2;
       sp.trace_tag = (step * P->depth + l) * 8 + 0;
-      rc = skinny_gemm_run(SK_EPI_QKV_ROPE, sp, L.w_qkv, L.w_qkv, rows, rows, xn, W, split_override, stream);
+      rc = skinny_gemm_run(SK_EPI_QKV_ROPE, sp, L.w_qkv, L.w_qkv, rows, rows, xn, W, so[0], stream);
       if (rc) break;
     }
     // attention over [prefix | suffix] keys
@@ -206,6 +222,10 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       ap.kv_len = kv_len;
       ap.head_dim = D;
       ap.scale = scale;
+      ap.status = ws.status;
+      ap.static_rows = P->prefix_len;  // prefix K/V rows and mask are fixed during the loop
+      ap.trace = P->trace;
+      ap.trace_tag = (step * P->depth + l) * 8 + 4;  // combine: + 5
       rc = mqa_attention_run(ap, ws.scratch, ws.scratch_bytes, P->attn_splits, stream);
       if (rc) break;
     }
@@ -228,7 +248,7 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.pf0 = N.w_o;
       sp.pf0_bytes = (size_t)W * HQ * D * 2;
       sp.trace_tag = (step * P->depth + l) * 8 + 1;
-      rc = skinny_gemm_run(SK_EPI_GATED_RESID, sp, L.w_o, L.w_o, W, W, attn, HQ * D, split_override, stream);
+      rc = skinny_gemm_run(SK_EPI_GATED_RESID, sp, L.w_o, L.w_o, W, W, attn, HQ * D, so[1], stream);
       if (rc) break;
     }
     // post_attention_layernorm (adaRMS)
@@ -252,7 +272,7 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.pf1 = N.w_up;
       sp.pf1_bytes = (size_t)F * W * 2;
       sp.trace_tag = (step * P->depth + l) * 8 + 2;
-      rc = skinny_gemm_run(SK_EPI_GEGLU, sp, L.w_gate, L.w_up, F, F, xn, W, split_override, stream);
+      rc = skinny_gemm_run(SK_EPI_GEGLU, sp, L.w_gate, L.w_up, F, F, xn, W, so[2], stream);
       if (rc) break;
     }
     // down + gated residual (gate = third chunk of mod2)
@@ -274,7 +294,7 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.pf0 = N.w_down;
       sp.pf0_bytes = (size_t)W * F * 2;
       sp.trace_tag = (step * P->depth + l) * 8 + 3;
-      rc = skinny_gemm_run(SK_EPI_GATED_RESID, sp, L.w_down, L.w_down, W, W, act, F, split_override, stream);
+      rc = skinny_gemm_run(SK_EPI_GATED_RESID, sp, L.w_down, L.w_down, W, W, act, F, so[3], stream);
       if (rc) break;
     }
   }

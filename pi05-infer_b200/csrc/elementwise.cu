@@ -173,7 +173,8 @@ __global__ void __launch_bounds__(1024) rope_table_kernel(const uint8_t* __restr
   __syncthreads();
   const int total = n > 0 ? cnt[n - 1] : 0;
   const int half = d / 2;
-  for (int idx = threadIdx.x; idx < rows * d; idx += blockDim.x) {
+  // Every CTA repeats the (cheap) scan and writes a grid-strided share of the table.
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < rows * d; idx += gridDim.x * blockDim.x) {
     const int r = idx / d, c = idx % d;
     const int pos = (mode == 0) ? cnt[r] - 1 : total + r;
     const float f = (float)pos * inv_freq[c % half];
@@ -280,7 +281,9 @@ int rope_table_run(const uint8_t* valid, int n_prefix, int mode, int rows, const
     set_last_error("rope_table: prefix > 4096 or rows > prefix");
     return PI05_ERR_SHAPE;
   }
-  return launch_pdl(rope_table_kernel, dim3(1), dim3(1024), 0, reinterpret_cast<cudaStream_t>(stream),
+  const int blocks = (rows * d + 1023) / 1024;
+  const int grid = blocks < 1 ? 1 : (blocks > 148 ? 148 : blocks);
+  return launch_pdl(rope_table_kernel, dim3(grid), dim3(1024), 0, reinterpret_cast<cudaStream_t>(stream),
                     pdl_enabled(), valid, n_prefix, mode, rows, inv_freq, d, static_cast<__nv_bfloat16*>(cos),
                     static_cast<__nv_bfloat16*>(sin));
 }

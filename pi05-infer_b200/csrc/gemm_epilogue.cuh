@@ -238,7 +238,8 @@ __device__ __forceinline__ void unit_finish(const SkinnyParams& p, int tile, int
 // selects the 128 epilogue threads, `et` is their index.
 template <int EPI, int KIND, int U>
 __device__ __forceinline__ void cluster_epilogue_body(const SkinnyParams& p, uint32_t st, int tile, int tok0,
-                                                      int u0, int u1, int et, bool epi) {
+                                                      int u0, int u1, int et, bool epi,
+                                                      unsigned long long* bar_stamp) {
   constexpr int H = (KIND == CK_GEGLU || KIND == CK_ROT) ? 2 : 1;
   constexpr int KS = 16 / (U * H) > 0 ? 16 / (U * H) : 1;  // splits per batch of DSMEM loads
   const int splits = p.splits;
@@ -252,6 +253,7 @@ __device__ __forceinline__ void cluster_epilogue_body(const SkinnyParams& p, uin
   }
   __syncwarp();
   cluster_sync_all();
+  if (bar_stamp != nullptr && epi && et == 0) *bar_stamp = globaltimer_ns();
   if (!epi) return;
   for (int base = u0 + et, pass = 0; base < u1; base += U * kEpiThreads, ++pass) {
     bool ok[U];
@@ -315,18 +317,18 @@ __device__ __forceinline__ void cluster_epilogue_body(const SkinnyParams& p, uin
 
 template <int EPI, int KIND>
 __device__ __forceinline__ void cluster_epilogue_kind(const SkinnyParams& p, uint32_t st, int tile, int tok0, int mt,
-                                                      int rank, int et, bool epi) {
+                                                      int rank, int et, bool epi, unsigned long long* bar_stamp) {
   constexpr int H = (KIND == CK_GEGLU || KIND == CK_ROT) ? 2 : 1;
   const int units = mt * (H == 2 ? 16 : 32);
   const int u0 = (int)(((long)rank * units) / p.splits);
   const int u1 = (int)(((long)(rank + 1) * units) / p.splits);
   const int per_thread = (u1 - u0 + kEpiThreads - 1) / kEpiThreads;
   if (per_thread >= 4 && p.splits * H * 4 <= 16)
-    cluster_epilogue_body<EPI, KIND, 4>(p, st, tile, tok0, u0, u1, et, epi);
+    cluster_epilogue_body<EPI, KIND, 4>(p, st, tile, tok0, u0, u1, et, epi, bar_stamp);
   else if (per_thread >= 2 && p.splits * H * 2 <= 16)
-    cluster_epilogue_body<EPI, KIND, 2>(p, st, tile, tok0, u0, u1, et, epi);
+    cluster_epilogue_body<EPI, KIND, 2>(p, st, tile, tok0, u0, u1, et, epi, bar_stamp);
   else
-    cluster_epilogue_body<EPI, KIND, 1>(p, st, tile, tok0, u0, u1, et, epi);
+    cluster_epilogue_body<EPI, KIND, 1>(p, st, tile, tok0, u0, u1, et, epi, bar_stamp);
 }
 
 // Whole cluster split-K epilogue (both cluster barriers included); every thread of
@@ -334,17 +336,18 @@ __device__ __forceinline__ void cluster_epilogue_kind(const SkinnyParams& p, uin
 // peers have finished reading it.
 template <int EPI>
 __device__ __forceinline__ void cluster_epilogue(const SkinnyParams& p, uint32_t st, int tile, int tok0, int mt,
-                                                 int rank, int et, bool epi) {
+                                                 int rank, int et, bool epi,
+                                                 unsigned long long* bar_stamp = nullptr) {
   if (EPI == SK_EPI_GEGLU) {
-    cluster_epilogue_kind<EPI, CK_GEGLU>(p, st, tile, tok0, mt, rank, et, epi);
+    cluster_epilogue_kind<EPI, CK_GEGLU>(p, st, tile, tok0, mt, rank, et, epi, bar_stamp);
   } else if (EPI == SK_EPI_QKV_ROPE) {
     const int n_rot_tiles = (p.n_q_heads + p.n_kv_heads) * (p.head_dim / 128);
     if (tile < n_rot_tiles)
-      cluster_epilogue_kind<EPI, CK_ROT>(p, st, tile, tok0, mt, rank, et, epi);
+      cluster_epilogue_kind<EPI, CK_ROT>(p, st, tile, tok0, mt, rank, et, epi, bar_stamp);
     else
-      cluster_epilogue_kind<EPI, CK_V>(p, st, tile, tok0, mt, rank, et, epi);
+      cluster_epilogue_kind<EPI, CK_V>(p, st, tile, tok0, mt, rank, et, epi, bar_stamp);
   } else {
-    cluster_epilogue_kind<EPI, CK_ROWS>(p, st, tile, tok0, mt, rank, et, epi);
+    cluster_epilogue_kind<EPI, CK_ROWS>(p, st, tile, tok0, mt, rank, et, epi, bar_stamp);
   }
   __syncwarp();
   cluster_sync_all();

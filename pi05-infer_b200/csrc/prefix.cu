@@ -142,6 +142,7 @@ int pi05_prefix_forward(const Pi05PrefixPlan* P, void* stream) {
       ap.rows = T * HQ;
       ap.kv_len = T;
       ap.head_dim = D;
+      ap.status = ws.status;
       ap.scale = scale;
       rc = mqa_attention_run(ap, ws.scratch, ws.scratch_bytes, 0, stream);
       if (rc) break;

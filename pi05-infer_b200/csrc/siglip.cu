@@ -138,7 +138,8 @@ __global__ void __launch_bounds__(128) mha72_kernel(const __nv_bfloat16* __restr
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const size_t ld = (size_t)3 * width;
   const __nv_bfloat16* base = qkv + (size_t)view * SEQ * ld + h * kHd;
-  // 9 chunks of 16 B per 72-element row; columns 72..79 zero.
+  // 9 chunks of 16 B per 72-element row, copied asynchronously (all in flight at
+  // once); chunk 9 (columns 72..79) is zero-filled.
   for (int i = tid; i < (64 + 2 * SEQ) * 10; i += 128) {
     const int row = i / 10, c = i % 10;
     __nv_bfloat16* dst;
@@ -153,10 +154,12 @@ __global__ void __launch_bounds__(128) mha72_kernel(const __nv_bfloat16* __restr
       dst = sV + (row - 64 - SEQ) * kRowE;
       srcp = base + (size_t)(row - 64 - SEQ) * ld + 2 * width;
     }
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (c < 9) v = *reinterpret_cast<const uint4*>(srcp + c * 8);
-    *reinterpret_cast<uint4*>(dst + c * 8) = v;
+    const int n = c < 9 ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst + c * 8)),
+                 "l"(srcp + (c < 9 ? c * 8 : 0)), "r"(n)
+                 : "memory");
   }
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
   __syncthreads();
   const uint32_t aQ = static_cast<uint32_t>(__cvta_generic_to_shared(sQ));
   const uint32_t aK = static_cast<uint32_t>(__cvta_generic_to_shared(sK));

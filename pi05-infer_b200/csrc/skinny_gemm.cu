@@ -258,9 +258,13 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
   // epilogue between its two cluster barriers.
   if (p.cluster) {
     __syncwarp();
+    unsigned long long* bar_stamp = reinterpret_cast<unsigned long long*>(accum + 4);
     cluster_epilogue<EPI>(p, smem_u32(stage_tile), tile, tok0, mt, (int)cluster_ctarank(), (int)threadIdx.x - 64,
-                          warp >= 2);
-    if (p.trace != nullptr) t_red = globaltimer_ns();
+                          warp >= 2, p.trace != nullptr ? bar_stamp : nullptr);
+    if (p.trace != nullptr) {
+      t_red = globaltimer_ns();
+      t_pub = *bar_stamp;  // written by this thread (epilogue thread 0) after the first cluster barrier
+    }
   }
 
   if (p.trace != nullptr && threadIdx.x == 64) {
