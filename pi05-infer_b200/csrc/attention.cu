@@ -24,6 +24,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <cstdlib>
 #include <cstring>
 
 #include "host_util.h"
@@ -287,13 +288,13 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
             __floats2bfloat162_rn(o[j][2 * h] * inv, o[j][2 * h + 1] * inv);
       }
     } else {
-      float* dst = p.part_o + ((size_t)split * p.rows + r) * kD;
+      float* dst = p.part_o + ((size_t)split * p.part_rows + r) * kD;
 #pragma unroll
       for (int j = 0; j < 32; ++j)
         *reinterpret_cast<float2*>(dst + j * 8 + 2 * t4) = make_float2(o[j][2 * h], o[j][2 * h + 1]);
       if (t4 == 0) {
-        p.part_ml[((size_t)split * p.rows + r) * 2] = m_run[h];
-        p.part_ml[((size_t)split * p.rows + r) * 2 + 1] = l_run[h];
+        p.part_ml[((size_t)split * p.part_rows + r) * 2] = m_run[h];
+        p.part_ml[((size_t)split * p.part_rows + r) * 2 + 1] = l_run[h];
       }
     }
   }
@@ -325,8 +326,8 @@ __global__ void __launch_bounds__(256) mqa_combine_kernel(const AttnParams p) {
   const int r = warp;
   float ms = -INFINITY, ls = 0.f;
   if (lane < p.splits) {
-    ms = p.part_ml[((size_t)lane * p.rows + r) * 2];
-    ls = p.part_ml[((size_t)lane * p.rows + r) * 2 + 1];
+    ms = p.part_ml[((size_t)lane * p.part_rows + r) * 2];
+    ls = p.part_ml[((size_t)lane * p.part_rows + r) * 2 + 1];
   }
   float mmax = ms;
   for (int o = 16; o > 0; o >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffff, mmax, o));
@@ -342,7 +343,8 @@ __global__ void __launch_bounds__(256) mqa_combine_kernel(const AttnParams p) {
       const int sj = s0 + j;
       ws[j] = __shfl_sync(0xffffffff, w, sj & 31);
       if (sj < p.splits) {
-        const float4* src = reinterpret_cast<const float4*>(p.part_o + ((size_t)sj * p.rows + r) * kD + lane * 8);
+        const float4* src =
+            reinterpret_cast<const float4*>(p.part_o + ((size_t)sj * p.part_rows + r) * kD + lane * 8);
         a[j] = __ldcg(src);
         b[j] = __ldcg(src + 1);
       } else {
@@ -388,7 +390,15 @@ int set_attn_smem() {
 
 }  // namespace
 
-constexpr int kTcMinRows = 1024;  // query rows above which the tcgen05 kernel is used
+// Query rows above which the tcgen05 kernel is used (PI05_ATTN_TC_MIN_ROWS overrides,
+// for tuning).
+int tc_min_rows() {
+  static int v = [] {
+    const char* e = getenv("PI05_ATTN_TC_MIN_ROWS");
+    return e != nullptr ? atoi(e) : 1024;
+  }();
+  return v;
+}
 
 int launch_combine(const AttnParams& p, cudaStream_t st) {
   return launch_pdl(mqa_combine_kernel, dim3((p.rows + 7) / 8), dim3(256), 0, st, pdl_enabled(), p);
@@ -406,7 +416,7 @@ int mqa_attention_run(AttnParams p, float* part, size_t part_bytes, int splits, 
   }
   // tcgen05 for many query rows (prefix LM: 968 x 8); the mma.sync kernel below is
   // faster for the denoise suffix (50 x 8 rows), where each CTA owns one key chunk.
-  if (tc_attention_enabled() && p.rows > kTcMinRows)
+  if (tc_attention_enabled() && p.rows > tc_min_rows())
     return mqa_tc_attention_run(p, part, part_bytes, splits, st, launch_combine);
   constexpr int W = 4;
   constexpr int kRows = 16 * W;
@@ -433,6 +443,7 @@ int mqa_attention_run(AttnParams p, float* part, size_t part_bytes, int splits, 
       set_last_error("attention: workspace too small (%zu needed)", need);
       return PI05_ERR_WORKSPACE;
     }
+    p.part_rows = p.rows;
     p.part_o = part;
     p.part_ml = part + (size_t)splits * p.rows * kD;
   }

@@ -28,8 +28,9 @@ struct AttnParams {
   int* status = nullptr;               // device status word (bounded-wait timeouts)
   unsigned long long* trace = nullptr; // optional per-CTA timestamps (same format as the GEMMs)
   int trace_tag = 0;
-  float* part_o = nullptr;             // [splits, rows, head_dim]
-  float* part_ml = nullptr;            // [splits, rows, 2]
+  float* part_o = nullptr;             // [splits, part_rows, head_dim]
+  float* part_ml = nullptr;            // [splits, part_rows, 2]
+  int part_rows = 0;                   // row pitch of one split's partials (>= rows)
 };
 
 // splits <= 0 picks a split count that covers the SMs.  head_dim 256 runs on the

@@ -51,8 +51,9 @@ constexpr uint32_t kColO = 128;              // S buffers at columns 0 and 64, O
 constexpr uint32_t kIdescS = umma_idesc_bf16(kBR, kBC);
 constexpr uint32_t kIdescPV = umma_idesc_bf16(kBR, kD) | (1u << 16);  // B (V) MN-major
 
+// out: bf16 [R, 256] output (no split); po: fp32 split partials [splits * part_rows, 256].
 struct TcMaps {
-  CUtensorMap q, k, v;
+  CUtensorMap q, k, v, out, po;
 };
 
 size_t tc_smem_bytes(int nst) { return 1024 + kQBytes + (size_t)nst * 2 * kKVBytes + kPBytes + 256; }
@@ -85,6 +86,9 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
   int* s_flag = reinterpret_cast<int*>(s_tmem + 1);  // [0] abort, [1] K/V chunks armed
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool tr = p.trace != nullptr && threadIdx.x == 64;
+  const uint64_t t_entry = tr ? globaltimer_ns() : 0;
+  uint64_t t_wait = 0, t_data = 0, t_loop = 0;
   const int row0 = blockIdx.x * kBR;
   const int split = blockIdx.y;
   const int n_chunks_total = (p.kv_len + kBC - 1) / kBC;
@@ -111,6 +115,7 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
     prefetch_tmap(&mp.q);
     prefetch_tmap(&mp.k);
     prefetch_tmap(&mp.v);
+    prefetch_tmap(p.splits == 1 ? &mp.out : &mp.po);
   }
   if (warp == 1) {
     tmem_alloc(s_tmem, kTmemCols);
@@ -198,6 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
   } else {
     // Softmax warps: TMEM lane quarter = warp % 4, one query row per thread.
     pdl_wait();
+    if (tr) t_wait = globaltimer_ns();
     const int q = warp & 3;
     const int r = q * 32 + lane;
     const int grow = row0 + r;
@@ -206,16 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
     bool ok = true;
     for (int j = 0; j < nc; ++j) {
       const int sb = j & 1;
-      if (!mbar_wait(&s_full[sb], (j >> 1) & 1)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      float s[64];
-      tmem_ld32(tmem + lane_base + sb * kBC, s);
-      tmem_ld32(tmem + lane_base + sb * kBC + 32, s + 32);
-      tc_fence_before();
-      mbar_arrive(&s_empty[sb]);
+      // The chunk's key mask (static) is read while the scores are computed.
       const int key0 = (c_begin + j) * kBC;
       uint8_t vk[64];
       if (key0 + kBC <= p.kv_len && (reinterpret_cast<uintptr_t>(p.key_valid) & 15) == 0) {
@@ -226,6 +223,17 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
 #pragma unroll
         for (int i = 0; i < 64; ++i) vk[i] = (key0 + i < p.kv_len) ? p.key_valid[key0 + i] : 0;
       }
+      if (!mbar_wait(&s_full[sb], (j >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (tr && j == 0) t_data = globaltimer_ns();
+      float s[64];
+      tmem_ld32(tmem + lane_base + sb * kBC, s);
+      tmem_ld32(tmem + lane_base + sb * kBC + 32, s + 32);
+      tc_fence_before();
+      mbar_arrive(&s_empty[sb]);
       float mx = -INFINITY;
 #pragma unroll
       for (int i = 0; i < 64; ++i) {
@@ -282,35 +290,76 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
     if (!ok) report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
     if (ok && nc > 0 && mbar_wait(p_empty, (nc - 1) & 1)) {
       tc_fence_after();
-      // Every lane runs the (warp-collective) TMEM loads; rows past R store nothing.
-      const bool live = grow < p.rows;
-      const float inv = l > 0.f ? 1.f / l : 0.f;
+      if (tr) t_loop = globaltimer_ns();
+      // Output through shared memory: Q and the K/V ring are free once every MMA
+      // is done.  Each warp stages its 32 rows in 128B-swizzled 4 KB slabs (32 KB
+      // per warp) and writes them with TMA tensor stores (rows past R are clipped).
+      uint8_t* slab0 = smem + (warp - 2) * 8 * 4096;
+      if (p.splits == 1) {
+        const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll 1
-      for (int c = 0; c < kD / 32; ++c) {
-        float o[32];
-        tmem_ld32(tmem + lane_base + kColO + c * 32, o);
-        if (!live) continue;
-        if (p.splits == 1) {
-          __nv_bfloat16* dst = p.out + (size_t)grow * p.out_stride + c * 32;
+        for (int jb = 0; jb < kD / 64; ++jb) {
+          uint8_t* slab = slab0 + jb * 4096;
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            float o[32];
+            tmem_ld32(tmem + lane_base + kColO + jb * 64 + h * 32, o);
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            uint4 u;
-            u.x = pack_bf16x2(o[g * 8 + 0] * inv, o[g * 8 + 1] * inv);
-            u.y = pack_bf16x2(o[g * 8 + 2] * inv, o[g * 8 + 3] * inv);
-            u.z = pack_bf16x2(o[g * 8 + 4] * inv, o[g * 8 + 5] * inv);
-            u.w = pack_bf16x2(o[g * 8 + 6] * inv, o[g * 8 + 7] * inv);
-            *reinterpret_cast<uint4*>(dst + g * 8) = u;
+            for (int g4 = 0; g4 < 4; ++g4) {
+              uint4 u;
+              u.x = pack_bf16x2(o[g4 * 8 + 0] * inv, o[g4 * 8 + 1] * inv);
+              u.y = pack_bf16x2(o[g4 * 8 + 2] * inv, o[g4 * 8 + 3] * inv);
+              u.z = pack_bf16x2(o[g4 * 8 + 4] * inv, o[g4 * 8 + 5] * inv);
+              u.w = pack_bf16x2(o[g4 * 8 + 6] * inv, o[g4 * 8 + 7] * inv);
+              *reinterpret_cast<uint4*>(slab + p_off(lane, h * 4 + g4)) = u;
+            }
           }
-        } else {
-          float* dst = p.part_o + ((size_t)split * p.rows + grow) * kD + c * 32;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          for (int jb = 0; jb < kD / 64; ++jb) tma_store_2d(&mp.out, slab0 + jb * 4096, jb * 64, row0 + q * 32);
+          bulk_commit_group();
+        }
+      } else {
+        const int y = split * p.part_rows + row0 + q * 32;
+#pragma unroll 1
+        for (int c = 0; c < kD / 32; ++c) {
+          uint8_t* slab = slab0 + c * 4096;
+          float o[32];
+          tmem_ld32(tmem + lane_base + kColO + c * 32, o);
 #pragma unroll
           for (int g = 0; g < 8; ++g)
-            *reinterpret_cast<float4*>(dst + g * 4) = make_float4(o[g * 4], o[g * 4 + 1], o[g * 4 + 2], o[g * 4 + 3]);
+            *reinterpret_cast<float4*>(slab + p_off(lane, g)) =
+                make_float4(o[g * 4], o[g * 4 + 1], o[g * 4 + 2], o[g * 4 + 3]);
         }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          for (int c = 0; c < kD / 32; ++c) tma_store_2d(&mp.po, slab0 + c * 4096, c * 32, y);
+          bulk_commit_group();
+        }
+        // (max, sum) of every row of the padded block; rows past R are padding.
+        p.part_ml[((size_t)split * p.part_rows + grow) * 2] = m;
+        p.part_ml[((size_t)split * p.part_rows + grow) * 2 + 1] = l;
       }
-      if (live && p.splits > 1) {
-        p.part_ml[((size_t)split * p.rows + grow) * 2] = m;
-        p.part_ml[((size_t)split * p.rows + grow) * 2 + 1] = l;
+      if (lane == 0) bulk_wait_group<0>();
+      __syncwarp();
+      // Trace record {tag << 32 | cta, entry, grid-dependency wait done, first S
+      // ready, last P.V done, output stored, 0, 0} (same layout as attention.cu).
+      if (tr) {
+        const unsigned long long slot = atomicAdd(p.trace, 1ull);
+        if (slot < p.trace[1]) {
+          unsigned long long* w = p.trace + 8 + slot * 8;
+          w[0] = ((unsigned long long)p.trace_tag << 32) | (blockIdx.y * gridDim.x + blockIdx.x);
+          w[1] = t_entry;
+          w[2] = t_wait;
+          w[3] = t_data;
+          w[4] = t_loop;
+          w[5] = globaltimer_ns();
+          w[6] = 0;
+          w[7] = 0;
+        }
       }
     } else if (ok && nc > 0) {
       report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
@@ -356,27 +405,37 @@ int mqa_tc_attention_run(AttnParams p, float* part, size_t part_bytes, int split
   }
   if (splits <= 0) {
     // Fill about one wave; fewer splits keep the partial round trip small.
+    // PI05_ATTN_TC_SPLITS overrides (tuning).
+    static const int force = [] {
+      const char* e = getenv("PI05_ATTN_TC_SPLITS");
+      return e != nullptr ? atoi(e) : 0;
+    }();
     splits = std::max(1, std::min(n_chunks, sms / std::max(1, row_blocks)));
     splits = std::min(splits, 16);
+    if (force > 0) splits = force;
   }
   splits = std::min(splits, n_chunks);
   splits = std::min(splits, 32);
   p.splits = splits;
   p.nbuf = (n_chunks + splits - 1) / splits > 1 ? 2 : 1;
+  p.part_rows = row_blocks * kBR;  // partial rows padded to whole row blocks
   if (splits > 1) {
-    const size_t need = (size_t)splits * p.rows * kD * sizeof(float) + (size_t)splits * p.rows * 2 * sizeof(float);
-    if (part == nullptr || need > part_bytes) {
+    const size_t rows_all = (size_t)splits * p.part_rows;
+    const size_t need = rows_all * kD * sizeof(float) + rows_all * 2 * sizeof(float);
+    if (part == nullptr || need > part_bytes || (reinterpret_cast<uintptr_t>(part) & 15) != 0) {
       set_last_error("attention: workspace too small (%zu needed)", need);
       return PI05_ERR_WORKSPACE;
     }
     p.part_o = part;
-    p.part_ml = part + (size_t)splits * p.rows * kD;
+    p.part_ml = part + rows_all * kD;
   }
   TcMaps mp;
   std::memset(&mp, 0, sizeof(mp));
   int rc = make_tmap_bf16_2d(&mp.q, p.q, p.rows, kD, p.q_stride, kBR, 64, true);
   if (!rc) rc = make_tmap_bf16_2d(&mp.k, p.k, p.kv_len, kD, p.kv_stride, kBC, 64, true);
   if (!rc) rc = make_tmap_bf16_2d(&mp.v, p.v, p.kv_len, kD, p.kv_stride, kBC, 64, true);
+  if (!rc && splits == 1) rc = make_tmap_bf16_2d(&mp.out, p.out, p.rows, kD, p.out_stride, 32, 64, true);
+  if (!rc && splits > 1) rc = make_tmap_f32_2d(&mp.po, p.part_o, (uint64_t)splits * p.part_rows, kD, kD, 32, 32, true);
   if (rc) return rc;
   const size_t smem = tc_smem_bytes(p.nbuf);
   static bool attr_done[16] = {false};

@@ -244,6 +244,11 @@ __device__ __forceinline__ void cluster_epilogue_body(const SkinnyParams& p, uin
   constexpr int KS = 16 / (U * H) > 0 ? 16 / (U * H) : 1;  // splits per batch of DSMEM loads
   const int splits = p.splits;
   UnitOps ops[U];
+  // Publish the staging tile, then issue the global operand loads of the first
+  // pass while the barrier completes (a release arrive would otherwise wait for
+  // them).
+  __syncwarp();
+  cluster_arrive_release();
   if (epi) {
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -252,7 +257,7 @@ __device__ __forceinline__ void cluster_epilogue_body(const SkinnyParams& p, uin
     }
   }
   __syncwarp();
-  cluster_sync_all();
+  cluster_wait();
   if (bar_stamp != nullptr && epi && et == 0) *bar_stamp = globaltimer_ns();
   if (!epi) return;
   for (int base = u0 + et, pass = 0; base < u1; base += U * kEpiThreads, ++pass) {
@@ -349,8 +354,11 @@ __device__ __forceinline__ void cluster_epilogue(const SkinnyParams& p, uint32_t
   } else {
     cluster_epilogue_kind<EPI, CK_ROWS>(p, st, tile, tok0, mt, rank, et, epi, bar_stamp);
   }
+  // Exit barrier: no CTA leaves while peers still read its staging tile.  The
+  // epilogue's global stores need no ordering here, so the arrive is relaxed.
   __syncwarp();
-  cluster_sync_all();
+  cluster_arrive_relaxed();
+  cluster_wait();
 }
 
 // Epilogue items are groups of 8 consecutive tile rows of one token: mt * 16

@@ -35,23 +35,22 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return g_encode;
 }
 
-int make_tmap_bf16_2d(CUtensorMap* tm, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
-                      uint32_t box_rows, uint32_t box_cols, bool swizzle128) {
+static int make_tmap_2d(CUtensorMap* tm, CUtensorMapDataType dt, uint32_t esize, const void* base, uint64_t rows,
+                       uint64_t cols, uint64_t ld, uint32_t box_rows, uint32_t box_cols, bool swizzle128) {
   auto fn = encode_fn();
   if (fn == nullptr) {
     set_last_error("cuTensorMapEncodeTiled entry point unavailable");
     return PI05_ERR_DRIVER;
   }
-  if (!aligned16(base) || (ld * 2) % 16 != 0) {
+  if (!aligned16(base) || (ld * esize) % 16 != 0) {
     set_last_error("tensor map base/pitch not 16-byte aligned");
     return PI05_ERR_ALIGN;
   }
   cuuint64_t dims[2] = {cols, rows};
-  cuuint64_t strides[1] = {ld * 2};
+  cuuint64_t strides[1] = {ld * esize};
   cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+  CUresult r = fn(tm, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
@@ -61,6 +60,16 @@ int make_tmap_bf16_2d(CUtensorMap* tm, const void* base, uint64_t rows, uint64_t
     return PI05_ERR_TMAP;
   }
   return PI05_OK;
+}
+
+int make_tmap_bf16_2d(CUtensorMap* tm, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                      uint32_t box_rows, uint32_t box_cols, bool swizzle128) {
+  return make_tmap_2d(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, rows, cols, ld, box_rows, box_cols, swizzle128);
+}
+
+int make_tmap_f32_2d(CUtensorMap* tm, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                     uint32_t box_rows, uint32_t box_cols, bool swizzle128) {
+  return make_tmap_2d(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, rows, cols, ld, box_rows, box_cols, swizzle128);
 }
 
 static std::atomic<long long> g_launches{0};

@@ -56,6 +56,10 @@ const char* get_last_error();
 int make_tmap_bf16_2d(CUtensorMap* tm, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
                       uint32_t box_rows, uint32_t box_cols, bool swizzle128);
 
+// Same for fp32 elements (box_cols * 4 == 128 with the swizzle).
+int make_tmap_f32_2d(CUtensorMap* tm, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                     uint32_t box_rows, uint32_t box_cols, bool swizzle128);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 // Count of kernel launches issued by this library (all threads, all devices).

@@ -277,6 +277,22 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// Split-phase cluster barrier.  arrive.release publishes this thread's earlier
+// shared-memory writes to the cluster; work issued between arrive and wait (e.g.
+// global loads that the release must not wait for) overlaps the barrier.
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+
+// Arrive without ordering earlier memory operations (for an exit barrier whose
+// only purpose is that no CTA leaves while peers still read its shared memory:
+// those reads have completed, their values consumed, before the arrive).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
