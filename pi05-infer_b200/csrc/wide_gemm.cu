@@ -71,7 +71,56 @@ struct WideSched {
   int m_tiles;
   int n_tiles;
   int kb_total;
+  int splits;  // split-K (STORE / GATED_RESID only)
 };
+
+// Work item t: m fastest (CTAs resident together share weight tiles), then the
+// K split, then n.
+struct WideTile {
+  int m, s, n, kb0, kb1;
+};
+
+__device__ __forceinline__ WideTile wide_tile(int t, const WideSched& ws) {
+  WideTile w;
+  w.m = t % ws.m_tiles;
+  const int r = t / ws.m_tiles;
+  w.s = r % ws.splits;
+  w.n = r / ws.splits;
+  w.kb0 = (w.s * ws.kb_total) / ws.splits;
+  w.kb1 = ((w.s + 1) * ws.kb_total) / ws.splits;
+  return w;
+}
+
+// Split-K partials of one output tile: [split][128 rows][BN] fp32, row-major, so
+// a thread (one row) moves whole 128-byte lines.
+struct WideSplit {
+  const float* part;  // this tile's partials; nullptr without split-K
+  int splits, own, row;
+};
+
+// Accumulator columns [col, col + 32) of this thread's row: from TMEM, or (the
+// split that finishes a split-K tile) the sum of every split's partial in split
+// order, its own taken from TMEM (bit-identical to the stored copy).
+template <int BN>
+__device__ __forceinline__ void wide_acc32(uint32_t taddr, int col, const WideSplit& sp, float* v) {
+  if (sp.part == nullptr) {
+    tmem_ld32(taddr + col, v);
+    return;
+  }
+  // Two splits (the launcher never uses more): the other split's 32 values are
+  // loaded before the TMEM read, so the row costs one L2 round trip per chunk.
+  const int other = 1 - sp.own;
+  const float4* src = reinterpret_cast<const float4*>(sp.part + ((size_t)other * 128 + sp.row) * BN + col);
+  float4 a[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) a[i] = __ldcg(src + i);
+  float own[32];
+  tmem_ld32(taddr + col, own);
+  const float* first = sp.own == 0 ? own : reinterpret_cast<const float*>(a);
+  const float* second = sp.own == 0 ? reinterpret_cast<const float*>(a) : own;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = (0.f + first[i]) + second[i];
+}
 
 // Tensor maps of one launch.  out: STORE / GATED_RESID / GEGLU output, or q_out
 // for QKV_ROPE.  in0 / in1: residual (GATED_RESID) or cos / sin (QKV_ROPE).
@@ -168,7 +217,7 @@ __device__ __forceinline__ void slab_store(const EpiWarp& e, const CUtensorMap* 
 // STORE / GATED_RESID (same arithmetic as apply_epilogue).
 template <int EPI, int BN>
 __device__ __forceinline__ bool wide_epi_rows(const SkinnyParams& p, const WideMaps& mp, EpiWarp& e, uint32_t taddr,
-                                              int n_tile, int m0) {
+                                              int n_tile, int m0, const WideSplit& sp) {
   constexpr int NS = BN / 64;
   const int r = e.lane;
   const int tok = m0 + e.q * 32 + r;
@@ -192,7 +241,7 @@ __device__ __forceinline__ bool wide_epi_rows(const SkinnyParams& p, const WideM
 #pragma unroll 1
     for (int h = 0; h < 2; ++h) {
       float v[32];
-      tmem_ld32(taddr + j * 64 + h * 32, v);
+      wide_acc32<BN>(taddr, j * 64 + h * 32, sp, v);
       if (EPI == SK_EPI_GATED_RESID && h == 0) ok = slab_wait(e, b, p.status) && ok;
 #pragma unroll
       for (int g4 = 0; g4 < 4; ++g4) {
@@ -363,7 +412,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
   const uint64_t t_entry = (p.trace != nullptr) ? globaltimer_ns() : 0;
   uint64_t t_setup = 0, t_acc = 0, t_epi = 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int total = ws.m_tiles * ws.n_tiles;
+  const int total = ws.m_tiles * ws.n_tiles * ws.splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -414,27 +463,29 @@ __global__ void __launch_bounds__(kWThreads, 1)
       int it = 0;
       bool waited = false;
       for (int t = blockIdx.x; t < total; t += gridDim.x) {
-        const int m = t % ws.m_tiles, n = t / ws.m_tiles;
+        const WideTile wt = wide_tile(t, ws);
+        const int m = wt.m;
         int row0, row1;
-        wide_rows<EPI, BN>(n, row0, row1);
+        wide_rows<EPI, BN>(wt.n, row0, row1);
         // First tile: weights do not depend on the previous kernel, so the first
         // ring's worth of W boxes is issued before the grid-dependency wait.
-        int kb = 0;
+        int kb = wt.kb0;
         if (!waited) {
-          const int pre = min(STAGES, ws.kb_total);
+          const int pre = min(STAGES, wt.kb1 - wt.kb0);
           for (int i = 0; i < pre; ++i) {
             mbar_arrive_expect_tx(&full[i], kStageBytes);
-            tma_load_2d(sB + i * kBBytes, &mp.w0, &full[i], i * kBK, row0, pol_w);
-            tma_load_2d(sB + i * kBBytes + kBBytes / 2, &mp.w1, &full[i], i * kBK, row1, pol_w);
+            tma_load_2d(sB + i * kBBytes, &mp.w0, &full[i], (wt.kb0 + i) * kBK, row0, pol_w);
+            tma_load_2d(sB + i * kBBytes + kBBytes / 2, &mp.w1, &full[i], (wt.kb0 + i) * kBK, row1, pol_w);
           }
           pdl_wait();
           waited = true;
           if (p.trace != nullptr) s_stamp[0] = globaltimer_ns();
-          for (int i = 0; i < pre; ++i) tma_load_2d(sA + i * kABytes, &mp.x, &full[i], i * kBK, m * kWBM, pol_x);
-          kb = pre;
+          for (int i = 0; i < pre; ++i)
+            tma_load_2d(sA + i * kABytes, &mp.x, &full[i], (wt.kb0 + i) * kBK, m * kWBM, pol_x);
+          kb = wt.kb0 + pre;
           it = pre;
         }
-        for (; kb < ws.kb_total; ++kb, ++it) {
+        for (; kb < wt.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1)) {
             report_status(p.status, PI05_DEV_TIMEOUT_PRODUCER);
@@ -465,7 +516,8 @@ __global__ void __launch_bounds__(kWThreads, 1)
         tc_fence_after();
         if (p.trace != nullptr && lt == 0) s_stamp[1] = globaltimer_ns();
         const uint32_t d = tmem + (uint32_t)(buf * BN);
-        for (int kb = 0; kb < ws.kb_total; ++kb, ++it) {
+        const WideTile wt = wide_tile(t, ws);
+        for (int kb = wt.kb0; kb < wt.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           if (!mbar_wait(&full[s], (it / STAGES) & 1)) {
             report_status(p.status, PI05_DEV_TIMEOUT_MMA);
@@ -478,7 +530,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)
             umma_bf16(d, umma_sdesc_sw128(a0 + kk * 32), umma_sdesc_sw128(b0 + kk * 32), kIdesc,
-                      (kb > 0 || kk > 0) ? 1u : 0u);
+                      (kb > wt.kb0 || kk > 0) ? 1u : 0u);
           umma_commit(&empty[s]);
         }
         if (ok) umma_commit(&accf[buf]);
@@ -499,7 +551,8 @@ __global__ void __launch_bounds__(kWThreads, 1)
     e.phase = 0;
     int lt = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++lt) {
-      const int m = t % ws.m_tiles, n = t / ws.m_tiles;
+      const WideTile wt = wide_tile(t, ws);
+      const int m = wt.m, n = wt.n;
       const int buf = lt & 1;
       wide_epi_prefetch<EPI, BN>(p, mp, e, n, m * kWBM);
       if (!mbar_wait(&accf[buf], (lt >> 1) & 1)) {
@@ -514,8 +567,48 @@ __global__ void __launch_bounds__(kWThreads, 1)
         wide_epi_geglu(mp, e, taddr, n, m * kWBM);
       else if (EPI == SK_EPI_QKV_ROPE)
         ok = wide_epi_qkv(p, mp, e, taddr, n, m * kWBM);
-      else
-        ok = wide_epi_rows<EPI, BN>(p, mp, e, taddr, n, m * kWBM);
+      else {
+        WideSplit sp{nullptr, ws.splits, wt.s, e.q * 32 + lane};
+        bool finish = true;
+        if (ws.splits > 1) {
+          // Publish this split's partial (whole 128-byte lines per row), take a
+          // ticket; the split taking the last ticket sums all partials in split
+          // order and runs the epilogue.  No CTA waits for another.
+          const int tile_mn = n * ws.m_tiles + m;
+          float* part = p.accum + (size_t)tile_mn * ws.splits * kWBM * BN;
+          float* mine = part + ((size_t)wt.s * kWBM + sp.row) * BN;
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            float v[32];
+            tmem_ld32(taddr + c * 32, v);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              __stcg(reinterpret_cast<float4*>(mine + c * 32) + i,
+                     make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
+          }
+          __threadfence();
+          named_bar_sync(1, kEpiThreads);
+          if (threadIdx.x == 64) {
+            const int old = atomicAdd(p.counters + tile_mn, 1);
+            const int last = old == ws.splits - 1 ? 1 : 0;
+            if (last) atomicExch(p.counters + tile_mn, 0);  // re-armed for the next launch
+            s_flag[1] = last;
+          }
+          named_bar_sync(1, kEpiThreads);
+          finish = s_flag[1] != 0;
+          named_bar_sync(1, kEpiThreads);  // s_flag[1] is rewritten by the next split tile
+          if (finish) __threadfence();
+          sp.part = part;
+        }
+        if (finish) {
+          ok = wide_epi_rows<EPI, BN>(p, mp, e, taddr, n, m * kWBM, sp);
+        } else if (EPI == SK_EPI_GATED_RESID && e.lane == 0) {
+          // The residual slab prefetched for this tile is not consumed: retire its load.
+          ok = slab_wait(e, 0, p.status);
+        } else if (EPI == SK_EPI_GATED_RESID) {
+          e.phase ^= 1u;
+        }
+      }
       tc_fence_before();
       mbar_arrive(&acce[buf]);
       if (!ok) break;
@@ -589,7 +682,7 @@ int wide_launch(const SkinnyParams& p, const WideSched& ws, const WideMaps& mp, 
     }
     attr_done[dev] = true;
   }
-  const int total = ws.m_tiles * ws.n_tiles;
+  const int total = ws.m_tiles * ws.n_tiles * ws.splits;
   const int grid = std::min(total, wide_sms());
   return launch_pdl(kern, dim3(grid), dim3(kWThreads), kSmem, stream, pdl_enabled(), mp, p, ws);
 }
@@ -602,28 +695,37 @@ int env_int(const char* name) {
 
 }  // namespace
 
-int wide_choose(int epi, int m_tiles, int n_cols, int kb_total, int sms, int* bn) {
+int wide_choose(int epi, int m_tiles, int n_cols, int kb_total, int sms, int* bn, int* splits) {
   static const int force_bn = env_int("PI05_WIDE_BN");
+  static const int force_splits = env_int("PI05_WIDE_SPLITS");
+  *splits = 1;
   if (epi == SK_EPI_GEGLU || epi == SK_EPI_QKV_ROPE) {
     *bn = 256;
     return 0;
   }
-  // Minimise waves x (per-tile MMA time + fixed per-tile cost).  A 128-wide tile
-  // streams as many operand bytes per MMA cycle as it computes, a 256-wide tile
-  // two thirds of that, so narrow tiles only win when they fill more SMs.
+  // Estimated µs: waves x (k-blocks per tile x time per k-block + fixed cost per
+  // tile) + the partial round trip of a split.  A k-block moves 48 KB (256-wide) or
+  // 32 KB (128-wide) of operands, at about 100 GB/s per SM.
   double best_cost = 1e30;
   for (int b : {256, 128}) {
     const int nt = (n_cols + b - 1) / b;
-    const long tiles = (long)m_tiles * nt;
-    const long waves = (tiles + sms - 1) / sms;
-    const double per_tile = (double)kb_total * (b == 256 ? 1.0 : 0.667) + 4.0;
-    const double cost = (double)waves * per_tile;
-    if (cost < best_cost - 1e-9) {
-      best_cost = cost;
-      *bn = b;
+    for (int s = 1; s <= 2 && s * 8 <= kb_total; ++s) {
+      const long tiles = (long)m_tiles * nt * s;
+      const long waves = (tiles + sms - 1) / sms;
+      const double kb_per = (double)((kb_total + s - 1) / s);
+      // A split adds the partial write + ticket and one L2 round trip per 32
+      // columns when the finishing split reads the other partial.
+      const double reduce = s > 1 ? 1.0 + 0.9 * (b / 32) : 0.0;
+      const double cost = (double)waves * (kb_per * (b == 256 ? 0.44 : 0.34) + 3.0) + reduce;
+      if (cost < best_cost - 1e-9) {
+        best_cost = cost;
+        *bn = b;
+        *splits = s;
+      }
     }
   }
   if (force_bn == 128 || force_bn == 256) *bn = force_bn;
+  if (force_splits >= 1 && force_splits <= 2) *splits = force_splits;
   return 0;
 }
 
@@ -649,15 +751,22 @@ int wide_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int w
   WideSched ws;
   ws.m_tiles = (p.m_tok + kWBM - 1) / kWBM;
   ws.kb_total = (p.k + kBK - 1) / kBK;
-  int bn = 256;
-  wide_choose(epi, ws.m_tiles, n_cols, ws.kb_total, wide_sms(), &bn);
+  int bn = 256, splits = 1;
+  wide_choose(epi, ws.m_tiles, n_cols, ws.kb_total, wide_sms(), &bn, &splits);
   if (epi == SK_EPI_GEGLU)
     ws.n_tiles = (n_cols + 127) / 128;
   else if (epi == SK_EPI_QKV_ROPE)
     ws.n_tiles = p.n_q_heads + 2 * p.n_kv_heads;
   else
     ws.n_tiles = (n_cols + bn - 1) / bn;
-  p.splits = 1;
+  if (splits > 1) {
+    const size_t need = (size_t)ws.m_tiles * ws.n_tiles * splits * kWBM * bn * sizeof(float);
+    if (p.accum == nullptr || p.counters == nullptr || need > p.accum_bytes ||
+        (long)ws.m_tiles * ws.n_tiles > kWsMaxCounters || splits > ws.kb_total)
+      splits = 1;
+  }
+  ws.splits = splits;
+  p.splits = splits;
   p.n_valid = n_cols;
   WideMaps mp;
   std::memset(&mp, 0, sizeof(mp));

@@ -10,8 +10,8 @@ namespace pi05 {
 int wide_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int w_rows0, int w_rows1, int n_cols,
                   const void* x, int ldx, void* stream);
 
-// Tile width (128 / 256) for an epilogue kind and shape.
-int wide_choose(int epi, int m_tiles, int n_cols, int kb_total, int sms, int* bn);
+// Tile width (128 / 256) and split-K count for an epilogue kind and shape.
+int wide_choose(int epi, int m_tiles, int n_cols, int kb_total, int sms, int* bn, int* splits);
 
 // PI05_WIDE=0 in the environment keeps every projection on the small-token kernel.
 bool wide_disabled();
