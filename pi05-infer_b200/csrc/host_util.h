@@ -62,6 +62,9 @@ int make_tmap_f32_2d(CUtensorMap* tm, const void* base, uint64_t rows, uint64_t 
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// Buffer set by pi05_debug_set_trace (per-CTA GEMM timestamps), or nullptr.
+unsigned long long* debug_trace_buffer();
+
 // Count of kernel launches issued by this library (all threads, all devices).
 void count_launch();
 long long launch_count();

@@ -33,6 +33,10 @@ int ws_for_skinny(void* ws, size_t bytes, SkinnyParams* p) {
 
 }  // namespace
 
+namespace pi05 {
+unsigned long long* debug_trace_buffer() { return g_trace.load(); }
+}  // namespace pi05
+
 extern "C" {
 
 int pi05_abi_version(void) { return 1; }

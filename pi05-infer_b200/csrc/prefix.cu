@@ -56,6 +56,7 @@ SkinnyParams base_params(const Workspace& ws) {
   sp.counters = ws.counters;
   sp.accum = ws.accum;
   sp.accum_bytes = ws.accum_bytes;
+  sp.trace = debug_trace_buffer();
   return sp;
 }
 

@@ -266,6 +266,7 @@ SkinnyParams base_params(const Workspace& ws) {
   sp.counters = ws.counters;
   sp.accum = ws.accum;
   sp.accum_bytes = ws.accum_bytes;
+  sp.trace = debug_trace_buffer();
   return sp;
 }
 
@@ -364,6 +365,7 @@ int pi05_siglip_forward(const Pi05SiglipPlan* P, void* stream) {
       sp.out = qkv;
       sp.ldo = 3 * W;
       sp.bias = L.b_qkv;
+      sp.trace_tag = l * 8 + 0;
       rc = skinny_gemm_run(SK_EPI_STORE, sp, L.w_qkv, L.w_qkv, 3 * W, 3 * W, xn, W, 0, stream);
       if (rc) return rc;
     }
@@ -379,6 +381,7 @@ int pi05_siglip_forward(const Pi05SiglipPlan* P, void* stream) {
       sp.resid = h;
       sp.ldr = W;
       sp.bias = L.b_o;
+      sp.trace_tag = l * 8 + 1;
       rc = skinny_gemm_run(SK_EPI_GATED_RESID, sp, L.w_o, L.w_o, W, W, attn, W, 0, stream);
       if (rc) return rc;
     }
@@ -394,6 +397,7 @@ int pi05_siglip_forward(const Pi05SiglipPlan* P, void* stream) {
       sp.ldo = F;
       sp.bias = L.b_fc1;
       sp.act = 1;
+      sp.trace_tag = l * 8 + 2;
       rc = skinny_gemm_run(SK_EPI_STORE, sp, L.w_fc1, L.w_fc1, F, F, xn, W, 0, stream);
       if (rc) return rc;
     }
@@ -407,6 +411,7 @@ int pi05_siglip_forward(const Pi05SiglipPlan* P, void* stream) {
       sp.resid = h;
       sp.ldr = W;
       sp.bias = L.b_fc2;
+      sp.trace_tag = l * 8 + 3;
       rc = skinny_gemm_run(SK_EPI_GATED_RESID, sp, L.w_fc2, L.w_fc2, W, W, act, F, 0, stream);
       if (rc) return rc;
     }

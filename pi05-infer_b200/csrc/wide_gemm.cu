@@ -51,7 +51,14 @@ namespace pi05 {
 namespace {
 
 using namespace gemm;
-constexpr int kWThreads = 192;
+// Epilogue warps EW: 4 (one per TMEM lane quarter), or 8 (two per quarter, each
+// taking every other 64-column slab) for STORE / GATED_RESID grids whose tiles
+// have a short mainloop, where the epilogue of a single wave is exposed; the 8
+// warps' slabs cost one pipeline stage.
+template <int EW>
+constexpr int wide_threads() {
+  return 64 + 32 * EW;
+}
 constexpr int kWBM = 128;         // tokens per tile
 constexpr int kSlabBytes = 4096;  // 32 rows x 64 bf16, 128B swizzle
 
@@ -62,9 +69,9 @@ constexpr int epi_slabs() {
   return EPI == SK_EPI_QKV_ROPE ? 4 : 2;
 }
 
-template <int EPI, int BN, int STAGES>
+template <int EPI, int BN, int STAGES, int EW>
 constexpr int wide_smem_bytes() {
-  return 1024 + STAGES * (kABytes + BN * 128) + 4 * epi_slabs<EPI>() * kSlabBytes + 256;
+  return 1024 + STAGES * (kABytes + BN * 128) + EW * epi_slabs<EPI>() * kSlabBytes + BN * 4 + 256;
 }
 
 struct WideSched {
@@ -164,6 +171,8 @@ __device__ __forceinline__ void sts16(uint8_t* slab, int r, int g, uint4 v) {
 // phase of each slab barrier (warp-uniform).
 struct EpiWarp {
   int q;          // TMEM lane quarter: rows q*32 .. q*32+31 of the tile
+  int half;       // which of the quarter's warps (8 epilogue warps): slabs j = half, half + 2, ...
+  int step;       // slab stride: 1 with 4 epilogue warps, 2 with 8
   int lane;
   uint8_t* slab;  // epi_slabs<EPI>() consecutive slabs
   uint64_t* bar;  // one barrier per double-buffered slab (QKV uses [0] only)
@@ -181,7 +190,8 @@ __device__ __forceinline__ void wide_epi_prefetch(const SkinnyParams& p, const W
   if (EPI == SK_EPI_GATED_RESID) {
     bulk_wait_group_read<0>();
     mbar_arrive_expect_tx(&e.bar[0], kSlabBytes);
-    tma_load_2d(slab_at(e, 0), &mp.in0, &e.bar[0], n_tile * BN, m0 + e.q * 32, l2_policy_evict_normal());
+    tma_load_2d(slab_at(e, 0), &mp.in0, &e.bar[0], n_tile * BN + e.half * 64, m0 + e.q * 32,
+                l2_policy_evict_normal());
   } else if (EPI == SK_EPI_QKV_ROPE) {
     if (n_tile < p.n_q_heads + p.n_kv_heads) {
       const uint64_t pol = l2_policy_evict_last();
@@ -217,21 +227,21 @@ __device__ __forceinline__ void slab_store(const EpiWarp& e, const CUtensorMap* 
 // STORE / GATED_RESID (same arithmetic as apply_epilogue).
 template <int EPI, int BN>
 __device__ __forceinline__ bool wide_epi_rows(const SkinnyParams& p, const WideMaps& mp, EpiWarp& e, uint32_t taddr,
-                                              int n_tile, int m0, const WideSplit& sp) {
+                                              int n_tile, int m0, const WideSplit& sp, const float* sbias) {
   constexpr int NS = BN / 64;
   const int r = e.lane;
   const int tok = m0 + e.q * 32 + r;
   const int n_valid = p.n_valid > 0 ? p.n_valid : 1 << 30;
   bool ok = true;
 #pragma unroll 1
-  for (int j = 0; j < NS; ++j) {
-    const int b = j & 1;
+  for (int j = e.half, i = 0; j < NS; j += e.step, ++i) {
+    const int b = i & 1;
     uint8_t* slab = slab_at(e, b);
     if (EPI == SK_EPI_GATED_RESID) {
-      if (j + 1 < NS && e.lane == 0) {  // next residual slab into the other buffer
+      if (j + e.step < NS && e.lane == 0) {  // next residual slab into the other buffer
         bulk_wait_group_read<0>();
         mbar_arrive_expect_tx(&e.bar[b ^ 1], kSlabBytes);
-        tma_load_2d(slab_at(e, b ^ 1), &mp.in0, &e.bar[b ^ 1], n_tile * BN + (j + 1) * 64, m0 + e.q * 32,
+        tma_load_2d(slab_at(e, b ^ 1), &mp.in0, &e.bar[b ^ 1], n_tile * BN + (j + e.step) * 64, m0 + e.q * 32,
                     l2_policy_evict_normal());
       }
     } else {
@@ -249,7 +259,7 @@ __device__ __forceinline__ bool wide_epi_rows(const SkinnyParams& p, const WideM
         const int n = n_tile * BN + j * 64 + g * 8;
         const bool in = n < n_valid;
         float bi[8], ps[8], gt[8], rs[8];
-        if (p.bias != nullptr && in) load8f(p.bias + n, bi);
+        if (p.bias != nullptr) load8f(sbias + j * 64 + g * 8, bi);  // staged per tile, zero past n_valid
         if (EPI == SK_EPI_STORE && p.pos != nullptr && in) load8f(p.pos + (size_t)(tok % p.pos_rows) * p.ldo + n, ps);
         if (EPI == SK_EPI_GATED_RESID) {
           unpack8(lds16(slab, r, g), rs);
@@ -259,10 +269,10 @@ __device__ __forceinline__ bool wide_epi_rows(const SkinnyParams& p, const WideM
 #pragma unroll
         for (int jj = 0; jj < 8; ++jj) {
           float y = v[g4 * 8 + jj];
-          if (p.bias != nullptr && in) y += bi[jj];
+          if (p.bias != nullptr) y += bi[jj];
           if (EPI == SK_EPI_STORE && p.pos != nullptr && in) y += ps[jj];
           y = bf16_round(y);
-          if (EPI == SK_EPI_STORE && p.act == 1) y = gelu_tanh_f(y);
+          if (EPI == SK_EPI_STORE && p.act == 1) y = gelu_tanh_fast(y);
           if (EPI == SK_EPI_GATED_RESID) y = (p.gate != nullptr && in) ? rs[jj] + y * bf16_round(gt[jj]) : rs[jj] + y;
           o[jj] = y;
         }
@@ -383,14 +393,17 @@ __device__ __forceinline__ bool wide_epi_qkv(const SkinnyParams& p, const WideMa
   return ok;
 }
 
-template <int EPI, int BN, int STAGES>
-__global__ void __launch_bounds__(kWThreads, 1)
+template <int EPI, int BN, int STAGES, int EW>
+__global__ void __launch_bounds__(wide_threads<EW>(), 1)
     wide_gemm_kernel(const __grid_constant__ WideMaps mp, const SkinnyParams p, const WideSched ws) {
   constexpr int kBBytes = BN * 128;
   constexpr int kStageBytes = kABytes + kBBytes;
   constexpr uint32_t kTmemCols = 2 * BN;
   constexpr uint32_t kIdesc = umma_idesc_bf16(kWBM, BN);
   constexpr int kSlabs = epi_slabs<EPI>();
+  constexpr int kEW = EW;
+  static_assert(EW == 4 || ((EPI == SK_EPI_STORE || EPI == SK_EPI_GATED_RESID) && EW == 8), "epilogue warps");
+  constexpr int kET = kEW * 32;  // epilogue threads
   static_assert(BN == 128 || BN == 256, "tile width");
   static_assert((EPI != SK_EPI_GEGLU && EPI != SK_EPI_QKV_ROPE) || BN == 256, "paired epilogues use BN = 256");
 
@@ -398,14 +411,15 @@ __global__ void __launch_bounds__(kWThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * kABytes;
-  uint8_t* sEpi = smem + STAGES * kStageBytes;  // 4 warps x kSlabs slabs, 1024-aligned
-  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + 4 * kSlabs * kSlabBytes);
+  uint8_t* sEpi = smem + STAGES * kStageBytes;  // kEW warps x kSlabs slabs, 1024-aligned
+  float* sbias = reinterpret_cast<float*>(sEpi + kEW * kSlabs * kSlabBytes);  // [BN] this tile's bias
+  uint64_t* full = reinterpret_cast<uint64_t*>(sbias + BN);
   uint64_t* empty = full + STAGES;
   uint64_t* accf = empty + STAGES;  // [2] accumulator ready (MMA commit)
   uint64_t* acce = accf + 2;        // [2] accumulator drained (128 epilogue arrivals)
   uint64_t* mdone = acce + 2;       // all MMAs of this CTA complete
-  uint64_t* sbar = mdone + 1;       // [4 warps][2] epilogue slab loads
-  unsigned long long* s_stamp = reinterpret_cast<unsigned long long*>(sbar + 8);  // [2] trace
+  uint64_t* sbar = mdone + 1;       // [kEW warps][2] epilogue slab loads
+  unsigned long long* s_stamp = reinterpret_cast<unsigned long long*>(sbar + 2 * kEW);  // [2] trace
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(s_stamp + 2);
   int* s_flag = reinterpret_cast<int*>(s_tmem + 1);  // [0] abort, [2] k-blocks armed
 
@@ -421,10 +435,10 @@ __global__ void __launch_bounds__(kWThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accf[b], 1);
-      mbar_init(&acce[b], kEpiThreads);
+      mbar_init(&acce[b], kET);
     }
     mbar_init(mdone, 1);
-    for (int i = 0; i < 8; ++i) mbar_init(&sbar[i], 1);
+    for (int i = 0; i < 2 * kEW; ++i) mbar_init(&sbar[i], 1);
     s_flag[0] = 0;
     s_flag[2] = 0;
     s_stamp[0] = 0;
@@ -545,6 +559,8 @@ __global__ void __launch_bounds__(kWThreads, 1)
     pdl_wait();
     EpiWarp e;
     e.q = warp & 3;
+    e.half = (warp - 2) >> 2;
+    e.step = kEW / 4;
     e.lane = lane;
     e.slab = sEpi + (warp - 2) * kSlabs * kSlabBytes;
     e.bar = sbar + (warp - 2) * 2;
@@ -555,6 +571,16 @@ __global__ void __launch_bounds__(kWThreads, 1)
       const int m = wt.m, n = wt.n;
       const int buf = lt & 1;
       wide_epi_prefetch<EPI, BN>(p, mp, e, n, m * kWBM);
+      if ((EPI == SK_EPI_STORE || EPI == SK_EPI_GATED_RESID) && p.bias != nullptr) {
+        // Stage the tile's bias columns once (read as broadcasts by the epilogue).
+        const int et = threadIdx.x - 64;
+        named_bar_sync(1, kET);  // the previous tile's epilogue is done with sbias
+        for (int i = et; i < BN; i += kET) {
+          const int col = n * BN + i;
+          sbias[i] = col < p.n_valid ? p.bias[col] : 0.f;
+        }
+        named_bar_sync(1, kET);
+      }
       if (!mbar_wait(&accf[buf], (lt >> 1) & 1)) {
         report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
         break;
@@ -579,6 +605,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
           float* mine = part + ((size_t)wt.s * kWBM + sp.row) * BN;
 #pragma unroll 1
           for (int c = 0; c < BN / 32; ++c) {
+            if (((c >> 1) % e.step) != e.half) continue;  // the quarter's other warp writes this slab
             float v[32];
             tmem_ld32(taddr + c * 32, v);
 #pragma unroll
@@ -587,21 +614,21 @@ __global__ void __launch_bounds__(kWThreads, 1)
                      make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
           }
           __threadfence();
-          named_bar_sync(1, kEpiThreads);
+          named_bar_sync(1, kET);
           if (threadIdx.x == 64) {
             const int old = atomicAdd(p.counters + tile_mn, 1);
             const int last = old == ws.splits - 1 ? 1 : 0;
             if (last) atomicExch(p.counters + tile_mn, 0);  // re-armed for the next launch
             s_flag[1] = last;
           }
-          named_bar_sync(1, kEpiThreads);
+          named_bar_sync(1, kET);
           finish = s_flag[1] != 0;
-          named_bar_sync(1, kEpiThreads);  // s_flag[1] is rewritten by the next split tile
+          named_bar_sync(1, kET);  // s_flag[1] is rewritten by the next split tile
           if (finish) __threadfence();
           sp.part = part;
         }
         if (finish) {
-          ok = wide_epi_rows<EPI, BN>(p, mp, e, taddr, n, m * kWBM, sp);
+          ok = wide_epi_rows<EPI, BN>(p, mp, e, taddr, n, m * kWBM, sp, sbias);
         } else if (EPI == SK_EPI_GATED_RESID && e.lane == 0) {
           // The residual slab prefetched for this tile is not consumed: retire its load.
           ok = slab_wait(e, 0, p.status);
@@ -666,11 +693,11 @@ int wide_sms() {
   return n;
 }
 
-template <int EPI, int BN, int STAGES>
+template <int EPI, int BN, int STAGES, int EW>
 int wide_launch(const SkinnyParams& p, const WideSched& ws, const WideMaps& mp, cudaStream_t stream) {
-  constexpr int kSmem = wide_smem_bytes<EPI, BN, STAGES>();
+  constexpr int kSmem = wide_smem_bytes<EPI, BN, STAGES, EW>();
   static_assert(kSmem <= 232448, "shared memory per block");
-  auto kern = wide_gemm_kernel<EPI, BN, STAGES>;
+  auto kern = wide_gemm_kernel<EPI, BN, STAGES, EW>;
   static bool attr_done[16] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -684,7 +711,7 @@ int wide_launch(const SkinnyParams& p, const WideSched& ws, const WideMaps& mp, 
   }
   const int total = ws.m_tiles * ws.n_tiles * ws.splits;
   const int grid = std::min(total, wide_sms());
-  return launch_pdl(kern, dim3(grid), dim3(kWThreads), kSmem, stream, pdl_enabled(), mp, p, ws);
+  return launch_pdl(kern, dim3(grid), dim3(wide_threads<EW>()), kSmem, stream, pdl_enabled(), mp, p, ws);
 }
 
 // Debug override read once: PI05_WIDE_BN (128 / 256) for STORE / GATED_RESID.
@@ -789,17 +816,24 @@ int wide_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int w
       rc = make_tmap_bf16_2d(&mp.in0, p.resid, p.m_tok, n_cols, p.ldr, 32, 64, true);
   }
   if (rc) return rc;
+  // Short mainloops (a tile of at most 40 k-blocks) leave the epilogue exposed: give
+  // it 8 warps; long ones keep the deeper pipeline.
+  const bool wide8 = (ws.kb_total + ws.splits - 1) / ws.splits <= 40;
   switch (epi) {
     case SK_EPI_STORE:
-      return bn == 256 ? wide_launch<SK_EPI_STORE, 256, 4>(p, ws, mp, st)
-                       : wide_launch<SK_EPI_STORE, 128, 6>(p, ws, mp, st);
+      if (wide8) return bn == 256 ? wide_launch<SK_EPI_STORE, 256, 3, 8>(p, ws, mp, st)
+                                  : wide_launch<SK_EPI_STORE, 128, 5, 8>(p, ws, mp, st);
+      return bn == 256 ? wide_launch<SK_EPI_STORE, 256, 4, 4>(p, ws, mp, st)
+                       : wide_launch<SK_EPI_STORE, 128, 6, 4>(p, ws, mp, st);
     case SK_EPI_GATED_RESID:
-      return bn == 256 ? wide_launch<SK_EPI_GATED_RESID, 256, 4>(p, ws, mp, st)
-                       : wide_launch<SK_EPI_GATED_RESID, 128, 6>(p, ws, mp, st);
+      if (wide8) return bn == 256 ? wide_launch<SK_EPI_GATED_RESID, 256, 3, 8>(p, ws, mp, st)
+                                  : wide_launch<SK_EPI_GATED_RESID, 128, 5, 8>(p, ws, mp, st);
+      return bn == 256 ? wide_launch<SK_EPI_GATED_RESID, 256, 4, 4>(p, ws, mp, st)
+                       : wide_launch<SK_EPI_GATED_RESID, 128, 6, 4>(p, ws, mp, st);
     case SK_EPI_GEGLU:
-      return wide_launch<SK_EPI_GEGLU, 256, 4>(p, ws, mp, st);
+      return wide_launch<SK_EPI_GEGLU, 256, 4, 4>(p, ws, mp, st);
     case SK_EPI_QKV_ROPE:
-      return wide_launch<SK_EPI_QKV_ROPE, 256, 3>(p, ws, mp, st);
+      return wide_launch<SK_EPI_QKV_ROPE, 256, 3, 4>(p, ws, mp, st);
     default:
       set_last_error("wide_gemm: unknown epilogue %d", epi);
       return PI05_ERR_INVALID_ARG;
