@@ -404,21 +404,10 @@ int launch_combine(const AttnParams& p, cudaStream_t st) {
   return launch_pdl(mqa_combine_kernel, dim3((p.rows + 7) / 8), dim3(256), 0, st, pdl_enabled(), p);
 }
 
-int mqa_attention_run(AttnParams p, float* part, size_t part_bytes, int splits, void* stream) {
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (p.head_dim != kD) {
-    set_last_error("attention: head_dim %d unsupported (256 only)", p.head_dim);
-    return PI05_ERR_SHAPE;
-  }
-  if (p.rows <= 0 || p.kv_len <= 0) {
-    set_last_error("attention: empty rows/keys");
-    return PI05_ERR_SHAPE;
-  }
-  // tcgen05 for many query rows (prefix LM: 968 x 8); the mma.sync kernel below is
-  // faster for the denoise suffix (50 x 8 rows), where each CTA owns one key chunk.
-  if (tc_attention_enabled() && p.rows > tc_min_rows())
-    return mqa_tc_attention_run(p, part, part_bytes, splits, st, launch_combine);
-  constexpr int W = 4;
+// mma.sync path: W warps of 16 query rows per CTA (default 2, which halves the
+// per-CTA tensor work of a chunk; PI05_ATTN_WARPS=4 selects 4, for tuning).
+template <int W>
+int mma_sync_attention(AttnParams p, float* part, size_t part_bytes, int splits, cudaStream_t st) {
   constexpr int kRows = 16 * W;
   const int row_blocks = (p.rows + kRows - 1) / kRows;
   const int n_chunks = (p.kv_len + kChunk - 1) / kChunk;
@@ -452,6 +441,28 @@ int mqa_attention_run(AttnParams p, float* part, size_t part_bytes, int splits, 
   rc = launch_pdl(mqa_flash_kernel<W>, dim3(row_blocks, splits), dim3(W * 32), smem, st, pdl_enabled(), p);
   if (rc || splits == 1) return rc;
   return launch_combine(p, st);
+}
+
+int mqa_attention_run(AttnParams p, float* part, size_t part_bytes, int splits, void* stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (p.head_dim != kD) {
+    set_last_error("attention: head_dim %d unsupported (256 only)", p.head_dim);
+    return PI05_ERR_SHAPE;
+  }
+  if (p.rows <= 0 || p.kv_len <= 0) {
+    set_last_error("attention: empty rows/keys");
+    return PI05_ERR_SHAPE;
+  }
+  // tcgen05 for many query rows (prefix LM: 968 x 8); the mma.sync kernel below is
+  // faster for the denoise suffix (50 x 8 rows), where each CTA owns one key chunk.
+  if (tc_attention_enabled() && p.rows > tc_min_rows())
+    return mqa_tc_attention_run(p, part, part_bytes, splits, st, launch_combine);
+  static const int warps = [] {
+    const char* e = getenv("PI05_ATTN_WARPS");
+    return (e != nullptr && atoi(e) == 4) ? 4 : 2;
+  }();
+  return warps == 2 ? mma_sync_attention<2>(p, part, part_bytes, splits, st)
+                    : mma_sync_attention<4>(p, part, part_bytes, splits, st);
 }
 
 }  // namespace pi05
