@@ -37,6 +37,19 @@ const int* debug_split_overrides() {
   return v;
 }
 
+// PI05_FUSED_NORM=1 in the environment folds the adaRMS norms after layer 0 into
+// the neighbouring GEMMs (row statistics from o_proj / down_proj, X normalised in
+// shared memory by gate/up and q|k|v).  Off by default: on B200 the in-place
+// normalisation of the X stages costs the consumer GEMMs more than the norm
+// kernels it removes.
+bool fused_norm_enabled() {
+  static int v = [] {
+    const char* e = getenv("PI05_FUSED_NORM");
+    return (e != nullptr && e[0] == '1') ? 1 : 0;
+  }();
+  return v != 0;
+}
+
 }  // namespace
 
 extern "C" {
@@ -167,6 +180,15 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
   auto* act = static_cast<__nv_bfloat16*>(P->act);
   const int kv_len = P->prefix_len + T;
   const float scale = 1.0f / std::sqrt((float)D);
+  // Fused norms: o_proj / down_proj write per-(128-column tile, token) sums of
+  // squares of the new residual stream next to it; the following gate/up and
+  // q|k|v GEMMs normalise their X tiles in shared memory from those sums, so the
+  // adaRMS norms after layer 0's first one need no kernel of their own.
+  const int n_parts = W / 128;
+  const bool fuse = fused_norm_enabled() && W <= kNormMaxK &&
+                    (size_t)2 * n_parts * T * sizeof(float) <= kWsStatsBytes;
+  float* ssq_attn = ws.stats;                        // input of input_layernorm (from down_proj)
+  float* ssq_mlp = ws.stats + (size_t)n_parts * T;   // input of post_attention_layernorm (from o_proj)
 
   int rc = action_in_run(P->x_t, P->w_in, P->b_in, h, T, P->action_dim, W, stream);
   for (int l = 0; l < P->depth && rc == PI05_OK; ++l) {
@@ -176,9 +198,12 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
     const Pi05ExpertLayer& N = P->layers[(l + 1) % P->depth];
     const float* mod1 = mods + (size_t)(2 * l) * 3 * W;
     const float* mod2 = mods + (size_t)(2 * l + 1) * 3 * W;
-    // input_layernorm (adaRMS)
-    rc = rms_norm_run(h, W, mod1, nullptr, xn, W, T, W, P->eps, stream);
-    if (rc) break;
+    // input_layernorm (adaRMS): fused into q|k|v after layer 0
+    const bool fuse1 = fuse && l > 0;
+    if (!fuse1) {
+      rc = rms_norm_run(h, W, mod1, nullptr, xn, W, T, W, P->eps, stream);
+      if (rc) break;
+    }
     // q|k|v + RoPE -> q, KV-cache tail rows [prefix_len, prefix_len + T)
     {
       SkinnyParams sp;
@@ -204,7 +229,15 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.pf0 = N.w_qkv;
       sp.pf0_bytes = (size_t)rows * W * 2;
       sp.trace_tag = (step * P->depth + l) * 8 + 0;
-      rc = skinny_gemm_run(SK_EPI_QKV_ROPE, sp, L.w_qkv, L.w_qkv, rows, rows, xn, W, so[0], stream);
+      if (fuse1) {
+        sp.norm_ssq = ssq_attn;
+        sp.norm_parts = n_parts;
+        sp.norm_ld = T;
+        sp.norm_mod = mod1;
+        sp.norm_d = W;
+        sp.norm_eps = P->eps;
+      }
+      rc = skinny_gemm_run(SK_EPI_QKV_ROPE, sp, L.w_qkv, L.w_qkv, rows, rows, fuse1 ? h : xn, W, so[0], stream);
       if (rc) break;
     }
     // attention over [prefix | suffix] keys
@@ -245,15 +278,21 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.resid = h;
       sp.ldr = W;
       sp.gate = mod1 + 2 * W;
+      if (fuse) {
+        sp.row_ssq = ssq_mlp;
+        sp.ssq_ld = T;
+      }
       sp.pf0 = N.w_o;
       sp.pf0_bytes = (size_t)W * HQ * D * 2;
       sp.trace_tag = (step * P->depth + l) * 8 + 1;
       rc = skinny_gemm_run(SK_EPI_GATED_RESID, sp, L.w_o, L.w_o, W, W, attn, HQ * D, so[1], stream);
       if (rc) break;
     }
-    // post_attention_layernorm (adaRMS)
-    rc = rms_norm_run(h, W, mod2, nullptr, xn, W, T, W, P->eps, stream);
-    if (rc) break;
+    // post_attention_layernorm (adaRMS): fused into gate/up
+    if (!fuse) {
+      rc = rms_norm_run(h, W, mod2, nullptr, xn, W, T, W, P->eps, stream);
+      if (rc) break;
+    }
     // gate/up + GeGLU
     {
       SkinnyParams sp;
@@ -272,7 +311,15 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.pf1 = N.w_up;
       sp.pf1_bytes = (size_t)F * W * 2;
       sp.trace_tag = (step * P->depth + l) * 8 + 2;
-      rc = skinny_gemm_run(SK_EPI_GEGLU, sp, L.w_gate, L.w_up, F, F, xn, W, so[2], stream);
+      if (fuse) {
+        sp.norm_ssq = ssq_mlp;
+        sp.norm_parts = n_parts;
+        sp.norm_ld = T;
+        sp.norm_mod = mod2;
+        sp.norm_d = W;
+        sp.norm_eps = P->eps;
+      }
+      rc = skinny_gemm_run(SK_EPI_GEGLU, sp, L.w_gate, L.w_up, F, F, fuse ? h : xn, W, so[2], stream);
       if (rc) break;
     }
     // down + gated residual (gate = third chunk of mod2)
@@ -291,6 +338,10 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.resid = h;
       sp.ldr = W;
       sp.gate = mod2 + 2 * W;
+      if (fuse && l + 1 < P->depth) {
+        sp.row_ssq = ssq_attn;
+        sp.ssq_ld = T;
+      }
       sp.pf0 = N.w_down;
       sp.pf0_bytes = (size_t)W * F * 2;
       sp.trace_tag = (step * P->depth + l) * 8 + 3;

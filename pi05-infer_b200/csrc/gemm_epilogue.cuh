@@ -196,10 +196,11 @@ __device__ __forceinline__ void unit_load_ops(const SkinnyParams& p, int tile, i
 }
 
 // y[h][j]: the reduced tile values of rows r + 64h + j.  Same arithmetic as
-// apply_epilogue for the corresponding epilogue.
+// apply_epilogue for the corresponding epilogue.  Returns, for CK_ROWS, the sum of
+// squares of the four bf16 outputs (in order), else 0.
 template <int EPI, int KIND>
-__device__ __forceinline__ void unit_finish(const SkinnyParams& p, int tile, int tok0, int idx, const UnitOps& o,
-                                            const float (&y)[2][4]) {
+__device__ __forceinline__ float unit_finish(const SkinnyParams& p, int tile, int tok0, int idx, const UnitOps& o,
+                                             const float (&y)[2][4]) {
   int t, r;
   unit_pos<KIND>(idx, t, r);
   const int tok = tok0 + t;
@@ -217,6 +218,13 @@ __device__ __forceinline__ void unit_finish(const SkinnyParams& p, int tile, int
       out[j] = v;
     }
     *reinterpret_cast<uint2*>(p.out + (size_t)tok * p.ldo + n) = pack4(out);
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float b = bf16_round(out[j]);
+      ss += b * b;
+    }
+    return ss;
   } else if (KIND == CK_GEGLU) {
     float out[4];
 #pragma unroll
@@ -244,6 +252,24 @@ __device__ __forceinline__ void unit_finish(const SkinnyParams& p, int tile, int
     *reinterpret_cast<uint2*>(p.v_cache + (size_t)vh * p.kv_head_stride + (size_t)(p.krow0 + tok) * hd + d) =
         pack4(y[0]);
   }
+  return 0.f;
+}
+
+// Sum over the 32 lanes of a warp (xor butterfly: the same order on every lane).
+__device__ __forceinline__ float warp_sum32(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Row statistics of a CK_ROWS pass: the warp's 32 consecutive units are the 128
+// tile rows of one token (unit ranges start on token boundaries), so the warp sum
+// of the per-unit sums of squares is that token's partial for this tile.
+template <int KIND>
+__device__ __forceinline__ void unit_row_ssq(const SkinnyParams& p, int tile, int tok0, int idx, int u1, float ss) {
+  if (KIND != CK_ROWS || p.row_ssq == nullptr) return;
+  ss = warp_sum32(ss);
+  if ((threadIdx.x & 31) == 0 && idx < u1) p.row_ssq[(size_t)tile * p.ssq_ld + tok0 + (idx >> 5)] = ss;
 }
 
 // Body of the cluster epilogue for one unit kind and U units per thread per pass.
@@ -252,11 +278,13 @@ __device__ __forceinline__ void unit_finish(const SkinnyParams& p, int tile, int
 template <int EPI, int KIND, int U>
 __device__ __forceinline__ void cluster_epilogue_body(const SkinnyParams& p, uint32_t st, int tile, int tok0,
                                                       int u0, int u1, int et, bool epi,
-                                                      unsigned long long* bar_stamp) {
+                                                      unsigned long long* stamps) {
   constexpr int H = (KIND == CK_GEGLU || KIND == CK_ROT) ? 2 : 1;
   constexpr int KS = 16 / (U * H) > 0 ? 16 / (U * H) : 1;  // splits per batch of DSMEM loads
   const int splits = p.splits;
   UnitOps ops[U];
+  const bool stamp = stamps != nullptr && epi && et == 0;
+  if (stamp) stamps[0] = globaltimer_ns();
   // Publish the staging tile, then issue the global operand loads of the first
   // pass while the barrier completes (a release arrive would otherwise wait for
   // them).
@@ -271,7 +299,7 @@ __device__ __forceinline__ void cluster_epilogue_body(const SkinnyParams& p, uin
   }
   __syncwarp();
   cluster_wait();
-  if (bar_stamp != nullptr && epi && et == 0) *bar_stamp = globaltimer_ns();
+  if (stamp) stamps[1] = globaltimer_ns();
   if (!epi) return;
   for (int base = u0 + et, pass = 0; base < u1; base += U * kEpiThreads, ++pass) {
     bool ok[U];
@@ -320,58 +348,228 @@ __device__ __forceinline__ void cluster_epilogue_body(const SkinnyParams& p, uin
         }
       }
     }
+    if (stamp && pass == 0) stamps[2] = globaltimer_ns();
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      if (!ok[u]) continue;
-      float y[2][4];
+      float ss = 0.f;
+      if (ok[u]) {
+        float y[2][4];
 #pragma unroll
-      for (int h = 0; h < 2; ++h)
+        for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) y[h][j] = acc[u][h < H ? h : 0][j];
-      unit_finish<EPI, KIND>(p, tile, tok0, base + u * kEpiThreads, ops[u], y);
+          for (int j = 0; j < 4; ++j) y[h][j] = acc[u][h < H ? h : 0][j];
+        ss = unit_finish<EPI, KIND>(p, tile, tok0, base + u * kEpiThreads, ops[u], y);
+      }
+      unit_row_ssq<KIND>(p, tile, tok0, base + u * kEpiThreads, u1, ss);
     }
   }
+  if (stamp) stamps[3] = globaltimer_ns();
 }
 
 template <int EPI, int KIND>
 __device__ __forceinline__ void cluster_epilogue_kind(const SkinnyParams& p, uint32_t st, int tile, int tok0, int mt,
-                                                      int rank, int et, bool epi, unsigned long long* bar_stamp) {
+                                                      int rank, int et, bool epi, unsigned long long* stamps) {
   constexpr int H = (KIND == CK_GEGLU || KIND == CK_ROT) ? 2 : 1;
   const int units = mt * (H == 2 ? 16 : 32);
-  const int u0 = (int)(((long)rank * units) / p.splits);
-  const int u1 = (int)(((long)(rank + 1) * units) / p.splits);
+  int u0 = (int)(((long)rank * units) / p.splits);
+  int u1 = (int)(((long)(rank + 1) * units) / p.splits);
+  if (KIND == CK_ROWS && p.row_ssq != nullptr) {  // whole tokens per rank (row statistics)
+    u0 = 32 * ((rank * mt) / p.splits);
+    u1 = 32 * (((rank + 1) * mt) / p.splits);
+  }
   const int per_thread = (u1 - u0 + kEpiThreads - 1) / kEpiThreads;
   if (per_thread >= 4 && p.splits * H * 4 <= 16)
-    cluster_epilogue_body<EPI, KIND, 4>(p, st, tile, tok0, u0, u1, et, epi, bar_stamp);
+    cluster_epilogue_body<EPI, KIND, 4>(p, st, tile, tok0, u0, u1, et, epi, stamps);
   else if (per_thread >= 2 && p.splits * H * 2 <= 16)
-    cluster_epilogue_body<EPI, KIND, 2>(p, st, tile, tok0, u0, u1, et, epi, bar_stamp);
+    cluster_epilogue_body<EPI, KIND, 2>(p, st, tile, tok0, u0, u1, et, epi, stamps);
   else
-    cluster_epilogue_body<EPI, KIND, 1>(p, st, tile, tok0, u0, u1, et, epi, bar_stamp);
+    cluster_epilogue_body<EPI, KIND, 1>(p, st, tile, tok0, u0, u1, et, epi, stamps);
 }
 
 // Whole cluster split-K epilogue (both cluster barriers included); every thread of
 // the CTA calls it.  The second barrier keeps each staging tile alive until all
-// peers have finished reading it.
+// peers have finished reading it.  `stamps` (optional, shared memory, 5 slots):
+// globaltimer before the first barrier, after it, after the first pass's DSMEM
+// loads, after the last store, after the exit barrier.
 template <int EPI>
 __device__ __forceinline__ void cluster_epilogue(const SkinnyParams& p, uint32_t st, int tile, int tok0, int mt,
                                                  int rank, int et, bool epi,
-                                                 unsigned long long* bar_stamp = nullptr) {
+                                                 unsigned long long* stamps = nullptr) {
   if (EPI == SK_EPI_GEGLU) {
-    cluster_epilogue_kind<EPI, CK_GEGLU>(p, st, tile, tok0, mt, rank, et, epi, bar_stamp);
+    cluster_epilogue_kind<EPI, CK_GEGLU>(p, st, tile, tok0, mt, rank, et, epi, stamps);
   } else if (EPI == SK_EPI_QKV_ROPE) {
     const int n_rot_tiles = (p.n_q_heads + p.n_kv_heads) * (p.head_dim / 128);
     if (tile < n_rot_tiles)
-      cluster_epilogue_kind<EPI, CK_ROT>(p, st, tile, tok0, mt, rank, et, epi, bar_stamp);
+      cluster_epilogue_kind<EPI, CK_ROT>(p, st, tile, tok0, mt, rank, et, epi, stamps);
     else
-      cluster_epilogue_kind<EPI, CK_V>(p, st, tile, tok0, mt, rank, et, epi, bar_stamp);
+      cluster_epilogue_kind<EPI, CK_V>(p, st, tile, tok0, mt, rank, et, epi, stamps);
   } else {
-    cluster_epilogue_kind<EPI, CK_ROWS>(p, st, tile, tok0, mt, rank, et, epi, bar_stamp);
+    cluster_epilogue_kind<EPI, CK_ROWS>(p, st, tile, tok0, mt, rank, et, epi, stamps);
   }
   // Exit barrier: no CTA leaves while peers still read its staging tile.  The
   // epilogue's global stores need no ordering here, so the arrive is relaxed.
   __syncwarp();
   cluster_arrive_relaxed();
   cluster_wait();
+  if (stamps != nullptr && epi && et == 0) stamps[4] = globaltimer_ns();
+}
+
+// ---------------------------------------------------------------------------
+// Split-K through distributed shared memory, push form.  Rank r of the cluster
+// owns tokens [r*mt/splits, (r+1)*mt/splits) of the tile.  After the first
+// cluster barrier (every CTA's mainloop is done, so its ring can receive), each
+// CTA sends the owner of every other token slice that slice of its staging tile
+// with one bulk copy (async proxy, SM-to-SM), completing transaction bytes on the
+// owner's barrier `rbar`.  The owner waits for its barrier and sums the partials
+// from its own shared memory in increasing rank order (0.f + p0 + p1 + ..., the
+// order of the pull form and of the global-memory split path), then applies the
+// epilogue.  The receive slots follow the staging tile in the (finished) ring:
+// slot s holds source s's partial of the owner's token slice, 512 bytes a token.
+// The exit barrier, arrived once a CTA has received everything, keeps every
+// source's staging tile alive until all copies out of it have landed.
+// Bytes this rank receives in the push form (its token slice from every other rank).
+__device__ __forceinline__ uint32_t push_recv_bytes(int splits, int mt, int rank) {
+  const int t0 = (rank * mt) / splits, t1 = ((rank + 1) * mt) / splits;
+  return (uint32_t)((splits - 1) * (t1 - t0) * kBM * 4);
+}
+
+// The epilogue threads' half of the first push barrier, called as soon as the
+// accumulator is ready (the ring is then free to receive): arm the receive
+// barrier, arrive on the cluster barrier.  The staging tile is written after this;
+// the writers fence it to the async proxy before the CTA barrier that precedes the
+// bulk copies.
+__device__ __forceinline__ void cluster_push_arrive(uint64_t* rbar, int splits, int mt, int rank, int et) {
+  if (et == 0) mbar_arrive_expect_tx(rbar, push_recv_bytes(splits, mt, rank));
+  __syncwarp();
+  cluster_arrive_release();
+}
+
+template <int EPI, int KIND, int U>
+__device__ __forceinline__ void cluster_push_body(const SkinnyParams& p, const float* st, const float* recv,
+                                                  uint64_t* rbar, int tile, int tok0, int mt, int rank, int et,
+                                                  bool epi, unsigned long long* stamps) {
+  constexpr int H = (KIND == CK_GEGLU || KIND == CK_ROT) ? 2 : 1;
+  constexpr int UPT = H == 2 ? 16 : 32;  // units per token
+  const int splits = p.splits;
+  const int t0 = (rank * mt) / splits, t1 = ((rank + 1) * mt) / splits;
+  const int u0 = UPT * t0, u1 = UPT * t1;
+  const int slot = (t1 - t0) * kBM;  // floats per receive slot
+  const bool stamp = stamps != nullptr && epi && et == 0;
+  UnitOps ops[U];
+  if (stamp) stamps[0] = globaltimer_ns();
+  // Epilogue threads arrived in cluster_push_arrive(); the others arrive here.
+  if (!epi) {
+    __syncwarp();
+    cluster_arrive_release();
+  }
+  if (epi) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int idx = u0 + u * kEpiThreads + et;
+      if (unit_valid<EPI, KIND>(p, tile, idx, u1)) unit_load_ops<EPI, KIND>(p, tile, tok0, idx, ops[u]);
+    }
+  }
+  __syncwarp();
+  cluster_wait();
+  if (stamp) stamps[1] = globaltimer_ns();
+  bool ok = true;
+  if (epi) {
+    if (et < splits && et != rank) {
+      const int d0 = (et * mt) / splits, d1 = ((et + 1) * mt) / splits;
+      const uint32_t bytes = (uint32_t)(d1 - d0) * kBM * 4u;
+      if (bytes > 0)
+        bulk_copy_to_peer(mapa_shared(smem_u32(recv) + (uint32_t)rank * bytes, (uint32_t)et),
+                          smem_u32(st) + (uint32_t)d0 * kBM * 4u, bytes, mapa_shared(smem_u32(rbar), (uint32_t)et));
+    }
+    ok = mbar_wait_cluster(rbar, 0);
+    if (!ok) report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
+  }
+  if (stamp) stamps[2] = globaltimer_ns();
+  // Everything this CTA receives has landed: its sources may leave once every
+  // owner has said so.
+  __syncwarp();
+  cluster_arrive_relaxed();
+  if (epi && ok) {
+    for (int base = u0 + et, pass = 0; base < u1; base += U * kEpiThreads, ++pass) {
+      // Rolled: this code runs once per launch and its instruction fetch, not the
+      // arithmetic, is what the units wait for when it is unrolled U times.
+#pragma unroll 1
+      for (int u = 0; u < U; ++u) {
+        const int idx = base + u * kEpiThreads;
+        float ss = 0.f;
+        if (unit_valid<EPI, KIND>(p, tile, idx, u1)) {
+          if (pass > 0) unit_load_ops<EPI, KIND>(p, tile, tok0, idx, ops[u]);
+          int t, r;
+          unit_pos<KIND>(idx, t, r);
+          const float* own = st + t * kBM + r;
+          const float* rcv = recv + (t - t0) * kBM + r;
+          float y[2][4];
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) y[h][j] = 0.f;
+          for (int s = 0; s < splits; ++s) {
+            const float* src = s == rank ? own : rcv + s * slot;
+#pragma unroll
+            for (int h = 0; h < H; ++h) {
+              const float4 v = *reinterpret_cast<const float4*>(src + h * 64);
+              y[h][0] += v.x;
+              y[h][1] += v.y;
+              y[h][2] += v.z;
+              y[h][3] += v.w;
+            }
+          }
+          if (H == 1) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) y[1][j] = y[0][j];
+          }
+          ss = unit_finish<EPI, KIND>(p, tile, tok0, idx, ops[u], y);
+        }
+        unit_row_ssq<KIND>(p, tile, tok0, idx, u1, ss);
+      }
+    }
+  }
+  if (stamp) stamps[3] = globaltimer_ns();
+  __syncwarp();
+  cluster_wait();
+  if (stamp) stamps[4] = globaltimer_ns();
+}
+
+template <int EPI, int KIND>
+__device__ __forceinline__ void cluster_push_kind(const SkinnyParams& p, const float* st, const float* recv,
+                                                  uint64_t* rbar, int tile, int tok0, int mt, int rank, int et,
+                                                  bool epi, unsigned long long* stamps) {
+  constexpr int H = (KIND == CK_GEGLU || KIND == CK_ROT) ? 2 : 1;
+  const int tmax = (mt + p.splits - 1) / p.splits;
+  const int per_thread = (tmax * (H == 2 ? 16 : 32) + kEpiThreads - 1) / kEpiThreads;
+  if (per_thread >= 4)
+    cluster_push_body<EPI, KIND, 4>(p, st, recv, rbar, tile, tok0, mt, rank, et, epi, stamps);
+  else if (per_thread >= 2)
+    cluster_push_body<EPI, KIND, 2>(p, st, recv, rbar, tile, tok0, mt, rank, et, epi, stamps);
+  else
+    cluster_push_body<EPI, KIND, 1>(p, st, recv, rbar, tile, tok0, mt, rank, et, epi, stamps);
+}
+
+// Whole push-form cluster epilogue; every thread of the CTA calls it, the epilogue
+// threads after cluster_push_arrive() and after fencing the staging tile they
+// wrote (fence.proxy.async) followed by a barrier among themselves.  `recv` must
+// hold splits * ceil(mt / splits) * 512 bytes; `rbar` was initialised with one
+// arrival (fence.mbarrier_init) before the mainloop.
+template <int EPI>
+__device__ __forceinline__ void cluster_push_epilogue(const SkinnyParams& p, const float* st, const float* recv,
+                                                      uint64_t* rbar, int tile, int tok0, int mt, int rank, int et,
+                                                      bool epi, unsigned long long* stamps = nullptr) {
+  if (EPI == SK_EPI_GEGLU) {
+    cluster_push_kind<EPI, CK_GEGLU>(p, st, recv, rbar, tile, tok0, mt, rank, et, epi, stamps);
+  } else if (EPI == SK_EPI_QKV_ROPE) {
+    const int n_rot_tiles = (p.n_q_heads + p.n_kv_heads) * (p.head_dim / 128);
+    if (tile < n_rot_tiles)
+      cluster_push_kind<EPI, CK_ROT>(p, st, recv, rbar, tile, tok0, mt, rank, et, epi, stamps);
+    else
+      cluster_push_kind<EPI, CK_V>(p, st, recv, rbar, tile, tok0, mt, rank, et, epi, stamps);
+  } else {
+    cluster_push_kind<EPI, CK_ROWS>(p, st, recv, rbar, tile, tok0, mt, rank, et, epi, stamps);
+  }
 }
 
 // Epilogue items are groups of 8 consecutive tile rows of one token: mt * 16
@@ -440,6 +638,7 @@ __device__ __forceinline__ void apply_epilogue(const SkinnyParams& p, const Src&
       for (int b = 0; b < kBatch; ++b) {
         const int idx = base + b * kEpiThreads;
         const int t = idx >> 4, r = (idx & 15) * 8, n = n0 + r, tok = tok0 + t;
+        float ss = 0.f;
         if (idx < i1 && n < n_valid) {
           float o[8];
 #pragma unroll
@@ -453,6 +652,19 @@ __device__ __forceinline__ void apply_epilogue(const SkinnyParams& p, const Src&
             o[j] = v;
           }
           *reinterpret_cast<uint4*>(p.out + (size_t)tok * p.ldo + n) = pack8(o);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float q = bf16_round(o[j]);
+            ss += q * q;
+          }
+        }
+        if (p.row_ssq != nullptr) {
+          // Row statistics: the 16 groups of a token are one half-warp (item
+          // ranges start on token boundaries when row_ssq is set).
+          const unsigned half = 0xffffu << (threadIdx.x & 16);
+#pragma unroll
+          for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(half, ss, o);
+          if ((threadIdx.x & 15) == 0 && idx < i1) p.row_ssq[(size_t)tile * p.ssq_ld + tok] = ss;
         }
       }
     }

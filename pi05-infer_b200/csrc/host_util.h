@@ -18,19 +18,23 @@ namespace pi05 {
 //   [0, 64)                      device status word (int32 at offset 0) + reserved
 //   [64, 64 + 16 KiB)            split-K tile barriers (2 x int32 per tile); zero between launches
 //   [kWsAccumOffset, +40 MiB)    fp32 split-K partials (scratch)
+//   [kWsStatsOffset, +64 KiB)    fp32 per-row sums of squares for the fused norms (two buffers)
 //   [kWsScratchOffset, end)      free scratch (split-KV attention partials, table build)
 constexpr size_t kWsStatusOffset = 0;
 constexpr size_t kWsCounterOffset = 64;
 constexpr int kWsMaxCounters = 4096;
 constexpr size_t kWsAccumOffset = 64 + kWsMaxCounters * 4 + 192;  // 16640, 256-aligned
 constexpr size_t kWsAccumBytes = size_t(40) << 20;
-constexpr size_t kWsScratchOffset = kWsAccumOffset + kWsAccumBytes;
+constexpr size_t kWsStatsOffset = kWsAccumOffset + kWsAccumBytes;
+constexpr size_t kWsStatsBytes = size_t(64) << 10;
+constexpr size_t kWsScratchOffset = kWsStatsOffset + kWsStatsBytes;
 
 struct Workspace {
   int* status = nullptr;
   int* counters = nullptr;
   float* accum = nullptr;
   size_t accum_bytes = 0;
+  float* stats = nullptr;  // kWsStatsBytes
   float* scratch = nullptr;
   size_t scratch_bytes = 0;
 };
@@ -43,6 +47,7 @@ inline int split_workspace(void* ws, size_t bytes, Workspace* out) {
   out->counters = reinterpret_cast<int*>(b + kWsCounterOffset);
   out->accum = reinterpret_cast<float*>(b + kWsAccumOffset);
   out->accum_bytes = kWsAccumBytes;
+  out->stats = reinterpret_cast<float*>(b + kWsStatsOffset);
   out->scratch = reinterpret_cast<float*>(b + kWsScratchOffset);
   out->scratch_bytes = bytes - kWsScratchOffset;
   return PI05_OK;
@@ -90,6 +95,34 @@ int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cud
   count_launch();
   if (e != cudaSuccess) {
     set_last_error("launch failed: %s", cudaGetErrorString(e));
+    return PI05_ERR_LAUNCH;
+  }
+  return PI05_OK;
+}
+
+// launch_pdl with a thread-block cluster of `cluster` CTAs.
+template <typename... KArgs, typename... Args>
+int launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
+                       dim3 cluster, Args&&... args) {
+  cudaLaunchConfig_t cfg;
+  std::memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster.x;
+  attr[0].val.clusterDim.y = cluster.y;
+  attr[0].val.clusterDim.z = cluster.z;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  count_launch();
+  if (e != cudaSuccess) {
+    set_last_error("cluster launch failed: %s", cudaGetErrorString(e));
     return PI05_ERR_LAUNCH;
   }
   return PI05_OK;

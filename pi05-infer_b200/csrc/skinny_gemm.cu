@@ -41,9 +41,11 @@ namespace {
 
 using namespace gemm;
 constexpr int kThreads = 192;     // warp0 TMA, warp1 MMA/TMEM, warps2-5 epilogue
+// Ring, barrier area (512 B), fused-norm area (rstd per token, scale and shift of
+// the CTA's K range).
 template <int TOK, int STAGES>
 constexpr int smem_bytes() {
-  return 1024 + STAGES * (kABytes + TOK * 128) + 512;
+  return 1024 + STAGES * (kABytes + TOK * 128) + 512 + TOK * 4 + 2 * kNormMaxK * 4;
 }
 
 // Small-token variants are limited to 170 registers so that two CTAs fit per SM:
@@ -72,7 +74,15 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
   unsigned long long* s_stamp = reinterpret_cast<unsigned long long*>(accum + 1);  // 8-byte aligned
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(accum + 2);
   int* s_flag = reinterpret_cast<int*>(s_tmem + 1);  // [0] abort, [1] ticket
+  uint64_t* rbar = accum + 9;                         // push-form split-K: partial slices received
+  uint64_t* xrdy = accum + 10;                        // [STAGES] fused norm: X stage normalised
+  float* s_rstd = reinterpret_cast<float*>(smem + STAGES * kStageBytes + 512);  // [TOK]
+  float* s_mod = s_rstd + TOK;                                                  // [2][kNormMaxK]
+  const bool norm = p.norm_ssq != nullptr;
   float* stage_tile = reinterpret_cast<float*>(smem);
+  // Push-form receive slots follow the staging tile inside the finished ring.
+  constexpr bool kPushFits = TOK * kBM * 4 + (TOK + 16) * kBM * 4 <= STAGES * kStageBytes;
+  float* recv = stage_tile + TOK * kBM;
 
   const uint64_t t_entry = (p.trace != nullptr) ? globaltimer_ns() : 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -89,6 +99,8 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
       mbar_init(&empty[s], 1);
     }
     mbar_init(accum, 1);
+    mbar_init(rbar, 1);
+    for (int s = 0; s < STAGES; ++s) mbar_init(&xrdy[s], 4);
     s_flag[0] = 0;
     s_flag[1] = 0;
     fence_mbar_init();
@@ -108,6 +120,7 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
   const uint32_t tmem_acc = *s_tmem;
   const uint64_t t_start = (p.trace != nullptr) ? globaltimer_ns() : 0;
   uint64_t t_pdl = 0, t_acc = 0, t_pub = 0, t_red = 0;
+  uint64_t t_nload = 0, t_nx0 = 0, t_nxl = 0;  // fused norm: loads done, first / last X stage normalised
   // Let the next kernel in the stream start its prologue / weight prefetch.
   pdl_launch_dependents();
 
@@ -148,7 +161,9 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
       bool ok = true;
       for (int i = 0; i < nk; ++i) {
         const int s = i % STAGES;
-        if (!mbar_wait(&full[s], (i / STAGES) & 1)) {
+        // With the fused norm the stage is ready once the epilogue warps have
+        // normalised its X tile.
+        if (!mbar_wait(norm ? &xrdy[s] : &full[s], (i / STAGES) & 1)) {
           report_status(p.status, PI05_DEV_TIMEOUT_MMA);
           s_flag[0] = 1;
           ok = false;
@@ -188,10 +203,98 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
     const int row = q * 32 + lane;
     const int et = threadIdx.x - 64;
     if (p.trace != nullptr) t_pdl = globaltimer_ns();
+    if (norm) {
+      // Fused (ada)RMS norm of X: per-token rstd from the producer's partial sums of
+      // squares, scale / shift of this CTA's K range, then every X stage is
+      // normalised in place (128B-swizzled rows of 64 bf16) before the MMA reads it.
+      // Every load is issued before the first is consumed (one L2 round trip).
+      const int d = p.norm_d;
+      constexpr int kTPT = (TOK + kEpiThreads - 1) / kEpiThreads;  // tokens per thread
+      float ssv[kTPT][kNormMaxParts];
+#pragma unroll
+      for (int a = 0; a < kTPT; ++a) {
+        const int t = et + a * kEpiThreads;
+#pragma unroll
+        for (int j = 0; j < kNormMaxParts; ++j)
+          ssv[a][j] = (t < mt && j < p.norm_parts) ? p.norm_ssq[(size_t)j * p.norm_ld + tok0 + t] : 0.f;
+      }
+      const int kbase = kb0 * kBK;
+      const int klen = min(nk * kBK, p.k - kbase);  // multiple of 8
+      constexpr int kMPT = kNormMaxK / 4 / kEpiThreads;  // float4 chunks per thread and table
+      float4 msc[kMPT], msh[kMPT];
+      const float4* msrc = reinterpret_cast<const float4*>(p.norm_mod + kbase);
+      const float4* hsrc = reinterpret_cast<const float4*>(p.norm_mod + d + kbase);
+#pragma unroll
+      for (int a = 0; a < kMPT; ++a) {
+        const int c = et + a * kEpiThreads;
+        if (4 * c < klen) {
+          msc[a] = msrc[c];
+          msh[a] = hsrc[c];
+        }
+      }
+#pragma unroll
+      for (int a = 0; a < kTPT; ++a) {
+        const int t = et + a * kEpiThreads;
+        if (t < TOK) {
+          float ss = 0.f;
+#pragma unroll
+          for (int j = 0; j < kNormMaxParts; ++j) ss += ssv[a][j];  // parts in order (zeros past the end)
+          s_rstd[t] = t < mt ? rsqrtf(ss / (float)d + p.norm_eps) : 0.f;
+        }
+      }
+#pragma unroll
+      for (int a = 0; a < kMPT; ++a) {
+        const int c = et + a * kEpiThreads;
+        if (4 * c < klen) {
+          reinterpret_cast<float4*>(s_mod)[c] = msc[a];
+          reinterpret_cast<float4*>(s_mod + kNormMaxK)[c] = msh[a];
+        }
+      }
+      named_bar_sync(1, kEpiThreads);
+      if (p.trace != nullptr) t_nload = globaltimer_ns();
+      const int g = et & 7;  // this thread's 16-byte chunk (8 k values) of every row
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % STAGES;
+        if (!mbar_wait(&full[s], (i / STAGES) & 1)) {
+          report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
+          break;
+        }
+        const int kc = i * kBK + g * 8;
+        float sc[8], sh[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const bool in = kc + j < klen;
+          sc[j] = in ? s_mod[kc + j] : 0.f;
+          sh[j] = in ? s_mod[kNormMaxK + kc + j] : 0.f;
+        }
+        uint8_t* xs = sB + s * kBBytes;
+        for (int t = et >> 3; t < TOK; t += kEpiThreads / 8) {
+          uint4* ptr = reinterpret_cast<uint4*>(xs + t * 128 + ((g ^ (t & 7)) << 4));
+          float x[8], o[8];
+          unpack8(*ptr, x);
+          const float rs = s_rstd[t];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float nv = x[j] * rs;
+            o[j] = (t < mt && kc + j < klen) ? nv * (1.0f + sc[j]) + sh[j] : 0.f;
+          }
+          *ptr = pack8(o);
+        }
+        fence_proxy_async_smem();  // generic-proxy writes -> the MMA's async-proxy reads
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&xrdy[s]);
+        if (p.trace != nullptr) {
+          if (i == 0) t_nx0 = globaltimer_ns();
+          t_nxl = globaltimer_ns();
+        }
+      }
+    }
     const bool ok = mbar_wait(accum, 0);
     if (!ok) report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
     if (p.trace != nullptr) t_acc = globaltimer_ns();
     tc_fence_after();
+    const bool push = kPushFits && p.cluster && p.push;
+    if (push) cluster_push_arrive(rbar, p.splits, mt, (int)cluster_ctarank(), et);
     if (ok) {
 #pragma unroll 1
       for (int c = 0; c < TOK / 32; ++c) {
@@ -201,6 +304,7 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
         for (int j = 0; j < 32; ++j) stage_tile[(c * 32 + j) * kBM + row] = v[j];
       }
     }
+    if (push) fence_proxy_async_smem();  // the bulk copies read the staging tile
     named_bar_sync(1, kEpiThreads);
     const int items = epi_items<EPI>(p, tile, mt);
     if (ok && p.splits == 1) {
@@ -240,8 +344,12 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
       if (s_flag[1]) {
         __threadfence();
         TileSrc src{nullptr, part, p.splits, TOK * kBM};
-        const int i0 = (int)(((long)split * items) / p.splits);
-        const int i1 = (int)(((long)(split + 1) * items) / p.splits);
+        int i0 = (int)(((long)split * items) / p.splits);
+        int i1 = (int)(((long)(split + 1) * items) / p.splits);
+        if (p.row_ssq != nullptr) {  // whole tokens per split (row statistics)
+          i0 = 16 * ((split * mt) / p.splits);
+          i1 = 16 * (((split + 1) * mt) / p.splits);
+        }
         apply_epilogue<EPI, 1>(p, src, tile, tok0, i0, i1, et);
       }
       named_bar_sync(1, kEpiThreads);
@@ -256,23 +364,28 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
   // Cluster split-K: every split CTA of the tile has its partial in its staging
   // tile; cluster_epilogue reduces this rank's slice through DSMEM and applies the
   // epilogue between its two cluster barriers.
+  unsigned long long* cl_stamps = reinterpret_cast<unsigned long long*>(accum + 4);  // [5]
   if (p.cluster) {
     __syncwarp();
-    unsigned long long* bar_stamp = reinterpret_cast<unsigned long long*>(accum + 4);
-    cluster_epilogue<EPI>(p, smem_u32(stage_tile), tile, tok0, mt, (int)cluster_ctarank(), (int)threadIdx.x - 64,
-                          warp >= 2, p.trace != nullptr ? bar_stamp : nullptr);
+    if (kPushFits && p.push)
+      cluster_push_epilogue<EPI>(p, stage_tile, recv, rbar, tile, tok0, mt, (int)cluster_ctarank(),
+                                 (int)threadIdx.x - 64, warp >= 2, p.trace != nullptr ? cl_stamps : nullptr);
+    else
+      cluster_epilogue<EPI>(p, smem_u32(stage_tile), tile, tok0, mt, (int)cluster_ctarank(), (int)threadIdx.x - 64,
+                            warp >= 2, p.trace != nullptr ? cl_stamps : nullptr);
     if (p.trace != nullptr) {
       t_red = globaltimer_ns();
-      t_pub = *bar_stamp;  // written by this thread (epilogue thread 0) after the first cluster barrier
+      t_pub = cl_stamps[1];  // written by this thread (epilogue thread 0) after the first cluster barrier
     }
   }
 
   if (p.trace != nullptr && threadIdx.x == 64) {
-    const unsigned long long slot = atomicAdd(p.trace, 1ull);
+    const unsigned long long cta = ((unsigned long long)smid() << 16) | (blockIdx.y * gridDim.x + blockIdx.x);
+    const unsigned long long slot = atomicAdd(p.trace, (p.cluster ? 2ull : 1ull) + (norm ? 1ull : 0ull));
     const unsigned long long cap = p.trace[1];  // records the buffer holds
     if (slot < cap) {
       unsigned long long* w = p.trace + 8 + slot * 8;
-      w[0] = ((unsigned long long)p.trace_tag << 32) | (blockIdx.y * gridDim.x + blockIdx.x);
+      w[0] = ((unsigned long long)p.trace_tag << 32) | cta;
       w[1] = t_entry;
       w[2] = t_start;
       w[3] = t_pdl;
@@ -280,6 +393,29 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
       w[5] = t_pub;
       w[6] = t_red != 0 ? t_red : globaltimer_ns();
       w[7] = s_stamp[0];
+    }
+    if (p.cluster && slot + 1 < cap) {
+      // Cluster epilogue record (tag + 2^30): before / after the first cluster
+      // barrier, first DSMEM pass summed, last store issued, exit barrier passed.
+      unsigned long long* w = p.trace + 8 + (slot + 1) * 8;
+      w[0] = ((unsigned long long)(p.trace_tag + (1 << 30)) << 32) | cta;
+      for (int i = 0; i < 5; ++i) w[1 + i] = cl_stamps[i];
+      w[6] = 0;
+      w[7] = 0;
+    }
+    const unsigned long long ns = slot + (p.cluster ? 2 : 1);
+    if (norm && ns < cap) {
+      // Fused-norm record (tag + 2^31): grid-dependency wait done, rstd / scale
+      // loads done, first and last X stage normalised.
+      unsigned long long* w = p.trace + 8 + ns * 8;
+      w[0] = ((unsigned long long)(p.trace_tag + (2u << 30)) << 32) | cta;
+      w[1] = t_pdl;
+      w[2] = t_nload;
+      w[3] = t_nx0;
+      w[4] = t_nxl;
+      w[5] = t_acc;
+      w[6] = 0;
+      w[7] = 0;
     }
   }
 
@@ -429,6 +565,23 @@ int skinny_choose_splits_cluster(int n_tiles, int kb_total, int tok_tiles, int s
   return best;
 }
 
+// PI05_L2_PREFETCH=0 in the environment drops the next-layer L2 prefetch ranges.
+bool l2_prefetch_enabled() {
+  static int v = [] {
+    const char* e = getenv("PI05_L2_PREFETCH");
+    return (e != nullptr && e[0] == '0') ? 0 : 1;
+  }();
+  return v != 0;
+}
+
+bool push_enabled() {
+  static int v = [] {
+    const char* e = getenv("PI05_PUSH");
+    return (e != nullptr && e[0] == '0') ? 0 : 1;
+  }();
+  return v != 0;
+}
+
 bool cluster_disabled() {
   static int v = [] {
     const char* e = getenv("PI05_CLUSTER");
@@ -444,7 +597,15 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
     set_last_error("skinny_gemm: bad shape m=%d k=%d tiles=%d", p.m_tok, p.k, p.n_tiles);
     return PI05_ERR_SHAPE;
   }
-  if (p.m_tok >= kWideMinTokens && !wide_disabled()) {
+  if (p.norm_ssq != nullptr &&
+      (p.norm_d != p.k || p.k > kNormMaxK || p.norm_parts <= 0 || p.norm_parts > kNormMaxParts ||
+       p.norm_mod == nullptr || !aligned16(p.norm_mod) || p.norm_d % 4 != 0)) {
+    set_last_error("skinny_gemm: fused norm needs norm_d == k <= %d, 1..%d parts, 16-byte aligned mod", kNormMaxK,
+                   kNormMaxParts);
+    return PI05_ERR_SHAPE;
+  }
+  const bool fused_rows = p.norm_ssq != nullptr || p.row_ssq != nullptr;  // small-token kernel only
+  if (p.m_tok >= kWideMinTokens && !wide_disabled() && !fused_rows) {
     int n_cols = 0;
     if (epi == SK_EPI_GEGLU)
       n_cols = p.n_tiles * 64;
@@ -500,6 +661,12 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
       return PI05_ERR_WORKSPACE;
     }
   }
+  if (!l2_prefetch_enabled()) {
+    p.pf0 = nullptr;
+    p.pf1 = nullptr;
+  }
+  // Push-form split-K for the small-token tile (splits <= 16 fit its receive slots).
+  p.push = (p.cluster && tok == 64 && p.splits <= 16 && push_enabled()) ? 1 : 0;
   CUtensorMap tw0, tw1, tx;
   int rc = make_tmap_bf16_2d(&tw0, w0, w_rows0, p.k, p.k, 64, 64, true);
   if (rc) return rc;

@@ -21,6 +21,7 @@ struct SkinnyParams {
   int splits = 1;    // set by the launcher
   int cluster = 0;   // set by the launcher: 1 = the splits of a tile form a cluster and reduce through DSMEM
   int allow_cluster = 1;  // 0 = split-K only through the global accumulator
+  int push = 0;      // set by the launcher: cluster split-K pushes partial slices to their owners (TOK 64)
   // STORE / GATED_RESID / GEGLU
   __nv_bfloat16* out = nullptr;
   int ldo = 0;
@@ -43,6 +44,22 @@ struct SkinnyParams {
   int n_q_heads = 0;
   int n_kv_heads = 0;
   int head_dim = 0;
+  // Row statistics for a following RMS norm (STORE / GATED_RESID): when set, the
+  // sum of squares of every token's bf16 outputs within each 128-row weight tile is
+  // written to row_ssq[tile * ssq_ld + token] (fixed summation order).
+  float* row_ssq = nullptr;
+  int ssq_ld = 0;
+  // Fused (ada)RMS norm of the X operand: when norm_ssq is set, X holds the raw
+  // residual stream h and each X tile is normalised in shared memory before the
+  // MMA: x = bf16(h * rstd[t] * (1 + norm_mod[k]) + norm_mod[norm_d + k]), with
+  // rstd[t] = rsqrt(sum_j norm_ssq[j * norm_ld + t] / norm_d + norm_eps) over
+  // norm_parts partial sums in order.  Needs k <= kNormMaxK.
+  const float* norm_ssq = nullptr;
+  int norm_parts = 0;
+  int norm_ld = 0;
+  const float* norm_mod = nullptr;
+  int norm_d = 0;
+  float norm_eps = 0.f;
   // L2 prefetch issued by every CTA for its share of these ranges (e.g. the same
   // op's weights of the next layer), so later launches read them from L2.
   const void* pf0 = nullptr;
@@ -63,10 +80,16 @@ struct SkinnyParams {
   int* status = nullptr;    // device status word
 };
 
+constexpr int kNormMaxK = 1024;    // fused-norm X operands: K range staged in shared memory
+constexpr int kNormMaxParts = 16;  // fused-norm partial sums of squares per token
+
 int skinny_choose_splits(int n_tiles, int kb_total, int tok_tiles, int sms);
 int skinny_choose_splits_cluster(int n_tiles, int kb_total, int tok_tiles, int sms, int max_cluster);
 // PI05_CLUSTER=0 in the environment selects the global-memory split-K path.
 bool cluster_disabled();
+// PI05_PUSH=0 in the environment selects the pull form of the cluster split-K.
+bool push_enabled();
+bool l2_prefetch_enabled();
 
 // w0/w1: weight matrices for the two 64-row boxes of each tile (the same matrix
 // except for GEGLU, where w0 = gate and w1 = up).  w_rows*: their row counts.
