@@ -6,24 +6,30 @@
 // GPU).  Per chunk j:
 //
 //   S_j  = Q . K_j^T          tcgen05.mma M=128 N=64  K=256 -> TMEM (two S buffers)
-//   P_j  = exp(S_j - m)       one thread per query row reads its S row from TMEM,
-//                             updates the running max / sum, rescales its O row in
-//                             TMEM when the max moved, writes P_j (bf16) to shared
-//                             memory in the 128B-swizzled K-major layout
+//   P_j  = exp(S_j - m)       two threads per query row (one per 32-key half) read
+//                             the row's S from TMEM, agree on the row max through
+//                             shared memory, keep partial row sums, rescale their
+//                             half of the O row in TMEM when the exponent base
+//                             moved, and write P_j (bf16) to shared memory in the
+//                             128B-swizzled K-major layout
 //   O   += P_j . V_j          tcgen05.mma M=128 N=256 K=64, V read MN-major straight
 //                             from the cache layout [key][256]
 //
 // Warp roles: warp 0 TMA (Q once, K/V chunks through a 1- or 2-stage ring),
 // warp 1 TMEM owner + MMA issuer (S_{j+1} is issued before P_j is ready, so the
-// tensor core works on the next scores while the softmax runs), warps 2-5
-// softmax and the output.  Chunks of the static part of the cache (the prefix
-// rows) are loaded before the grid-dependency wait.
+// tensor core works on the next scores while the softmax runs), warps 2-9
+// softmax and the output (two per TMEM lane quarter, so every SM sub-partition
+// runs two of them).  Chunks of the static part of the cache (the prefix rows) are
+// loaded before the grid-dependency wait; the key mask of the CTA's keys is staged
+// in shared memory once.
 //
 // Numerics follow eager_attention_forward (pi05_infer/gemma/modeling_gemma.py:
 // 252-275) the same way as the mma.sync kernel in attention.cu: the score is the
 // bf16-rounded Q.K^T times the scale rounded again to bf16, masked keys are
 // excluded, softmax in fp32 with a running max, probabilities enter P.V as bf16,
-// fp32 accumulation.  Split-KV partials use that kernel's layout and combine.
+// fp32 accumulation.  The exponent base is the running max held back by up to 8
+// (lazy rescaling), which changes no normalised value.  Split-KV partials use the
+// mma.sync kernel's layout and combine.
 #include <cuda_bf16.h>
 #include <stdint.h>
 
@@ -44,8 +50,8 @@ constexpr int kBC = 64;                      // keys per chunk
 constexpr int kQBytes = kBR * kD * 2;        // 4 boxes of [128 rows x 64 dims]
 constexpr int kKVBytes = kBC * kD * 2;       // 4 boxes of [64 keys x 64 dims]
 constexpr int kPBytes = kBR * kBC * 2;       // [128 rows x 64 keys]
-constexpr int kThreads = 192;
-constexpr int kSoftThreads = 128;
+constexpr int kThreads = 320;       // warp 0 TMA, warp 1 MMA, warps 2-9 softmax / output
+constexpr int kSoftThreads = 256;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 128;              // S buffers at columns 0 and 64, O at 128..383
 constexpr uint32_t kIdescS = umma_idesc_bf16(kBR, kBC);
@@ -56,9 +62,20 @@ struct TcMaps {
   CUtensorMap q, k, v, out, po;
 };
 
-size_t tc_smem_bytes(int nst) { return 1024 + kQBytes + (size_t)nst * 2 * kKVBytes + kPBytes + 256; }
+constexpr int kMaxChunks = 64;  // key chunks per CTA whose mask bytes are staged (4096 keys)
+// Ring, barriers, the row-max / row-sum exchange [6][128], the staged key mask.
+size_t tc_smem_bytes(int nst) {
+  return 1024 + kQBytes + (size_t)nst * 2 * kKVBytes + kPBytes + 28 * 8 + 6 * kBR * 4 + kMaxChunks * kBC;
+}
 
 __device__ __forceinline__ uint32_t p_off(int r, int g) { return (uint32_t)(r * 128 + ((g ^ (r & 7)) << 4)); }
+
+// 32-bit word wd (bytes 4wd .. 4wd+3) of a 32-byte key mask held in two uint4.
+__device__ __forceinline__ uint32_t& mask_word(uint4* vk, int wd) { return (&vk[wd >> 2].x)[wd & 3]; }
+
+__device__ __forceinline__ bool key_ok(uint4* vk, int i) { return ((mask_word(vk, i >> 2) >> ((i & 3) * 8)) & 0xffu) != 0; }
+
+__device__ __forceinline__ bool has_zero_byte(uint32_t w) { return ((w - 0x01010101u) & ~w & 0x80808080u) != 0; }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -84,6 +101,13 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
   uint64_t* mdone = bars + 11;    // every MMA of the CTA complete
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 12);
   int* s_flag = reinterpret_cast<int*>(s_tmem + 1);  // [0] abort, [1] K/V chunks armed
+  // Row-max exchange of the two warps of each TMEM lane quarter: [quarter][S parity]
+  // (64 arrivals), then the final row-sum exchange [quarter].
+  uint64_t* xbar = bars + 14;
+  uint64_t* lbar = bars + 22;  // [4] row sums, [4] mask staged
+  // Row max of each half for the two S parities [2][2][128], then the row sums [2][128].
+  float* s_red = reinterpret_cast<float*>(bars + 28);
+  uint8_t* s_mask = reinterpret_cast<uint8_t*>(s_red + 6 * kBR);  // [nc * 64] key-mask bytes of this CTA
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool tr = p.trace != nullptr && threadIdx.x == 64;
@@ -107,6 +131,9 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
     mbar_init(p_full, kSoftThreads);
     mbar_init(p_empty, 1);
     mbar_init(mdone, 1);
+    mbar_init(&lbar[4], kSoftThreads);  // mask bytes staged
+    for (int i = 0; i < 8; ++i) mbar_init(&xbar[i], 64);
+    for (int i = 0; i < 4; ++i) mbar_init(&lbar[i], 64);
     s_flag[0] = 0;
     s_flag[1] = 0;
     fence_mbar_init();
@@ -201,58 +228,103 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
       if (!mbar_wait(mdone, 0)) report_status(p.status, PI05_DEV_TIMEOUT_DRAIN);
     }
   } else {
-    // Softmax warps: TMEM lane quarter = warp % 4, one query row per thread.
+    // Softmax warps 2..9: TMEM lane quarter = warp % 4 (rows q*32 .. q*32+31, one
+    // per thread).  The quarter's two warps split the chunk's 64 score columns
+    // (half hh takes keys hh*32 .. hh*32+31) and the 256 O columns (hh*128 ..
+    // hh*128+127): they agree on the row max through shared memory once per chunk
+    // and keep partial row sums, added at the end.  Two warps per SM sub-partition
+    // hide each other's latencies.
     pdl_wait();
     if (tr) t_wait = globaltimer_ns();
     const int q = warp & 3;
+    const int hh = (warp - 2) >> 2;
     const int r = q * 32 + lane;
     const int grow = row0 + r;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    float m = -INFINITY, l = 0.f;
+
     bool ok = true;
+    {
+      // Stage this CTA's key-mask bytes (0 past kv_len) once: four per thread.
+      const int et = threadIdx.x - 64;
+      const int kbeg = c_begin * kBC;
+      for (int i = et * 4; i < nc * kBC; i += kSoftThreads * 4) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const int key = kbeg + i + b;
+          if (key < p.kv_len && p.key_valid[key] != 0) word |= 1u << (8 * b);
+        }
+        *reinterpret_cast<uint32_t*>(s_mask + i) = word;
+      }
+      mbar_arrive(&lbar[4]);
+      if (!mbar_wait(&lbar[4], 0)) ok = false;
+    }
+    float m = -INFINITY, l = 0.f;
+    constexpr float kLog2e = 1.4426950408889634f;
+    int sexp;
+    const bool scale_pow2 = frexpf(p.scale, &sexp) == 0.5f;
     for (int j = 0; j < nc; ++j) {
       const int sb = j & 1;
-      // The chunk's key mask (static) is read while the scores are computed.
-      const int key0 = (c_begin + j) * kBC;
-      uint8_t vk[64];
-      if (key0 + kBC <= p.kv_len && (reinterpret_cast<uintptr_t>(p.key_valid) & 15) == 0) {
+      // This half's 32 key-mask bytes.
+      uint4 vk[2];
+      vk[0] = *reinterpret_cast<const uint4*>(s_mask + j * kBC + hh * 32);
+      vk[1] = *reinterpret_cast<const uint4*>(s_mask + j * kBC + hh * 32 + 16);
+      bool all_valid = true;
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          *reinterpret_cast<uint4*>(vk + i * 16) = *reinterpret_cast<const uint4*>(p.key_valid + key0 + i * 16);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 64; ++i) vk[i] = (key0 + i < p.kv_len) ? p.key_valid[key0 + i] : 0;
-      }
+      for (int wd = 0; wd < 8; ++wd) all_valid = all_valid && !has_zero_byte(mask_word(vk, wd));
       if (!mbar_wait(&s_full[sb], (j >> 1) & 1)) {
         ok = false;
         break;
       }
       tc_fence_after();
       if (tr && j == 0) t_data = globaltimer_ns();
-      float s[64];
-      tmem_ld32(tmem + lane_base + sb * kBC, s);
-      tmem_ld32(tmem + lane_base + sb * kBC + 32, s + 32);
+      float s[32];
+      tmem_ld32(tmem + lane_base + sb * kBC + hh * 32, s);
       tc_fence_before();
       mbar_arrive(&s_empty[sb]);
-      float mx = -INFINITY;
+      // Scores: bf16(bf16(q.k) * scale); a power-of-two scale needs no second
+      // rounding (the product is exact).
+      float mx4[4];
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        float v = bf16_round(bf16_round(s[i]) * p.scale);
-        v = vk[i] ? v : -INFINITY;
+      for (int i = 0; i < 4; ++i) mx4[i] = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        float v = bf16_round(s[i]) * p.scale;
+        if (!scale_pow2) v = bf16_round(v);
+        if (!all_valid) v = key_ok(vk, i) ? v : -INFINITY;
         s[i] = v;
-        mx = fmaxf(mx, v);
+        mx4[i & 3] = fmaxf(mx4[i & 3], v);
       }
+      s_red[(sb * 2 + hh) * kBR + r] = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      mbar_arrive(&xbar[q * 2 + sb]);
+      if (!mbar_wait(&xbar[q * 2 + sb], (j >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      const float mx = fmaxf(s_red[(sb * 2) * kBR + r], s_red[(sb * 2 + 1) * kBR + r]);
+      // Lazy rescale: the exponent base m moves only when the chunk's max exceeds
+      // it by more than 8 (P entries stay below e^8 in bf16, whose relative
+      // precision does not depend on magnitude); O and l always refer to the same
+      // m, so the normalised result is unchanged.  Both halves decide alike.
       const float m_new = fmaxf(m, mx);
-      const float corr = (m_new == -INFINITY || m == m_new) ? 1.f : __expf(m - m_new);
-      m = m_new;
-      float ls = 0.f;
-#pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const float pv = (s[i] == -INFINITY) ? 0.f : __expf(s[i] - m);
-        s[i] = pv;
-        ls += pv;
+      float corr = 1.f;
+      if (m == -INFINITY) {
+        m = m_new;
+      } else if (m_new - m > 8.f) {
+        corr = __expf(m - m_new);
+        m = m_new;
       }
-      l = l * corr + ls;
+      const float mb = m == -INFINITY ? 0.f : m * kLog2e;
+      float ls4[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) ls4[i] = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float pv = ex2_approx(fmaf(s[i], kLog2e, -mb));  // exp(s - m); masked keys give 0
+        s[i] = pv;
+        ls4[i & 3] += pv;
+      }
+      l = l * corr + ((ls4[0] + ls4[1]) + (ls4[2] + ls4[3]));
       if (j > 0) {
         // P.V of the previous chunk must be done: P is single-buffered and O may
         // need rescaling.
@@ -262,48 +334,57 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
         }
         tc_fence_after();
         // tcgen05.ld/st are warp-collective: rescale when any row of the warp moved
-        // (rows whose max did not move multiply by 1).
+        // (rows whose base did not move multiply by 1).
         if (__any_sync(0xffffffff, corr != 1.f)) {
 #pragma unroll 1
-          for (int c = 0; c < kD / 32; ++c) {
+          for (int c = 0; c < 4; ++c) {
             float o[32];
-            tmem_ld32(tmem + lane_base + kColO + c * 32, o);
+            tmem_ld32(tmem + lane_base + kColO + hh * 128 + c * 32, o);
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] *= corr;
-            tmem_st32(tmem + lane_base + kColO + c * 32, o);
+            tmem_st32(tmem + lane_base + kColO + hh * 128 + c * 32, o);
           }
         }
       }
 #pragma unroll
-      for (int g = 0; g < 8; ++g) {
+      for (int g4 = 0; g4 < 4; ++g4) {
         uint4 u;
-        u.x = pack_bf16x2(s[g * 8 + 0], s[g * 8 + 1]);
-        u.y = pack_bf16x2(s[g * 8 + 2], s[g * 8 + 3]);
-        u.z = pack_bf16x2(s[g * 8 + 4], s[g * 8 + 5]);
-        u.w = pack_bf16x2(s[g * 8 + 6], s[g * 8 + 7]);
-        *reinterpret_cast<uint4*>(sP + p_off(r, g)) = u;
+        u.x = pack_bf16x2(s[g4 * 8 + 0], s[g4 * 8 + 1]);
+        u.y = pack_bf16x2(s[g4 * 8 + 2], s[g4 * 8 + 3]);
+        u.z = pack_bf16x2(s[g4 * 8 + 4], s[g4 * 8 + 5]);
+        u.w = pack_bf16x2(s[g4 * 8 + 6], s[g4 * 8 + 7]);
+        *reinterpret_cast<uint4*>(sP + p_off(r, hh * 4 + g4)) = u;
       }
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
     }
     if (!ok) report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
+    // Row sums of the two halves (fixed order: half 0 + half 1).
+    s_red[4 * kBR + hh * kBR + r] = l;
+    mbar_arrive(&lbar[q]);
+    if (ok && !mbar_wait(&lbar[q], 0)) {
+      report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
+      ok = false;
+    }
+    const float lt = s_red[4 * kBR + r] + s_red[5 * kBR + r];
     if (ok && nc > 0 && mbar_wait(p_empty, (nc - 1) & 1)) {
       tc_fence_after();
       if (tr) t_loop = globaltimer_ns();
       // Output through shared memory: Q and the K/V ring are free once every MMA
-      // is done.  Each warp stages its 32 rows in 128B-swizzled 4 KB slabs (32 KB
-      // per warp) and writes them with TMA tensor stores (rows past R are clipped).
-      uint8_t* slab0 = smem + (warp - 2) * 8 * 4096;
+      // is done.  Each warp stages its 32 rows x 128 columns in 128B-swizzled 4 KB
+      // slabs (16 KB per warp) and writes them with TMA tensor stores (rows past R
+      // are clipped).
+      uint8_t* slab0 = smem + (warp - 2) * 4 * 4096;
       if (p.splits == 1) {
-        const float inv = l > 0.f ? 1.f / l : 0.f;
+        const float inv = lt > 0.f ? 1.f / lt : 0.f;
 #pragma unroll 1
-        for (int jb = 0; jb < kD / 64; ++jb) {
+        for (int jb = 0; jb < 2; ++jb) {
           uint8_t* slab = slab0 + jb * 4096;
 #pragma unroll 1
           for (int h = 0; h < 2; ++h) {
             float o[32];
-            tmem_ld32(tmem + lane_base + kColO + jb * 64 + h * 32, o);
+            tmem_ld32(tmem + lane_base + kColO + hh * 128 + jb * 64 + h * 32, o);
 #pragma unroll
             for (int g4 = 0; g4 < 4; ++g4) {
               uint4 u;
@@ -318,16 +399,17 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          for (int jb = 0; jb < kD / 64; ++jb) tma_store_2d(&mp.out, slab0 + jb * 4096, jb * 64, row0 + q * 32);
+          for (int jb = 0; jb < 2; ++jb)
+            tma_store_2d(&mp.out, slab0 + jb * 4096, hh * 128 + jb * 64, row0 + q * 32);
           bulk_commit_group();
         }
       } else {
         const int y = split * p.part_rows + row0 + q * 32;
 #pragma unroll 1
-        for (int c = 0; c < kD / 32; ++c) {
+        for (int c = 0; c < 4; ++c) {
           uint8_t* slab = slab0 + c * 4096;
           float o[32];
-          tmem_ld32(tmem + lane_base + kColO + c * 32, o);
+          tmem_ld32(tmem + lane_base + kColO + hh * 128 + c * 32, o);
 #pragma unroll
           for (int g = 0; g < 8; ++g)
             *reinterpret_cast<float4*>(slab + p_off(lane, g)) =
@@ -336,12 +418,14 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          for (int c = 0; c < kD / 32; ++c) tma_store_2d(&mp.po, slab0 + c * 4096, c * 32, y);
+          for (int c = 0; c < 4; ++c) tma_store_2d(&mp.po, slab0 + c * 4096, hh * 128 + c * 32, y);
           bulk_commit_group();
         }
         // (max, sum) of every row of the padded block; rows past R are padding.
-        p.part_ml[((size_t)split * p.part_rows + grow) * 2] = m;
-        p.part_ml[((size_t)split * p.part_rows + grow) * 2 + 1] = l;
+        if (hh == 0) {
+          p.part_ml[((size_t)split * p.part_rows + grow) * 2] = m;
+          p.part_ml[((size_t)split * p.part_rows + grow) * 2 + 1] = lt;
+        }
       }
       if (lane == 0) bulk_wait_group<0>();
       __syncwarp();
@@ -416,6 +500,11 @@ int mqa_tc_attention_run(AttnParams p, float* part, size_t part_bytes, int split
   }
   splits = std::min(splits, n_chunks);
   splits = std::min(splits, 32);
+  splits = std::max(splits, (n_chunks + kMaxChunks - 1) / kMaxChunks);  // staged mask bytes per CTA
+  if ((n_chunks + splits - 1) / splits > kMaxChunks) {
+    set_last_error("attention: %d keys exceed %d per split", p.kv_len, kMaxChunks * kBC);
+    return PI05_ERR_SHAPE;
+  }
   p.splits = splits;
   p.nbuf = (n_chunks + splits - 1) / splits > 1 ? 2 : 1;
   p.part_rows = row_blocks * kBR;  // partial rows padded to whole row blocks

@@ -409,4 +409,11 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16(x)); }
 
+// 2^x on the special-function unit (PTX ex2.approx.ftz.f32: -inf -> +0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 }  // namespace pi05

@@ -13,6 +13,8 @@ launches of interest on a small device footprint:
   prefix_qkv     many-token GEMM + RoPE into the KV cache, M=968, N=10x256, K=2048
   siglip_fc1     many-token GEMM + bias + GELU, M=768, N=4304, K=1152
   mqa_attention  denoise attention: 50 x 8 query rows over a 1018-key cache, d=256
+  prefix_attention  prefix-LM attention: 968 x 8 query rows over 968 keys, d=256
+                 (tcgen05 kernel, split-KV partials + combine)
 """
 
 import argparse
@@ -28,7 +30,7 @@ if __package__ in (None, ""):
 from pi05_infer import abi, ops  # noqa: E402
 
 CASES = ("denoise_geglu", "denoise_down", "prefix_geglu", "prefix_down", "prefix_qkv", "siglip_fc1",
-         "mqa_attention")
+         "mqa_attention", "prefix_attention")
 
 
 def _bf(t):
@@ -91,6 +93,19 @@ def build(case: str, dev="cuda"):
         w = rnd(4352, 1152, s=0.02)
         out = torch.empty(768, 4352, dtype=torch.bfloat16, device=dev)
         return (lambda: ops.linear(x, w, out=out)), None, 2 * 768 * 4352 * 1152
+    if case == "prefix_attention":
+        p, d = 968, 256
+        q = rnd(p, 8, d)
+        k = rnd(p, d)
+        v = rnd(p, d)
+        valid = torch.ones(p, dtype=torch.uint8, device=dev)
+        out = torch.empty(p, 8 * d, dtype=torch.bfloat16, device=dev)
+        wsp = ops.workspace(torch.device(dev))
+
+        def f():
+            abi.attention(q, k, v, valid, out, 1.0 / math.sqrt(d), 0, wsp)
+
+        return f, p * d * 2 * 2 + 2 * p * 8 * d * 2, 4 * p * 8 * p * d
     if case == "mqa_attention":
         p, s, d = 968, 50, 256
         q = rnd(s, 8, d)
