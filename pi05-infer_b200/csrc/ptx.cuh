@@ -95,6 +95,18 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, ui
       : "memory");
 }
 
+// The same 2-D load for a CTA pair (cta_group::2): the tile lands in this CTA's
+// shared memory and its bytes complete on the barrier at shared::cluster address
+// `bar` (the even CTA's).  A plain load of this GPU's global memory: no multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* tm, uint32_t bar, int x, int y,
+                                                 uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(x), "r"(y), "l"(policy)
+      : "memory");
+}
+
 // 2-D tiled store shared -> global (bulk-group completion).  The smem tile must
 // have been made visible to the async proxy (fence_proxy_async_smem) first.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, const void* src, int x, int y) {

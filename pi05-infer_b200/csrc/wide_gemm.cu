@@ -69,9 +69,17 @@ constexpr int epi_slabs() {
   return EPI == SK_EPI_QKV_ROPE ? 4 : 2;
 }
 
-template <int EPI, int BN, int STAGES, int EW>
+// B rows a CTA holds per stage: all BN, or half of them when a CTA pair shares
+// the tile (cta_group::2).
+template <int BN, bool PAIR>
+constexpr int wide_b_bytes() {
+  return (PAIR ? BN / 2 : BN) * 128;
+}
+
+template <int EPI, int BN, int STAGES, int EW, bool PAIR>
 constexpr int wide_smem_bytes() {
-  return 1024 + STAGES * (kABytes + BN * 128) + EW * epi_slabs<EPI>() * kSlabBytes + BN * 4 + 256;
+  // + 512: barriers, stamps and flags (up to ~300 bytes with 8 epilogue warps).
+  return 1024 + STAGES * (kABytes + wide_b_bytes<BN, PAIR>()) + EW * epi_slabs<EPI>() * kSlabBytes + BN * 4 + 512;
 }
 
 struct WideSched {
@@ -393,13 +401,24 @@ __device__ __forceinline__ bool wide_epi_qkv(const SkinnyParams& p, const WideMa
   return ok;
 }
 
-template <int EPI, int BN, int STAGES, int EW>
+// PAIR: the two CTAs of a 2-CTA cluster share each tile of 256 tokens x BN (= 256)
+// columns.  CTA r loads tokens r*128 .. r*128+127 of the tile and weight box r
+// (w0 rows for r = 0, w1 rows for r = 1); the even CTA (leader) issues
+// tcgen05.mma.cta_group::2 with M = 256, which reads both CTAs' shared memory and
+// accumulates into both CTAs' TMEM (CTA r: rows r*128 ..), so each SM streams
+// 32 KB of operands per k-block instead of 48 KB for the same FLOPs.  Both CTAs'
+// TMA loads (cta_group::2 form, no multicast) complete on the leader's full
+// barrier, which the leader arms for both; the leader's commits arrive on both
+// CTAs' barriers (multicast commit); the epilogues are per CTA, the odd CTA's
+// warps signalling "accumulator drained" to the leader remotely.
+template <int EPI, int BN, int STAGES, int EW, bool PAIR>
 __global__ void __launch_bounds__(wide_threads<EW>(), 1)
     wide_gemm_kernel(const __grid_constant__ WideMaps mp, const SkinnyParams p, const WideSched ws) {
-  constexpr int kBBytes = BN * 128;
+  constexpr int kBBytes = wide_b_bytes<BN, PAIR>();
   constexpr int kStageBytes = kABytes + kBBytes;
   constexpr uint32_t kTmemCols = 2 * BN;
-  constexpr uint32_t kIdesc = umma_idesc_bf16(kWBM, BN);
+  constexpr uint32_t kIdesc = umma_idesc_bf16(PAIR ? 2 * kWBM : kWBM, BN);
+  static_assert(!PAIR || BN == 256, "CTA pairs use 256-wide tiles");
   constexpr int kSlabs = epi_slabs<EPI>();
   constexpr int kEW = EW;
   static_assert(EW == 4 || ((EPI == SK_EPI_STORE || EPI == SK_EPI_GATED_RESID) && EW == 8), "epilogue warps");
@@ -427,15 +446,21 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
   uint64_t t_setup = 0, t_acc = 0, t_epi = 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total = ws.m_tiles * ws.n_tiles * ws.splits;
+  // Work units: CTAs, or CTA pairs (ws.m_tiles then counts 256-token pair tiles).
+  const int rank = PAIR ? (int)cluster_ctarank() : 0;
+  const bool leader = rank == 0;
+  const int unit0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int n_units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const int cta_m_tiles = PAIR ? 2 * ws.m_tiles : ws.m_tiles;  // 128-token tiles
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], 1);  // pairs: the leader's, completed by both CTAs' copies
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accf[b], 1);
-      mbar_init(&acce[b], kET);
+      mbar_init(&acce[b], PAIR ? 2 * kEW : kET);  // pairs: one arrival per epilogue warp of either CTA
     }
     mbar_init(mdone, 1);
     for (int i = 0; i < 2 * kEW; ++i) mbar_init(&sbar[i], 1);
@@ -460,11 +485,21 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
     }
   }
   if (warp == 1) {
-    tmem_alloc(s_tmem, kTmemCols);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(s_tmem, kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(s_tmem, kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) {
+    // Both CTAs' barriers are initialised before either signals the other.
+    cluster_arrive_release();
+    cluster_wait();
+  }
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
   if (p.trace != nullptr) t_setup = globaltimer_ns();
@@ -476,9 +511,29 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
       const uint64_t pol_x = l2_policy_evict_last();
       int it = 0;
       bool waited = false;
-      for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      // Pairs: every copy completes on the leader's barrier of the stage.
+      const uint32_t lead_full = PAIR ? mapa_shared(smem_u32(full), 0) : 0u;
+      auto load = [&](void* dst, const CUtensorMap* tm, int st, int x, int y, uint64_t pol) {
+        if (PAIR)
+          tma_load_2d_pair(dst, tm, lead_full + (uint32_t)st * 8u, x, y, pol);
+        else
+          tma_load_2d(dst, tm, &full[st], x, y, pol);
+      };
+      // The leader arms its barrier for both CTAs' bytes; the odd CTA arms none.
+      auto arm = [&](int st) {
+        if (!PAIR)
+          mbar_arrive_expect_tx(&full[st], kStageBytes);
+        else if (leader)
+          mbar_arrive_expect_tx(&full[st], 2 * kStageBytes);
+      };
+      // W boxes of a stage: both (one CTA per tile) or this CTA's (pairs).
+      auto load_w = [&](int st, int kb, int row0, int row1) {
+        if (!PAIR || leader) load(sB + st * kBBytes, &mp.w0, st, kb * kBK, row0, pol_w);
+        if (!PAIR || !leader) load(sB + st * kBBytes + (PAIR ? 0 : kBBytes / 2), &mp.w1, st, kb * kBK, row1, pol_w);
+      };
+      for (int t = unit0; t < total; t += n_units) {
         const WideTile wt = wide_tile(t, ws);
-        const int m = wt.m;
+        const int m = PAIR ? 2 * wt.m + rank : wt.m;  // this CTA's 128-token tile
         int row0, row1;
         wide_rows<EPI, BN>(wt.n, row0, row1);
         // First tile: weights do not depend on the previous kernel, so the first
@@ -487,15 +542,13 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
         if (!waited) {
           const int pre = min(STAGES, wt.kb1 - wt.kb0);
           for (int i = 0; i < pre; ++i) {
-            mbar_arrive_expect_tx(&full[i], kStageBytes);
-            tma_load_2d(sB + i * kBBytes, &mp.w0, &full[i], (wt.kb0 + i) * kBK, row0, pol_w);
-            tma_load_2d(sB + i * kBBytes + kBBytes / 2, &mp.w1, &full[i], (wt.kb0 + i) * kBK, row1, pol_w);
+            arm(i);
+            load_w(i, wt.kb0 + i, row0, row1);
           }
           pdl_wait();
           waited = true;
           if (p.trace != nullptr) s_stamp[0] = globaltimer_ns();
-          for (int i = 0; i < pre; ++i)
-            tma_load_2d(sA + i * kABytes, &mp.x, &full[i], (wt.kb0 + i) * kBK, m * kWBM, pol_x);
+          for (int i = 0; i < pre; ++i) load(sA + i * kABytes, &mp.x, i, (wt.kb0 + i) * kBK, m * kWBM, pol_x);
           kb = wt.kb0 + pre;
           it = pre;
         }
@@ -506,10 +559,9 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
             s_flag[0] = 1;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], kStageBytes);
-          tma_load_2d(sB + s * kBBytes, &mp.w0, &full[s], kb * kBK, row0, pol_w);
-          tma_load_2d(sB + s * kBBytes + kBBytes / 2, &mp.w1, &full[s], kb * kBK, row1, pol_w);
-          tma_load_2d(sA + s * kABytes, &mp.x, &full[s], kb * kBK, m * kWBM, pol_x);
+          arm(s);
+          load_w(s, kb, row0, row1);
+          load(sA + s * kABytes, &mp.x, s, kb * kBK, m * kWBM, pol_x);
         }
         if (s_flag[0] != 0) break;
       }
@@ -517,10 +569,12 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
       s_flag[2] = it;
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (PAIR && !leader) {
+      // Odd CTA of a pair: the leader issues every MMA.
+    } else if (lane == 0) {
       int it = 0, lt = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++lt) {
+      for (int t = unit0; t < total && ok; t += n_units, ++lt) {
         const int buf = lt & 1;
         if (!mbar_wait(&acce[buf], ((lt >> 1) & 1) ^ 1)) {
           report_status(p.status, PI05_DEV_TIMEOUT_MMA);
@@ -533,7 +587,8 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
         const WideTile wt = wide_tile(t, ws);
         for (int kb = wt.kb0; kb < wt.kb1; ++kb, ++it) {
           const int s = it % STAGES;
-          if (!mbar_wait(&full[s], (it / STAGES) & 1)) {
+          // Pairs: the odd CTA's copies complete the phase too.
+          if (!(PAIR ? mbar_wait_cluster(&full[s], (it / STAGES) & 1) : mbar_wait(&full[s], (it / STAGES) & 1))) {
             report_status(p.status, PI05_DEV_TIMEOUT_MMA);
             ok = false;
             break;
@@ -542,16 +597,31 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
           const uint32_t a0 = smem_u32(sA + s * kABytes);
           const uint32_t b0 = smem_u32(sB + s * kBBytes);
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)
-            umma_bf16(d, umma_sdesc_sw128(a0 + kk * 32), umma_sdesc_sw128(b0 + kk * 32), kIdesc,
-                      (kb > wt.kb0 || kk > 0) ? 1u : 0u);
-          umma_commit(&empty[s]);
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint32_t acc = (kb > wt.kb0 || kk > 0) ? 1u : 0u;
+            if (PAIR)
+              umma_bf16_pair(d, umma_sdesc_sw128(a0 + kk * 32), umma_sdesc_sw128(b0 + kk * 32), kIdesc, acc);
+            else
+              umma_bf16(d, umma_sdesc_sw128(a0 + kk * 32), umma_sdesc_sw128(b0 + kk * 32), kIdesc, acc);
+          }
+          if (PAIR)
+            umma_commit_pair(&empty[s], 0x3);
+          else
+            umma_commit(&empty[s]);
         }
-        if (ok) umma_commit(&accf[buf]);
+        if (ok) {
+          if (PAIR)
+            umma_commit_pair(&accf[buf], 0x3);
+          else
+            umma_commit(&accf[buf]);
+        }
       }
       if (!ok) s_flag[0] = 1;
       // Every MMA issued by this thread has completed once mdone fires.
-      umma_commit(mdone);
+      if (PAIR)
+        umma_commit_pair(mdone, 0x3);
+      else
+        umma_commit(mdone);
       if (!mbar_wait(mdone, 0)) report_status(p.status, PI05_DEV_TIMEOUT_DRAIN);
     }
   } else {
@@ -566,9 +636,9 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
     e.bar = sbar + (warp - 2) * 2;
     e.phase = 0;
     int lt = 0;
-    for (int t = blockIdx.x; t < total; t += gridDim.x, ++lt) {
+    for (int t = unit0; t < total; t += n_units, ++lt) {
       const WideTile wt = wide_tile(t, ws);
-      const int m = wt.m, n = wt.n;
+      const int m = PAIR ? 2 * wt.m + rank : wt.m, n = wt.n;  // this CTA's 128-token tile
       const int buf = lt & 1;
       wide_epi_prefetch<EPI, BN>(p, mp, e, n, m * kWBM);
       if ((EPI == SK_EPI_STORE || EPI == SK_EPI_GATED_RESID) && p.bias != nullptr) {
@@ -600,7 +670,7 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
           // Publish this split's partial (whole 128-byte lines per row), take a
           // ticket; the split taking the last ticket sums all partials in split
           // order and runs the epilogue.  No CTA waits for another.
-          const int tile_mn = n * ws.m_tiles + m;
+          const int tile_mn = n * cta_m_tiles + m;
           float* part = p.accum + (size_t)tile_mn * ws.splits * kWBM * BN;
           float* mine = part + ((size_t)wt.s * kWBM + sp.row) * BN;
 #pragma unroll 1
@@ -637,7 +707,18 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&acce[buf]);
+      if (PAIR) {
+        // One arrival per warp on the leader's barrier (remote for the odd CTA).
+        __syncwarp();
+        if (lane == 0) {
+          if (leader)
+            mbar_arrive(&acce[buf]);
+          else
+            mbar_arrive_cluster(mapa_shared(smem_u32(&acce[buf]), 0));
+        }
+      } else {
+        mbar_arrive(&acce[buf]);
+      }
       if (!ok) break;
     }
     // All of this warp's tensor stores complete (and stop reading shared memory)
@@ -650,7 +731,7 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
   // Teardown.  If the producer stopped early, wait (bounded) for the copies it
   // armed before shared memory is released.
   __syncthreads();
-  if (s_flag[0] != 0 && warp == 0 && lane == 0) {
+  if (s_flag[0] != 0 && warp == 0 && lane == 0 && (!PAIR || leader)) {
     const int armed = s_flag[2];
     for (int s = 0; s < STAGES && s < armed; ++s) {
       const int uses = (armed - s + STAGES - 1) / STAGES;  // armings of stage s
@@ -659,9 +740,19 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) {
+    // Neither CTA leaves (releasing shared memory the leader's MMAs read, or the
+    // barriers the other signals) before both are done; the leader's MMAs have
+    // all completed (mdone) before it arrives.
+    cluster_arrive_release();
+    cluster_wait();
+  }
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    if (PAIR)
+      tmem_dealloc_pair(tmem, kTmemCols);
+    else
+      tmem_dealloc(tmem, kTmemCols);
   }
   // Trace record {tag << 32 | cta, entry, setup done, first X TMA after the grid
   // dependency wait, MMA passed the first accumulator-free wait, first
@@ -693,11 +784,11 @@ int wide_sms() {
   return n;
 }
 
-template <int EPI, int BN, int STAGES, int EW>
+template <int EPI, int BN, int STAGES, int EW, bool PAIR = false>
 int wide_launch(const SkinnyParams& p, const WideSched& ws, const WideMaps& mp, cudaStream_t stream) {
-  constexpr int kSmem = wide_smem_bytes<EPI, BN, STAGES, EW>();
+  constexpr int kSmem = wide_smem_bytes<EPI, BN, STAGES, EW, PAIR>();
   static_assert(kSmem <= 232448, "shared memory per block");
-  auto kern = wide_gemm_kernel<EPI, BN, STAGES, EW>;
+  auto kern = wide_gemm_kernel<EPI, BN, STAGES, EW, PAIR>;
   static bool attr_done[16] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -710,6 +801,34 @@ int wide_launch(const SkinnyParams& p, const WideSched& ws, const WideMaps& mp, 
     attr_done[dev] = true;
   }
   const int total = ws.m_tiles * ws.n_tiles * ws.splits;
+  if (PAIR) {
+    // Persistent pairs: as many as can be resident at once (a GPC with an odd
+    // number of free SMs leaves one unpaired), or a late wave doubles the time.
+    static int max_pairs[16] = {0};
+    if (dev < 16 && max_pairs[dev] == 0) {
+      cudaLaunchConfig_t cfg;
+      std::memset(&cfg, 0, sizeof(cfg));
+      cfg.gridDim = dim3(2 * (wide_sms() / 2));
+      cfg.blockDim = dim3(wide_threads<EW>());
+      cfg.dynamicSmemBytes = kSmem;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = wide_sms() / 2;
+      }
+      max_pairs[dev] = n;
+    }
+    const int pairs = std::min(total, dev < 16 ? max_pairs[dev] : wide_sms() / 2);
+    return launch_pdl_cluster(kern, dim3(2 * pairs), dim3(wide_threads<EW>()), kSmem, stream, pdl_enabled(),
+                              dim3(2, 1, 1), mp, p, ws);
+  }
   const int grid = std::min(total, wide_sms());
   return launch_pdl(kern, dim3(grid), dim3(wide_threads<EW>()), kSmem, stream, pdl_enabled(), mp, p, ws);
 }
@@ -722,10 +841,34 @@ int env_int(const char* name) {
 
 }  // namespace
 
-int wide_choose(int epi, int m_tiles, int n_cols, int kb_total, int sms, int* bn, int* splits) {
+int wide_choose(int epi, int m_tiles, int n_cols, int kb_total, int sms, int* bn, int* splits, int* pair) {
   static const int force_bn = env_int("PI05_WIDE_BN");
   static const int force_splits = env_int("PI05_WIDE_SPLITS");
+  static const int force_pair = [] {
+    const char* e = getenv("PI05_WIDE_PAIR");
+    return e != nullptr ? atoi(e) : -1;
+  }();
   *splits = 1;
+  *pair = 0;
+  // CTA pairs pay a longer prologue and (with split-K) a slower epilogue; they win
+  // on the long-running projections: gate/up at full token tiles and long-K ones
+  // (the prefix down_proj).  PI05_WIDE_PAIR=0 / 1 disables / forces them.
+  const bool pair_auto = m_tiles >= 4 && ((epi == SK_EPI_GEGLU && kb_total >= 16) ||
+                                          ((epi == SK_EPI_STORE || epi == SK_EPI_GATED_RESID) && kb_total >= 128));
+  if (force_pair > 0 || (force_pair < 0 && pair_auto)) {
+    // CTA pairs: 256 x 256 tiles; split-K (STORE / GATED_RESID) until the pairs
+    // cover the SMs.
+    *bn = 256;
+    *pair = 1;
+    if (epi == SK_EPI_STORE || epi == SK_EPI_GATED_RESID) {
+      const long tiles = (long)((m_tiles + 1) / 2) * ((n_cols + 255) / 256);
+      if (force_splits >= 1 && force_splits <= 2)
+        *splits = force_splits;
+      else if (tiles * 2 <= sms / 2 && kb_total >= 16)
+        *splits = 2;
+    }
+    return 0;
+  }
   if (epi == SK_EPI_GEGLU || epi == SK_EPI_QKV_ROPE) {
     *bn = 256;
     return 0;
@@ -776,10 +919,13 @@ int wide_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int w
     return PI05_ERR_SHAPE;
   }
   WideSched ws;
-  ws.m_tiles = (p.m_tok + kWBM - 1) / kWBM;
+  const int cta_m_tiles = (p.m_tok + kWBM - 1) / kWBM;
   ws.kb_total = (p.k + kBK - 1) / kBK;
-  int bn = 256, splits = 1;
-  wide_choose(epi, ws.m_tiles, n_cols, ws.kb_total, wide_sms(), &bn, &splits);
+  int bn = 256, splits = 1, pair = 0;
+  wide_choose(epi, cta_m_tiles, n_cols, ws.kb_total, wide_sms(), &bn, &splits, &pair);
+  // Pairs schedule 256-token tiles; every CTA still owns 128 tokens of one.
+  ws.m_tiles = pair ? (cta_m_tiles + 1) / 2 : cta_m_tiles;
+  const int m_tiles_cta = pair ? 2 * ws.m_tiles : ws.m_tiles;
   if (epi == SK_EPI_GEGLU)
     ws.n_tiles = (n_cols + 127) / 128;
   else if (epi == SK_EPI_QKV_ROPE)
@@ -787,9 +933,9 @@ int wide_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int w
   else
     ws.n_tiles = (n_cols + bn - 1) / bn;
   if (splits > 1) {
-    const size_t need = (size_t)ws.m_tiles * ws.n_tiles * splits * kWBM * bn * sizeof(float);
+    const size_t need = (size_t)m_tiles_cta * ws.n_tiles * splits * kWBM * bn * sizeof(float);
     if (p.accum == nullptr || p.counters == nullptr || need > p.accum_bytes ||
-        (long)ws.m_tiles * ws.n_tiles > kWsMaxCounters || splits > ws.kb_total)
+        (long)m_tiles_cta * ws.n_tiles > kWsMaxCounters || splits > ws.kb_total)
       splits = 1;
   }
   ws.splits = splits;
@@ -819,6 +965,23 @@ int wide_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int w
   // Short mainloops (a tile of at most 40 k-blocks) leave the epilogue exposed: give
   // it 8 warps; long ones keep the deeper pipeline.
   const bool wide8 = (ws.kb_total + ws.splits - 1) / ws.splits <= 40;
+  if (pair) {
+    switch (epi) {
+      case SK_EPI_STORE:
+        return wide8 ? wide_launch<SK_EPI_STORE, 256, 5, 8, true>(p, ws, mp, st)
+                     : wide_launch<SK_EPI_STORE, 256, 6, 4, true>(p, ws, mp, st);
+      case SK_EPI_GATED_RESID:
+        return wide8 ? wide_launch<SK_EPI_GATED_RESID, 256, 5, 8, true>(p, ws, mp, st)
+                     : wide_launch<SK_EPI_GATED_RESID, 256, 6, 4, true>(p, ws, mp, st);
+      case SK_EPI_GEGLU:
+        return wide_launch<SK_EPI_GEGLU, 256, 6, 4, true>(p, ws, mp, st);
+      case SK_EPI_QKV_ROPE:
+        return wide_launch<SK_EPI_QKV_ROPE, 256, 5, 4, true>(p, ws, mp, st);
+      default:
+        set_last_error("wide_gemm: unknown epilogue %d", epi);
+        return PI05_ERR_INVALID_ARG;
+    }
+  }
   switch (epi) {
     case SK_EPI_STORE:
       if (wide8) return bn == 256 ? wide_launch<SK_EPI_STORE, 256, 3, 8>(p, ws, mp, st)
