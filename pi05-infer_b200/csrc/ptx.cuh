@@ -97,7 +97,7 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, ui
 
 // The same 2-D load for a CTA pair (cta_group::2): the tile lands in this CTA's
 // shared memory and its bytes complete on the barrier at shared::cluster address
-// `bar` (the even CTA's).  A plain load of this GPU's global memory: no multicast.
+// `bar` (the even CTA's).  One destination, this GPU's global memory as source.
 __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* tm, uint32_t bar, int x, int y,
                                                  uint64_t policy) {
   asm volatile(

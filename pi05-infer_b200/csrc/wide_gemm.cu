@@ -407,9 +407,9 @@ __device__ __forceinline__ bool wide_epi_qkv(const SkinnyParams& p, const WideMa
 // tcgen05.mma.cta_group::2 with M = 256, which reads both CTAs' shared memory and
 // accumulates into both CTAs' TMEM (CTA r: rows r*128 ..), so each SM streams
 // 32 KB of operands per k-block instead of 48 KB for the same FLOPs.  Both CTAs'
-// TMA loads (cta_group::2 form, no multicast) complete on the leader's full
+// TMA loads (cta_group::2 form, one destination each) complete on the leader's full
 // barrier, which the leader arms for both; the leader's commits arrive on both
-// CTAs' barriers (multicast commit); the epilogues are per CTA, the odd CTA's
+// CTAs' barriers (one commit with a two-CTA mask); the epilogues are per CTA, the odd CTA's
 // warps signalling "accumulator drained" to the leader remotely.
 template <int EPI, int BN, int STAGES, int EW, bool PAIR>
 __global__ void __launch_bounds__(wide_threads<EW>(), 1)
