@@ -594,9 +594,10 @@ int mma_sync_attention(AttnParams p, float* part, size_t part_bytes, int splits,
   }
   const bool auto_splits = splits <= 0;
   if (auto_splits) {
-    // Enough CTAs to cover the SMs, at least two chunks per split when possible.
+    // Up to two CTAs per SM (a CTA's 2 warps use half of the SM's sub-partitions;
+    // the key loop is bound by the mma.sync rate per sub-partition).
     splits = 1;
-    while (row_blocks * splits * 2 <= sms && splits * 2 <= n_chunks) splits *= 2;
+    while (row_blocks * splits * 2 <= 2 * sms && splits * 2 <= n_chunks) splits *= 2;
   }
   splits = splits > n_chunks ? n_chunks : splits;
   splits = splits > 32 ? 32 : splits;

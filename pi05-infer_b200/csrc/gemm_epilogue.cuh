@@ -416,32 +416,21 @@ __device__ __forceinline__ void cluster_epilogue(const SkinnyParams& p, uint32_t
 
 // ---------------------------------------------------------------------------
 // Split-K through distributed shared memory, push form.  Rank r of the cluster
-// owns tokens [r*mt/splits, (r+1)*mt/splits) of the tile.  After the first
-// cluster barrier (every CTA's mainloop is done, so its ring can receive), each
-// CTA sends the owner of every other token slice that slice of its staging tile
-// with one bulk copy (async proxy, SM-to-SM), completing transaction bytes on the
-// owner's barrier `rbar`.  The owner waits for its barrier and sums the partials
-// from its own shared memory in increasing rank order (0.f + p0 + p1 + ..., the
-// order of the pull form and of the global-memory split path), then applies the
-// epilogue.  The receive slots follow the staging tile in the (finished) ring:
-// slot s holds source s's partial of the owner's token slice, 512 bytes a token.
-// The exit barrier, arrived once a CTA has received everything, keeps every
-// source's staging tile alive until all copies out of it have landed.
+// owns tokens [r*mt/splits, (r+1)*mt/splits) of the tile.  As soon as its partial
+// is staged, each CTA sends the owner of every other token slice that slice of its
+// staging tile with one bulk copy (async proxy, SM-to-SM), completing transaction
+// bytes on the owner's barrier `rbar` (armed, and made visible to the cluster by a
+// cluster barrier, at kernel start).  The owner waits for its barrier and sums the
+// partials from its own shared memory in increasing rank order (0.f + p0 + p1 +
+// ..., the order of the pull form and of the global-memory split path), then
+// applies the epilogue.  The receive slots are a region of their own: slot s holds
+// source s's partial of the owner's token slice, 512 bytes a token.  The exit
+// barrier, arrived once a CTA has received everything, keeps every source's
+// staging tile alive until all copies out of it have landed.
 // Bytes this rank receives in the push form (its token slice from every other rank).
 __device__ __forceinline__ uint32_t push_recv_bytes(int splits, int mt, int rank) {
   const int t0 = (rank * mt) / splits, t1 = ((rank + 1) * mt) / splits;
   return (uint32_t)((splits - 1) * (t1 - t0) * kBM * 4);
-}
-
-// The epilogue threads' half of the first push barrier, called as soon as the
-// accumulator is ready (the ring is then free to receive): arm the receive
-// barrier, arrive on the cluster barrier.  The staging tile is written after this;
-// the writers fence it to the async proxy before the CTA barrier that precedes the
-// bulk copies.
-__device__ __forceinline__ void cluster_push_arrive(uint64_t* rbar, int splits, int mt, int rank, int et) {
-  if (et == 0) mbar_arrive_expect_tx(rbar, push_recv_bytes(splits, mt, rank));
-  __syncwarp();
-  cluster_arrive_release();
 }
 
 template <int EPI, int KIND, int U>
@@ -455,25 +444,13 @@ __device__ __forceinline__ void cluster_push_body(const SkinnyParams& p, const f
   const int u0 = UPT * t0, u1 = UPT * t1;
   const int slot = (t1 - t0) * kBM;  // floats per receive slot
   const bool stamp = stamps != nullptr && epi && et == 0;
-  UnitOps ops[U];
+  constexpr int kSU = H == 1 ? 4 : 2;  // splits whose loads are in flight together
+  UnitOps ops0;  // operands of this thread's first unit, loaded before the receive wait
   if (stamp) stamps[0] = globaltimer_ns();
-  // Epilogue threads arrived in cluster_push_arrive(); the others arrive here.
-  if (!epi) {
-    __syncwarp();
-    cluster_arrive_release();
-  }
-  if (epi) {
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int idx = u0 + u * kEpiThreads + et;
-      if (unit_valid<EPI, KIND>(p, tile, idx, u1)) unit_load_ops<EPI, KIND>(p, tile, tok0, idx, ops[u]);
-    }
-  }
-  __syncwarp();
-  cluster_wait();
-  if (stamp) stamps[1] = globaltimer_ns();
   bool ok = true;
   if (epi) {
+    // The receive slots are this CTA's own (not the ring), armed at kernel start:
+    // copy each owner its slice right away.
     if (et < splits && et != rank) {
       const int d0 = (et * mt) / splits, d1 = ((et + 1) * mt) / splits;
       const uint32_t bytes = (uint32_t)(d1 - d0) * kBM * 4u;
@@ -481,6 +458,8 @@ __device__ __forceinline__ void cluster_push_body(const SkinnyParams& p, const f
         bulk_copy_to_peer(mapa_shared(smem_u32(recv) + (uint32_t)rank * bytes, (uint32_t)et),
                           smem_u32(st) + (uint32_t)d0 * kBM * 4u, bytes, mapa_shared(smem_u32(rbar), (uint32_t)et));
     }
+    if (stamp) stamps[1] = globaltimer_ns();
+    if (unit_valid<EPI, KIND>(p, tile, u0 + et, u1)) unit_load_ops<EPI, KIND>(p, tile, tok0, u0 + et, ops0);
     ok = mbar_wait_cluster(rbar, 0);
     if (!ok) report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
   }
@@ -498,7 +477,11 @@ __device__ __forceinline__ void cluster_push_body(const SkinnyParams& p, const f
         const int idx = base + u * kEpiThreads;
         float ss = 0.f;
         if (unit_valid<EPI, KIND>(p, tile, idx, u1)) {
-          if (pass > 0) unit_load_ops<EPI, KIND>(p, tile, tok0, idx, ops[u]);
+          UnitOps o;
+          if (pass == 0 && u == 0)
+            o = ops0;
+          else
+            unit_load_ops<EPI, KIND>(p, tile, tok0, idx, o);
           int t, r;
           unit_pos<KIND>(idx, t, r);
           const float* own = st + t * kBM + r;
@@ -508,7 +491,8 @@ __device__ __forceinline__ void cluster_push_body(const SkinnyParams& p, const f
           for (int h = 0; h < 2; ++h)
 #pragma unroll
             for (int j = 0; j < 4; ++j) y[h][j] = 0.f;
-          for (int s = 0; s < splits; ++s) {
+#pragma unroll kSU
+          for (int s = 0; s < splits; ++s) {  // loads of kSU splits in flight, sums in split order
             const float* src = s == rank ? own : rcv + s * slot;
 #pragma unroll
             for (int h = 0; h < H; ++h) {
@@ -523,7 +507,7 @@ __device__ __forceinline__ void cluster_push_body(const SkinnyParams& p, const f
 #pragma unroll
             for (int j = 0; j < 4; ++j) y[1][j] = y[0][j];
           }
-          ss = unit_finish<EPI, KIND>(p, tile, tok0, idx, ops[u], y);
+          ss = unit_finish<EPI, KIND>(p, tile, tok0, idx, o, y);
         }
         unit_row_ssq<KIND>(p, tile, tok0, idx, u1, ss);
       }
@@ -551,10 +535,10 @@ __device__ __forceinline__ void cluster_push_kind(const SkinnyParams& p, const f
 }
 
 // Whole push-form cluster epilogue; every thread of the CTA calls it, the epilogue
-// threads after cluster_push_arrive() and after fencing the staging tile they
-// wrote (fence.proxy.async) followed by a barrier among themselves.  `recv` must
-// hold splits * ceil(mt / splits) * 512 bytes; `rbar` was initialised with one
-// arrival (fence.mbarrier_init) before the mainloop.
+// threads after fencing the staging tile they wrote (fence.proxy.async) followed by
+// a barrier among themselves.  `recv` must hold splits * ceil(mt / splits) * 512
+// bytes; `rbar` was initialised with one arrival, armed with push_recv_bytes() and
+// published by a cluster barrier before the mainloop.
 template <int EPI>
 __device__ __forceinline__ void cluster_push_epilogue(const SkinnyParams& p, const float* st, const float* recv,
                                                       uint64_t* rbar, int tile, int tok0, int mt, int rank, int et,

@@ -41,11 +41,29 @@ namespace {
 
 using namespace gemm;
 constexpr int kThreads = 192;     // warp0 TMA, warp1 MMA/TMEM, warps2-5 epilogue
-// Ring, barrier area (512 B), fused-norm area (rstd per token, scale and shift of
-// the CTA's K range).
+// Dedicated receive slots of the push-form split-K (64-token tile only): at most
+// (splits - 1) * ceil(tokens / splits) rows of 512 bytes; the launcher checks.
+template <int TOK>
+constexpr int recv_bytes() {
+  return TOK == 64 ? 32768 : 0;
+}
+
+// Fused-norm area: rstd per token, scale and shift of the CTA's K range.
+template <int TOK>
+constexpr int norm_bytes() {
+  return TOK * 4 + 2 * kNormMaxK * 4;
+}
+
+// Ring, barrier area (512 B), receive slots; the fused-norm area follows and is
+// only allocated for launches that normalise X.
+template <int TOK, int STAGES>
+constexpr int smem_base_bytes() {
+  return 1024 + STAGES * (kABytes + TOK * 128) + 512 + recv_bytes<TOK>();
+}
+
 template <int TOK, int STAGES>
 constexpr int smem_bytes() {
-  return 1024 + STAGES * (kABytes + TOK * 128) + 512 + TOK * 4 + 2 * kNormMaxK * 4;
+  return smem_base_bytes<TOK, STAGES>() + norm_bytes<TOK>();
 }
 
 // Small-token variants are limited to 170 registers so that two CTAs fit per SM:
@@ -76,13 +94,13 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
   int* s_flag = reinterpret_cast<int*>(s_tmem + 1);  // [0] abort, [1] ticket
   uint64_t* rbar = accum + 9;                         // push-form split-K: partial slices received
   uint64_t* xrdy = accum + 10;                        // [STAGES] fused norm: X stage normalised
-  float* s_rstd = reinterpret_cast<float*>(smem + STAGES * kStageBytes + 512);  // [TOK]
+  float* recv = reinterpret_cast<float*>(smem + STAGES * kStageBytes + 512);     // push-form receive slots
+  float* s_rstd = recv + recv_bytes<TOK>() / 4;                                   // [TOK]
   float* s_mod = s_rstd + TOK;                                                  // [2][kNormMaxK]
   const bool norm = p.norm_ssq != nullptr;
   float* stage_tile = reinterpret_cast<float*>(smem);
-  // Push-form receive slots follow the staging tile inside the finished ring.
-  constexpr bool kPushFits = TOK * kBM * 4 + (TOK + 16) * kBM * 4 <= STAGES * kStageBytes;
-  float* recv = stage_tile + TOK * kBM;
+  constexpr bool kPushFits = recv_bytes<TOK>() > 0;
+  const bool push = kPushFits && p.cluster && p.push;
 
   const uint64_t t_entry = (p.trace != nullptr) ? globaltimer_ns() : 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -104,6 +122,8 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
     s_flag[0] = 0;
     s_flag[1] = 0;
     fence_mbar_init();
+    // Push form: expect this rank's token slice from every other split.
+    if (push) mbar_arrive_expect_tx(rbar, push_recv_bytes(p.splits, mt, (int)cluster_ctarank()));
   }
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tm_w0);
@@ -116,6 +136,12 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
   }
   tc_fence_before();
   __syncthreads();
+  if (push) {
+    // Every receive barrier of the cluster is armed before any CTA can copy into
+    // it (a peer copies as soon as its own partial is staged).
+    cluster_arrive_release();
+    cluster_wait();
+  }
   tc_fence_after();
   const uint32_t tmem_acc = *s_tmem;
   const uint64_t t_start = (p.trace != nullptr) ? globaltimer_ns() : 0;
@@ -293,8 +319,6 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
     if (!ok) report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
     if (p.trace != nullptr) t_acc = globaltimer_ns();
     tc_fence_after();
-    const bool push = kPushFits && p.cluster && p.push;
-    if (push) cluster_push_arrive(rbar, p.splits, mt, (int)cluster_ctarank(), et);
     if (ok) {
 #pragma unroll 1
       for (int c = 0; c < TOK / 32; ++c) {
@@ -367,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
   unsigned long long* cl_stamps = reinterpret_cast<unsigned long long*>(accum + 4);  // [5]
   if (p.cluster) {
     __syncwarp();
-    if (kPushFits && p.push)
+    if (push)
       cluster_push_epilogue<EPI>(p, stage_tile, recv, rbar, tile, tok0, mt, (int)cluster_ctarank(),
                                  (int)threadIdx.x - 64, warp >= 2, p.trace != nullptr ? cl_stamps : nullptr);
     else
@@ -440,13 +464,15 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
 template <int EPI, int TOK, int STAGES>
 int launch_one(const SkinnyParams& p, const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x,
                int tok_tiles, cudaStream_t stream) {
-  constexpr int kSmem = smem_bytes<TOK, STAGES>();
+  constexpr int kSmemMax = smem_bytes<TOK, STAGES>();
+  // Without the fused norm its area is left out, so two CTAs fit per SM.
+  const int kSmem = p.norm_ssq != nullptr ? kSmemMax : smem_base_bytes<TOK, STAGES>();
   auto kern = skinny_gemm_kernel<EPI, TOK, STAGES>;
   static bool attr_done[16] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 16 && !attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
     if (e != cudaSuccess) {
       set_last_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e));
       return PI05_ERR_LAUNCH;
@@ -484,13 +510,13 @@ int launch_one(const SkinnyParams& p, const CUtensorMap& w0, const CUtensorMap& 
 // (queried once per device: clusters of `s` CTAs with this kernel's resources).
 template <int EPI, int TOK, int STAGES>
 int max_cluster_size() {
-  constexpr int kSmem = smem_bytes<TOK, STAGES>();
+  constexpr int kSmem = smem_base_bytes<TOK, STAGES>();
   static int cached[16] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 16 && cached[dev]) return cached[dev];
   auto kern = skinny_gemm_kernel<EPI, TOK, STAGES>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes<TOK, STAGES>());
   cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   int best = 1;
   for (int s = 2; s <= 16; ++s) {
@@ -625,7 +651,7 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
     switch (epi) {
 #define PI05_SK_MAXCL(E)                                                      \
   case E:                                                                     \
-    max_cl = tok == 64    ? max_cluster_size<E, 64, 4>()                      \
+    max_cl = tok == 64    ? max_cluster_size<E, 64, 3>()                      \
              : tok == 128 ? max_cluster_size<E, 128, S>()                     \
                           : max_cluster_size<E, 256, 3>();                    \
     break;
@@ -643,7 +669,9 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
     p.splits = std::min(splits_override, p.kb_total);
     p.cluster = (use_cluster && p.splits > 1 && p.splits <= max_cl) ? 1 : 0;
   } else if (use_cluster) {
-    p.splits = skinny_choose_splits_cluster(p.n_tiles, p.kb_total, tok_tiles, num_sms(), max_cl);
+    // Small-token CTAs other than QKV+RoPE fit two per SM.
+    const int slots = num_sms() * ((tok <= 128 && epi != SK_EPI_QKV_ROPE) ? 2 : 1);
+    p.splits = skinny_choose_splits_cluster(p.n_tiles, p.kb_total, tok_tiles, slots, max_cl);
     p.cluster = p.splits > 1 ? 1 : 0;
   } else {
     p.splits = skinny_choose_splits(p.n_tiles, p.kb_total, tok_tiles, num_sms());
@@ -666,7 +694,11 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
     p.pf1 = nullptr;
   }
   // Push-form split-K for the small-token tile (splits <= 16 fit its receive slots).
-  p.push = (p.cluster && tok == 64 && p.splits <= 16 && push_enabled()) ? 1 : 0;
+  {
+    const int mt = std::min(p.m_tok, tok);
+    const long need = (long)(p.splits - 1) * ((mt + p.splits - 1) / p.splits) * kBM * 4;
+    p.push = (p.cluster && tok == 64 && p.splits <= 16 && need <= 32768 && push_enabled()) ? 1 : 0;
+  }
   CUtensorMap tw0, tw1, tx;
   int rc = make_tmap_bf16_2d(&tw0, w0, w_rows0, p.k, p.k, 64, 64, true);
   if (rc) return rc;
@@ -678,7 +710,7 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
   switch (epi) {
 #define PI05_SK_CASE(E)                                                                 \
   case E:                                                                               \
-    if (tok == 64) return launch_one<E, 64, 4>(p, tw0, tw1, tx, tok_tiles, st);         \
+    if (tok == 64) return launch_one<E, 64, 3>(p, tw0, tw1, tx, tok_tiles, st);         \
     if (tok == 128) return launch_one<E, 128, S>(p, tw0, tw1, tx, tok_tiles, st);       \
     return launch_one<E, 256, 3>(p, tw0, tw1, tx, tok_tiles, st);
     PI05_SK_CASE(SK_EPI_STORE)
