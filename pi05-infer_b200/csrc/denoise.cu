@@ -37,11 +37,11 @@ const int* debug_split_overrides() {
   return v;
 }
 
-// PI05_FUSED_NORM=1 in the environment folds the adaRMS norms after layer 0 into
-// the neighbouring GEMMs (row statistics from o_proj / down_proj, X normalised in
-// shared memory by gate/up and q|k|v).  Off by default: on B200 the in-place
-// normalisation of the X stages costs the consumer GEMMs more than the norm
-// kernels it removes.
+// PI05_FUSED_NORM=1 in the environment folds input_layernorm (after layer 0) into
+// the q|k|v GEMM: down_proj writes row statistics, q|k|v normalises h while
+// staging its X operand.  Off by default: on B200 the staging (L2 loads of h and
+// the statistics, then the normalisation, before the first MMA) costs q|k|v about
+// as much as the norm kernel it removes.
 bool fused_norm_enabled() {
   static int v = [] {
     const char* e = getenv("PI05_FUSED_NORM");
@@ -181,15 +181,14 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
   auto* act = static_cast<__nv_bfloat16*>(P->act);
   const int kv_len = P->prefix_len + T;
   const float scale = 1.0f / std::sqrt((float)D);
-  // Fused norms: o_proj / down_proj write per-(128-column tile, token) sums of
-  // squares of the new residual stream next to it; the following gate/up and
-  // q|k|v GEMMs normalise their X tiles in shared memory from those sums, so the
-  // adaRMS norms after layer 0's first one need no kernel of their own.
+  // Fused input_layernorm: down_proj writes per-(128-column tile, token) sums of
+  // squares of the new residual stream next to it, and the next layer's q|k|v GEMM
+  // normalises h from those sums while staging its X operand, so that norm needs
+  // no kernel of its own after layer 0.
   const int n_parts = W / 128;
-  const bool fuse = fused_norm_enabled() && W <= kNormMaxK &&
-                    (size_t)2 * n_parts * T * sizeof(float) <= kWsStatsBytes;
-  float* ssq_attn = ws.stats;                        // input of input_layernorm (from down_proj)
-  float* ssq_mlp = ws.stats + (size_t)n_parts * T;   // input of post_attention_layernorm (from o_proj)
+  const bool fuse = fused_norm_enabled() && W <= kNormMaxK && T <= 64 && n_parts <= kNormMaxParts &&
+                    (size_t)n_parts * T * sizeof(float) <= kWsStatsBytes;
+  float* ssq_attn = ws.stats;  // input of input_layernorm (from down_proj)
 
   int rc = action_in_run(P->x_t, P->w_in, P->b_in, h, T, P->action_dim, W, stream);
   for (int l = 0; l < P->depth && rc == PI05_OK; ++l) {
@@ -279,21 +278,15 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.resid = h;
       sp.ldr = W;
       sp.gate = mod1 + 2 * W;
-      if (fuse) {
-        sp.row_ssq = ssq_mlp;
-        sp.ssq_ld = T;
-      }
       sp.pf0 = N.w_o;
       sp.pf0_bytes = (size_t)W * HQ * D * 2;
       sp.trace_tag = (step * P->depth + l) * 8 + 1;
       rc = skinny_gemm_run(SK_EPI_GATED_RESID, sp, L.w_o, L.w_o, W, W, attn, HQ * D, so[1], stream);
       if (rc) break;
     }
-    // post_attention_layernorm (adaRMS): fused into gate/up
-    if (!fuse) {
-      rc = rms_norm_run(h, W, mod2, nullptr, xn, W, T, W, P->eps, stream);
-      if (rc) break;
-    }
+    // post_attention_layernorm (adaRMS)
+    rc = rms_norm_run(h, W, mod2, nullptr, xn, W, T, W, P->eps, stream);
+    if (rc) break;
     // gate/up + GeGLU
     {
       SkinnyParams sp;
@@ -312,15 +305,7 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.pf1 = N.w_up;
       sp.pf1_bytes = (size_t)F * W * 2;
       sp.trace_tag = (step * P->depth + l) * 8 + 2;
-      if (fuse) {
-        sp.norm_ssq = ssq_mlp;
-        sp.norm_parts = n_parts;
-        sp.norm_ld = T;
-        sp.norm_mod = mod2;
-        sp.norm_d = W;
-        sp.norm_eps = P->eps;
-      }
-      rc = skinny_gemm_run(SK_EPI_GEGLU, sp, L.w_gate, L.w_up, F, F, fuse ? h : xn, W, so[2], stream);
+      rc = skinny_gemm_run(SK_EPI_GEGLU, sp, L.w_gate, L.w_up, F, F, xn, W, so[2], stream);
       if (rc) break;
     }
     // down + gated residual (gate = third chunk of mod2)

@@ -48,10 +48,11 @@ constexpr int recv_bytes() {
   return TOK == 64 ? 32768 : 0;
 }
 
-// Fused-norm area: rstd per token, scale and shift of the CTA's K range.
-template <int TOK>
+// Fused-norm area: rstd per token, scale and shift of the CTA's K range (at most
+// STAGES k-blocks).
+template <int TOK, int STAGES>
 constexpr int norm_bytes() {
-  return TOK * 4 + 2 * kNormMaxK * 4;
+  return TOK * 4 + 2 * STAGES * 64 * 4;
 }
 
 // Ring, barrier area (512 B), receive slots; the fused-norm area follows and is
@@ -63,7 +64,7 @@ constexpr int smem_base_bytes() {
 
 template <int TOK, int STAGES>
 constexpr int smem_bytes() {
-  return smem_base_bytes<TOK, STAGES>() + norm_bytes<TOK>();
+  return smem_base_bytes<TOK, STAGES>() + norm_bytes<TOK, STAGES>();
 }
 
 // Small-token variants are limited to 170 registers so that two CTAs fit per SM:
@@ -96,8 +97,10 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
   uint64_t* xrdy = accum + 10;                        // [STAGES] fused norm: X stage normalised
   float* recv = reinterpret_cast<float*>(smem + STAGES * kStageBytes + 512);     // push-form receive slots
   float* s_rstd = recv + recv_bytes<TOK>() / 4;                                   // [TOK]
-  float* s_mod = s_rstd + TOK;                                                  // [2][kNormMaxK]
-  const bool norm = p.norm_ssq != nullptr;
+  float* s_mod = s_rstd + TOK;                                                    // [2][STAGES * 64]
+  // Fused norm of X (q|k|v only; its K range is at most STAGES k-blocks).
+  constexpr bool kNormCapable = EPI == SK_EPI_QKV_ROPE && TOK == 64;
+  const bool norm = kNormCapable && p.norm_ssq != nullptr;
   float* stage_tile = reinterpret_cast<float*>(smem);
   constexpr bool kPushFits = recv_bytes<TOK>() > 0;
   const bool push = kPushFits && p.cluster && p.push;
@@ -158,15 +161,17 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
       const int pre = min(STAGES, nk);
       // Weights do not depend on the previous kernel: issue them before the grid-dependency wait.
       if (p.trace != nullptr) s_stamp[0] = globaltimer_ns();
+      // With the fused norm the epilogue warps fill the X slots; stages carry W only.
+      const uint32_t stage_tx = norm ? kABytes : kStageBytes;
       for (int i = 0; i < pre; ++i) {
-        mbar_arrive_expect_tx(&full[i], kStageBytes);
+        mbar_arrive_expect_tx(&full[i], stage_tx);
         const int kx = (kb0 + i) * kBK;
         tma_load_2d(sA + i * kABytes, &tm_w0, &full[i], kx, tr.row0, pol_w);
         tma_load_2d(sA + i * kABytes + kABytes / 2, &tm_w1, &full[i], kx, tr.row1, pol_w);
       }
       pdl_wait();
-      for (int i = 0; i < pre; ++i)
-        tma_load_2d(sB + i * kBBytes, &tm_x, &full[i], (kb0 + i) * kBK, tok0, pol_x);
+      if (!norm)
+        for (int i = 0; i < pre; ++i) tma_load_2d(sB + i * kBBytes, &tm_x, &full[i], (kb0 + i) * kBK, tok0, pol_x);
       for (int i = pre; i < nk; ++i) {
         const int s = i % STAGES;
         if (!mbar_wait(&empty[s], ((i / STAGES) & 1) ^ 1)) {
@@ -185,11 +190,15 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
     pdl_wait();
     if (lane == 0) {
       bool ok = true;
-      for (int i = 0; i < nk; ++i) {
+      // Fused norm: the epilogue warps write the whole X operand once.
+      if (norm && !mbar_wait(&xrdy[0], 0)) {
+        report_status(p.status, PI05_DEV_TIMEOUT_MMA);
+        s_flag[0] = 1;
+        ok = false;
+      }
+      for (int i = 0; i < nk && ok; ++i) {
         const int s = i % STAGES;
-        // With the fused norm the stage is ready once the epilogue warps have
-        // normalised its X tile.
-        if (!mbar_wait(norm ? &xrdy[s] : &full[s], (i / STAGES) & 1)) {
+        if (!mbar_wait(&full[s], (i / STAGES) & 1)) {
           report_status(p.status, PI05_DEV_TIMEOUT_MMA);
           s_flag[0] = 1;
           ok = false;
@@ -229,90 +238,84 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
     const int row = q * 32 + lane;
     const int et = threadIdx.x - 64;
     if (p.trace != nullptr) t_pdl = globaltimer_ns();
-    if (norm) {
-      // Fused (ada)RMS norm of X: per-token rstd from the producer's partial sums of
-      // squares, scale / shift of this CTA's K range, then every X stage is
-      // normalised in place (128B-swizzled rows of 64 bf16) before the MMA reads it.
-      // Every load is issued before the first is consumed (one L2 round trip).
-      const int d = p.norm_d;
-      constexpr int kTPT = (TOK + kEpiThreads - 1) / kEpiThreads;  // tokens per thread
-      float ssv[kTPT][kNormMaxParts];
+    if constexpr (kNormCapable) {
+      if (norm) {
+        // Fused (ada)RMS norm of X.  The CTA's K range holds at most STAGES
+        // k-blocks, so its whole X operand fits the ring's X slots: every X
+        // k-block is loaded straight from the residual stream h (L2), normalised in
+        // registers, x = bf16(h * rstd * (1 + scale) + shift), and written once in
+        // the 128B-swizzled operand layout; the producer streams only weights.  rstd
+        // comes from the producer's per-tile partial sums of squares (in order).
+        const int d = p.norm_d;
+        const int kbase = kb0 * kBK;
+        const int klen = min(nk * kBK, p.k - kbase);  // multiple of 8
+        // rstd of token et (threads < TOK), published through shared memory.
+        if (et < TOK) {
+          float ssv[kNormMaxParts];
 #pragma unroll
-      for (int a = 0; a < kTPT; ++a) {
-        const int t = et + a * kEpiThreads;
-#pragma unroll
-        for (int j = 0; j < kNormMaxParts; ++j)
-          ssv[a][j] = (t < mt && j < p.norm_parts) ? p.norm_ssq[(size_t)j * p.norm_ld + tok0 + t] : 0.f;
-      }
-      const int kbase = kb0 * kBK;
-      const int klen = min(nk * kBK, p.k - kbase);  // multiple of 8
-      constexpr int kMPT = kNormMaxK / 4 / kEpiThreads;  // float4 chunks per thread and table
-      float4 msc[kMPT], msh[kMPT];
-      const float4* msrc = reinterpret_cast<const float4*>(p.norm_mod + kbase);
-      const float4* hsrc = reinterpret_cast<const float4*>(p.norm_mod + d + kbase);
-#pragma unroll
-      for (int a = 0; a < kMPT; ++a) {
-        const int c = et + a * kEpiThreads;
-        if (4 * c < klen) {
-          msc[a] = msrc[c];
-          msh[a] = hsrc[c];
-        }
-      }
-#pragma unroll
-      for (int a = 0; a < kTPT; ++a) {
-        const int t = et + a * kEpiThreads;
-        if (t < TOK) {
+          for (int j = 0; j < kNormMaxParts; ++j)
+            ssv[j] = (et < mt && j < p.norm_parts) ? p.norm_ssq[(size_t)j * p.norm_ld + tok0 + et] : 0.f;
           float ss = 0.f;
 #pragma unroll
-          for (int j = 0; j < kNormMaxParts; ++j) ss += ssv[a][j];  // parts in order (zeros past the end)
-          s_rstd[t] = t < mt ? rsqrtf(ss / (float)d + p.norm_eps) : 0.f;
+          for (int j = 0; j < kNormMaxParts; ++j) ss += ssv[j];  // parts in order (zeros past the end)
+          s_rstd[et] = et < mt ? rsqrtf(ss / (float)d + p.norm_eps) : 0.f;
         }
-      }
+        // Scale / shift of the CTA's K range into shared memory (float4 chunks).
+        for (int c = et; 4 * c < klen; c += kEpiThreads) {
+          reinterpret_cast<float4*>(s_mod)[c] = reinterpret_cast<const float4*>(p.norm_mod + kbase)[c];
+          reinterpret_cast<float4*>(s_mod + STAGES * kBK)[c] = reinterpret_cast<const float4*>(p.norm_mod + d + kbase)[c];
+        }
+        // This thread's chunk g (8 k values) of rows t = et/8 + 16 r, all k-blocks:
+        // every load issued before the first is used.
+        constexpr int kRPT = TOK / 16;
+        const int g = et & 7, t0r = et >> 3;
+        uint4 hx[STAGES][kRPT];
 #pragma unroll
-      for (int a = 0; a < kMPT; ++a) {
-        const int c = et + a * kEpiThreads;
-        if (4 * c < klen) {
-          reinterpret_cast<float4*>(s_mod)[c] = msc[a];
-          reinterpret_cast<float4*>(s_mod + kNormMaxK)[c] = msh[a];
-        }
-      }
-      named_bar_sync(1, kEpiThreads);
-      if (p.trace != nullptr) t_nload = globaltimer_ns();
-      const int g = et & 7;  // this thread's 16-byte chunk (8 k values) of every row
-      for (int i = 0; i < nk; ++i) {
-        const int s = i % STAGES;
-        if (!mbar_wait(&full[s], (i / STAGES) & 1)) {
-          report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
-          break;
-        }
-        const int kc = i * kBK + g * 8;
-        float sc[8], sh[8];
+        for (int i = 0; i < STAGES; ++i) {
+          const int kc = i * kBK + g * 8;  // within the CTA's K range
+          const bool kin = i < nk && kc < klen;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const bool in = kc + j < klen;
-          sc[j] = in ? s_mod[kc + j] : 0.f;
-          sh[j] = in ? s_mod[kNormMaxK + kc + j] : 0.f;
-        }
-        uint8_t* xs = sB + s * kBBytes;
-        for (int t = et >> 3; t < TOK; t += kEpiThreads / 8) {
-          uint4* ptr = reinterpret_cast<uint4*>(xs + t * 128 + ((g ^ (t & 7)) << 4));
-          float x[8], o[8];
-          unpack8(*ptr, x);
-          const float rs = s_rstd[t];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float nv = x[j] * rs;
-            o[j] = (t < mt && kc + j < klen) ? nv * (1.0f + sc[j]) + sh[j] : 0.f;
+          for (int r = 0; r < kRPT; ++r) {
+            const int t = t0r + 16 * r;
+            hx[i][r] = (kin && t < mt)
+                           ? *reinterpret_cast<const uint4*>(p.norm_x + (size_t)(tok0 + t) * p.norm_ldx + kbase + kc)
+                           : make_uint4(0u, 0u, 0u, 0u);
           }
-          *ptr = pack8(o);
+        }
+        named_bar_sync(1, kEpiThreads);  // s_rstd, s_mod
+        if (p.trace != nullptr) t_nload = globaltimer_ns();
+#pragma unroll
+        for (int i = 0; i < STAGES; ++i) {
+          if (i >= nk) break;
+          const int kc = i * kBK + g * 8;
+          const bool kin = kc < klen;
+          float scv[8], shv[8];
+          if (kin) {
+            load8f(s_mod + kc, scv);
+            load8f(s_mod + STAGES * kBK + kc, shv);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) scv[j] = shv[j] = 0.f;
+          }
+          uint8_t* xs = sB + i * kBBytes;
+#pragma unroll
+          for (int r = 0; r < kRPT; ++r) {
+            const int t = t0r + 16 * r;
+            float x[8], o[8];
+            unpack8(hx[i][r], x);
+            const float rs = s_rstd[t];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float nv = x[j] * rs;
+              o[j] = t < mt ? nv * (1.0f + scv[j]) + shv[j] : 0.f;  // zero-padded k gives 0 * ... + 0
+            }
+            *reinterpret_cast<uint4*>(xs + t * 128 + ((g ^ (t & 7)) << 4)) = pack8(o);
+          }
         }
         fence_proxy_async_smem();  // generic-proxy writes -> the MMA's async-proxy reads
         __syncwarp();
-        if (lane == 0) mbar_arrive(&xrdy[s]);
-        if (p.trace != nullptr) {
-          if (i == 0) t_nx0 = globaltimer_ns();
-          t_nxl = globaltimer_ns();
-        }
+        if (lane == 0) mbar_arrive(&xrdy[0]);
+        if (p.trace != nullptr) t_nx0 = t_nxl = globaltimer_ns();
       }
     }
     const bool ok = mbar_wait(accum, 0);
@@ -624,11 +627,16 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
     return PI05_ERR_SHAPE;
   }
   if (p.norm_ssq != nullptr &&
-      (p.norm_d != p.k || p.k > kNormMaxK || p.norm_parts <= 0 || p.norm_parts > kNormMaxParts ||
-       p.norm_mod == nullptr || !aligned16(p.norm_mod) || p.norm_d % 4 != 0)) {
-    set_last_error("skinny_gemm: fused norm needs norm_d == k <= %d, 1..%d parts, 16-byte aligned mod", kNormMaxK,
-                   kNormMaxParts);
+      (epi != SK_EPI_QKV_ROPE || p.norm_d != p.k || p.k > kNormMaxK || p.norm_parts <= 0 ||
+       p.norm_parts > kNormMaxParts || p.norm_mod == nullptr || !aligned16(p.norm_mod) || p.norm_d % 8 != 0 ||
+       !aligned16(x) || ldx % 8 != 0 || p.m_tok > 64)) {
+    set_last_error("skinny_gemm: fused norm needs q|k|v, <= 64 tokens, norm_d == k <= %d, 1..%d parts, aligned "
+                   "operands", kNormMaxK, kNormMaxParts);
     return PI05_ERR_SHAPE;
+  }
+  if (p.norm_ssq != nullptr) {
+    p.norm_x = static_cast<const __nv_bfloat16*>(x);
+    p.norm_ldx = ldx;
   }
   const bool fused_rows = p.norm_ssq != nullptr || p.row_ssq != nullptr;  // small-token kernel only
   if (p.m_tok >= kWideMinTokens && !wide_disabled() && !fused_rows) {
@@ -676,6 +684,22 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
   } else {
     p.splits = skinny_choose_splits(p.n_tiles, p.kb_total, tok_tiles, num_sms());
     p.cluster = 0;
+  }
+  if (p.norm_ssq != nullptr) {
+    // The whole X operand of a CTA must fit the ring's three X slots.
+    const int need = (p.kb_total + 2) / 3;
+    if (p.splits < need) {
+      if (need > 1 && use_cluster && need <= max_cl) {
+        p.splits = need;
+        p.cluster = 1;
+      } else if (need > 1 && (long)tok_tiles * p.n_tiles * need <= num_sms()) {
+        p.splits = need;
+        p.cluster = 0;
+      } else {
+        set_last_error("skinny_gemm: fused norm needs %d splits", need);
+        return PI05_ERR_SHAPE;
+      }
+    }
   }
   if (p.splits > 1 && !p.cluster) {
     const size_t need = (size_t)tok_tiles * p.n_tiles * p.splits * tok * kBM * sizeof(float);

@@ -49,12 +49,14 @@ struct SkinnyParams {
   // written to row_ssq[tile * ssq_ld + token] (fixed summation order).
   float* row_ssq = nullptr;
   int ssq_ld = 0;
-  // Fused (ada)RMS norm of the X operand: when norm_ssq is set, X holds the raw
-  // residual stream h and each X tile is normalised in shared memory before the
-  // MMA: x = bf16(h * rstd[t] * (1 + norm_mod[k]) + norm_mod[norm_d + k]), with
+  // Fused (ada)RMS norm of the X operand (QKV_ROPE, <= 64 tokens): when norm_ssq is
+  // set, X holds the raw residual stream h, which the kernel normalises while
+  // staging it: x = bf16(h * rstd[t] * (1 + norm_mod[k]) + norm_mod[norm_d + k]),
   // rstd[t] = rsqrt(sum_j norm_ssq[j * norm_ld + t] / norm_d + norm_eps) over
   // norm_parts partial sums in order.  Needs k <= kNormMaxK.
   const float* norm_ssq = nullptr;
+  const __nv_bfloat16* norm_x = nullptr;  // set by the launcher: X (= h) and its row stride
+  int norm_ldx = 0;
   int norm_parts = 0;
   int norm_ld = 0;
   const float* norm_mod = nullptr;

@@ -1,0 +1,78 @@
+"""GPU parity of the optional execution paths against the default one.
+
+The switches are environment variables read once per process, so each variant runs
+the 10-step denoise loop (config 2 shapes: Gemma-300M expert, 968-token prefix,
+seeded synthetic weights / KV / noise) in a child process; the test compares the
+final actions with the default path's under the denoise tolerance (max-abs <= 2e-2,
+cosine >= 0.9999):
+
+  PI05_FUSED_NORM=1   input_layernorm folded into the q|k|v GEMM (row statistics
+                      from down_proj, h normalised while staging X)
+  PI05_ATTN_MERGE=1   split-KV attention partials merged inside a thread-block
+                      cluster instead of global partials and a combine kernel
+  PI05_PUSH=0         pull form of the cluster split-K (DSMEM loads)
+  PI05_CLUSTER=0      global-memory split-K with a counter barrier
+"""
+
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+from conftest import PKG_ROOT
+
+pytestmark = pytest.mark.gpu
+
+_SCRIPT = r"""
+import sys
+import torch
+sys.path.insert(0, sys.argv[1])
+from pi05_infer import ops, synthetic
+from pi05_infer.config import GEMMA_300M
+from pi05_infer.expert import DenoiseRunner, ExpertWeights
+
+sd = synthetic.make_expert_weights(0)
+kv = synthetic.make_prefix_kv(1, 18, 968)
+kv = [(k[0, 0].bfloat16().cuda(), v[0, 0].bfloat16().cuda()) for k, v in kv]
+noise = synthetic.make_noise(2)[0]
+pad = torch.ones(968, dtype=torch.bool)
+pad[-37:] = False
+w = ExpertWeights(sd, GEMMA_300M, "cuda")
+r = DenoiseRunner(w, prefix_len=968, num_steps=10)
+r.set_prefix(kv, pad.cuda())
+out = r.run(noise.cuda(), use_graph=True).float().cpu()
+assert ops.read_device_status() == 0
+torch.save(out, sys.argv[2])
+"""
+
+
+def _run(env_extra, path):
+    env = dict(os.environ)
+    for k in ("PI05_FUSED_NORM", "PI05_ATTN_MERGE", "PI05_PUSH", "PI05_CLUSTER"):
+        env.pop(k, None)
+    env.update(env_extra)
+    subprocess.run([sys.executable, "-c", _SCRIPT, PKG_ROOT, path], env=env, check=True, timeout=600)
+    return torch.load(path)
+
+
+@pytest.fixture(scope="module")
+def default_actions(tmp_path_factory):
+    return _run({}, str(tmp_path_factory.mktemp("sw") / "default.pt"))
+
+
+@pytest.mark.parametrize(
+    "switch",
+    [{"PI05_FUSED_NORM": "1"}, {"PI05_ATTN_MERGE": "1"}, {"PI05_PUSH": "0"}, {"PI05_CLUSTER": "0"}],
+    ids=["fused_norm", "attn_merge", "pull_split_k", "global_split_k"],
+)
+def test_switch_matches_default(default_actions, switch, tmp_path):
+    got = _run(switch, str(tmp_path / "variant.pt"))
+    ref = default_actions
+    assert got.shape == ref.shape
+    err = (got - ref).abs().max().item()
+    cos = float((got.flatten().double() @ ref.flatten().double()) /
+                (got.flatten().double().norm() * ref.flatten().double().norm()))
+    assert err <= 2e-2, f"max-abs {err}"
+    assert cos >= 0.9999, f"cosine {cos}"
