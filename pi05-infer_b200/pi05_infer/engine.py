@@ -181,9 +181,19 @@ class OpenPi0Inference:
         base = len(names) * npatch
         embed_tokens(self.embed_table, self._ids, prefix.h[base: base + self.prompt_len],
                      math.sqrt(self.embed_table.shape[1]), ops.workspace(self.device), abi.stream_of(self.device))
-        valid = torch.cat([obs.image_masks[n].to(self.device).reshape(-1, 1).expand(-1, npatch).reshape(-1)
-                           for n in names] + [obs.tokenized_prompt_mask.reshape(-1).to(self.device)])
-        return valid
+        return self._prefix_valid(obs)
+
+    def _prefix_valid(self, obs: Observation) -> torch.Tensor:
+        """Key-validity of the prefix: every patch of a present view, then the prompt mask."""
+        npatch = self.config.siglip.num_patches
+        return torch.cat([obs.image_masks[n].to(self.device).reshape(-1, 1).expand(-1, npatch).reshape(-1)
+                          for n in obs.images] + [obs.tokenized_prompt_mask.reshape(-1).to(self.device)])
+
+    def _set_key_valid(self, valid: torch.Tensor) -> None:
+        prefix, den = self._runners()
+        prefix.key_valid.copy_(valid.to(torch.uint8))
+        den.key_valid[: self.prefix_len].copy_(valid.to(torch.uint8))
+        den.key_valid[self.prefix_len:].fill_(1)
 
     # ------------------------------------------------------------ public API
     @torch.no_grad()
@@ -193,12 +203,27 @@ class OpenPi0Inference:
         if noise is None:
             noise = torch.randn((1, self.config.action_horizon, self.config.action_dim), dtype=torch.float32,
                                 device=self.device)
-        valid = self._embed_prefix(observation)
-        prefix.key_valid.copy_(valid.to(torch.uint8))
-        prefix.enqueue(abi.stream_of(self.device))
-        den.key_valid[: self.prefix_len].copy_(valid.to(torch.uint8))
-        den.key_valid[self.prefix_len:].fill_(1)
-        actions = den.run(noise.to(self.device, non_blocking=True).float(), use_graph=self.use_cuda_graph)
+        if self.use_cuda_graph and self.vision is not None and self.embed_table is not None:
+            # The whole pipeline (SigLIP, embeddings, prefix LM, Euler loop) replays as
+            # one CUDA graph captured on the first call; each call only refreshes its
+            # static inputs (images, prompt ids, key masks, noise).
+            key = (tuple(observation.images.keys()), tuple(observation.images[n].shape for n in observation.images))
+            if self._graphs.get("full") is None or getattr(self, "_full_key", None) != key:
+                self._set_key_valid(self._prefix_valid(observation))
+                self.capture_full(observation, noise.to(self.device).float())
+                self._full_key = key
+            self._set_key_valid(self._prefix_valid(observation))
+            for i, n in enumerate(observation.images):
+                self._static_imgs[i: i + 1].copy_(observation.images[n], non_blocking=True)
+            self._ids.copy_(observation.tokenized_prompt.reshape(-1), non_blocking=True)
+            den.x_t.copy_(noise.reshape(den.horizon, den.action_dim), non_blocking=True)
+            self._graphs["full"].replay()
+            actions = den.x_t
+        else:
+            valid = self._embed_prefix(observation)
+            self._set_key_valid(valid)
+            prefix.enqueue(abi.stream_of(self.device))
+            actions = den.run(noise.to(self.device, non_blocking=True).float(), use_graph=self.use_cuda_graph)
         return {"actions": actions.clone().reshape(1, self.config.action_horizon, self.config.action_dim)}
 
     @torch.no_grad()
@@ -281,6 +306,7 @@ class OpenPi0Inference:
         with torch.cuda.graph(g):
             enqueue(torch.cuda.current_stream(self.device).cuda_stream)
         self._graphs["full"] = g
+        self._full_key = (tuple(obs.images.keys()), tuple(obs.images[n].shape for n in obs.images))
 
         def step():
             den.x_t.copy_(noise.reshape(den.horizon, den.action_dim))

@@ -77,3 +77,21 @@ def test_sample_actions_end_to_end_small():
     # a second call (graph replay path) gives the same result
     act2 = eng.sample_actions(obs, noise=noise)["actions"][0].cpu()
     assert (act2 - act).abs().max().item() <= 1e-3
+    # a new observation through the replayed graph (its static inputs refreshed)
+    # matches the eager path on the same observation
+    g2 = torch.Generator().manual_seed(101)
+    imgs2 = {k: torch.rand((1, 3, 224, 224), generator=g2) * 2 - 1 for k in imgs}
+    masks2 = dict(masks)
+    masks2["cam2"] = torch.zeros(1, dtype=torch.bool)  # a missing view
+    toks2 = torch.randint(0, synthetic.VOCAB_SIZE, (1, 200), generator=g2)
+    tmask2 = torch.ones(1, 200, dtype=torch.bool)
+    tmask2[0, 150:] = False
+    obs2 = Observation(imgs2, masks2, toks2, tmask2, torch.zeros(1, 32))
+    noise2 = synthetic.make_noise(3)
+    act3 = eng.sample_actions(obs2, noise=noise2)["actions"][0].cpu()
+    eng.use_cuda_graph = False
+    act3_eager = eng.sample_actions(obs2, noise=noise2)["actions"][0].cpu()
+    eng.use_cuda_graph = True
+    assert (act3 - act3_eager).abs().max().item() <= 1e-3
+    assert (act3 - act).abs().max().item() > 1e-3  # the new inputs were used
+    assert ops.read_device_status() == 0
