@@ -138,7 +138,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     return reinterpret_cast<uint64_t*>(merge_recv() +
                                        (size_t)p.splits * ((kRows + p.splits - 1) / p.splits) * kMergeFloats);
   };
-  if (MERGE) {
+  if constexpr (MERGE) {
     int mr0, mr1;
     merge_rows(mr0, mr1);
     const int n_split = p.splits, slot_floats = (mr1 - mr0) * kMergeFloats;
@@ -219,13 +219,11 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     const uint32_t sKa = static_cast<uint32_t>(__cvta_generic_to_shared(sK + buf * kChunk * kRowBytes));
     const uint32_t sVa = static_cast<uint32_t>(__cvta_generic_to_shared(sV + buf * kChunk * kRowBytes));
 
-    // S = Q_w (16 x 256) . K_chunk^T (256 x 64).  The k loop stays rolled: this code
-    // runs once or twice per launch, so its instruction fetch is on the critical
-    // path, and each step already has eight independent MMAs.
+    // S = Q_w (16 x 256) . K_chunk^T (256 x 64)
     float s[8][4];
 #pragma unroll
     for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
-#pragma unroll 1
+#pragma unroll
     for (int kk = 0; kk < kD / 16; ++kk) {
       uint32_t a0, a1, a2, a3;
       {
@@ -333,7 +331,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     }
   };
 
-  if (MERGE) {
+  if constexpr (MERGE) {
     int mr0, mr1;
     merge_rows(mr0, mr1);
     const int n_split = p.splits, slot_floats = (mr1 - mr0) * kMergeFloats;
@@ -366,31 +364,43 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     __syncwarp();
     cluster_arrive_relaxed();
     if (ok) {
-      // Merge rows mr0..mr1-1: thread handles 4 columns of one row per pass.
+      // Merge rows mr0..mr1-1.  First each row's split weights w_s = exp(m_s - max)
+      // and 1 / sum_s l_s w_s (one warp per row, lane s = split s), into the free Q
+      // buffer; then every thread sums 4 columns of a row over the splits in order.
       const int n_own = mr1 - mr0;
+      float* s_w = reinterpret_cast<float*>(sQ);  // [n_own][33]: w_0 .. w_31, 1 / l
+      auto src = [&](int i, int sp) -> const float* {
+        return sp == split ? stg + (mr0 + i) * kMergeFloats : s_recv + sp * slot_floats + i * kMergeFloats;
+      };
+      for (int i = warp; i < n_own; i += WARPS) {
+        const float ms = lane < n_split ? src(i, lane)[kD] : -INFINITY;
+        const float ls = lane < n_split ? src(i, lane)[kD + 1] : 0.f;
+        float mmax = ms;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffff, mmax, o));
+        const float w = ms != -INFINITY ? __expf(ms - mmax) : 0.f;
+        float l = ls * w;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffff, l, o);
+        s_w[i * 33 + lane] = w;
+        if (lane == 0) s_w[i * 33 + 32] = l > 0.f ? 1.f / l : 0.f;
+      }
+      __syncthreads();
       for (int idx = tid; idx < n_own * (kD / 4); idx += WARPS * 32) {
         const int i = idx / (kD / 4), c = (idx % (kD / 4)) * 4;
         const int r = row0 + mr0 + i;
         if (r >= p.rows) continue;
-        auto src = [&](int sp) -> const float* {
-          return sp == split ? stg + (mr0 + i) * kMergeFloats : s_recv + sp * slot_floats + i * kMergeFloats;
-        };
-        float mmax = -INFINITY;
-        for (int sp = 0; sp < n_split; ++sp) mmax = fmaxf(mmax, src(sp)[kD]);
-        float l = 0.f;
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int sp = 0; sp < n_split; ++sp) {
-          const float* q = src(sp);
-          const float ms = q[kD];
-          const float w = ms != -INFINITY ? __expf(ms - mmax) : 0.f;
-          l += q[kD + 1] * w;
-          const float4 a = *reinterpret_cast<const float4*>(q + c);
+#pragma unroll 4
+        for (int sp = 0; sp < n_split; ++sp) {  // loads of four splits in flight, sums in split order
+          const float w = s_w[i * 33 + sp];
+          const float4 a = *reinterpret_cast<const float4*>(src(i, sp) + c);
           acc[0] += a.x * w;
           acc[1] += a.y * w;
           acc[2] += a.z * w;
           acc[3] += a.w * w;
         }
-        const float inv = l > 0.f ? 1.f / l : 0.f;
+        const float inv = s_w[i * 33 + 32];
         uint2 pk;
         pk.x = pack_bf16(acc[0] * inv, acc[1] * inv);
         pk.y = pack_bf16(acc[2] * inv, acc[3] * inv);
@@ -432,9 +442,12 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 }
 
 // One warp per row: merge the split partials (O unnormalised, running max m,
-// sum l).  Lane s holds split s's (m, l); the O loads of eight splits are issued
-// together per pass.
-__global__ void __launch_bounds__(256) mqa_combine_kernel(const AttnParams p) {
+// sum l).  Lane s holds split s's (m, l); each lane owns 8 columns.  Every load of
+// the row (all splits' O columns and the (m, l) pairs) is issued before the first is
+// consumed, so the merge costs one L2 round trip.
+constexpr int kCombineMaxSplits = 16;
+
+__global__ void __launch_bounds__(64) mqa_combine_kernel(const AttnParams p) {
   const bool tr = p.trace != nullptr && threadIdx.x == 0;
   const uint64_t t_entry = tr ? globaltimer_ns() : 0;
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -459,42 +472,56 @@ __global__ void __launch_bounds__(256) mqa_combine_kernel(const AttnParams p) {
     ms = p.part_ml[((size_t)lane * p.part_rows + r) * 2];
     ls = p.part_ml[((size_t)lane * p.part_rows + r) * 2 + 1];
   }
-  float mmax = ms;
-  for (int o = 16; o > 0; o >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffff, mmax, o));
-  const float w = (lane < p.splits && ms != -INFINITY) ? __expf(ms - mmax) : 0.f;
-  float l = ls * w;
-  for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffff, l, o);
   float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  for (int s0 = 0; s0 < p.splits; s0 += 8) {
-    float4 a[8], b[8];
-    float ws[8];
+  if (p.splits <= kCombineMaxSplits) {
+    float4 a[kCombineMaxSplits], b[kCombineMaxSplits];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int sj = s0 + j;
-      ws[j] = __shfl_sync(0xffffffff, w, sj & 31);
-      if (sj < p.splits) {
-        const float4* src =
-            reinterpret_cast<const float4*>(p.part_o + ((size_t)sj * p.part_rows + r) * kD + lane * 8);
+    for (int j = 0; j < kCombineMaxSplits; ++j) {
+      if (j < p.splits) {
+        const float4* src = reinterpret_cast<const float4*>(p.part_o + ((size_t)j * p.part_rows + r) * kD + lane * 8);
         a[j] = __ldcg(src);
         b[j] = __ldcg(src + 1);
-      } else {
-        ws[j] = 0.f;
-        a[j] = b[j] = make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
+    float mmax = ms;
+    for (int o = 16; o > 0; o >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffff, mmax, o));
+    const float w = (lane < p.splits && ms != -INFINITY) ? __expf(ms - mmax) : 0.f;
+    float l = ls * w;
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffff, l, o);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      acc[0] += a[j].x * ws[j]; acc[1] += a[j].y * ws[j]; acc[2] += a[j].z * ws[j]; acc[3] += a[j].w * ws[j];
-      acc[4] += b[j].x * ws[j]; acc[5] += b[j].y * ws[j]; acc[6] += b[j].z * ws[j]; acc[7] += b[j].w * ws[j];
+    for (int j = 0; j < kCombineMaxSplits; ++j) {
+      if (j < p.splits) {
+        const float wj = __shfl_sync(0xffffffff, w, j);
+        acc[0] += a[j].x * wj; acc[1] += a[j].y * wj; acc[2] += a[j].z * wj; acc[3] += a[j].w * wj;
+        acc[4] += b[j].x * wj; acc[5] += b[j].y * wj; acc[6] += b[j].z * wj; acc[7] += b[j].w * wj;
+      }
     }
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] *= inv;
+  } else {
+    float mmax = ms;
+    for (int o = 16; o > 0; o >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffff, mmax, o));
+    const float w = (lane < p.splits && ms != -INFINITY) ? __expf(ms - mmax) : 0.f;
+    float l = ls * w;
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffff, l, o);
+    for (int j = 0; j < p.splits; ++j) {
+      const float wj = __shfl_sync(0xffffffff, w, j & 31);
+      const float4* src = reinterpret_cast<const float4*>(p.part_o + ((size_t)j * p.part_rows + r) * kD + lane * 8);
+      const float4 x = __ldcg(src), y = __ldcg(src + 1);
+      acc[0] += x.x * wj; acc[1] += x.y * wj; acc[2] += x.z * wj; acc[3] += x.w * wj;
+      acc[4] += y.x * wj; acc[5] += y.y * wj; acc[6] += y.z * wj; acc[7] += y.w * wj;
+    }
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] *= inv;
   }
-  const float inv = l > 0.f ? 1.f / l : 0.f;
   __nv_bfloat16* dst = p.out + (size_t)r * p.out_stride + lane * 8;
   uint4 pk;
-  pk.x = pack_bf16(acc[0] * inv, acc[1] * inv);
-  pk.y = pack_bf16(acc[2] * inv, acc[3] * inv);
-  pk.z = pack_bf16(acc[4] * inv, acc[5] * inv);
-  pk.w = pack_bf16(acc[6] * inv, acc[7] * inv);
+  pk.x = pack_bf16(acc[0], acc[1]);
+  pk.y = pack_bf16(acc[2], acc[3]);
+  pk.z = pack_bf16(acc[4], acc[5]);
+  pk.w = pack_bf16(acc[6], acc[7]);
   *reinterpret_cast<uint4*>(dst) = pk;
 }
 
@@ -575,8 +602,9 @@ int tc_min_rows() {
   return v;
 }
 
+// Two rows (warps) per CTA, so the partial reads spread over every SM.
 int launch_combine(const AttnParams& p, cudaStream_t st) {
-  return launch_pdl(mqa_combine_kernel, dim3((p.rows + 7) / 8), dim3(256), 0, st, pdl_enabled(), p);
+  return launch_pdl(mqa_combine_kernel, dim3((p.rows + 1) / 2), dim3(64), 0, st, pdl_enabled(), p);
 }
 
 // mma.sync path: W warps of 16 query rows per CTA (default 2, which halves the
