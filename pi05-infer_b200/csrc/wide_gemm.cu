@@ -82,59 +82,80 @@ constexpr int wide_smem_bytes() {
   return 1024 + STAGES * (kABytes + wide_b_bytes<BN, PAIR>()) + EW * epi_slabs<EPI>() * kSlabBytes + BN * 4 + 512;
 }
 
+constexpr int kMaxSegs = 4;  // stream-K: CTAs sharing one tile at most
+
 struct WideSched {
   int m_tiles;
   int n_tiles;
   int kb_total;
-  int splits;  // split-K (STORE / GATED_RESID only)
+  int splits;   // split-K (STORE / GATED_RESID only): splits, or partial slots per tile (stream-K)
+  int streamk;  // 1: every unit takes an equal contiguous range of the (tile, k-block) space
+  int grid;     // stream-K: the number of units (the launch grid)
 };
 
-// Work item t: m fastest (CTAs resident together share weight tiles), then the
-// K split, then n.
+// A unit's work item: tile (m, n), k-block range [kb0, kb1), and the segment s of
+// nseg that cut the tile's K range (split-K / stream-K; nseg = 1 for a whole tile).
 struct WideTile {
-  int m, s, n, kb0, kb1;
+  int m, s, n, kb0, kb1, nseg;
 };
 
-__device__ __forceinline__ WideTile wide_tile(int t, const WideSched& ws) {
-  WideTile w;
-  w.m = t % ws.m_tiles;
-  const int r = t / ws.m_tiles;
-  w.s = r % ws.splits;
-  w.n = r / ws.splits;
-  w.kb0 = (w.s * ws.kb_total) / ws.splits;
-  w.kb1 = ((w.s + 1) * ws.kb_total) / ws.splits;
-  return w;
+// Stream-K: unit c owns units [start(c), start(c+1)) of the tile-major (tile, k-block)
+// space; the unit holding k-block u.
+__device__ __forceinline__ long sk_start(int c, long total_units, int n_units) {
+  return (long)c * total_units / n_units;
 }
 
-// Split-K partials of one output tile: [split][128 rows][BN] fp32, row-major, so
-// a thread (one row) moves whole 128-byte lines.
+__device__ __forceinline__ int sk_owner(long u, long total_units, int n_units) {
+  int c = (int)((u * n_units) / total_units);
+  while (c + 1 < n_units && sk_start(c + 1, total_units, n_units) <= u) ++c;
+  while (c > 0 && sk_start(c, total_units, n_units) > u) --c;
+  return c;
+}
+
+// Item i of unit `unit` (false past its last).  Tiles are ordered m fastest, so
+// units running together share weight tiles.
+__device__ __forceinline__ bool wide_item(int unit, int i, int n_units, const WideSched& ws, WideTile& w) {
+  const int tiles = ws.m_tiles * ws.n_tiles;
+  if (!ws.streamk) {
+    const int t = unit + i * n_units;
+    if (t >= tiles * ws.splits) return false;
+    w.m = t % ws.m_tiles;
+    const int r = t / ws.m_tiles;
+    w.s = r % ws.splits;
+    w.n = r / ws.splits;
+    w.kb0 = (w.s * ws.kb_total) / ws.splits;
+    w.kb1 = ((w.s + 1) * ws.kb_total) / ws.splits;
+    w.nseg = ws.splits;
+    return true;
+  }
+  const long kb = ws.kb_total, total = (long)tiles * kb;
+  const long u0 = sk_start(unit, total, n_units), u1 = sk_start(unit + 1, total, n_units);
+  const long tile = u0 / kb + i;
+  const long a = max(u0, tile * kb), b = min(u1, (tile + 1) * kb);
+  if (a >= b) return false;
+  w.m = (int)(tile % ws.m_tiles);
+  w.n = (int)(tile / ws.m_tiles);
+  w.kb0 = (int)(a - tile * kb);
+  w.kb1 = (int)(b - tile * kb);
+  const int first = sk_owner(tile * kb, total, n_units);
+  w.s = unit - first;
+  w.nseg = sk_owner((tile + 1) * kb - 1, total, n_units) - first + 1;
+  return true;
+}
+
+// Split-K partials of one output tile: [slot][128 rows][BN] fp32, row-major, so a
+// thread (one row) moves whole 128-byte lines.
 struct WideSplit {
   const float* part;  // this tile's partials; nullptr without split-K
-  int splits, own, row;
+  int nseg, own, row;
 };
 
-// Accumulator columns [col, col + 32) of this thread's row: from TMEM, or (the
-// split that finishes a split-K tile) the sum of every split's partial in split
-// order, its own taken from TMEM (bit-identical to the stored copy).
+// Accumulator columns [col, col + 32) of this thread's row (TMEM; a split tile's
+// finishing segment has already summed every segment into it).
 template <int BN>
 __device__ __forceinline__ void wide_acc32(uint32_t taddr, int col, const WideSplit& sp, float* v) {
-  if (sp.part == nullptr) {
-    tmem_ld32(taddr + col, v);
-    return;
-  }
-  // Two splits (the launcher never uses more): the other split's 32 values are
-  // loaded before the TMEM read, so the row costs one L2 round trip per chunk.
-  const int other = 1 - sp.own;
-  const float4* src = reinterpret_cast<const float4*>(sp.part + ((size_t)other * 128 + sp.row) * BN + col);
-  float4 a[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) a[i] = __ldcg(src + i);
-  float own[32];
-  tmem_ld32(taddr + col, own);
-  const float* first = sp.own == 0 ? own : reinterpret_cast<const float*>(a);
-  const float* second = sp.own == 0 ? reinterpret_cast<const float*>(a) : own;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = (0.f + first[i]) + second[i];
+  (void)sp;
+  tmem_ld32(taddr + col, v);
 }
 
 // Tensor maps of one launch.  out: STORE / GATED_RESID / GEGLU output, or q_out
@@ -445,7 +466,6 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
   const uint64_t t_entry = (p.trace != nullptr) ? globaltimer_ns() : 0;
   uint64_t t_setup = 0, t_acc = 0, t_epi = 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int total = ws.m_tiles * ws.n_tiles * ws.splits;
   // Work units: CTAs, or CTA pairs (ws.m_tiles then counts 256-token pair tiles).
   const int rank = PAIR ? (int)cluster_ctarank() : 0;
   const bool leader = rank == 0;
@@ -531,8 +551,8 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
         if (!PAIR || leader) load(sB + st * kBBytes, &mp.w0, st, kb * kBK, row0, pol_w);
         if (!PAIR || !leader) load(sB + st * kBBytes + (PAIR ? 0 : kBBytes / 2), &mp.w1, st, kb * kBK, row1, pol_w);
       };
-      for (int t = unit0; t < total; t += n_units) {
-        const WideTile wt = wide_tile(t, ws);
+      WideTile wt;
+      for (int item = 0; wide_item(unit0, item, n_units, ws, wt); ++item) {
         const int m = PAIR ? 2 * wt.m + rank : wt.m;  // this CTA's 128-token tile
         int row0, row1;
         wide_rows<EPI, BN>(wt.n, row0, row1);
@@ -574,7 +594,8 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
     } else if (lane == 0) {
       int it = 0, lt = 0;
       bool ok = true;
-      for (int t = unit0; t < total && ok; t += n_units, ++lt) {
+      WideTile wt;
+      for (int item = 0; ok && wide_item(unit0, item, n_units, ws, wt); ++item, ++lt) {
         const int buf = lt & 1;
         if (!mbar_wait(&acce[buf], ((lt >> 1) & 1) ^ 1)) {
           report_status(p.status, PI05_DEV_TIMEOUT_MMA);
@@ -584,7 +605,6 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
         tc_fence_after();
         if (p.trace != nullptr && lt == 0) s_stamp[1] = globaltimer_ns();
         const uint32_t d = tmem + (uint32_t)(buf * BN);
-        const WideTile wt = wide_tile(t, ws);
         for (int kb = wt.kb0; kb < wt.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           // Pairs: the odd CTA's copies complete the phase too.
@@ -636,8 +656,8 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
     e.bar = sbar + (warp - 2) * 2;
     e.phase = 0;
     int lt = 0;
-    for (int t = unit0; t < total; t += n_units, ++lt) {
-      const WideTile wt = wide_tile(t, ws);
+    WideTile wt;
+    for (int item = 0; wide_item(unit0, item, n_units, ws, wt); ++item, ++lt) {
       const int m = PAIR ? 2 * wt.m + rank : wt.m, n = wt.n;  // this CTA's 128-token tile
       const int buf = lt & 1;
       wide_epi_prefetch<EPI, BN>(p, mp, e, n, m * kWBM);
@@ -664,38 +684,93 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
       else if (EPI == SK_EPI_QKV_ROPE)
         ok = wide_epi_qkv(p, mp, e, taddr, n, m * kWBM);
       else {
-        WideSplit sp{nullptr, ws.splits, wt.s, e.q * 32 + lane};
+        WideSplit sp{nullptr, wt.nseg, wt.s, e.q * 32 + lane};
         bool finish = true;
-        if (ws.splits > 1) {
-          // Publish this split's partial (whole 128-byte lines per row), take a
-          // ticket; the split taking the last ticket sums all partials in split
-          // order and runs the epilogue.  No CTA waits for another.
+        if (wt.nseg > 1) {
+          // Publish this segment's partial, take a ticket; the segment taking the
+          // last ticket sums every segment's partial in segment order into its
+          // TMEM accumulator and runs the epilogue.  No CTA waits for another.
+          // Partials move warp-cooperatively through slab 1 (slab 0 may hold the
+          // prefetched residual): a thread owns a TMEM row, while 8 lanes together
+          // move one 128-byte line of a row in global memory.
           const int tile_mn = n * cta_m_tiles + m;
           float* part = p.accum + (size_t)tile_mn * ws.splits * kWBM * BN;
-          float* mine = part + ((size_t)wt.s * kWBM + sp.row) * BN;
+          uint8_t* xs = slab_at(e, 1);
+          const int g = lane & 7;  // this lane's 16-byte piece of a 128-byte line
+          if (e.lane == 0) bulk_wait_group_read<0>();  // slab 1's last TMA store has read it
+          __syncwarp();
+          const size_t my_rows = (size_t)wt.s * kWBM + e.q * 32;
 #pragma unroll 1
           for (int c = 0; c < BN / 32; ++c) {
-            if (((c >> 1) % e.step) != e.half) continue;  // the quarter's other warp writes this slab
+            if (((c >> 1) % e.step) != e.half) continue;  // the quarter's other warp takes this slab
             float v[32];
             tmem_ld32(taddr + c * 32, v);
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-              __stcg(reinterpret_cast<float4*>(mine + c * 32) + i,
-                     make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
+            for (int q4 = 0; q4 < 8; ++q4)
+              *reinterpret_cast<float4*>(xs + lane * 128 + ((q4 ^ (lane & 7)) << 4)) =
+                  make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int rr = (lane >> 3) + 4 * i;
+              __stcg(reinterpret_cast<float4*>(part + (my_rows + rr) * BN + c * 32 + g * 4),
+                     *reinterpret_cast<const float4*>(xs + rr * 128 + ((g ^ (rr & 7)) << 4)));
+            }
+            __syncwarp();
           }
           __threadfence();
           named_bar_sync(1, kET);
           if (threadIdx.x == 64) {
             const int old = atomicAdd(p.counters + tile_mn, 1);
-            const int last = old == ws.splits - 1 ? 1 : 0;
+            const int last = old == wt.nseg - 1 ? 1 : 0;
             if (last) atomicExch(p.counters + tile_mn, 0);  // re-armed for the next launch
             s_flag[1] = last;
           }
           named_bar_sync(1, kET);
           finish = s_flag[1] != 0;
           named_bar_sync(1, kET);  // s_flag[1] is rewritten by the next split tile
-          if (finish) __threadfence();
-          sp.part = part;
+          if (finish) {
+            __threadfence();
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+              if (((c >> 1) % e.step) != e.half) continue;
+              float own[32], acc[32];
+              tmem_ld32(taddr + c * 32, own);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+#pragma unroll 1
+              for (int sg = 0; sg < wt.nseg; ++sg) {
+                if (sg == wt.s) {
+#pragma unroll
+                  for (int i = 0; i < 32; ++i) acc[i] += own[i];
+                  continue;
+                }
+                const size_t rows = (size_t)sg * kWBM + e.q * 32;
+                float4 t[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  const int rr = (lane >> 3) + 4 * i;
+                  t[i] = __ldcg(reinterpret_cast<const float4*>(part + (rows + rr) * BN + c * 32 + g * 4));
+                }
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  const int rr = (lane >> 3) + 4 * i;
+                  *reinterpret_cast<float4*>(xs + rr * 128 + ((g ^ (rr & 7)) << 4)) = t[i];
+                }
+                __syncwarp();
+#pragma unroll
+                for (int q4 = 0; q4 < 8; ++q4) {
+                  const float4 u = *reinterpret_cast<const float4*>(xs + lane * 128 + ((q4 ^ (lane & 7)) << 4));
+                  acc[4 * q4] += u.x;
+                  acc[4 * q4 + 1] += u.y;
+                  acc[4 * q4 + 2] += u.z;
+                  acc[4 * q4 + 3] += u.w;
+                }
+                __syncwarp();
+              }
+              tmem_st32(taddr + c * 32, acc);
+            }
+          }
         }
         if (finish) {
           ok = wide_epi_rows<EPI, BN>(p, mp, e, taddr, n, m * kWBM, sp, sbias);
@@ -829,8 +904,24 @@ int wide_launch(const SkinnyParams& p, const WideSched& ws, const WideMaps& mp, 
     return launch_pdl_cluster(kern, dim3(2 * pairs), dim3(wide_threads<EW>()), kSmem, stream, pdl_enabled(),
                               dim3(2, 1, 1), mp, p, ws);
   }
-  const int grid = std::min(total, wide_sms());
+  const int grid = ws.streamk ? ws.grid : std::min(total, wide_sms());
   return launch_pdl(kern, dim3(grid), dim3(wide_threads<EW>()), kSmem, stream, pdl_enabled(), mp, p, ws);
+}
+
+// Host copy of the stream-K schedule: the largest number of units sharing one tile
+// when `units` units split tiles x kb k-blocks evenly.
+int sk_max_segs(long tiles, long kb, int units) {
+  const long total = tiles * kb;
+  auto start = [&](int c) { return (long)c * total / units; };
+  auto owner = [&](long u) {
+    int c = (int)((u * units) / total);
+    while (c + 1 < units && start(c + 1) <= u) ++c;
+    while (c > 0 && start(c) > u) --c;
+    return c;
+  };
+  int best = 1;
+  for (long t = 0; t < tiles; ++t) best = std::max(best, owner((t + 1) * kb - 1) - owner(t * kb) + 1);
+  return best;
 }
 
 // Debug override read once: PI05_WIDE_BN (128 / 256) for STORE / GATED_RESID.
@@ -841,15 +932,21 @@ int env_int(const char* name) {
 
 }  // namespace
 
-int wide_choose(int epi, int m_tiles, int n_cols, int kb_total, int sms, int* bn, int* splits, int* pair) {
+int wide_choose(int epi, int m_tiles, int n_cols, int kb_total, int sms, int* bn, int* splits, int* pair,
+                int* streamk) {
   static const int force_bn = env_int("PI05_WIDE_BN");
   static const int force_splits = env_int("PI05_WIDE_SPLITS");
   static const int force_pair = [] {
     const char* e = getenv("PI05_WIDE_PAIR");
     return e != nullptr ? atoi(e) : -1;
   }();
+  static const int force_sk = [] {
+    const char* e = getenv("PI05_WIDE_STREAMK");
+    return e != nullptr ? atoi(e) : -1;
+  }();
   *splits = 1;
   *pair = 0;
+  *streamk = 0;
   // CTA pairs pay a longer prologue and (with split-K) a slower epilogue; they win
   // on the long-running projections: gate/up at full token tiles and long-K ones
   // (the prefix down_proj).  PI05_WIDE_PAIR=0 / 1 disables / forces them.
@@ -894,6 +991,23 @@ int wide_choose(int epi, int m_tiles, int n_cols, int kb_total, int sms, int* bn
       }
     }
   }
+  // Stream-K (PI05_WIDE_STREAMK=1): every SM takes an equal share of the (tile,
+  // k-block) space, tiles cut across SMs finished by their last segment.
+  if (force_sk > 0) {
+    const int b = 128;
+    const long tiles = (long)m_tiles * ((n_cols + b - 1) / b);
+    int units = (int)std::min<long>(sms, tiles * kb_total);
+    while (units > 1 && sk_max_segs(tiles, kb_total, units) > kMaxSegs) --units;
+    const int segs = sk_max_segs(tiles, kb_total, units);
+    // Measured slower than the classic schedule on the prefix / SigLIP shapes (the
+    // partial round trips of 3-4 segments per tile): on request only.
+    if (force_sk > 0 && segs > 1) {
+      *bn = b;
+      *splits = segs;  // partial slots per tile
+      *streamk = units;
+      return 0;
+    }
+  }
   if (force_bn == 128 || force_bn == 256) *bn = force_bn;
   if (force_splits >= 1 && force_splits <= 2) *splits = force_splits;
   return 0;
@@ -921,8 +1035,10 @@ int wide_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int w
   WideSched ws;
   const int cta_m_tiles = (p.m_tok + kWBM - 1) / kWBM;
   ws.kb_total = (p.k + kBK - 1) / kBK;
-  int bn = 256, splits = 1, pair = 0;
-  wide_choose(epi, cta_m_tiles, n_cols, ws.kb_total, wide_sms(), &bn, &splits, &pair);
+  int bn = 256, splits = 1, pair = 0, sk_units = 0;
+  wide_choose(epi, cta_m_tiles, n_cols, ws.kb_total, wide_sms(), &bn, &splits, &pair, &sk_units);
+  ws.streamk = sk_units > 0 ? 1 : 0;
+  ws.grid = sk_units;
   // Pairs schedule 256-token tiles; every CTA still owns 128 tokens of one.
   ws.m_tiles = pair ? (cta_m_tiles + 1) / 2 : cta_m_tiles;
   const int m_tiles_cta = pair ? 2 * ws.m_tiles : ws.m_tiles;
@@ -935,8 +1051,11 @@ int wide_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int w
   if (splits > 1) {
     const size_t need = (size_t)m_tiles_cta * ws.n_tiles * splits * kWBM * bn * sizeof(float);
     if (p.accum == nullptr || p.counters == nullptr || need > p.accum_bytes ||
-        (long)m_tiles_cta * ws.n_tiles > kWsMaxCounters || splits > ws.kb_total)
+        (long)m_tiles_cta * ws.n_tiles > kWsMaxCounters || splits > ws.kb_total) {
       splits = 1;
+      ws.streamk = 0;
+      ws.grid = 0;
+    }
   }
   ws.splits = splits;
   p.splits = splits;
