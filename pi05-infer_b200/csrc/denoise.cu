@@ -50,6 +50,21 @@ bool fused_norm_enabled() {
   return v != 0;
 }
 
+// PI05_PRODUCER_NORM=1 runs the norms after layer 0's input_layernorm in the
+// epilogue of the GEMM that produces their input (o_proj for
+// post_attention_layernorm, down_proj for the next layer's input_layernorm): the
+// last owner of each token slice, elected by a ticket, normalises the slice's whole
+// rows.  Off by default: on B200 the ticket and the row loads are two L2 round
+// trips while the next GEMM's weight stream fills the memory system, which lengthens
+// the producer's tail by more than the norm kernel and its launch gap cost.
+bool producer_norm_enabled() {
+  static int v = [] {
+    const char* e = getenv("PI05_PRODUCER_NORM");
+    return (e != nullptr && e[0] == '1') ? 1 : 0;
+  }();
+  return v != 0;
+}
+
 }  // namespace
 
 extern "C" {
@@ -189,6 +204,18 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
   const bool fuse = fused_norm_enabled() && W <= kNormMaxK && T <= 64 && n_parts <= kNormMaxParts &&
                     (size_t)n_parts * T * sizeof(float) <= kWsStatsBytes;
   float* ssq_attn = ws.stats;  // input of input_layernorm (from down_proj)
+  const bool prod = !fuse && producer_norm_enabled() && T <= 64 && (size_t)n_parts * T * sizeof(float) <= kWsStatsBytes;
+  // Producer-side norm of the GEMM output `h` into xn with modulation `mod`.
+  auto producer_norm = [&](SkinnyParams& sp, const float* mod) {
+    sp.row_ssq = ws.stats;
+    sp.ssq_ld = T;
+    sp.norm_out = xn;
+    sp.norm_ldo = W;
+    sp.norm_mod = mod;
+    sp.norm_d = W;
+    sp.norm_eps = P->eps;
+    sp.norm_tickets = ws.counters + kWsNormTicketBase;
+  };
 
   int rc = action_in_run(P->x_t, P->w_in, P->b_in, h, T, P->action_dim, W, stream);
   for (int l = 0; l < P->depth && rc == PI05_OK; ++l) {
@@ -198,9 +225,10 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
     const Pi05ExpertLayer& N = P->layers[(l + 1) % P->depth];
     const float* mod1 = mods + (size_t)(2 * l) * 3 * W;
     const float* mod2 = mods + (size_t)(2 * l + 1) * 3 * W;
-    // input_layernorm (adaRMS): fused into q|k|v after layer 0
+    // input_layernorm (adaRMS): after layer 0 fused into q|k|v, or produced by the
+    // previous down_proj
     const bool fuse1 = fuse && l > 0;
-    if (!fuse1) {
+    if (!fuse1 && !(prod && l > 0)) {
       rc = rms_norm_run(h, W, mod1, nullptr, xn, W, T, W, P->eps, stream);
       if (rc) break;
     }
@@ -281,12 +309,15 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.pf0 = N.w_o;
       sp.pf0_bytes = (size_t)W * HQ * D * 2;
       sp.trace_tag = (step * P->depth + l) * 8 + 1;
+      if (prod) producer_norm(sp, mod2);  // post_attention_layernorm
       rc = skinny_gemm_run(SK_EPI_GATED_RESID, sp, L.w_o, L.w_o, W, W, attn, HQ * D, so[1], stream);
       if (rc) break;
     }
     // post_attention_layernorm (adaRMS)
-    rc = rms_norm_run(h, W, mod2, nullptr, xn, W, T, W, P->eps, stream);
-    if (rc) break;
+    if (!prod) {
+      rc = rms_norm_run(h, W, mod2, nullptr, xn, W, T, W, P->eps, stream);
+      if (rc) break;
+    }
     // gate/up + GeGLU
     {
       SkinnyParams sp;
@@ -328,6 +359,7 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
         sp.row_ssq = ssq_attn;
         sp.ssq_ld = T;
       }
+      if (prod && l + 1 < P->depth) producer_norm(sp, mods + (size_t)(2 * (l + 1)) * 3 * W);  // next input_layernorm
       sp.pf0 = N.w_down;
       sp.pf0_bytes = (size_t)W * F * 2;
       sp.trace_tag = (step * P->depth + l) * 8 + 3;

@@ -23,6 +23,8 @@ namespace pi05 {
 constexpr size_t kWsStatusOffset = 0;
 constexpr size_t kWsCounterOffset = 64;
 constexpr int kWsMaxCounters = 4096;
+// The top counters are the producer-side norm tickets (one per token slice).
+constexpr int kWsNormTicketBase = kWsMaxCounters - 64;
 constexpr size_t kWsAccumOffset = 64 + kWsMaxCounters * 4 + 192;  // 16640, 256-aligned
 constexpr size_t kWsAccumBytes = size_t(40) << 20;
 constexpr size_t kWsStatsOffset = kWsAccumOffset + kWsAccumBytes;

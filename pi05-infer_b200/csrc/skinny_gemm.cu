@@ -29,6 +29,7 @@
 #include <cstdlib>
 #include <cstring>
 
+#include "elementwise.h"
 #include "gemm_epilogue.cuh"
 #include "host_util.h"
 #include "ptx.cuh"
@@ -124,6 +125,7 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
     for (int s = 0; s < STAGES; ++s) mbar_init(&xrdy[s], 4);
     s_flag[0] = 0;
     s_flag[1] = 0;
+    for (int i = 14; i < 19; ++i) accum[i] = 0;  // trace: producer-side norm stamps
     fence_mbar_init();
     // Push form: expect this rank's token slice from every other split.
     if (push) mbar_arrive_expect_tx(rbar, push_recv_bytes(p.splits, mt, (int)cluster_ctarank()));
@@ -396,7 +398,7 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
     __syncwarp();
     if (push)
       cluster_push_epilogue<EPI>(p, stage_tile, recv, rbar, tile, tok0, mt, (int)cluster_ctarank(),
-                                 (int)threadIdx.x - 64, warp >= 2, p.trace != nullptr ? cl_stamps : nullptr);
+                                 (int)threadIdx.x - 64, warp >= 2, p.trace != nullptr ? cl_stamps : nullptr, &s_flag[1]);
     else
       cluster_epilogue<EPI>(p, smem_u32(stage_tile), tile, tok0, mt, (int)cluster_ctarank(), (int)threadIdx.x - 64,
                             warp >= 2, p.trace != nullptr ? cl_stamps : nullptr);
@@ -408,7 +410,8 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
 
   if (p.trace != nullptr && threadIdx.x == 64) {
     const unsigned long long cta = ((unsigned long long)smid() << 16) | (blockIdx.y * gridDim.x + blockIdx.x);
-    const unsigned long long slot = atomicAdd(p.trace, (p.cluster ? 2ull : 1ull) + (norm ? 1ull : 0ull));
+    const unsigned long long slot =
+        atomicAdd(p.trace, (p.cluster ? 2ull : 1ull) + (norm ? 1ull : 0ull) + (p.cluster && p.norm_out ? 1ull : 0ull));
     const unsigned long long cap = p.trace[1];  // records the buffer holds
     if (slot < cap) {
       unsigned long long* w = p.trace + 8 + slot * 8;
@@ -423,14 +426,24 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
     }
     if (p.cluster && slot + 1 < cap) {
       // Cluster epilogue record (tag + 2^30): before / after the first cluster
-      // barrier, first DSMEM pass summed, last store issued, exit barrier passed.
+      // barrier, first DSMEM pass summed, last store issued, exit barrier passed,
+      // then (producer-side norm) the ticket time and whether this CTA was last.
       unsigned long long* w = p.trace + 8 + (slot + 1) * 8;
       w[0] = ((unsigned long long)(p.trace_tag + (1 << 30)) << 32) | cta;
       for (int i = 0; i < 5; ++i) w[1 + i] = cl_stamps[i];
+      w[6] = cl_stamps[10];  // producer-side norm: ticket taken, last owner
+      w[7] = cl_stamps[11];
+    }
+    if (p.cluster && p.norm_out != nullptr && slot + 2 < cap) {
+      // Producer-side norm record (tag + 3 * 2^30): ticket, last flag, then in the
+      // last owner: flag barrier passed, loads' barrier passed, first row computed.
+      unsigned long long* w = p.trace + 8 + (slot + 2) * 8;
+      w[0] = ((unsigned long long)(p.trace_tag + (3u << 30)) << 32) | cta;
+      for (int i = 0; i < 5; ++i) w[1 + i] = cl_stamps[10 + i];
       w[6] = 0;
       w[7] = 0;
     }
-    const unsigned long long ns = slot + (p.cluster ? 2 : 1);
+    const unsigned long long ns = slot + (p.cluster ? 2 : 1) + (p.cluster && p.norm_out != nullptr ? 1 : 0);
     if (norm && ns < cap) {
       // Fused-norm record (tag + 2^31): grid-dependency wait done, rstd / scale
       // loads done, first and last X stage normalised.
@@ -634,6 +647,15 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
                    "operands", kNormMaxK, kNormMaxParts);
     return PI05_ERR_SHAPE;
   }
+  if (p.norm_out != nullptr &&
+      (epi != SK_EPI_GATED_RESID || p.row_ssq == nullptr || p.ssq_ld < p.m_tok || p.norm_tickets == nullptr ||
+       p.norm_mod == nullptr || !aligned16(p.norm_mod) || !aligned16(p.norm_out) || !aligned16(p.out) ||
+       p.norm_ldo % 8 != 0 || p.ldo % 8 != 0 || p.norm_d != p.n_tiles * kBM || p.n_valid != 0 ||
+       p.norm_ssq != nullptr || p.m_tok > 64)) {
+    set_last_error("skinny_gemm: producer-side norm needs gated residual, <= 64 tokens, row statistics, "
+                   "norm_d == output width, aligned operands");
+    return PI05_ERR_SHAPE;
+  }
   if (p.norm_ssq != nullptr) {
     p.norm_x = static_cast<const __nv_bfloat16*>(x);
     p.norm_ldx = ldx;
@@ -708,7 +730,7 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
       return PI05_ERR_SHAPE;
     }
     if (p.accum == nullptr || p.counters == nullptr || need > p.accum_bytes ||
-        2 * tok_tiles * p.n_tiles > kWsMaxCounters) {
+        2 * tok_tiles * p.n_tiles > kWsNormTicketBase) {
       set_last_error("skinny_gemm: workspace too small (%zu needed)", need);
       return PI05_ERR_WORKSPACE;
     }
@@ -723,6 +745,17 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
     const long need = (long)(p.splits - 1) * ((mt + p.splits - 1) / p.splits) * kBM * 4;
     p.push = (p.cluster && tok == 64 && p.splits <= 16 && need <= 32768 && push_enabled()) ? 1 : 0;
   }
+  // The producer-side norm runs in the push form's epilogue (one token tile, rows
+  // of at most 8 columns per epilogue thread, the slice's rows within the receive
+  // slots); any other schedule normalises with the norm kernel after the GEMM.
+  __nv_bfloat16* norm_after = nullptr;
+  const bool norm_in_epilogue =
+      p.push && tok_tiles == 1 && p.norm_d <= 8 * kEpiThreads &&
+      norm_scratch_bytes((std::min(p.m_tok, tok) + p.splits - 1) / p.splits, p.n_tiles, p.norm_d) <= recv_bytes<64>();
+  if (p.norm_out != nullptr && !norm_in_epilogue) {
+    norm_after = p.norm_out;
+    p.norm_out = nullptr;
+  }
   CUtensorMap tw0, tw1, tx;
   int rc = make_tmap_bf16_2d(&tw0, w0, w_rows0, p.k, p.k, 64, 64, true);
   if (rc) return rc;
@@ -734,9 +767,13 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
   switch (epi) {
 #define PI05_SK_CASE(E)                                                                 \
   case E:                                                                               \
-    if (tok == 64) return launch_one<E, 64, 3>(p, tw0, tw1, tx, tok_tiles, st);         \
-    if (tok == 128) return launch_one<E, 128, S>(p, tw0, tw1, tx, tok_tiles, st);       \
-    return launch_one<E, 256, 3>(p, tw0, tw1, tx, tok_tiles, st);
+    if (tok == 64)                                                                      \
+      rc = launch_one<E, 64, 3>(p, tw0, tw1, tx, tok_tiles, st);                        \
+    else if (tok == 128)                                                                \
+      rc = launch_one<E, 128, S>(p, tw0, tw1, tx, tok_tiles, st);                       \
+    else                                                                                \
+      rc = launch_one<E, 256, 3>(p, tw0, tw1, tx, tok_tiles, st);                       \
+    break;
     PI05_SK_CASE(SK_EPI_STORE)
     PI05_SK_CASE(SK_EPI_GATED_RESID)
     PI05_SK_CASE(SK_EPI_GEGLU)
@@ -746,6 +783,10 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
       set_last_error("skinny_gemm: unknown epilogue %d", epi);
       return PI05_ERR_INVALID_ARG;
   }
+  if (rc == 0 && norm_after != nullptr)
+    rc = rms_norm_run(p.out, p.ldo, p.norm_mod, nullptr, norm_after, p.norm_ldo, p.m_tok, p.norm_d, p.norm_eps,
+                      stream);
+  return rc;
 }
 
 }  // namespace pi05

@@ -49,6 +49,15 @@ struct SkinnyParams {
   // written to row_ssq[tile * ssq_ld + token] (fixed summation order).
   float* row_ssq = nullptr;
   int ssq_ld = 0;
+  // Normalised copy of the output for the next (ada)RMS norm (GATED_RESID, push-form
+  // cluster split-K, one token tile): when norm_out is set, the owner of each token
+  // slice of a tile writes the slice's sums of squares to row_ssq, and the last of
+  // the n_tiles owners of a slice (ticket norm_tickets[slice]) writes
+  // norm_out[t, k] = bf16(out[t, k] * rstd[t] * (1 + norm_mod[k]) + norm_mod[norm_d + k]),
+  // rstd as for the fused norm below (norm_parts = n_tiles, norm_ld = ssq_ld).
+  __nv_bfloat16* norm_out = nullptr;
+  int norm_ldo = 0;
+  int* norm_tickets = nullptr;  // [cluster size], zero on entry, left zero
   // Fused (ada)RMS norm of the X operand (QKV_ROPE, <= 64 tokens): when norm_ssq is
   // set, X holds the raw residual stream h, which the kernel normalises while
   // staging it: x = bf16(h * rstd[t] * (1 + norm_mod[k]) + norm_mod[norm_d + k]),

@@ -1051,7 +1051,7 @@ int wide_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int w
   if (splits > 1) {
     const size_t need = (size_t)m_tiles_cta * ws.n_tiles * splits * kWBM * bn * sizeof(float);
     if (p.accum == nullptr || p.counters == nullptr || need > p.accum_bytes ||
-        (long)m_tiles_cta * ws.n_tiles > kWsMaxCounters || splits > ws.kb_total) {
+        (long)m_tiles_cta * ws.n_tiles > kWsNormTicketBase || splits > ws.kb_total) {
       splits = 1;
       ws.streamk = 0;
       ws.grid = 0;
