@@ -158,6 +158,19 @@ typedef struct Pi05ExpertLayer {
   void* v_cache;
 } Pi05ExpertLayer;
 
+/* Per-(step, layer) folded projections for the folded-norm denoise path (see
+ * pi05_fold_adarms): the layer's q|k|v and gate/up weights with that step's
+ * input_layernorm / post_attention_layernorm (1 + scale) folded into their columns,
+ * and the matching fp32 biases W . shift. */
+typedef struct Pi05ExpertFold {
+  const void* w_qkv;    /* [(hq + 2*hkv) * d, width] bf16 */
+  const void* w_gate;   /* [mlp, width] bf16 */
+  const void* w_up;     /* [mlp, width] bf16 */
+  const float* b_qkv;   /* [(hq + 2*hkv) * d] */
+  const float* b_gate;  /* [mlp] */
+  const float* b_up;    /* [mlp] */
+} Pi05ExpertFold;
+
 /* Everything one denoise step touches.  Host memory owned by the caller. */
 typedef struct Pi05ExpertPlan {
   int depth, width, mlp_dim, n_q_heads, n_kv_heads, head_dim;
@@ -189,7 +202,22 @@ typedef struct Pi05ExpertPlan {
   int attn_splits;                /* <= 0: automatic */
   unsigned long long* trace;      /* optional device buffer for the persistent kernel's phase timestamps
                                      ([SMs][pi05_trace_slots()] ns), NULL = off */
+  const Pi05ExpertFold* fold;     /* host array [num_steps * depth] (step-major), or NULL.  When set
+                                     (and tokens <= 64), pi05_denoise_step runs no norm kernel inside
+                                     the layers: q|k|v and gate/up read the residual stream h with these
+                                     folded weights and scale each token by its rstd from the row
+                                     statistics that action_in / o_proj / down_proj write. */
 } Pi05ExpertPlan;
+
+/* Folds an adaRMS norm into the projection that consumes its output, for the
+ * folded-norm denoise path (Pi05ExpertFold).  The reference normalises first and
+ * projects the bf16 result (GemmaRMSNorm adaRMS, modeling_gemma.py:82-116, then
+ * the q|k|v or gate/up projection); with
+ *   w_out[n, j] = bf16(w[n, j] * (1 + scale[j])),   b_out[n] = sum_j w[n, j] * shift[j] (fp32)
+ * that projection becomes rstd[t] * (w_out . h[t]) + b_out.  w, w_out [rows, k]
+ * bf16 (16-byte aligned, k % 8 == 0); scale, shift [k] fp32; b_out [rows] fp32. */
+int pi05_fold_adarms(const void* w, int rows, int k, const float* scale, const float* shift, void* w_out,
+                     float* b_out, void* stream);
 
 /* Timestamp slots per CTA that pi05_denoise_loop_persistent writes when plan->trace is set. */
 int pi05_trace_slots(void);

@@ -65,9 +65,28 @@ bool producer_norm_enabled() {
   return v != 0;
 }
 
+// PI05_FOLD_NORM=0 in the environment keeps the norm kernels even when the plan
+// carries folded weights (A/B and parity tests of the folded-norm path).
+bool fold_norm_enabled() {
+  static int v = [] {
+    const char* e = getenv("PI05_FOLD_NORM");
+    return (e != nullptr && e[0] == '0') ? 0 : 1;
+  }();
+  return v != 0;
+}
+
 }  // namespace
 
 extern "C" {
+
+int pi05_fold_adarms(const void* w, int rows, int k, const float* scale, const float* shift, void* w_out,
+                     float* b_out, void* stream) {
+  if (!nz(w) || !nz(scale) || !nz(shift) || !nz(w_out) || !nz(b_out)) {
+    set_last_error("fold_adarms: null pointer");
+    return PI05_ERR_INVALID_ARG;
+  }
+  return fold_adarms_run(w, rows, k, scale, shift, w_out, b_out, stream);
+}
 
 int pi05_rms_norm(const void* x, int ldx, const float* mod, const float* weight, void* out, int ldo, int rows, int d,
                   float eps, void* stream) {
@@ -205,6 +224,22 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
                     (size_t)n_parts * T * sizeof(float) <= kWsStatsBytes;
   float* ssq_attn = ws.stats;  // input of input_layernorm (from down_proj)
   const bool prod = !fuse && producer_norm_enabled() && T <= 64 && (size_t)n_parts * T * sizeof(float) <= kWsStatsBytes;
+  // Folded norms (default when the plan carries folded weights): no norm kernel
+  // inside the layers.  action_in (layer 0, one part) and down_proj write the row
+  // statistics of input_layernorm's input to ssq_attn, o_proj those of
+  // post_attention_layernorm's input to ssq_mlp; q|k|v and gate/up read h with the
+  // step's folded weights and apply rstd and the folded bias to their accumulators.
+  const bool fold = P->fold != nullptr && !fuse && !prod && fold_norm_enabled() && T <= 64 &&
+                    n_parts <= kNormMaxParts && (size_t)2 * n_parts * T * sizeof(float) <= kWsStatsBytes;
+  float* ssq_mlp = ws.stats + (size_t)n_parts * T;
+  const Pi05ExpertFold* FS = fold ? P->fold + (size_t)step * P->depth : nullptr;
+  // Folded weights of the op after layer l's: layer l + 1 of this step, or layer 0
+  // of the next step (of step 0 after the last one).
+  auto fold_next = [&](int l) -> const Pi05ExpertFold& {
+    if (l + 1 < P->depth) return FS[l + 1];
+    const int ns = step + 1 < P->num_steps ? step + 1 : 0;
+    return P->fold[(size_t)ns * P->depth];
+  };
   // Producer-side norm of the GEMM output `h` into xn with modulation `mod`.
   auto producer_norm = [&](SkinnyParams& sp, const float* mod) {
     sp.row_ssq = ws.stats;
@@ -217,7 +252,7 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
     sp.norm_tickets = ws.counters + kWsNormTicketBase;
   };
 
-  int rc = action_in_run(P->x_t, P->w_in, P->b_in, h, T, P->action_dim, W, stream);
+  int rc = action_in_run(P->x_t, P->w_in, P->b_in, h, T, P->action_dim, W, stream, fold ? ssq_attn : nullptr);
   for (int l = 0; l < P->depth && rc == PI05_OK; ++l) {
     const Pi05ExpertLayer& L = P->layers[l];
     // The same op of the next layer (layer 0 again for the next Euler step) is
@@ -228,7 +263,7 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
     // input_layernorm (adaRMS): after layer 0 fused into q|k|v, or produced by the
     // previous down_proj
     const bool fuse1 = fuse && l > 0;
-    if (!fuse1 && !(prod && l > 0)) {
+    if (!fold && !fuse1 && !(prod && l > 0)) {
       rc = rms_norm_run(h, W, mod1, nullptr, xn, W, T, W, P->eps, stream);
       if (rc) break;
     }
@@ -265,7 +300,19 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
         sp.norm_d = W;
         sp.norm_eps = P->eps;
       }
-      rc = skinny_gemm_run(SK_EPI_QKV_ROPE, sp, L.w_qkv, L.w_qkv, rows, rows, fuse1 ? h : xn, W, so[0], stream);
+      const void* wq = L.w_qkv;
+      if (fold) {
+        wq = FS[l].w_qkv;
+        sp.fold_ssq = ssq_attn;
+        sp.fold_parts = l == 0 ? 1 : n_parts;
+        sp.fold_ld = T;
+        sp.fold_d = W;
+        sp.fold_eps = P->eps;
+        sp.fold_bias0 = FS[l].b_qkv;
+        sp.fold_bias1 = FS[l].b_qkv;
+        sp.pf0 = fold_next(l).w_qkv;
+      }
+      rc = skinny_gemm_run(SK_EPI_QKV_ROPE, sp, wq, wq, rows, rows, (fuse1 || fold) ? h : xn, W, so[0], stream);
       if (rc) break;
     }
     // attention over [prefix | suffix] keys
@@ -310,11 +357,15 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.pf0_bytes = (size_t)W * HQ * D * 2;
       sp.trace_tag = (step * P->depth + l) * 8 + 1;
       if (prod) producer_norm(sp, mod2);  // post_attention_layernorm
+      if (fold) {
+        sp.row_ssq = ssq_mlp;
+        sp.ssq_ld = T;
+      }
       rc = skinny_gemm_run(SK_EPI_GATED_RESID, sp, L.w_o, L.w_o, W, W, attn, HQ * D, so[1], stream);
       if (rc) break;
     }
     // post_attention_layernorm (adaRMS)
-    if (!prod) {
+    if (!prod && !fold) {
       rc = rms_norm_run(h, W, mod2, nullptr, xn, W, T, W, P->eps, stream);
       if (rc) break;
     }
@@ -336,7 +387,22 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.pf1 = N.w_up;
       sp.pf1_bytes = (size_t)F * W * 2;
       sp.trace_tag = (step * P->depth + l) * 8 + 2;
-      rc = skinny_gemm_run(SK_EPI_GEGLU, sp, L.w_gate, L.w_up, F, F, xn, W, so[2], stream);
+      const void* wg = L.w_gate;
+      const void* wu = L.w_up;
+      if (fold) {
+        wg = FS[l].w_gate;
+        wu = FS[l].w_up;
+        sp.fold_ssq = ssq_mlp;
+        sp.fold_parts = n_parts;
+        sp.fold_ld = T;
+        sp.fold_d = W;
+        sp.fold_eps = P->eps;
+        sp.fold_bias0 = FS[l].b_gate;
+        sp.fold_bias1 = FS[l].b_up;
+        sp.pf0 = fold_next(l).w_gate;
+        sp.pf1 = fold_next(l).w_up;
+      }
+      rc = skinny_gemm_run(SK_EPI_GEGLU, sp, wg, wu, F, F, fold ? h : xn, W, so[2], stream);
       if (rc) break;
     }
     // down + gated residual (gate = third chunk of mod2)
@@ -355,7 +421,7 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.resid = h;
       sp.ldr = W;
       sp.gate = mod2 + 2 * W;
-      if (fuse && l + 1 < P->depth) {
+      if ((fuse || fold) && l + 1 < P->depth) {
         sp.row_ssq = ssq_attn;
         sp.ssq_ld = T;
       }

@@ -62,21 +62,62 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const __nv_bfloat16* __re
 }
 
 // action_in_proj (pi0_pytorch.py:303-323): h[t, n] = bf16(sum_k x[t, k] w[n, k] + b[n]), fp32 math.
+// ssq (optional): ssq[t] = sum_n bf16(h[t, n])^2, the row statistics of the first
+// input_layernorm for the folded-norm q|k|v GEMM.
 __global__ void __launch_bounds__(256) action_in_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                         const float* __restrict__ b, __nv_bfloat16* __restrict__ h,
-                                                        int din, int dout) {
+                                                        float* __restrict__ ssq, int din, int dout) {
   extern __shared__ float xs[];
+  __shared__ float red[32];
   pdl_wait();
   pdl_launch_dependents();  // let the next kernel's CTAs start their prologue / weight prefetch
   const int t = blockIdx.x;
   for (int k = threadIdx.x; k < din; k += blockDim.x) xs[k] = x[(size_t)t * din + k];
   __syncthreads();
+  float ss = 0.f;
   for (int n = threadIdx.x; n < dout; n += blockDim.x) {
     float acc = b[n];
     const float* wr = w + (size_t)n * din;
     for (int k = 0; k < din; ++k) acc = fmaf(xs[k], wr[k], acc);
-    h[(size_t)t * dout + n] = __float2bfloat16(acc);
+    const __nv_bfloat16 o = __float2bfloat16(acc);
+    h[(size_t)t * dout + n] = o;
+    const float f = __bfloat162float(o);
+    ss = fmaf(f, f, ss);
   }
+  if (ssq != nullptr) {
+    const float total = block_sum(ss, red);
+    if (threadIdx.x == 0) ssq[t] = total;
+  }
+}
+
+// Folds an adaRMS norm (modeling_gemma.py:82-116) into the projection W [rows, k]
+// that consumes its output:
+//   w_out[n, j] = bf16(W[n, j] * (1 + scale[j])),   b_out[n] = sum_j W[n, j] * shift[j]  (fp32)
+// so that W . bf16(h * rstd * (1 + scale) + shift) = rstd * (w_out . h) + b_out up
+// to bf16 rounding.  One warp per row, 8 columns per lane and pass.
+__global__ void __launch_bounds__(256) fold_adarms_kernel(const __nv_bfloat16* __restrict__ w, int rows, int k,
+                                                          const float* __restrict__ scale,
+                                                          const float* __restrict__ shift,
+                                                          __nv_bfloat16* __restrict__ w_out, float* __restrict__ b_out) {
+  const int r = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const __nv_bfloat16* wr = w + (size_t)r * k;
+  __nv_bfloat16* wo = w_out + (size_t)r * k;
+  float acc = 0.f;
+  for (int j0 = lane * 8; j0 < k; j0 += 256) {
+    const uint4 u = *reinterpret_cast<const uint4*>(wr + j0);
+    const __nv_bfloat16* bv = reinterpret_cast<const __nv_bfloat16*>(&u);
+    __align__(16) __nv_bfloat16 o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float v = __bfloat162float(bv[j]);
+      o[j] = __float2bfloat16(v * (1.0f + scale[j0 + j]));
+      acc = fmaf(v, shift[j0 + j], acc);
+    }
+    *reinterpret_cast<uint4*>(wo + j0) = *reinterpret_cast<const uint4*>(o);
+  }
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) b_out[r] = acc;
 }
 
 // Final adaRMS norm -> fp32 -> action_out_proj -> flow_ode Euler step
@@ -258,10 +299,32 @@ int rms_norm_run(const void* x, int ldx, const float* mod, const float* w, void*
 }
 
 int action_in_run(const float* x, const float* w, const float* b, void* h, int rows, int din, int dout,
-                  void* stream) {
+                  void* stream, float* ssq) {
   return launch_pdl(action_in_kernel, dim3(rows), dim3(256), din * sizeof(float),
                     reinterpret_cast<cudaStream_t>(stream), pdl_enabled(), x, w, b, static_cast<__nv_bfloat16*>(h),
-                    din, dout);
+                    ssq, din, dout);
+}
+
+int fold_adarms_run(const void* w, int rows, int k, const float* scale, const float* shift, void* w_out,
+                    float* b_out, void* stream) {
+  if (rows <= 0 || k <= 0 || k % 8 != 0) {
+    set_last_error("fold_adarms: bad shape rows=%d k=%d (k %% 8 == 0)", rows, k);
+    return PI05_ERR_SHAPE;
+  }
+  if (!aligned16(w) || !aligned16(w_out)) {
+    set_last_error("fold_adarms: weights must be 16-byte aligned");
+    return PI05_ERR_ALIGN;
+  }
+  const int blocks = (rows + 7) / 8;
+  fold_adarms_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(w), rows, k, scale, shift, static_cast<__nv_bfloat16*>(w_out), b_out);
+  count_launch();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_last_error("fold_adarms: %s", cudaGetErrorString(e));
+    return PI05_ERR_LAUNCH;
+  }
+  return PI05_OK;
 }
 
 int final_euler_run(const void* h, const float* mod, const float* w, const float* b, float* x_t, float* v_out,

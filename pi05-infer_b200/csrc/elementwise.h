@@ -8,8 +8,12 @@ namespace pi05 {
 // mod != null: adaRMS with mod = [scale | shift | gate] (fp32, 3*d); else plain RMSNorm with weight w (fp32, d).
 int rms_norm_run(const void* x, int ldx, const float* mod, const float* w, void* out, int ldo, int rows, int d,
                  float eps, void* stream);
+// ssq (optional): per-token sum of squares of the bf16 outputs, ssq[t].
 int action_in_run(const float* x, const float* w, const float* b, void* h, int rows, int din, int dout,
-                  void* stream);
+                  void* stream, float* ssq = nullptr);
+// w_out = bf16(w * (1 + scale)) column-wise, b_out = w . shift (fp32); w [rows, k], k % 8 == 0.
+int fold_adarms_run(const void* w, int rows, int k, const float* scale, const float* shift, void* w_out,
+                    float* b_out, void* stream);
 int final_euler_run(const void* h, const float* mod, const float* w, const float* b, float* x_t, float* v_out,
                     int rows, int d, int dout, float eps, float t, float delta, void* stream);
 int rope_table_run(const uint8_t* valid, int n_prefix, int mode, int rows, const float* inv_freq, int d, void* cos,

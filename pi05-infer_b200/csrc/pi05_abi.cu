@@ -39,7 +39,7 @@ unsigned long long* debug_trace_buffer() { return g_trace.load(); }
 
 extern "C" {
 
-int pi05_abi_version(void) { return 1; }
+int pi05_abi_version(void) { return 2; }
 
 const char* pi05_last_error(void) { return get_last_error(); }
 

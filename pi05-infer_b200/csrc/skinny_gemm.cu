@@ -102,6 +102,11 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
   // Fused norm of X (q|k|v only; its K range is at most STAGES k-blocks).
   constexpr bool kNormCapable = EPI == SK_EPI_QKV_ROPE && TOK == 64;
   const bool norm = kNormCapable && p.norm_ssq != nullptr;
+  // Folded norm of X (gate/up, q|k|v; 64-token tile): rstd per token (s_rstd) and
+  // the bias of the tile's 128 rows (in the fused-norm area; the two exclude each other).
+  constexpr bool kFoldCapable = TOK == 64 && (EPI == SK_EPI_GEGLU || EPI == SK_EPI_QKV_ROPE);
+  const bool fold = kFoldCapable && p.fold_ssq != nullptr;
+  float* s_fbias = s_mod;  // [kBM]
   float* stage_tile = reinterpret_cast<float*>(smem);
   constexpr bool kPushFits = recv_bytes<TOK>() > 0;
   const bool push = kPushFits && p.cluster && p.push;
@@ -235,11 +240,36 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
         }
       }
     }
+    if constexpr (kFoldCapable) {
+      if (fold) {
+        // The folded bias is a weight: staged before the grid-dependency wait.
+        const TileRows tr = tile_rows<EPI>(p, tile);
+        const int i = threadIdx.x - 64;
+        s_fbias[i] = split != 0 ? 0.f : (i < 64 ? p.fold_bias0[tr.row0 + i] : p.fold_bias1[tr.row1 + i - 64]);
+      }
+    }
     pdl_wait();
     const int q = warp & 3;
     const int row = q * 32 + lane;
     const int et = threadIdx.x - 64;
     if (p.trace != nullptr) t_pdl = globaltimer_ns();
+    if constexpr (kFoldCapable) {
+      if (fold) {
+        // rstd of token et from the producer's partial sums of squares (in order);
+        // these loads overlap the X load and the MMAs.
+        if (et < TOK) {
+          float ssv[kNormMaxParts];
+#pragma unroll
+          for (int j = 0; j < kNormMaxParts; ++j)
+            ssv[j] = (et < mt && j < p.fold_parts) ? __ldcg(p.fold_ssq + (size_t)j * p.fold_ld + tok0 + et) : 0.f;
+          float ss = 0.f;
+#pragma unroll
+          for (int j = 0; j < kNormMaxParts; ++j) ss += ssv[j];
+          s_rstd[et] = et < mt ? rsqrtf(ss / (float)p.fold_d + p.fold_eps) : 0.f;
+        }
+        named_bar_sync(1, kEpiThreads);  // s_rstd, s_fbias
+      }
+    }
     if constexpr (kNormCapable) {
       if (norm) {
         // Fused (ada)RMS norm of X.  The CTA's K range holds at most STAGES
@@ -329,6 +359,13 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 && EPI != SK_EPI_QKV_ROP
       for (int c = 0; c < TOK / 32; ++c) {
         float v[32];
         tmem_ld32(tmem_acc + ((uint32_t)(q * 32) << 16) + c * 32, v);
+        if constexpr (kFoldCapable) {
+          if (fold) {  // each split scales its partial; split 0 adds the bias
+            const float fb = s_fbias[row];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = fmaf(v[j], s_rstd[c * 32 + j], fb);
+          }
+        }
 #pragma unroll
         for (int j = 0; j < 32; ++j) stage_tile[(c * 32 + j) * kBM + row] = v[j];
       }
@@ -481,8 +518,8 @@ template <int EPI, int TOK, int STAGES>
 int launch_one(const SkinnyParams& p, const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x,
                int tok_tiles, cudaStream_t stream) {
   constexpr int kSmemMax = smem_bytes<TOK, STAGES>();
-  // Without the fused norm its area is left out, so two CTAs fit per SM.
-  const int kSmem = p.norm_ssq != nullptr ? kSmemMax : smem_base_bytes<TOK, STAGES>();
+  // Without the fused or folded norm their area is left out.
+  const int kSmem = (p.norm_ssq != nullptr || p.fold_ssq != nullptr) ? kSmemMax : smem_base_bytes<TOK, STAGES>();
   auto kern = skinny_gemm_kernel<EPI, TOK, STAGES>;
   static bool attr_done[16] = {false};
   int dev = 0;
@@ -656,11 +693,19 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
                    "norm_d == output width, aligned operands");
     return PI05_ERR_SHAPE;
   }
+  if (p.fold_ssq != nullptr &&
+      ((epi != SK_EPI_GEGLU && epi != SK_EPI_QKV_ROPE) || p.m_tok > 64 || p.fold_parts <= 0 ||
+       p.fold_parts > kNormMaxParts || p.fold_d <= 0 || p.fold_ld < p.m_tok || p.fold_bias0 == nullptr ||
+       p.fold_bias1 == nullptr || p.norm_ssq != nullptr)) {
+    set_last_error("skinny_gemm: folded norm needs gate/up or q|k|v, <= 64 tokens, 1..%d parts, both bias "
+                   "vectors, no fused norm", kNormMaxParts);
+    return PI05_ERR_SHAPE;
+  }
   if (p.norm_ssq != nullptr) {
     p.norm_x = static_cast<const __nv_bfloat16*>(x);
     p.norm_ldx = ldx;
   }
-  const bool fused_rows = p.norm_ssq != nullptr || p.row_ssq != nullptr;  // small-token kernel only
+  const bool fused_rows = p.norm_ssq != nullptr || p.row_ssq != nullptr || p.fold_ssq != nullptr;  // small-token kernel only
   if (p.m_tok >= kWideMinTokens && !wide_disabled() && !fused_rows) {
     int n_cols = 0;
     if (epi == SK_EPI_GEGLU)

@@ -71,6 +71,21 @@ struct SkinnyParams {
   const float* norm_mod = nullptr;
   int norm_d = 0;
   float norm_eps = 0.f;
+  // Folded (ada)RMS norm of the X operand (GEGLU / QKV_ROPE, <= 64 tokens): X holds
+  // the raw residual stream h and the weights carry the norm's (1 + scale) in their
+  // columns (pi05_fold_adarms), so the norm reduces to a per-token factor and a
+  // per-row bias applied to the accumulator before the epilogue:
+  //   y[r, t] = acc[r, t] * rstd[t] + bias(r)      (bias added by split 0 only)
+  //   rstd[t] = rsqrt(sum_j fold_ssq[j * fold_ld + t] / fold_d + fold_eps)
+  // over fold_parts partial sums in order; bias(r) = fold_bias0[weight row] for the
+  // rows of map 0 and fold_bias1[weight row] for those of map 1 (W . shift, fp32).
+  const float* fold_ssq = nullptr;
+  int fold_parts = 0;
+  int fold_ld = 0;
+  int fold_d = 0;
+  float fold_eps = 0.f;
+  const float* fold_bias0 = nullptr;
+  const float* fold_bias1 = nullptr;
   // L2 prefetch issued by every CTA for its share of these ranges (e.g. the same
   // op's weights of the next layer), so later launches read them from L2.
   const void* pf0 = nullptr;

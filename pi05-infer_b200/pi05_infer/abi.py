@@ -22,6 +22,12 @@ class Pi05ExpertLayer(ctypes.Structure):
     ]
 
 
+class Pi05ExpertFold(ctypes.Structure):
+    _fields_ = [
+        ("w_qkv", _P), ("w_gate", _P), ("w_up", _P), ("b_qkv", _P), ("b_gate", _P), ("b_up", _P),
+    ]
+
+
 class Pi05ExpertPlan(ctypes.Structure):
     _fields_ = [
         ("depth", _I), ("width", _I), ("mlp_dim", _I), ("n_q_heads", _I), ("n_kv_heads", _I), ("head_dim", _I),
@@ -32,6 +38,7 @@ class Pi05ExpertPlan(ctypes.Structure):
         ("rope_cos", _P), ("rope_sin", _P), ("key_valid", _P),
         ("x_t", _P), ("v_t", _P), ("h", _P), ("xn", _P), ("q", _P), ("attn", _P), ("act", _P),
         ("workspace", _P), ("workspace_bytes", _Z), ("attn_splits", _I), ("trace", _P),
+        ("fold", ctypes.POINTER(Pi05ExpertFold)),
     ]
 
 
@@ -46,6 +53,7 @@ _EXTRA = {
     "pi05_denoise_loop": (_I, [ctypes.POINTER(Pi05ExpertPlan), _P]),
     "pi05_denoise_loop_persistent": (_I, [ctypes.POINTER(Pi05ExpertPlan), _P]),
     "pi05_trace_slots": (_I, []),
+    "pi05_fold_adarms": (_I, [_P, _I, _I, _P, _P, _P, _P, _P]),
 }
 _lib.SIGNATURES.update(_EXTRA)
 
@@ -96,6 +104,15 @@ def adarms_table(timesteps, width, w_tin, b_tin, w_tout, b_tout, w_dense, b_dens
     _lib.call("pi05_adarms_table", ptr(timesteps), timesteps.numel(), width, ptr(w_tin), ptr(b_tin), ptr(w_tout),
               ptr(b_tout), ptr(w_dense), ptr(b_dense), n_norm, ptr(table), ptr(ws), ws.numel(),
               stream if stream is not None else stream_of(table.device))
+
+
+def fold_adarms(w, scale, shift, w_out, b_out, stream=None):
+    """``w_out = bf16(w * (1 + scale))`` column-wise and ``b_out = w @ shift`` (fp32)."""
+    _bind()
+    rows, k = w.shape
+    assert w_out.shape == w.shape and b_out.numel() == rows and scale.numel() == k and shift.numel() == k
+    _lib.call("pi05_fold_adarms", ptr(w), rows, k, ptr(scale), ptr(shift), ptr(w_out), ptr(b_out),
+              stream if stream is not None else stream_of(w.device))
 
 
 def denoise_loop(plan: Pi05ExpertPlan, stream: int):

@@ -135,6 +135,23 @@ class DenoiseRunner:
         self.ts = timesteps(num_steps)
         self._host_ts = (ctypes.c_float * (num_steps + 1))(*[float(v) for v in self.ts])
         self.table = torch.empty((num_steps, weights.n_norm * 3 * s.width), **f32)
+        # Folded norms (default for <= 64 tokens, PI05_FOLD_NORM=0 to keep the norm
+        # kernels): per step and layer, q|k|v and gate/up with that step's
+        # input_layernorm / post_attention_layernorm (1 + scale) folded into their
+        # columns, plus the biases W . shift (pi05_fold_adarms).  The step's
+        # weight stream keeps its size; the copies cost num_steps x 22 MB per layer
+        # of HBM (4 GB for the 10-step Gemma-300M loop).
+        self.fold = None
+        if horizon <= 64 and os.environ.get("PI05_FOLD_NORM", "1") != "0":
+            n = num_steps * s.depth
+            self.fold = {
+                "w_qkv": torch.empty((n, s.qkv_dim, s.width), **bf),
+                "w_gate": torch.empty((n, s.mlp_dim, s.width), **bf),
+                "w_up": torch.empty((n, s.mlp_dim, s.width), **bf),
+                "b_qkv": torch.empty((n, s.qkv_dim), **f32),
+                "b_gate": torch.empty((n, s.mlp_dim), **f32),
+                "b_up": torch.empty((n, s.mlp_dim), **f32),
+            }
         self.build_table()
         self._layers = (abi.Pi05ExpertLayer * s.depth)()
         for i, L in enumerate(weights.layers):
@@ -154,6 +171,13 @@ class DenoiseRunner:
             v_t=self.v_t.data_ptr(), h=self.h.data_ptr(), xn=self.xn.data_ptr(), q=self.q.data_ptr(),
             attn=self.attn.data_ptr(), act=self.act.data_ptr(), workspace=self.ws.data_ptr(),
             workspace_bytes=self.ws.numel(), attn_splits=attn_splits)
+        if self.fold is not None:
+            fd = self.fold
+            self._fold = (abi.Pi05ExpertFold * (num_steps * s.depth))()
+            for i in range(num_steps * s.depth):
+                self._fold[i] = abi.Pi05ExpertFold(*(fd[k][i].data_ptr() for k in
+                                                     ("w_qkv", "w_gate", "w_up", "b_qkv", "b_gate", "b_up")))
+            self.plan.fold = ctypes.cast(self._fold, ctypes.POINTER(abi.Pi05ExpertFold))
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         # pi05_denoise_loop (one launch per kernel phase) by default;
         # pi05_denoise_loop_persistent (one launch for the loop) on request or with
@@ -176,6 +200,24 @@ class DenoiseRunner:
         ts_dev = self.ts[: self.num_steps].to(self.device)
         abi.adarms_table(ts_dev, s.width, g["time_mlp_in.weight"], g["time_mlp_in.bias"], g["time_mlp_out.weight"],
                          g["time_mlp_out.bias"], self.w.w_dense, self.w.b_dense, self.w.n_norm, self.table, self.ws)
+        self.build_fold()
+
+    def build_fold(self) -> None:
+        """Fold every step's layer norms into the q|k|v and gate/up copies, in place
+        (after the table; a captured graph keeps its addresses)."""
+        if self.fold is None:
+            return
+        s = self.w.shape
+        W = s.width
+        tab = self.table.view(self.num_steps, self.w.n_norm, 3, W)  # [scale | shift | gate] per norm
+        fd = self.fold
+        for st in range(self.num_steps):
+            for l, L in enumerate(self.w.layers):
+                i = st * s.depth + l
+                m1, m2 = tab[st, 2 * l], tab[st, 2 * l + 1]  # input_layernorm, post_attention_layernorm
+                abi.fold_adarms(L["w_qkv"], m1[0], m1[1], fd["w_qkv"][i], fd["b_qkv"][i])
+                abi.fold_adarms(L["w_gate"], m2[0], m2[1], fd["w_gate"][i], fd["b_gate"][i])
+                abi.fold_adarms(L["w_up"], m2[0], m2[1], fd["w_up"][i], fd["b_up"][i])
 
     def set_prefix(self, kv: Sequence[Tuple[torch.Tensor, torch.Tensor]], prefix_valid: torch.Tensor) -> None:
         """Fill the prefix rows of every layer's static KV buffer (``prime_kv_static``)

@@ -105,6 +105,45 @@ def test_attention_op(t, s):
         assert _cos(out.float().cpu(), ref) > 0.9999
 
 
+def test_fold_adarms_op():
+    # w_out = bf16(w * (1 + scale)) matches torch bit for bit (same fp32 product,
+    # one rounding); b_out = w . shift within fp32 summation-order noise.
+    g = torch.Generator(device="cuda").manual_seed(8)
+    w = (torch.randn(2560, 1024, device="cuda", generator=g) * 0.02).bfloat16()
+    scale = torch.randn(1024, device="cuda", generator=g) * 0.5
+    shift = torch.randn(1024, device="cuda", generator=g) * 0.5
+    w_out = torch.empty_like(w)
+    b_out = torch.empty(2560, device="cuda")
+    abi.fold_adarms(w, scale, shift, w_out, b_out)
+    assert torch.equal(w_out, (w.float() * (1.0 + scale)).bfloat16())
+    ref = w.double() @ shift.double()
+    assert (b_out.double() - ref).abs().max().item() < 1e-4
+
+
+def test_folded_norm_matches_norm_kernels(setup):
+    # One step of the folded-norm schedule (no norm kernels inside the layers)
+    # against the same step with explicit adaRMS norm kernels: velocity cosine and
+    # max-abs within the denoise tolerance.
+    sd, kv, noise, w = setup
+    pad = torch.ones(968, dtype=torch.bool)
+    outs = []
+    for folded in (True, False):
+        r = DenoiseRunner(w, prefix_len=968, num_steps=10)
+        assert r.fold is not None
+        if not folded:
+            r.plan.fold = None
+        r.set_prefix([(k.cuda(), v.cuda()) for k, v in kv], pad.cuda())
+        r.x_t.copy_(noise.cuda())
+        abi.rope_table(r.key_valid, 968, 1, 50, r.inv_freq, 256, r.rope_cos, r.rope_sin)
+        for s in range(3):
+            abi.denoise_step(r.plan, s, abi.stream_of(r.device))
+        outs.append((r.v_t.clone().cpu(), r.x_t.clone().cpu()))
+        del r
+    assert ops.read_device_status() == 0
+    assert _cos(outs[0][0], outs[1][0]) >= 0.9999
+    assert (outs[0][1] - outs[1][1]).abs().max().item() <= 2e-2
+
+
 def test_rms_norm_ops():
     g = torch.Generator(device="cuda").manual_seed(6)
     x = torch.randn(50, 1024, device="cuda", generator=g).bfloat16()

@@ -40,7 +40,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_host_validation_without_gpu():
     L = _lib.lib()
-    assert L.pi05_abi_version() == 1
+    assert L.pi05_abi_version() == 2
     ws = L.pi05_workspace_bytes(50, 1018)
     assert ws > 40 << 20
     assert L.pi05_gate_up_geglu(None, None, None, None, 50, 4096, 1024, None, 0, None) == 1
