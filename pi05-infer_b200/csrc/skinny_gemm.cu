@@ -644,11 +644,15 @@ int skinny_choose_splits_cluster(int n_tiles, int kb_total, int tok_tiles, int s
   return best;
 }
 
-// PI05_L2_PREFETCH=0 in the environment drops the next-layer L2 prefetch ranges.
+// PI05_L2_PREFETCH=1 in the environment issues the next-layer L2 prefetch ranges
+// that callers pass (pf0 / pf1).  Off by default: the small-token GEMMs issue their
+// first ring of weight TMA loads before the grid-dependency wait, which already
+// covers most of a split's K range, and on B200 the extra prefetch stream made the
+// denoise step slower (760 -> 746 us/step without it).
 bool l2_prefetch_enabled() {
   static int v = [] {
     const char* e = getenv("PI05_L2_PREFETCH");
-    return (e != nullptr && e[0] == '0') ? 0 : 1;
+    return (e != nullptr && e[0] == '1') ? 1 : 0;
   }();
   return v != 0;
 }
