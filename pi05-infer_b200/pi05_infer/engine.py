@@ -72,6 +72,10 @@ class OpenPi0Inference:
         self._denoise = None
         self._prefix = None
         self._graphs = {}
+        self._kv_host = None      # host copy of the key masks last written to the device
+        self._kv_pinned = None
+        self._ids_pinned = None   # pinned int32 staging of the prompt ids
+        self._ids_event = None
         if state_dict is not None:
             self.load_state_dict(state_dict)
 
@@ -189,7 +193,39 @@ class OpenPi0Inference:
         return torch.cat([obs.image_masks[n].to(self.device).reshape(-1, 1).expand(-1, npatch).reshape(-1)
                           for n in obs.images] + [obs.tokenized_prompt_mask.reshape(-1).to(self.device)])
 
+    def _host_key_valid(self, obs: Observation) -> Optional[torch.Tensor]:
+        """The prefix key-validity mask built on the host (uint8), or None when a mask
+        of the observation lives on the device."""
+        npatch = self.config.siglip.num_patches
+        parts = []
+        for n in obs.images:
+            m = obs.image_masks[n]
+            if m.is_cuda:
+                return None
+            parts.append(m.reshape(-1, 1).expand(-1, npatch).reshape(-1))
+        pm = obs.tokenized_prompt_mask
+        if pm.is_cuda:
+            return None
+        parts.append(pm.reshape(-1))
+        return torch.cat(parts).to(torch.uint8)
+
+    def _refresh_key_valid(self, obs: Observation) -> None:
+        """Key masks of the captured pipeline: built on the host and copied (pinned,
+        asynchronously) only when they differ from the last call's."""
+        hv = self._host_key_valid(obs)
+        if hv is None:
+            self._set_key_valid(self._prefix_valid(obs))
+            return
+        if self._kv_host is not None and torch.equal(hv, self._kv_host):
+            return
+        prefix, den = self._runners()
+        pinned = hv.pin_memory()
+        prefix.key_valid.copy_(pinned, non_blocking=True)
+        den.key_valid[: self.prefix_len].copy_(pinned, non_blocking=True)
+        self._kv_host, self._kv_pinned = hv, pinned  # the pinned copy stays alive until replaced
+
     def _set_key_valid(self, valid: torch.Tensor) -> None:
+        self._kv_host = None  # the device masks no longer match the host cache
         prefix, den = self._runners()
         prefix.key_valid.copy_(valid.to(torch.uint8))
         den.key_valid[: self.prefix_len].copy_(valid.to(torch.uint8))
@@ -212,10 +248,23 @@ class OpenPi0Inference:
                 self._set_key_valid(self._prefix_valid(observation))
                 self.capture_full(observation, noise.to(self.device).float())
                 self._full_key = key
-            self._set_key_valid(self._prefix_valid(observation))
+            self._refresh_key_valid(observation)
             for i, n in enumerate(observation.images):
                 self._static_imgs[i: i + 1].copy_(observation.images[n], non_blocking=True)
-            self._ids.copy_(observation.tokenized_prompt.reshape(-1), non_blocking=True)
+            ids = observation.tokenized_prompt.reshape(-1)
+            if ids.is_cuda:
+                self._ids.copy_(ids)
+            else:
+                # int32 on the host into a pinned buffer, then one asynchronous copy;
+                # the buffer is rewritten only after the previous call's copy read it.
+                if self._ids_pinned is None or self._ids_pinned.numel() != ids.numel():
+                    self._ids_pinned = torch.empty(ids.numel(), dtype=torch.int32).pin_memory()
+                    self._ids_event = torch.cuda.Event()
+                else:
+                    self._ids_event.synchronize()
+                self._ids_pinned.copy_(ids)
+                self._ids.copy_(self._ids_pinned, non_blocking=True)
+                self._ids_event.record(torch.cuda.current_stream(self.device))
             den.x_t.copy_(noise.reshape(den.horizon, den.action_dim), non_blocking=True)
             self._graphs["full"].replay()
             actions = den.x_t
@@ -244,8 +293,11 @@ class OpenPi0Inference:
 
     # ------------------------------------------------------------ bench hooks
     def synthetic_observation(self, seed: int = 100) -> Observation:
+        """Seeded synthetic observation in pinned host memory (the form a serving
+        client hands over; pinned images copy to the device asynchronously)."""
         g = torch.Generator().manual_seed(seed)
-        imgs = {f"cam{i}": (torch.rand((1, 3, 224, 224), generator=g) * 2 - 1) for i in range(self.num_views)}
+        imgs = {f"cam{i}": (torch.rand((1, 3, 224, 224), generator=g) * 2 - 1).pin_memory()
+                for i in range(self.num_views)}
         masks = {k: torch.ones(1, dtype=torch.bool) for k in imgs}
         toks = torch.randint(0, synthetic.VOCAB_SIZE, (1, self.prompt_len), generator=g)
         return Observation(imgs, masks, toks, torch.ones(1, self.prompt_len, dtype=torch.bool),

@@ -94,4 +94,8 @@ def test_sample_actions_end_to_end_small():
     eng.use_cuda_graph = True
     assert (act3 - act3_eager).abs().max().item() <= 1e-3
     assert (act3 - act).abs().max().item() > 1e-3  # the new inputs were used
+    # back to the first observation: its key masks (cached on the host) are written
+    # again after the eager call and the changed masks
+    act4 = eng.sample_actions(obs, noise=noise)["actions"][0].cpu()
+    assert (act4 - act).abs().max().item() <= 1e-3
     assert ops.read_device_status() == 0
