@@ -259,6 +259,12 @@ typedef struct Pi05PrefixLayer {
   const float* ln2_w;   /* post_attention_layernorm weight fp32 [width] */
   void* k_cache;        /* [hkv, kv_rows, d]: rows [0, tokens) receive this layer's prefix K */
   void* v_cache;
+  /* Folded copies for the folded-norm path, or NULL (then the norm kernels run):
+   * w_qkv with (1 + ln1_w) and w_gate / w_up with (1 + ln2_w) folded into their
+   * columns (pi05_fold_adarms with a zero shift). */
+  const void* wf_qkv;
+  const void* wf_gate;
+  const void* wf_up;
 } Pi05PrefixLayer;
 
 typedef struct Pi05PrefixPlan {
@@ -279,6 +285,10 @@ typedef struct Pi05PrefixPlan {
   void* workspace;
   size_t workspace_bytes;
   int kv_only_last_layer;        /* 1: the last layer stops after K/V (prefix_last_layer.py:46-112) */
+  float* row_stats;              /* [width / 64, tokens] fp32 scratch for the folded norms, or NULL.  With
+                                    it and every layer's wf_* set, no norm kernel runs: the residual
+                                    GEMMs write per-64-column sums of squares of h, and q|k|v and
+                                    gate/up scale their accumulators by each token's rstd. */
 } Pi05PrefixPlan;
 
 /* Prefix LM forward with use_cache=True: fills every layer's K/V cache rows

@@ -90,6 +90,30 @@ __global__ void __launch_bounds__(256) action_in_kernel(const float* __restrict_
   }
 }
 
+// Row statistics of x [rows, d] for a folded RMS norm: ssq[part * ld + row] =
+// sum over the part's `part_cols` columns of x^2 (x bf16, fp32 sums).  One CTA per
+// row, 8 columns per thread; part_cols is a multiple of 8 and at most 256.
+__global__ void __launch_bounds__(256) row_ssq_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int d,
+                                                      int part_cols, float* __restrict__ ssq, int ld) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int row = blockIdx.x, c = threadIdx.x * 8;
+  float s = 0.f;
+  if (c < d) {
+    const uint4 u = *reinterpret_cast<const uint4*>(x + (size_t)row * ldx + c);
+    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float f = __bfloat162float(b[j]);
+      s = fmaf(f, f, s);
+    }
+  }
+  // Sum over the part's threads (part_cols / 8 consecutive lanes, a power of two).
+  const int tpp = part_cols / 8;
+  for (int o = 1; o < tpp; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (c < d && (threadIdx.x % tpp) == 0) ssq[(size_t)(c / part_cols) * ld + row] = s;
+}
+
 // Folds an adaRMS norm (modeling_gemma.py:82-116) into the projection W [rows, k]
 // that consumes its output:
 //   w_out[n, j] = bf16(W[n, j] * (1 + scale[j])),   b_out[n] = sum_j W[n, j] * shift[j]  (fp32)
@@ -303,6 +327,16 @@ int action_in_run(const float* x, const float* w, const float* b, void* h, int r
   return launch_pdl(action_in_kernel, dim3(rows), dim3(256), din * sizeof(float),
                     reinterpret_cast<cudaStream_t>(stream), pdl_enabled(), x, w, b, static_cast<__nv_bfloat16*>(h),
                     ssq, din, dout);
+}
+
+int row_ssq_run(const void* x, int ldx, int rows, int d, int part_cols, float* ssq, int ld, void* stream) {
+  if (rows <= 0 || d <= 0 || d > 2048 || d % 8 || ldx % 8 || part_cols < 8 || part_cols > 256 ||
+      (part_cols & (part_cols - 1)) || d % part_cols || ld < rows || !aligned16(x)) {
+    set_last_error("row_ssq: unsupported shape rows=%d d=%d part=%d", rows, d, part_cols);
+    return PI05_ERR_SHAPE;
+  }
+  return launch_pdl(row_ssq_kernel, dim3(rows), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), pdl_enabled(),
+                    static_cast<const __nv_bfloat16*>(x), ldx, d, part_cols, ssq, ld);
 }
 
 int fold_adarms_run(const void* w, int rows, int k, const float* scale, const float* shift, void* w_out,

@@ -11,6 +11,8 @@ int rms_norm_run(const void* x, int ldx, const float* mod, const float* w, void*
 // ssq (optional): per-token sum of squares of the bf16 outputs, ssq[t].
 int action_in_run(const float* x, const float* w, const float* b, void* h, int rows, int din, int dout,
                   void* stream, float* ssq = nullptr);
+// ssq[part * ld + row] = sum of x^2 over each part_cols-column part of a row (d <= 2048).
+int row_ssq_run(const void* x, int ldx, int rows, int d, int part_cols, float* ssq, int ld, void* stream);
 // w_out = bf16(w * (1 + scale)) column-wise, b_out = w . shift (fp32); w [rows, k], k % 8 == 0.
 int fold_adarms_run(const void* w, int rows, int k, const float* scale, const float* shift, void* w_out,
                     float* b_out, void* stream);

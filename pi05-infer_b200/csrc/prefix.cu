@@ -12,6 +12,7 @@
 //   h = h + bf16(GeGLU(hn) @ Wd^T)
 // The last layer stops after K/V (prefix_last_layer.py:46-112).
 #include <cmath>
+#include <cstdlib>
 
 #include "../../include/pi05_b200.h"
 #include "attention.h"
@@ -49,6 +50,16 @@ __global__ void __launch_bounds__(256) embed_tokens_kernel(const __nv_bfloat16* 
 }
 
 inline bool nz(const void* p) { return p != nullptr; }
+
+// PI05_FOLD_NORM=0 in the environment keeps the RMSNorm kernels (A/B and parity
+// tests of the folded path).
+bool prefix_fold_enabled() {
+  static int v = [] {
+    const char* e = getenv("PI05_FOLD_NORM");
+    return (e != nullptr && e[0] == '0') ? 0 : 1;
+  }();
+  return v != 0;
+}
 
 SkinnyParams base_params(const Workspace& ws) {
   SkinnyParams sp;
@@ -104,11 +115,30 @@ int pi05_prefix_forward(const Pi05PrefixPlan* P, void* stream) {
   auto* act = static_cast<__nv_bfloat16*>(P->act);
   const float scale = 1.0f / std::sqrt((float)D);
 
+  // Folded norms: the RMSNorm weights (1 + w) live in folded copies of q|k|v and
+  // gate/up; the residual GEMMs (o_proj, down_proj) write per-part sums of squares
+  // of h to row_stats, and q|k|v / gate/up scale each token's accumulator by its
+  // rstd (Gemma RMSNorm, fp32 statistics: modeling_gemma.py:94-99), so no norm
+  // kernel runs.  The embeddings' statistics come from one row_ssq launch.
+  bool fold = P->row_stats != nullptr && prefix_fold_enabled() && W <= 2048 && W % 64 == 0 &&
+              row_ssq_parts(T, W) == W / 64;
+  for (int l = 0; fold && l < P->depth; ++l)
+    fold = nz(P->layers[l].wf_qkv) && nz(P->layers[l].wf_gate) && nz(P->layers[l].wf_up);
+  const int parts = W / 64;
+  auto fold_params = [&](SkinnyParams& sp) {
+    sp.fold_ssq = P->row_stats;
+    sp.fold_parts = parts;
+    sp.fold_ld = T;
+    sp.fold_d = W;
+    sp.fold_eps = P->eps;
+  };
+
   int rc = rope_table_run(P->key_valid, T, 0, T, P->inv_freq, D, P->rope_cos, P->rope_sin, stream);
+  if (rc == PI05_OK && fold) rc = row_ssq_run(h, W, T, W, 64, P->row_stats, T, stream);
   for (int l = 0; l < P->depth && rc == PI05_OK; ++l) {
     const Pi05PrefixLayer& L = P->layers[l];
     const bool last = (l == P->depth - 1);
-    rc = rms_norm_run(h, W, nullptr, L.ln1_w, xn, W, T, W, P->eps, stream);
+    if (!fold) rc = rms_norm_run(h, W, nullptr, L.ln1_w, xn, W, T, W, P->eps, stream);
     if (rc) break;
     {
       SkinnyParams sp = base_params(ws);
@@ -126,7 +156,9 @@ int pi05_prefix_forward(const Pi05PrefixPlan* P, void* stream) {
       sp.n_kv_heads = HKV;
       sp.head_dim = D;
       const int rows = (HQ + 2 * HKV) * D;
-      rc = skinny_gemm_run(SK_EPI_QKV_ROPE, sp, L.w_qkv, L.w_qkv, rows, rows, xn, W, 0, stream);
+      if (fold) fold_params(sp);
+      const void* wq = fold ? L.wf_qkv : L.w_qkv;
+      rc = skinny_gemm_run(SK_EPI_QKV_ROPE, sp, wq, wq, rows, rows, fold ? h : xn, W, 0, stream);
       if (rc) break;
     }
     if (last && P->kv_only_last_layer) break;
@@ -158,10 +190,14 @@ int pi05_prefix_forward(const Pi05PrefixPlan* P, void* stream) {
       sp.resid = h;
       sp.ldr = W;
       sp.gate = nullptr;
+      if (fold) {
+        sp.row_ssq = P->row_stats;
+        sp.ssq_ld = T;
+      }
       rc = skinny_gemm_run(SK_EPI_GATED_RESID, sp, L.w_o, L.w_o, W, W, attn, HQ * D, 0, stream);
       if (rc) break;
     }
-    rc = rms_norm_run(h, W, nullptr, L.ln2_w, xn, W, T, W, P->eps, stream);
+    if (!fold) rc = rms_norm_run(h, W, nullptr, L.ln2_w, xn, W, T, W, P->eps, stream);
     if (rc) break;
     {
       SkinnyParams sp = base_params(ws);
@@ -170,7 +206,9 @@ int pi05_prefix_forward(const Pi05PrefixPlan* P, void* stream) {
       sp.n_tiles = F / 64;
       sp.out = act;
       sp.ldo = F;
-      rc = skinny_gemm_run(SK_EPI_GEGLU, sp, L.w_gate, L.w_up, F, F, xn, W, 0, stream);
+      if (fold) fold_params(sp);
+      rc = skinny_gemm_run(SK_EPI_GEGLU, sp, fold ? L.wf_gate : L.w_gate, fold ? L.wf_up : L.w_up, F, F,
+                           fold ? h : xn, W, 0, stream);
       if (rc) break;
     }
     {
@@ -183,6 +221,10 @@ int pi05_prefix_forward(const Pi05PrefixPlan* P, void* stream) {
       sp.resid = h;
       sp.ldr = W;
       sp.gate = nullptr;
+      if (fold) {
+        sp.row_ssq = P->row_stats;
+        sp.ssq_ld = T;
+      }
       rc = skinny_gemm_run(SK_EPI_GATED_RESID, sp, L.w_down, L.w_down, W, W, act, F, 0, stream);
       if (rc) break;
     }

@@ -606,6 +606,10 @@ int num_sms() {
 
 }  // namespace
 
+int row_ssq_parts(int m_tok, int n_cols) {
+  return (m_tok >= kWideMinTokens && !wide_disabled()) ? n_cols / 64 : n_cols / 128;
+}
+
 int skinny_choose_splits(int n_tiles, int kb_total, int tok_tiles, int sms) {
   // Minimise (waves x k-blocks per CTA) plus a small per-split reduction cost.
   int best = 1;
@@ -697,20 +701,30 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
                    "norm_d == output width, aligned operands");
     return PI05_ERR_SHAPE;
   }
-  if (p.fold_ssq != nullptr &&
-      ((epi != SK_EPI_GEGLU && epi != SK_EPI_QKV_ROPE) || p.m_tok > 64 || p.fold_parts <= 0 ||
-       p.fold_parts > kNormMaxParts || p.fold_d <= 0 || p.fold_ld < p.m_tok || p.fold_bias0 == nullptr ||
-       p.fold_bias1 == nullptr || p.norm_ssq != nullptr)) {
-    set_last_error("skinny_gemm: folded norm needs gate/up or q|k|v, <= 64 tokens, 1..%d parts, both bias "
-                   "vectors, no fused norm", kNormMaxParts);
-    return PI05_ERR_SHAPE;
+  const bool wide_ok = p.m_tok >= kWideMinTokens && !wide_disabled();
+  if (p.fold_ssq != nullptr) {
+    // Small-token kernel: <= 64 tokens, rstd and the folded bias (denoise adaRMS);
+    // many-token kernel: rstd only (the prefix LM's RMSNorm has no shift).
+    bool bad = (epi != SK_EPI_GEGLU && epi != SK_EPI_QKV_ROPE) || p.fold_parts <= 0 || p.fold_d <= 0 ||
+               p.fold_ld < p.m_tok || p.norm_ssq != nullptr;
+    if (wide_ok)
+      bad = bad || p.fold_bias0 != nullptr || p.fold_bias1 != nullptr ||
+            (epi == SK_EPI_QKV_ROPE && p.head_dim != 256);
+    else
+      bad = bad || p.m_tok > 64 || p.fold_parts > kNormMaxParts || p.fold_bias0 == nullptr || p.fold_bias1 == nullptr;
+    if (bad) {
+      set_last_error("skinny_gemm: folded norm needs gate/up or q|k|v; <= 64 tokens with 1..%d parts and both bias "
+                     "vectors, or >= %d tokens without bias; no fused norm", kNormMaxParts, kWideMinTokens);
+      return PI05_ERR_SHAPE;
+    }
   }
   if (p.norm_ssq != nullptr) {
     p.norm_x = static_cast<const __nv_bfloat16*>(x);
     p.norm_ldx = ldx;
   }
-  const bool fused_rows = p.norm_ssq != nullptr || p.row_ssq != nullptr || p.fold_ssq != nullptr;  // small-token kernel only
-  if (p.m_tok >= kWideMinTokens && !wide_disabled() && !fused_rows) {
+  // The fused and producer-side norms exist only in the small-token kernel.
+  const bool skinny_only = p.norm_ssq != nullptr || p.norm_out != nullptr;
+  if (wide_ok && !skinny_only) {
     int n_cols = 0;
     if (epi == SK_EPI_GEGLU)
       n_cols = p.n_tiles * 64;

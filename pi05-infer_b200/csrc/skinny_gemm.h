@@ -45,8 +45,10 @@ struct SkinnyParams {
   int n_kv_heads = 0;
   int head_dim = 0;
   // Row statistics for a following RMS norm (STORE / GATED_RESID): when set, the
-  // sum of squares of every token's bf16 outputs within each 128-row weight tile is
-  // written to row_ssq[tile * ssq_ld + token] (fixed summation order).
+  // sum of squares of every token's bf16 outputs within each part of the output
+  // columns is written to row_ssq[part * ssq_ld + token] (fixed summation order).
+  // A part is a 128-row weight tile in the small-token kernel and a 64-column slab
+  // in the many-token one; row_ssq_parts() gives the count for a launch.
   float* row_ssq = nullptr;
   int ssq_ld = 0;
   // Normalised copy of the output for the next (ada)RMS norm (GATED_RESID, push-form
@@ -71,7 +73,7 @@ struct SkinnyParams {
   const float* norm_mod = nullptr;
   int norm_d = 0;
   float norm_eps = 0.f;
-  // Folded (ada)RMS norm of the X operand (GEGLU / QKV_ROPE, <= 64 tokens): X holds
+  // Folded (ada)RMS norm of the X operand (GEGLU / QKV_ROPE): X holds
   // the raw residual stream h and the weights carry the norm's (1 + scale) in their
   // columns (pi05_fold_adarms), so the norm reduces to a per-token factor and a
   // per-row bias applied to the accumulator before the epilogue:
@@ -79,6 +81,9 @@ struct SkinnyParams {
   //   rstd[t] = rsqrt(sum_j fold_ssq[j * fold_ld + t] / fold_d + fold_eps)
   // over fold_parts partial sums in order; bias(r) = fold_bias0[weight row] for the
   // rows of map 0 and fold_bias1[weight row] for those of map 1 (W . shift, fp32).
+  // The small-token kernel (<= 64 tokens) needs both bias vectors; the many-token
+  // kernel applies rstd only (plain RMSNorm: its (1 + w) lives in the weights) and
+  // takes no bias.
   const float* fold_ssq = nullptr;
   int fold_parts = 0;
   int fold_ld = 0;
@@ -109,6 +114,9 @@ struct SkinnyParams {
 constexpr int kNormMaxK = 1024;    // fused-norm X operands: K range staged in shared memory
 constexpr int kNormMaxParts = 16;  // fused-norm partial sums of squares per token
 
+// Parts per token that a GATED_RESID / STORE launch of m_tok tokens and n_cols
+// output columns writes to row_ssq (the kernel it will run on decides).
+int row_ssq_parts(int m_tok, int n_cols);
 int skinny_choose_splits(int n_tiles, int kb_total, int tok_tiles, int sms);
 int skinny_choose_splits_cluster(int n_tiles, int kb_total, int tok_tiles, int sms, int max_cluster);
 // PI05_CLUSTER=0 in the environment selects the global-memory split-K path.

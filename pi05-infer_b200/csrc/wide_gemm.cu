@@ -266,6 +266,7 @@ __device__ __forceinline__ bool wide_epi_rows(const SkinnyParams& p, const WideM
   for (int j = e.half, i = 0; j < NS; j += e.step, ++i) {
     const int b = i & 1;
     uint8_t* slab = slab_at(e, b);
+    float ss = 0.f;  // row statistics: this row's sum of squares over the slab (row_ssq)
     if (EPI == SK_EPI_GATED_RESID) {
       if (j + e.step < NS && e.lane == 0) {  // next residual slab into the other buffer
         bulk_wait_group_read<0>();
@@ -305,16 +306,26 @@ __device__ __forceinline__ bool wide_epi_rows(const SkinnyParams& p, const WideM
           if (EPI == SK_EPI_GATED_RESID) y = (p.gate != nullptr && in) ? rs[jj] + y * bf16_round(gt[jj]) : rs[jj] + y;
           o[jj] = y;
         }
-        sts16(slab, r, g, pack8(o));
+        const uint4 pk = pack8(o);
+        if (p.row_ssq != nullptr && in) {  // the stored (bf16) values
+          float q8[8];
+          unpack8(pk, q8);
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) ss = fmaf(q8[jj], q8[jj], ss);
+        }
+        sts16(slab, r, g, pk);
       }
     }
+    if (p.row_ssq != nullptr && tok < p.m_tok && n_tile * BN + j * 64 < n_valid)
+      p.row_ssq[(size_t)(n_tile * (BN / 64) + j) * p.ssq_ld + tok] = ss;
     slab_store(e, &mp.out, slab, n_tile * BN + j * 64, m0 + e.q * 32);
   }
   return ok;
 }
 
 // GEGLU: TMEM columns [0, 128) are gate rows, [128, 256) the matching up rows.
-__device__ __forceinline__ void wide_epi_geglu(const WideMaps& mp, EpiWarp& e, uint32_t taddr, int n_tile, int m0) {
+__device__ __forceinline__ void wide_epi_geglu(const WideMaps& mp, EpiWarp& e, uint32_t taddr, int n_tile, int m0,
+                                               float rs) {
   const int r = e.lane;
 #pragma unroll 1
   for (int j = 0; j < 2; ++j) {
@@ -326,6 +337,11 @@ __device__ __forceinline__ void wide_epi_geglu(const WideMaps& mp, EpiWarp& e, u
       float g[32], u[32];
       tmem_ld32(taddr + j * 64 + h * 32, g);
       tmem_ld32(taddr + 128 + j * 64 + h * 32, u);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {  // folded norm: the row's rstd (1 otherwise)
+        g[i] *= rs;
+        u[i] *= rs;
+      }
 #pragma unroll
       for (int g4 = 0; g4 < 4; ++g4) {
         float o[8];
@@ -341,7 +357,7 @@ __device__ __forceinline__ void wide_epi_geglu(const WideMaps& mp, EpiWarp& e, u
 // QKV_ROPE, one 256-dim head per tile (n_kv_heads == 1): q / k heads are rotated
 // (pairs d, d + 128) into q_out / the K cache; the v head is copied to the V cache.
 __device__ __forceinline__ bool wide_epi_qkv(const SkinnyParams& p, const WideMaps& mp, EpiWarp& e, uint32_t taddr,
-                                             int head, int m0) {
+                                             int head, int m0, float rs) {
   const int r = e.lane;
   const int y_q = m0 + e.q * 32;
   const int y_kv = p.krow0 + m0 + e.q * 32;
@@ -372,6 +388,11 @@ __device__ __forceinline__ bool wide_epi_qkv(const SkinnyParams& p, const WideMa
         float lo[32], hi[32];
         tmem_ld32(taddr + c * 64 + h * 32, lo);
         tmem_ld32(taddr + 128 + c * 64 + h * 32, hi);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {  // folded norm: the row's rstd (1 otherwise)
+          lo[i] *= rs;
+          hi[i] *= rs;
+        }
 #pragma unroll
         for (int g4 = 0; g4 < 4; ++g4) {
           const int g = h * 4 + g4;
@@ -413,6 +434,8 @@ __device__ __forceinline__ bool wide_epi_qkv(const SkinnyParams& p, const WideMa
       for (int h = 0; h < 2; ++h) {
         float v[32];
         tmem_ld32(taddr + j * 64 + h * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] *= rs;
 #pragma unroll
         for (int g4 = 0; g4 < 4; ++g4) sts16(slab, r, h * 4 + g4, pack8(v + g4 * 8));
       }
@@ -671,6 +694,18 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
         }
         named_bar_sync(1, kET);
       }
+      // Folded norm (q|k|v, gate/up): rstd of this thread's token row from the
+      // producer's per-slab sums of squares, loaded while the mainloop runs.
+      float rs = 1.f;
+      if ((EPI == SK_EPI_GEGLU || EPI == SK_EPI_QKV_ROPE) && p.fold_ssq != nullptr) {
+        const int tok = m * kWBM + e.q * 32 + lane;
+        float ss = 0.f;
+        if (tok < p.m_tok) {
+#pragma unroll 8
+          for (int j = 0; j < p.fold_parts; ++j) ss += __ldcg(p.fold_ssq + (size_t)j * p.fold_ld + tok);
+        }
+        rs = tok < p.m_tok ? rsqrtf(ss / (float)p.fold_d + p.fold_eps) : 0.f;
+      }
       if (!mbar_wait(&accf[buf], (lt >> 1) & 1)) {
         report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
         break;
@@ -680,9 +715,9 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
       const uint32_t taddr = tmem + ((uint32_t)(e.q * 32) << 16) + (uint32_t)(buf * BN);
       bool ok = true;
       if (EPI == SK_EPI_GEGLU)
-        wide_epi_geglu(mp, e, taddr, n, m * kWBM);
+        wide_epi_geglu(mp, e, taddr, n, m * kWBM, rs);
       else if (EPI == SK_EPI_QKV_ROPE)
-        ok = wide_epi_qkv(p, mp, e, taddr, n, m * kWBM);
+        ok = wide_epi_qkv(p, mp, e, taddr, n, m * kWBM, rs);
       else {
         WideSplit sp{nullptr, wt.nseg, wt.s, e.q * 32 + lane};
         bool finish = true;

@@ -9,6 +9,7 @@ rotated K and raw V straight into those buffers.
 from __future__ import annotations
 
 import ctypes
+import os
 from typing import Dict, List, Sequence
 
 import torch
@@ -22,7 +23,8 @@ from .synthetic import LM_PREFIX
 class Pi05PrefixLayer(ctypes.Structure):
     _fields_ = [("w_qkv", ctypes.c_void_p), ("w_o", ctypes.c_void_p), ("w_gate", ctypes.c_void_p),
                 ("w_up", ctypes.c_void_p), ("w_down", ctypes.c_void_p), ("ln1_w", ctypes.c_void_p),
-                ("ln2_w", ctypes.c_void_p), ("k_cache", ctypes.c_void_p), ("v_cache", ctypes.c_void_p)]
+                ("ln2_w", ctypes.c_void_p), ("k_cache", ctypes.c_void_p), ("v_cache", ctypes.c_void_p),
+                ("wf_qkv", ctypes.c_void_p), ("wf_gate", ctypes.c_void_p), ("wf_up", ctypes.c_void_p)]
 
 
 class Pi05PrefixPlan(ctypes.Structure):
@@ -33,7 +35,7 @@ class Pi05PrefixPlan(ctypes.Structure):
         ("inv_freq", ctypes.c_void_p), ("rope_cos", ctypes.c_void_p), ("rope_sin", ctypes.c_void_p),
         ("h", ctypes.c_void_p), ("xn", ctypes.c_void_p), ("q", ctypes.c_void_p), ("attn", ctypes.c_void_p),
         ("act", ctypes.c_void_p), ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
-        ("kv_only_last_layer", ctypes.c_int),
+        ("kv_only_last_layer", ctypes.c_int), ("row_stats", ctypes.c_void_p),
     ]
 
 
@@ -76,6 +78,15 @@ class PrefixWeights:
                 "ln1": torch.empty((shape.width,), **f32),
                 "ln2": torch.empty((shape.width,), **f32),
             })
+        # Folded copies (folded RMSNorms, PI05_FOLD_NORM=0 to run the norm kernels
+        # instead): q|k|v with (1 + ln1) and gate / up with (1 + ln2) folded into their
+        # columns; 2.7 GB at Gemma-2B.
+        self.fold = os.environ.get("PI05_FOLD_NORM", "1") != "0"
+        if self.fold:
+            for L in self.layers:
+                L["wf_qkv"] = torch.empty_like(L["w_qkv"])
+                L["wf_gate"] = torch.empty_like(L["w_gate"])
+                L["wf_up"] = torch.empty_like(L["w_up"])
         self.load(sd)
 
     def load(self, sd: Dict[str, torch.Tensor]) -> None:
@@ -90,6 +101,18 @@ class PrefixWeights:
             L["w_down"].copy_(sd[p + "mlp.down_proj.weight"])
             L["ln1"].copy_(sd[p + "input_layernorm.weight"])
             L["ln2"].copy_(sd[p + "post_attention_layernorm.weight"])
+        if self.fold:
+            self.build_fold()
+
+    def build_fold(self) -> None:
+        """Fold each layer's RMSNorm weights into its q|k|v and gate/up copies, in place."""
+        s = self.shape
+        zero = torch.zeros(s.width, dtype=torch.float32, device=self.device)
+        bias = torch.empty(max(s.qkv_dim, s.mlp_dim), dtype=torch.float32, device=self.device)
+        for L in self.layers:
+            abi.fold_adarms(L["w_qkv"], L["ln1"], zero, L["wf_qkv"], bias[: s.qkv_dim])
+            abi.fold_adarms(L["w_gate"], L["ln2"], zero, L["wf_gate"], bias[: s.mlp_dim])
+            abi.fold_adarms(L["w_up"], L["ln2"], zero, L["wf_up"], bias[: s.mlp_dim])
 
 
 class PrefixRunner:
@@ -115,9 +138,13 @@ class PrefixRunner:
         self.ws = ops.workspace(dev)
         self._layers = (Pi05PrefixLayer * s.depth)()
         for i, L in enumerate(weights.layers):
+            wf = [L[k].data_ptr() if weights.fold else None for k in ("wf_qkv", "wf_gate", "wf_up")]
             self._layers[i] = Pi05PrefixLayer(L["w_qkv"].data_ptr(), L["w_o"].data_ptr(), L["w_gate"].data_ptr(),
                                               L["w_up"].data_ptr(), L["w_down"].data_ptr(), L["ln1"].data_ptr(),
-                                              L["ln2"].data_ptr(), k_cache[i].data_ptr(), v_cache[i].data_ptr())
+                                              L["ln2"].data_ptr(), k_cache[i].data_ptr(), v_cache[i].data_ptr(),
+                                              *wf)
+        # per-64-column sums of squares of h for the folded norms
+        self.row_stats = torch.zeros((s.width // 64, tokens), dtype=torch.float32, device=dev)
         self.plan = Pi05PrefixPlan(
             depth=s.depth, width=s.width, mlp_dim=s.mlp_dim, n_q_heads=s.num_heads, n_kv_heads=s.num_kv_heads,
             head_dim=s.head_dim, tokens=tokens, kv_rows=self.kv_rows, eps=s.rms_eps,
@@ -125,7 +152,8 @@ class PrefixRunner:
             inv_freq=self.inv_freq.data_ptr(), rope_cos=self.rope_cos.data_ptr(), rope_sin=self.rope_sin.data_ptr(),
             h=self.h.data_ptr(), xn=self.xn.data_ptr(), q=self.q.data_ptr(), attn=self.attn.data_ptr(),
             act=self.act.data_ptr(), workspace=self.ws.data_ptr(), workspace_bytes=self.ws.numel(),
-            kv_only_last_layer=1 if kv_only_last_layer else 0)
+            kv_only_last_layer=1 if kv_only_last_layer else 0,
+            row_stats=self.row_stats.data_ptr() if weights.fold else None)
 
     def enqueue(self, stream: int) -> None:
         _bind()

@@ -54,6 +54,37 @@ def test_prefix_kv_parity(p, n_pad, depth):
         assert cache[i][0, p:].abs().sum().item() == 0  # suffix rows untouched
 
 
+def test_prefix_folded_norm_matches_norm_kernels():
+    # The folded RMSNorms (weights carry (1 + w); q|k|v and gate/up scale each token
+    # by its rstd from the residual GEMMs' row statistics) against the same layers
+    # with the RMSNorm kernels: per-layer K/V within the prefix tolerance.
+    p, depth = 968, 3
+    shape = GemmaShape(width=2048, depth=depth, mlp_dim=16384, num_heads=8, num_kv_heads=1, head_dim=256)
+    sd = synthetic.make_prefix_lm_weights(10, shape)
+    embs = synthetic.make_prefix_embeddings(3, p, 2048)[0].cuda()
+    valid = torch.ones(p, dtype=torch.bool, device="cuda")
+    valid[-20:] = False
+    w = PrefixWeights(sd, shape, "cuda")
+    assert w.fold
+    caches = []
+    for folded in (True, False):
+        kc = [torch.zeros(1, p + 50, 256, dtype=torch.bfloat16, device="cuda") for _ in range(depth)]
+        vc = [torch.zeros(1, p + 50, 256, dtype=torch.bfloat16, device="cuda") for _ in range(depth)]
+        r = PrefixRunner(w, p, kc, vc)
+        if not folded:
+            r.plan.row_stats = None
+        r.run(embs, valid)
+        caches.append((kc, vc))
+    assert ops.read_device_status() == 0
+    vm = valid.cpu()
+    for i in range(depth):
+        for j in range(2):
+            a = caches[0][j][i][0, :p].float().cpu()[vm]
+            b = caches[1][j][i][0, :p].float().cpu()[vm]
+            assert _cos(a, b) >= 0.9999, (i, j)
+            assert (a - b).abs().max().item() <= 0.05 * b.abs().max().item(), (i, j)
+
+
 def test_embed_tokens():
     g = torch.Generator(device="cuda").manual_seed(7)
     table = (torch.randn(1000, 2048, device="cuda", generator=g) * 0.02).bfloat16()
