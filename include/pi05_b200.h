@@ -323,6 +323,15 @@ typedef struct Pi05SiglipLayer {
   const float* ln1_b;
   const float* ln2_w;
   const float* ln2_b;
+  /* Folded LayerNorms, or NULL (then the LayerNorm kernels run): q|k|v and fc1 with
+   * the preceding LayerNorm's gamma folded into their columns (bf16), their biases
+   * b + W . beta (fp32), and the column sums sum_k W'[n, k] of the folded weights. */
+  const void* wf_qkv;
+  const float* bf_qkv;
+  const float* cs_qkv;
+  const void* wf_fc1;
+  const float* bf_fc1;
+  const float* cs_fc1;
 } Pi05SiglipLayer;
 
 typedef struct Pi05SiglipPlan {
@@ -348,6 +357,13 @@ typedef struct Pi05SiglipPlan {
   int ldo;
   void* workspace;
   size_t workspace_bytes;
+  const void* wf_proj;            /* projector with post_layernorm folded in, or NULL */
+  const float* bf_proj;
+  const float* cs_proj;
+  float* row_stats;               /* [2][width / 64][views*patches] fp32 (sums, sums of squares), or NULL.
+                                     With it and every wf_* set, no LayerNorm kernel runs: the residual
+                                     GEMMs and the patch embedding write per-64-column statistics of h,
+                                     and q|k|v, fc1 and the projector normalise in their epilogues. */
 } Pi05SiglipPlan;
 
 /* All views through SigLIP and the projector into `out`.  Replaces embed_image /

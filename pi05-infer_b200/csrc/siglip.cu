@@ -12,6 +12,7 @@
 // Attention here is per-head (16 heads x 72 dims, 256 tokens per view, no mask):
 // mma.sync flash kernel, head dim zero-padded to 80.
 #include <cmath>
+#include <cstdlib>
 
 #include "../../include/pi05_b200.h"
 #include "elementwise.h"
@@ -260,6 +261,15 @@ __global__ void __launch_bounds__(128) mha72_kernel(const __nv_bfloat16* __restr
 
 inline bool nz(const void* p) { return p != nullptr; }
 
+// PI05_FOLD_NORM=0 in the environment keeps the LayerNorm kernels.
+bool siglip_fold_enabled() {
+  static int v = [] {
+    const char* e = getenv("PI05_FOLD_NORM");
+    return (e != nullptr && e[0] == '0') ? 0 : 1;
+  }();
+  return v != 0;
+}
+
 SkinnyParams base_params(const Workspace& ws) {
   SkinnyParams sp;
   sp.status = ws.status;
@@ -335,6 +345,35 @@ int pi05_siglip_forward(const Pi05SiglipPlan* P, void* stream) {
   auto* qkv = static_cast<__nv_bfloat16*>(P->qkv);
   auto* attn = static_cast<__nv_bfloat16*>(P->attn);
   auto* act = static_cast<__nv_bfloat16*>(P->act);
+  // Folded LayerNorms: statistics of h per 64-column part (sums, then sums of
+  // squares) from the GEMMs that write h; the consumers normalise in their epilogue
+  // (rstd * (acc - mean * colsum) + b + W . beta; LayerNorm fp32 statistics as in
+  // torch.nn.LayerNorm, the variance as E[x^2] - mean^2).
+  const int parts = W / 64;
+  bool fold = P->row_stats != nullptr && siglip_fold_enabled() && W % 64 == 0 && row_ssq_parts(T, W) == parts &&
+              nz(P->wf_proj) && nz(P->bf_proj) && nz(P->cs_proj);
+  for (int l = 0; fold && l < P->depth; ++l) {
+    const Pi05SiglipLayer& L = P->layers[l];
+    fold = nz(L.wf_qkv) && nz(L.bf_qkv) && nz(L.cs_qkv) && nz(L.wf_fc1) && nz(L.bf_fc1) && nz(L.cs_fc1);
+  }
+  float* st_sum = P->row_stats;
+  float* st_ssq = fold ? P->row_stats + (size_t)parts * T : nullptr;
+  auto producer = [&](SkinnyParams& sp) {
+    if (!fold) return;
+    sp.row_ssq = st_ssq;
+    sp.row_sum = st_sum;
+    sp.ssq_ld = T;
+  };
+  auto consumer = [&](SkinnyParams& sp, const float* folded_bias, const float* colsum) {
+    sp.fold_ssq = st_ssq;
+    sp.ln_sum = st_sum;
+    sp.fold_parts = parts;
+    sp.fold_ld = T;
+    sp.fold_d = W;
+    sp.fold_eps = P->eps;
+    sp.ln_colsum = colsum;
+    sp.bias = folded_bias;
+  };
   const size_t total = (size_t)T * P->k_pad;
   int rc = launch_pdl(im2col_kernel, dim3((unsigned)std::min<size_t>((total + 255) / 256, 148 * 16)), dim3(256), 0,
                       st, pdl_enabled(), P->images, V, P->image_size, P->patch, P->k_pad,
@@ -350,12 +389,13 @@ int pi05_siglip_forward(const Pi05SiglipPlan* P, void* stream) {
     sp.bias = P->b_patch;
     sp.pos = P->pos_emb;
     sp.pos_rows = S;
+    producer(sp);
     rc = skinny_gemm_run(SK_EPI_STORE, sp, P->w_patch, P->w_patch, W, W, P->cols, P->k_pad, 0, stream);
     if (rc) return rc;
   }
   for (int l = 0; l < P->depth; ++l) {
     const Pi05SiglipLayer& L = P->layers[l];
-    rc = pi05_layer_norm(h, L.ln1_w, L.ln1_b, xn, W, T, W, P->eps, stream);
+    if (!fold) rc = pi05_layer_norm(h, L.ln1_w, L.ln1_b, xn, W, T, W, P->eps, stream);
     if (rc) return rc;
     {
       SkinnyParams sp = base_params(ws);
@@ -366,7 +406,9 @@ int pi05_siglip_forward(const Pi05SiglipPlan* P, void* stream) {
       sp.ldo = 3 * W;
       sp.bias = L.b_qkv;
       sp.trace_tag = l * 8 + 0;
-      rc = skinny_gemm_run(SK_EPI_STORE, sp, L.w_qkv, L.w_qkv, 3 * W, 3 * W, xn, W, 0, stream);
+      if (fold) consumer(sp, L.bf_qkv, L.cs_qkv);
+      const void* wq = fold ? L.wf_qkv : L.w_qkv;
+      rc = skinny_gemm_run(SK_EPI_STORE, sp, wq, wq, 3 * W, 3 * W, fold ? h : xn, W, 0, stream);
       if (rc) return rc;
     }
     rc = pi05_siglip_attention(qkv, V, S, W, P->n_heads, P->head_dim, attn, stream);
@@ -382,10 +424,11 @@ int pi05_siglip_forward(const Pi05SiglipPlan* P, void* stream) {
       sp.ldr = W;
       sp.bias = L.b_o;
       sp.trace_tag = l * 8 + 1;
+      producer(sp);
       rc = skinny_gemm_run(SK_EPI_GATED_RESID, sp, L.w_o, L.w_o, W, W, attn, W, 0, stream);
       if (rc) return rc;
     }
-    rc = pi05_layer_norm(h, L.ln2_w, L.ln2_b, xn, W, T, W, P->eps, stream);
+    if (!fold) rc = pi05_layer_norm(h, L.ln2_w, L.ln2_b, xn, W, T, W, P->eps, stream);
     if (rc) return rc;
     {
       SkinnyParams sp = base_params(ws);
@@ -398,7 +441,9 @@ int pi05_siglip_forward(const Pi05SiglipPlan* P, void* stream) {
       sp.bias = L.b_fc1;
       sp.act = 1;
       sp.trace_tag = l * 8 + 2;
-      rc = skinny_gemm_run(SK_EPI_STORE, sp, L.w_fc1, L.w_fc1, F, F, xn, W, 0, stream);
+      if (fold) consumer(sp, L.bf_fc1, L.cs_fc1);
+      const void* w1 = fold ? L.wf_fc1 : L.w_fc1;
+      rc = skinny_gemm_run(SK_EPI_STORE, sp, w1, w1, F, F, fold ? h : xn, W, 0, stream);
       if (rc) return rc;
     }
     {
@@ -412,11 +457,12 @@ int pi05_siglip_forward(const Pi05SiglipPlan* P, void* stream) {
       sp.ldr = W;
       sp.bias = L.b_fc2;
       sp.trace_tag = l * 8 + 3;
+      producer(sp);
       rc = skinny_gemm_run(SK_EPI_GATED_RESID, sp, L.w_fc2, L.w_fc2, W, W, act, F, 0, stream);
       if (rc) return rc;
     }
   }
-  rc = pi05_layer_norm(h, P->post_ln_w, P->post_ln_b, xn, W, T, W, P->eps, stream);
+  if (!fold) rc = pi05_layer_norm(h, P->post_ln_w, P->post_ln_b, xn, W, T, W, P->eps, stream);
   if (rc) return rc;
   SkinnyParams sp = base_params(ws);
   sp.m_tok = T;
@@ -425,7 +471,9 @@ int pi05_siglip_forward(const Pi05SiglipPlan* P, void* stream) {
   sp.out = static_cast<__nv_bfloat16*>(P->out);
   sp.ldo = P->ldo;
   sp.bias = P->b_proj;
-  return skinny_gemm_run(SK_EPI_STORE, sp, P->w_proj, P->w_proj, P->proj_dim, P->proj_dim, xn, W, 0, stream);
+  if (fold) consumer(sp, P->bf_proj, P->cs_proj);
+  const void* wp = fold ? P->wf_proj : P->w_proj;
+  return skinny_gemm_run(SK_EPI_STORE, sp, wp, wp, P->proj_dim, P->proj_dim, fold ? h : xn, W, 0, stream);
 }
 
 }  // extern "C"

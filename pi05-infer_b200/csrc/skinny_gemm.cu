@@ -702,11 +702,19 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
     return PI05_ERR_SHAPE;
   }
   const bool wide_ok = p.m_tok >= kWideMinTokens && !wide_disabled();
-  if (p.fold_ssq != nullptr) {
+  if (p.fold_ssq != nullptr && epi == SK_EPI_STORE) {
+    // Folded LayerNorm: many-token kernel only, sums, sums of squares and column sums.
+    if (!wide_ok || p.ln_sum == nullptr || p.ln_colsum == nullptr || p.fold_parts <= 0 || p.fold_d <= 0 ||
+        p.fold_ld < p.m_tok || p.fold_bias0 != nullptr || p.fold_bias1 != nullptr) {
+      set_last_error("skinny_gemm: folded LayerNorm needs >= %d tokens, row sums, sums of squares and column sums",
+                     kWideMinTokens);
+      return PI05_ERR_SHAPE;
+    }
+  } else if (p.fold_ssq != nullptr) {
     // Small-token kernel: <= 64 tokens, rstd and the folded bias (denoise adaRMS);
     // many-token kernel: rstd only (the prefix LM's RMSNorm has no shift).
     bool bad = (epi != SK_EPI_GEGLU && epi != SK_EPI_QKV_ROPE) || p.fold_parts <= 0 || p.fold_d <= 0 ||
-               p.fold_ld < p.m_tok || p.norm_ssq != nullptr;
+               p.fold_ld < p.m_tok || p.norm_ssq != nullptr || p.ln_sum != nullptr;
     if (wide_ok)
       bad = bad || p.fold_bias0 != nullptr || p.fold_bias1 != nullptr ||
             (epi == SK_EPI_QKV_ROPE && p.head_dim != 256);

@@ -51,6 +51,7 @@ struct SkinnyParams {
   // in the many-token one; row_ssq_parts() gives the count for a launch.
   float* row_ssq = nullptr;
   int ssq_ld = 0;
+  float* row_sum = nullptr;  // many-token kernel: the parts' plain sums, same layout (LayerNorm means)
   // Normalised copy of the output for the next (ada)RMS norm (GATED_RESID, push-form
   // cluster split-K, one token tile): when norm_out is set, the owner of each token
   // slice of a tile writes the slice's sums of squares to row_ssq, and the last of
@@ -91,6 +92,13 @@ struct SkinnyParams {
   float fold_eps = 0.f;
   const float* fold_bias0 = nullptr;
   const float* fold_bias1 = nullptr;
+  // Folded LayerNorm (STORE, many-token kernel): with ln_sum set (per-part sums of x
+  // in fold_ssq's layout) the weights carry the LayerNorm's gamma, `bias` holds
+  // b + W . beta, and ln_colsum[n] = sum_k W'[n, k] of the folded bf16 weights; the
+  // accumulator becomes  y = rstd[t] * (acc - mean[t] * ln_colsum[n]) + bias[n]  with
+  // mean = sum / fold_d, rstd = rsqrt(ssq / fold_d - mean^2 + fold_eps).
+  const float* ln_sum = nullptr;
+  const float* ln_colsum = nullptr;
   // L2 prefetch issued by every CTA for its share of these ranges (e.g. the same
   // op's weights of the next layer), so later launches read them from L2.
   const void* pf0 = nullptr;

@@ -77,9 +77,21 @@ constexpr int wide_b_bytes() {
 }
 
 template <int EPI, int BN, int STAGES, int EW, bool PAIR>
-constexpr int wide_smem_bytes() {
+constexpr int wide_smem_base() {
   // + 512: barriers, stamps and flags (up to ~300 bytes with 8 epilogue warps).
   return 1024 + STAGES * (kABytes + wide_b_bytes<BN, PAIR>()) + EW * epi_slabs<EPI>() * kSlabBytes + BN * 4 + 512;
+}
+
+// Single-CTA STORE tiles also stage the folded LayerNorm's column sums per tile
+// when they fit; elsewhere the epilogue reads them from global memory.
+template <int EPI, int BN, int STAGES, int EW, bool PAIR>
+constexpr bool wide_scol() {
+  return !PAIR && EPI == SK_EPI_STORE && wide_smem_base<EPI, BN, STAGES, EW, PAIR>() + BN * 4 <= 232448;
+}
+
+template <int EPI, int BN, int STAGES, int EW, bool PAIR>
+constexpr int wide_smem_bytes() {
+  return wide_smem_base<EPI, BN, STAGES, EW, PAIR>() + (wide_scol<EPI, BN, STAGES, EW, PAIR>() ? BN * 4 : 0);
 }
 
 constexpr int kMaxSegs = 4;  // stream-K: CTAs sharing one tile at most
@@ -256,7 +268,8 @@ __device__ __forceinline__ void slab_store(const EpiWarp& e, const CUtensorMap* 
 // STORE / GATED_RESID (same arithmetic as apply_epilogue).
 template <int EPI, int BN>
 __device__ __forceinline__ bool wide_epi_rows(const SkinnyParams& p, const WideMaps& mp, EpiWarp& e, uint32_t taddr,
-                                              int n_tile, int m0, const WideSplit& sp, const float* sbias) {
+                                              int n_tile, int m0, const WideSplit& sp, const float* sbias,
+                                              const float* scol = nullptr, float ln_rs = 1.f, float ln_rm = 0.f) {
   constexpr int NS = BN / 64;
   const int r = e.lane;
   const int tok = m0 + e.q * 32 + r;
@@ -266,7 +279,7 @@ __device__ __forceinline__ bool wide_epi_rows(const SkinnyParams& p, const WideM
   for (int j = e.half, i = 0; j < NS; j += e.step, ++i) {
     const int b = i & 1;
     uint8_t* slab = slab_at(e, b);
-    float ss = 0.f;  // row statistics: this row's sum of squares over the slab (row_ssq)
+    float ss = 0.f, sx = 0.f;  // row statistics: this row's sum of squares and sum over the slab
     if (EPI == SK_EPI_GATED_RESID) {
       if (j + e.step < NS && e.lane == 0) {  // next residual slab into the other buffer
         bulk_wait_group_read<0>();
@@ -282,6 +295,16 @@ __device__ __forceinline__ bool wide_epi_rows(const SkinnyParams& p, const WideM
     for (int h = 0; h < 2; ++h) {
       float v[32];
       wide_acc32<BN>(taddr, j * 64 + h * 32, sp, v);
+      if (EPI == SK_EPI_STORE && p.ln_colsum != nullptr) {
+        // Folded LayerNorm: rstd * (acc - mean * colsum), column sums staged per tile
+        // (zero past n_valid) or read from global memory.
+        const int c0 = n_tile * BN + j * 64 + h * 32;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float cs = scol != nullptr ? scol[j * 64 + h * 32 + i] : (c0 + i < n_valid ? p.ln_colsum[c0 + i] : 0.f);
+          v[i] = v[i] * ln_rs - ln_rm * cs;
+        }
+      }
       if (EPI == SK_EPI_GATED_RESID && h == 0) ok = slab_wait(e, b, p.status) && ok;
 #pragma unroll
       for (int g4 = 0; g4 < 4; ++g4) {
@@ -311,13 +334,18 @@ __device__ __forceinline__ bool wide_epi_rows(const SkinnyParams& p, const WideM
           float q8[8];
           unpack8(pk, q8);
 #pragma unroll
-          for (int jj = 0; jj < 8; ++jj) ss = fmaf(q8[jj], q8[jj], ss);
+          for (int jj = 0; jj < 8; ++jj) {
+            ss = fmaf(q8[jj], q8[jj], ss);
+            sx += q8[jj];
+          }
         }
         sts16(slab, r, g, pk);
       }
     }
-    if (p.row_ssq != nullptr && tok < p.m_tok && n_tile * BN + j * 64 < n_valid)
+    if (p.row_ssq != nullptr && tok < p.m_tok && n_tile * BN + j * 64 < n_valid) {
       p.row_ssq[(size_t)(n_tile * (BN / 64) + j) * p.ssq_ld + tok] = ss;
+      if (p.row_sum != nullptr) p.row_sum[(size_t)(n_tile * (BN / 64) + j) * p.ssq_ld + tok] = sx;
+    }
     slab_store(e, &mp.out, slab, n_tile * BN + j * 64, m0 + e.q * 32);
   }
   return ok;
@@ -476,7 +504,9 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
   uint8_t* sB = smem + STAGES * kABytes;
   uint8_t* sEpi = smem + STAGES * kStageBytes;  // kEW warps x kSlabs slabs, 1024-aligned
   float* sbias = reinterpret_cast<float*>(sEpi + kEW * kSlabs * kSlabBytes);  // [BN] this tile's bias
-  uint64_t* full = reinterpret_cast<uint64_t*>(sbias + BN);
+  constexpr bool kScol = wide_scol<EPI, BN, STAGES, EW, PAIR>();
+  float* scol = sbias + BN;  // [BN] folded LayerNorm column sums (kScol)
+  uint64_t* full = reinterpret_cast<uint64_t*>(sbias + (kScol ? 2 : 1) * BN);
   uint64_t* empty = full + STAGES;
   uint64_t* accf = empty + STAGES;  // [2] accumulator ready (MMA commit)
   uint64_t* acce = accf + 2;        // [2] accumulator drained (128 epilogue arrivals)
@@ -684,13 +714,15 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
       const int m = PAIR ? 2 * wt.m + rank : wt.m, n = wt.n;  // this CTA's 128-token tile
       const int buf = lt & 1;
       wide_epi_prefetch<EPI, BN>(p, mp, e, n, m * kWBM);
-      if ((EPI == SK_EPI_STORE || EPI == SK_EPI_GATED_RESID) && p.bias != nullptr) {
-        // Stage the tile's bias columns once (read as broadcasts by the epilogue).
+      if ((EPI == SK_EPI_STORE || EPI == SK_EPI_GATED_RESID) && (p.bias != nullptr || p.ln_colsum != nullptr)) {
+        // Stage the tile's bias (and folded LayerNorm column sums) once; the
+        // epilogue reads them as shared-memory broadcasts.
         const int et = threadIdx.x - 64;
-        named_bar_sync(1, kET);  // the previous tile's epilogue is done with sbias
+        named_bar_sync(1, kET);  // the previous tile's epilogue is done with sbias / scol
         for (int i = et; i < BN; i += kET) {
           const int col = n * BN + i;
-          sbias[i] = col < p.n_valid ? p.bias[col] : 0.f;
+          if (p.bias != nullptr) sbias[i] = col < p.n_valid ? p.bias[col] : 0.f;
+          if (kScol && p.ln_colsum != nullptr) scol[i] = col < p.n_valid ? p.ln_colsum[col] : 0.f;
         }
         named_bar_sync(1, kET);
       }
@@ -705,6 +737,24 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
           for (int j = 0; j < p.fold_parts; ++j) ss += __ldcg(p.fold_ssq + (size_t)j * p.fold_ld + tok);
         }
         rs = tok < p.m_tok ? rsqrtf(ss / (float)p.fold_d + p.fold_eps) : 0.f;
+      }
+      // Folded LayerNorm (STORE): rstd and rstd * mean of the row from the producer's
+      // per-slab sums and sums of squares.
+      float ln_rs = 1.f, ln_rm = 0.f;
+      if (EPI == SK_EPI_STORE && p.ln_sum != nullptr) {
+        const int tok = m * kWBM + e.q * 32 + lane;
+        float s1 = 0.f, s2 = 0.f;
+        if (tok < p.m_tok) {
+#pragma unroll 6
+          for (int j = 0; j < p.fold_parts; ++j) {
+            s1 += __ldcg(p.ln_sum + (size_t)j * p.fold_ld + tok);
+            s2 += __ldcg(p.fold_ssq + (size_t)j * p.fold_ld + tok);
+          }
+        }
+        const float mean = s1 / (float)p.fold_d;
+        const float var = fmaxf(s2 / (float)p.fold_d - mean * mean, 0.f);
+        ln_rs = tok < p.m_tok ? rsqrtf(var + p.fold_eps) : 0.f;
+        ln_rm = ln_rs * mean;
       }
       if (!mbar_wait(&accf[buf], (lt >> 1) & 1)) {
         report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
@@ -808,7 +858,8 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
           }
         }
         if (finish) {
-          ok = wide_epi_rows<EPI, BN>(p, mp, e, taddr, n, m * kWBM, sp, sbias);
+          ok = wide_epi_rows<EPI, BN>(p, mp, e, taddr, n, m * kWBM, sp, sbias, kScol ? scol : nullptr, ln_rs,
+                                      ln_rm);
         } else if (EPI == SK_EPI_GATED_RESID && e.lane == 0) {
           // The residual slab prefetched for this tile is not consumed: retire its load.
           ok = slab_wait(e, 0, p.status);
@@ -968,7 +1019,7 @@ int env_int(const char* name) {
 }  // namespace
 
 int wide_choose(int epi, int m_tiles, int n_cols, int kb_total, int sms, int* bn, int* splits, int* pair,
-                int* streamk) {
+                int* streamk, bool allow_pair) {
   static const int force_bn = env_int("PI05_WIDE_BN");
   static const int force_splits = env_int("PI05_WIDE_SPLITS");
   static const int force_pair = [] {
@@ -987,7 +1038,7 @@ int wide_choose(int epi, int m_tiles, int n_cols, int kb_total, int sms, int* bn
   // (the prefix down_proj).  PI05_WIDE_PAIR=0 / 1 disables / forces them.
   const bool pair_auto = m_tiles >= 4 && ((epi == SK_EPI_GEGLU && kb_total >= 16) ||
                                           ((epi == SK_EPI_STORE || epi == SK_EPI_GATED_RESID) && kb_total >= 128));
-  if (force_pair > 0 || (force_pair < 0 && pair_auto)) {
+  if (allow_pair && (force_pair > 0 || (force_pair < 0 && pair_auto))) {
     // CTA pairs: 256 x 256 tiles; split-K (STORE / GATED_RESID) until the pairs
     // cover the SMs.
     *bn = 256;
@@ -1071,7 +1122,9 @@ int wide_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int w
   const int cta_m_tiles = (p.m_tok + kWBM - 1) / kWBM;
   ws.kb_total = (p.k + kBK - 1) / kBK;
   int bn = 256, splits = 1, pair = 0, sk_units = 0;
-  wide_choose(epi, cta_m_tiles, n_cols, ws.kb_total, wide_sms(), &bn, &splits, &pair, &sk_units);
+  // The folded LayerNorm runs on single CTAs (its column sums are staged per CTA).
+  wide_choose(epi, cta_m_tiles, n_cols, ws.kb_total, wide_sms(), &bn, &splits, &pair, &sk_units,
+              p.ln_colsum == nullptr);
   ws.streamk = sk_units > 0 ? 1 : 0;
   ws.grid = sk_units;
   // Pairs schedule 256-token tiles; every CTA still owns 128 tokens of one.

@@ -15,7 +15,7 @@ int wide_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int w
 // `splits` is the partial slots per tile) for an epilogue kind and shape; m_tiles
 // counts 128-token tiles.
 int wide_choose(int epi, int m_tiles, int n_cols, int kb_total, int sms, int* bn, int* splits, int* pair,
-                int* streamk);
+                int* streamk, bool allow_pair = true);
 
 // PI05_WIDE=0 in the environment keeps every projection on the small-token kernel.
 bool wide_disabled();

@@ -10,6 +10,7 @@ position embedding added before the single rounding.
 from __future__ import annotations
 
 import ctypes
+import os
 from typing import Dict, List
 
 import torch
@@ -23,7 +24,8 @@ _P = ctypes.c_void_p
 
 class Pi05SiglipLayer(ctypes.Structure):
     _fields_ = [(n, _P) for n in ("w_qkv", "b_qkv", "w_o", "b_o", "w_fc1", "b_fc1", "w_fc2", "b_fc2",
-                                  "ln1_w", "ln1_b", "ln2_w", "ln2_b")]
+                                  "ln1_w", "ln1_b", "ln2_w", "ln2_b",
+                                  "wf_qkv", "bf_qkv", "cs_qkv", "wf_fc1", "bf_fc1", "cs_fc1")]
 
 
 class Pi05SiglipPlan(ctypes.Structure):
@@ -33,6 +35,7 @@ class Pi05SiglipPlan(ctypes.Structure):
         ("pos_emb", _P), ("k_pad", ctypes.c_int), ("post_ln_w", _P), ("post_ln_b", _P), ("w_proj", _P),
         ("b_proj", _P), ("images", _P), ("cols", _P), ("h", _P), ("xn", _P), ("qkv", _P), ("attn", _P),
         ("act", _P), ("out", _P), ("ldo", ctypes.c_int), ("workspace", _P), ("workspace_bytes", ctypes.c_size_t),
+        ("wf_proj", _P), ("bf_proj", _P), ("cs_proj", _P), ("row_stats", _P),
     ]
 
 
@@ -88,6 +91,20 @@ class SiglipWeights:
         self.post_b = torch.empty((w,), **f32)
         self.w_proj = torch.empty((shape.proj_dim, w), **bf)
         self.b_proj = torch.empty((shape.proj_dim,), **f32)
+        # Folded LayerNorms (PI05_FOLD_NORM=0 runs the LayerNorm kernels instead):
+        # q|k|v, fc1 and the projector with the preceding LayerNorm's gamma folded
+        # into their columns, biases b + W . beta, and column sums of the folded
+        # weights (the mean term of the normalisation).
+        self.fold = os.environ.get("PI05_FOLD_NORM", "1") != "0"
+        if self.fold:
+            for L in self.layers:
+                for n, rows in (("qkv", 3 * w), ("fc1", shape.mlp_dim)):
+                    L["wf_" + n] = torch.empty((rows, w), **bf)
+                    L["bf_" + n] = torch.empty((rows,), **f32)
+                    L["cs_" + n] = torch.empty((rows,), **f32)
+            self.wf_proj = torch.empty_like(self.w_proj)
+            self.bf_proj = torch.empty_like(self.b_proj)
+            self.cs_proj = torch.empty_like(self.b_proj)
         self.load(sd)
 
     def load(self, sd: Dict[str, torch.Tensor]) -> None:
@@ -114,6 +131,28 @@ class SiglipWeights:
         self.post_b.copy_(_bf16_as_f32(sd[p + "post_layernorm.bias"], dev))
         self.w_proj.copy_(sd[self.proj_prefix + "weight"])
         self.b_proj.copy_(_bf16_as_f32(sd[self.proj_prefix + "bias"], dev))
+        if self.fold:
+            self.build_fold()
+
+    def build_fold(self) -> None:
+        """LayerNorm(x) = (x - mean) * rstd * gamma + beta, so
+        W . LayerNorm(x) + b = rstd * (W' . x - mean * colsum(W')) + (b + W . beta)
+        with W' = bf16(W * gamma); the column sums are taken of the rounded W', so
+        the mean term cancels its rounding exactly.  Built in place."""
+        w = self.shape.width
+        ones = torch.ones(w, dtype=torch.float32, device=self.device)
+        zeros = torch.zeros(w, dtype=torch.float32, device=self.device)
+
+        def fold(wt, gamma, beta, b, wf, bf, cs):
+            abi.fold_adarms(wt, gamma - 1.0, beta, wf, bf)  # wf = bf16(W * gamma), bf = W . beta
+            bf.add_(b)
+            scratch = torch.empty_like(wf)
+            abi.fold_adarms(wf, zeros, ones, scratch, cs)  # cs = sum_k wf[n, k]
+
+        for L in self.layers:
+            fold(L["w_qkv"], L["ln1_w"], L["ln1_b"], L["b_qkv"], L["wf_qkv"], L["bf_qkv"], L["cs_qkv"])
+            fold(L["w_fc1"], L["ln2_w"], L["ln2_b"], L["b_fc1"], L["wf_fc1"], L["bf_fc1"], L["cs_fc1"])
+        fold(self.w_proj, self.post_w, self.post_b, self.b_proj, self.wf_proj, self.bf_proj, self.cs_proj)
 
 
 class SiglipRunner:
@@ -135,9 +174,14 @@ class SiglipRunner:
         self.act = torch.zeros((t, s.mlp_dim), **bf)
         self.ws = ops.workspace(dev)
         self._layers = (Pi05SiglipLayer * s.depth)()
+        fk = ("wf_qkv", "bf_qkv", "cs_qkv", "wf_fc1", "bf_fc1", "cs_fc1")
         for i, L in enumerate(weights.layers):
             self._layers[i] = Pi05SiglipLayer(*[L[k].data_ptr() for k in (
-                "w_qkv", "b_qkv", "w_o", "b_o", "w_fc1", "b_fc1", "w_fc2", "b_fc2", "ln1_w", "ln1_b", "ln2_w", "ln2_b")])
+                "w_qkv", "b_qkv", "w_o", "b_o", "w_fc1", "b_fc1", "w_fc2", "b_fc2", "ln1_w", "ln1_b", "ln2_w", "ln2_b")],
+                *[L[k].data_ptr() if weights.fold else None for k in fk])
+        # per-64-column sums and sums of squares of h for the folded LayerNorms
+        self.row_stats = torch.zeros((2, s.width // 64, t), dtype=torch.float32, device=dev)
+        self.use_fold = weights.fold  # False: the LayerNorm kernels (tests)
         self.plan = None
 
     def _plan(self, images: torch.Tensor, out: torch.Tensor) -> Pi05SiglipPlan:
@@ -150,7 +194,10 @@ class SiglipRunner:
             post_ln_b=w.post_b.data_ptr(), w_proj=w.w_proj.data_ptr(), b_proj=w.b_proj.data_ptr(),
             images=images.data_ptr(), cols=self.cols.data_ptr(), h=self.h.data_ptr(), xn=self.xn.data_ptr(),
             qkv=self.qkv.data_ptr(), attn=self.attn.data_ptr(), act=self.act.data_ptr(), out=out.data_ptr(),
-            ldo=out.stride(0), workspace=self.ws.data_ptr(), workspace_bytes=self.ws.numel())
+            ldo=out.stride(0), workspace=self.ws.data_ptr(), workspace_bytes=self.ws.numel(),
+            wf_proj=w.wf_proj.data_ptr() if w.fold else None, bf_proj=w.bf_proj.data_ptr() if w.fold else None,
+            cs_proj=w.cs_proj.data_ptr() if w.fold else None,
+            row_stats=self.row_stats.data_ptr() if (w.fold and self.use_fold) else None)
 
     def enqueue(self, images: torch.Tensor, out: torch.Tensor, stream: int) -> None:
         """images [views, 3, H, W] fp32 (device), out rows [views*patches, proj] (bf16, row pitch any)."""

@@ -44,6 +44,27 @@ def test_siglip_features():
         assert c >= 0.999, (v, c)
 
 
+def test_siglip_folded_layernorm_matches_layernorm_kernels():
+    # Folded LayerNorms (gamma in the weights, mean and rstd from the residual GEMMs'
+    # row statistics, applied in the q|k|v / fc1 / projector epilogues) against the
+    # LayerNorm kernels on the same weights and images.
+    shape = SiglipShape(depth=3)
+    sd = synthetic.make_siglip_weights(21, shape)
+    imgs = synthetic.make_images(5, 3, 224).cuda()
+    w = SiglipWeights(sd, shape, "cuda")
+    assert w.fold
+    outs = []
+    for folded in (True, False):
+        r = SiglipRunner(w, 3)
+        r.use_fold = folded
+        out = torch.zeros(768, 2048, dtype=torch.bfloat16, device="cuda")
+        r.run(imgs, out)
+        outs.append(out.float().cpu())
+    assert ops.read_device_status() == 0
+    assert _cos(outs[0], outs[1]) >= 0.9999
+    assert (outs[0] - outs[1]).abs().max().item() <= 0.03 * outs[1].abs().max().item()
+
+
 def test_sample_actions_end_to_end_small():
     expert = GemmaShape(width=1024, depth=2, mlp_dim=4096, num_heads=8, num_kv_heads=1, head_dim=256)
     lm = GemmaShape(width=2048, depth=2, mlp_dim=16384, num_heads=8, num_kv_heads=1, head_dim=256)
