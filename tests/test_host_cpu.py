@@ -55,6 +55,13 @@ def test_host_validation_without_gpu():
     assert L.pi05_linear(buf, buf, buf, 50, 1024, 1024, None, 0, None) == 4
     with pytest.raises(_lib.Pi05Error, match="PI05_ERR_INVALID_ARG"):
         _lib.call("pi05_gate_up_geglu", None, None, None, None, 50, 4096, 1024, None, 0, None)
+    # weight folding for the folded norms: argument checks before any launch
+    from pi05_infer import abi  # noqa: F401  (binds the signature)
+    f = L.pi05_fold_adarms
+    f.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int] + [ctypes.c_void_p] * 5
+    assert f(None, 8, 64, buf, buf, buf, buf, None) == 1 and "null" in _lib.last_error()
+    assert f(buf, 8, 60, buf, buf, buf, buf, None) == 2 and "k % 8" in _lib.last_error()
+    assert f(buf, 0, 64, buf, buf, buf, buf, None) == 2
 
 
 STRUCT_PROBE = r"""
