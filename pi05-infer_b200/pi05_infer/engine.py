@@ -248,9 +248,10 @@ class OpenPi0Inference:
                 self._set_key_valid(self._prefix_valid(observation))
                 self.capture_full(observation, noise.to(self.device).float())
                 self._full_key = key
-            self._refresh_key_valid(observation)
+            # Images first: their copy (1.8 MB) overlaps the host work that follows.
             for i, n in enumerate(observation.images):
                 self._static_imgs[i: i + 1].copy_(observation.images[n], non_blocking=True)
+            self._refresh_key_valid(observation)
             ids = observation.tokenized_prompt.reshape(-1)
             if ids.is_cuda:
                 self._ids.copy_(ids)
