@@ -1,22 +1,31 @@
 #!/usr/bin/env python
 """Benchmark: pi0.5 sample_actions hot path on B200 (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload denoise|e2e]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload e2e|long|denoise] [--no-cpu-baseline] [--no-duel]
 
 Workloads:
+  e2e     : config 3 -- sample_actions end to end at bs=1: SigLIP over 3 views +
+            200 prompt tokens -> 968-token prefix LM -> 10-step Euler denoise loop.
+  long    : config 5 -- the same with 5 views (P = 1480 prefix tokens).
   denoise : config 2 -- the 10-step Euler denoise loop of the Gemma-300M action
-            expert at bs=1 over a 968-token prefix KV cache that a random-init
-            Gemma-2B prefix LM fills from N(0,1) embeddings (one "step" = one full
-            10-step loop = what sample_actions spends after the prefix).
-  e2e     : config 3 -- sample_actions end to end (SigLIP + embeddings + prefix LM +
-            denoise loop).
+            expert over a 968-token prefix KV cache that a random-init Gemma-2B
+            prefix LM fills from N(0,1) embeddings.
 Synthetic seeded weights and inputs; no checkpoint or dataset.
+
+Besides `value` (ms per sample_actions, graph replayed, inputs resident) the line
+carries `e2e` (the public API with host inputs and a host read of the actions),
+`stages` (SigLIP, prefix LM and denoise timed alone, with TFLOP/s or GB/s against
+the measured peaks), the roofline of the dominant kernel, `cpu_baseline` and
+`kernel_duel` (the reference's Triton denoise kernels against this library's).
 
 Multi-GPU (torchrun): independent engine replicas, one observation each, no
 collective on the data path; timing is the max over ranks.
 
---impl reference times the reference's math on the host CPU (the oracle port of
-the reference path, all host threads) on bounded samples of the same workload.
+--impl reference runs the reference's own model code on the host CPU (its
+vendored GemmaModel from baseline/_ref for the expert and the prefix LM, the
+transformers SigLIP it imports) through full sample_actions calls of the same
+workload, on all host threads.
 """
 
 from __future__ import annotations
@@ -127,113 +136,134 @@ def _dist():
     return ws, rank, local
 
 
-def _load_oracle():
+def _load_file(name: str, path: str):
     import importlib.util
 
-    spec = importlib.util.spec_from_file_location("pi05_oracle", os.path.join(HERE, "oracle", "pi05_oracle.py"))
-    oracle = importlib.util.module_from_spec(spec)
-    spec.loader.exec_module(oracle)
-    return oracle
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, path)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
 
 
-class CpuSampler:
-    """Bounded CPU samples of the reference path (oracle port, fp32, all host threads).
+def _load_oracle():
+    return _load_file("pi05_oracle", os.path.join(HERE, "oracle", "pi05_oracle.py"))
 
-    One sample times one component of sample_actions on the host CPU: a SigLIP
-    encoder layer over the 3 views (768 tokens), a Gemma-2B prefix layer over 968
-    tokens, or one velocity evaluation of the 18-layer action expert (one Euler
-    step).  The whole call is estimated as 27 x SigLIP layer + 18 x prefix layer +
-    10 x velocity (config 3), or 10 x velocity (config 2).
-    """
+
+def _workload_shape(workload: str):
+    """(num_views, prefix_len) of a workload."""
+    return (5, 5 * 256 + 200) if workload == "long" else (3, PREFIX_LEN)
+
+
+def siglip_flops(views: int) -> float:
+    """Algorithmic FLOPs of SigLIP So400m/14 + projector over `views` 224^2 images
+    (patch embedding, 27 layers of q|k|v, attention, out-projection, MLP, projector)."""
+    t, w, f, h, d = 256, 1152, 4304, 16, 72
+    per = t * 588 * w * 2 + 27 * (t * w * 3 * w * 2 + 2 * 2 * t * t * d * h + t * w * w * 2 + 2 * t * w * f * 2)
+    return views * (per + t * w * 2048 * 2)
+
+
+def prefix_flops(p: int) -> float:
+    """Algorithmic FLOPs of the Gemma-2B prefix LM over p tokens: 17 full layers and a
+    last layer that only projects K and V."""
+    w, f, d, h = 2048, 16384, 256, 8
+    layer = p * w * 2560 * 2 + 2 * 2 * p * p * d * h + p * w * w * 2 + p * w * 2 * f * 2 + p * f * w * 2
+    return 17 * layer + p * w * 512 * 2
+
+
+class RefCpu:
+    """The reference's own model code on the host CPU (fp32, all host threads):
+    full sample_actions calls (e2e / long) or full 10-step denoise loops (denoise)
+    through ``baseline/ref_pipeline.py``; falls back to the CPU oracle port when
+    the reference is not installed under baseline/_ref."""
 
     def __init__(self, workload: str):
         import torch
 
         from pi05_infer import synthetic
-        from pi05_infer.config import GemmaShape, SiglipShape
 
         torch.set_num_threads(os.cpu_count() or 1)
         self.torch = torch
-        self.oracle = _load_oracle()
         self.workload = workload
-        self.sd = synthetic.make_expert_weights(0)
-        self.kv = [(k[0, 0], v[0, 0]) for k, v in synthetic.make_prefix_kv(1, 18, PREFIX_LEN)]
-        self.noise = synthetic.make_noise(2)[0]
-        self.pad = torch.ones(PREFIX_LEN, dtype=torch.bool)
-        self.table = self.oracle.adarms_table(self.sd, 18, 10, synthetic.EXPERT_PREFIX)
-        self.components = ["velocity"]
-        if workload == "e2e":
-            lm1 = GemmaShape(width=2048, depth=1, mlp_dim=16384, num_heads=8, num_kv_heads=1, head_dim=256)
-            self.sd_lm = synthetic.make_prefix_lm_weights(10, lm1)
-            self.embs = synthetic.make_prefix_embeddings(3, PREFIX_LEN, 2048)[0]
-            self.sd_vis = synthetic.make_siglip_weights(20, SiglipShape(depth=1))
-            self.imgs = synthetic.make_images(4, 3, 224)
-            self.components = ["siglip_layer", "prefix_layer", "velocity"]
-        self.times = {c: [] for c in self.components}
-
-    def run(self, comp: str, record: bool = True) -> float:
-        o = self.oracle
-        t0 = time.perf_counter()
-        if comp == "velocity":
-            o.velocity(self.sd, self.noise, self.kv, self.table[0], self.pad, 18, "fp32")
-        elif comp == "prefix_layer":
-            self._prefix_layer()
+        views, p = _workload_shape(workload)
+        self.views, self.p = views, p
+        g = torch.Generator().manual_seed(100)
+        self.images = torch.rand((views, 3, 224, 224), generator=g) * 2 - 1
+        self.tokens = torch.randint(0, synthetic.VOCAB_SIZE, (200,), generator=g)
+        self.pad = torch.ones(p, dtype=torch.bool)
+        self.noise = synthetic.make_noise(2)
+        self.kv = None
+        rl = _load_file("pi05_ref_loader", os.path.join(HERE, "baseline", "ref_loader.py"))
+        self.kind = "reference" if rl.available() else "port"
+        e2e = workload != "denoise"
+        if self.kind == "reference":
+            rp = _load_file("pi05_ref_pipeline", os.path.join(HERE, "baseline", "ref_pipeline.py"))
+            self.pipe = rp.RefCpuPipeline("e2e" if e2e else "denoise", num_views=views)
+            if not e2e:
+                self.kv = [(k, v) for k, v in synthetic.make_prefix_kv(1, 18, p)]
         else:
-            o.siglip_image_features(self.sd_vis, self.imgs, 1, "fp32")
-        dt = time.perf_counter() - t0
-        if record:
-            self.times[comp].append(dt)
-        return dt
+            self.oracle = _load_oracle()
+            sd = synthetic.make_expert_weights(0)
+            if e2e:
+                sd.update(synthetic.make_prefix_lm_weights(10, with_embedding=True))
+                sd.update(synthetic.make_siglip_weights(20))
+            self.sd = sd
+            self.kv = [(k[0, 0], v[0, 0]) for k, v in synthetic.make_prefix_kv(1, 18, p)]
 
-    def _prefix_layer(self):
-        """One full Gemma-2B decoder layer over the prefix (oracle math, fp32)."""
-        o = self.oracle
-        w, p = self.sd_lm, "paligemma_with_expert.paligemma.model.language_model.layers.0."
-        h = self.embs
-        xn = o.rms_norm(h, w[p + "input_layernorm.weight"], 1e-6, "fp32")
-        q = (xn @ w[p + "self_attn.q_proj.weight"].t()).view(-1, 8, 256)
-        k = xn @ w[p + "self_attn.k_proj.weight"].t()
-        v = xn @ w[p + "self_attn.v_proj.weight"].t()
-        a = o.attention(q, k, v, o.prefix_mask(self.pad), 1 / 16, "fp32")
-        h = h + a @ w[p + "self_attn.o_proj.weight"].t()
-        hn = o.rms_norm(h, w[p + "post_attention_layernorm.weight"], 1e-6, "fp32")
-        act = o.gelu_tanh(hn @ w[p + "mlp.gate_proj.weight"].t()) * (hn @ w[p + "mlp.up_proj.weight"].t())
-        return h + act @ w[p + "mlp.down_proj.weight"].t()
+    def run(self) -> float:
+        """One full call; returns its wall time in ms."""
+        t0 = time.perf_counter()
+        with self.torch.no_grad():
+            if self.kind == "reference":
+                self.pipe.sample_actions(self.images, self.tokens, self.pad, self.noise, kv=self.kv)
+            else:
+                o = self.oracle
+                kv = self.kv
+                if self.workload != "denoise":
+                    feats = o.siglip_image_features(self.sd, self.images, 27, "fp32")
+                    from pi05_infer import synthetic
 
-    def estimate_ms(self) -> float:
-        mean = {c: statistics.mean(v) for c, v in self.times.items() if v}
-        ms = 10 * mean["velocity"]
-        if self.workload == "e2e":
-            ms += 27 * mean["siglip_layer"] + 18 * mean["prefix_layer"]
-        return ms * 1e3
+                    lang = o.embed_language(self.sd[synthetic.EMBED_KEY], self.tokens, "fp32")
+                    kv = o.prefix_lm_kv(self.sd, o.embed_prefix(feats, lang), self.pad, 18, "fp32")
+                o.denoise_loop(self.sd, self.noise[0], kv, self.pad, 18, 10, "fp32")
+        return (time.perf_counter() - t0) * 1e3
 
     def describe(self) -> str:
-        n = {c: len(v) for c, v in self.times.items()}
-        if self.workload == "e2e":
-            return (f"{n} timed component samples (fp32 torch CPU restatement of the reference path); "
-                    "sample_actions estimated as 27 x SigLIP layer + 18 x Gemma-2B prefix layer + 10 x expert velocity")
-        return f"{n['velocity']} expert velocity evaluations (fp32); loop = 10 x velocity"
+        what = ("full sample_actions calls (SigLIP So400m over %d views, Gemma-2B prefix LM over %d tokens with "
+                "use_cache=True, 10 Euler steps of the Gemma-300M expert)" % (self.views, self.p)
+                if self.workload != "denoise" else
+                "full 10-step Euler denoise loops of the Gemma-300M expert over a %d-token prefix KV cache" % self.p)
+        if self.kind == "reference":
+            return ("the reference's vendored GemmaModel (pi05_infer/gemma/modeling_gemma.py from baseline/_ref) for "
+                    "the expert and the prefix LM, transformers SiglipVisionModel, fp32 torch on the host CPU: " + what)
+        return "CPU oracle port of the reference path (fp32 torch): " + what
 
 
 def run_reference(args):
-    """CPU reference arm: the oracle port of the reference path on the host cores."""
+    """CPU reference arm: the reference's model code on the host cores, full calls."""
     ws, rank, _ = _dist()
     if rank != 0:
         return 0
-    cs = CpuSampler(args.workload)
-    for i in range(min(args.warmup, len(cs.components))):
-        cs.run(cs.components[i % len(cs.components)], record=False)
-    n = max(len(cs.components), min(args.steps, 60))
-    for i in range(n):
-        cs.run(cs.components[i % len(cs.components)])
-    ms = cs.estimate_ms()
+    rc = RefCpu(args.workload)
+    warm = min(args.warmup, 3)
+    for _ in range(warm):
+        rc.run()
+    # Each step is one full call of the workload; the count is capped so that the
+    # run ends within a few minutes (about 4 s per e2e call on 16 host cores).
+    cap = 15 if args.workload != "denoise" else 30
+    n = max(1, min(args.steps, cap))
+    times = [rc.run() for _ in range(n)]
+    ms = statistics.mean(times)
     line = {
-        "impl": "reference", "metric": METRIC, "value": ms, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,0.02) weights, N(0,1) inputs)",
+        "impl": "reference", "metric": METRIC, "value": ms, "unit": UNIT, "n_gpus": ws, "steps": n,
+        "steps_requested": args.steps, "warmup": warm, "ms_per_step": ms, "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,0.02) weights, U[-1,1] images, uniform token ids, N(0,1) noise)",
         "config": _config(args, ws),
-        "cpu_baseline": {"value": ms, "unit": UNIT, "cores": cs.torch.get_num_threads(), "kind": "port",
-                         "sample": cs.describe() + f" (timed samples capped at 60 of --steps {args.steps})"},
+        "cpu_baseline": {"value": ms, "unit": UNIT, "cores": rc.torch.get_num_threads(), "kind": rc.kind,
+                         "sample": rc.describe() + f"; mean of {n} timed calls after {warm} warm-up calls"},
         "e2e": {"value": ms, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -241,13 +271,33 @@ def run_reference(args):
 
 
 def _config(args, ws):
-    if args.workload == "e2e":
-        return {"workload": "config3: sample_actions end to end (SigLIP 3x224^2 + 200 tokens -> 968-token prefix LM -> 10-step denoise)",
-                "global_batch": ws, "seq_len": PREFIX_LEN, "parallelism": f"replicas{ws}",
-                "l2": "inputs larger than L2 (weights streamed every call)"}
-    return {"workload": "config2: 10-step Euler denoise loop, Gemma-300M expert, bs=1, 968-token prefix KV from a random Gemma-2B prefix",
+    views, p = _workload_shape(args.workload)
+    if args.workload in ("e2e", "long"):
+        name = "config3" if args.workload == "e2e" else "config5"
+        return {"workload": f"{name}: sample_actions end to end (SigLIP {views}x224^2 + 200 tokens -> {p}-token "
+                            "prefix LM -> 10-step denoise)",
+                "global_batch": ws, "seq_len": p, "parallelism": f"replicas{ws}",
+                "l2": "inputs larger than L2 (6.5 GB of weights streamed every call)"}
+    return {"workload": "config2: 10-step Euler denoise loop, Gemma-300M expert, bs=1, 968-token prefix KV from a "
+                        "random Gemma-2B prefix",
             "global_batch": ws, "seq_len": PREFIX_LEN + 50, "parallelism": f"replicas{ws}",
             "l2": "inputs larger than L2: 623 MB of bf16 expert weights streamed per Euler step (5x L2)"}
+
+
+def _time_replays(fn, n: int, dev, stream) -> float:
+    import torch
+
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(n):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    return e0.elapsed_time(e1) / n
 
 
 def run_ours(args):
@@ -266,19 +316,19 @@ def run_ours(args):
         pg = dist
 
     from pi05_infer import _lib, synthetic
-    from pi05_infer.config import GEMMA_2B, GEMMA_300M
     from pi05_infer.engine import OpenPi0Inference
-    from pi05_infer.expert import DenoiseRunner, ExpertWeights
 
     hbm_peak, bf16_peak, bf16_sus, peak_src = _peaks()
+    views, p = _workload_shape(args.workload)
+    e2e_work = args.workload in ("e2e", "long")
     # Weights: same model on every replica; observation seeds differ per rank.
-    engine = OpenPi0Inference.synthetic(device=dev, seed=0, with_vision=(args.workload == "e2e"))
+    engine = OpenPi0Inference.synthetic(device=dev, seed=0, with_vision=e2e_work, num_views=views)
     obs = engine.synthetic_observation(seed=100 + rank)
     noise = synthetic.make_noise(2 + rank).to(dev)
     engine.prepare(obs)  # prefix LM fills the KV cache (and SigLIP for e2e)
 
     launches0 = _lib.lib().pi05_launch_count()
-    if args.workload == "e2e":
+    if e2e_work:
         step_fn = engine.capture_full(obs, noise)
     else:
         step_fn = engine.capture_denoise(noise)
@@ -287,6 +337,13 @@ def run_ours(args):
     def barrier():
         if pg is not None:
             pg.barrier()
+
+    def max_over_ranks(v):
+        if pg is None:
+            return v
+        t = torch.tensor([v], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return float(t.item())
 
     for _ in range(args.warmup):
         step_fn()
@@ -304,36 +361,32 @@ def run_ours(args):
         clk.sample_once()  # the replays queued above are still executing
         torch.cuda.synchronize(dev)
     barrier()
-    ms = e0.elapsed_time(e1) / args.steps
-    if pg is not None:
-        t = torch.tensor([ms], device=dev)
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
 
-    # Denoise-step sub-metric: the config-2 loop (10 Euler steps over the prefix
-    # cache just filled) replayed alone as its own CUDA graph.
-    den_fn = step_fn if args.workload == "denoise" else engine.capture_denoise(noise)
-    den_ms = ms
-    if args.workload != "denoise":
-        for _ in range(3):
-            den_fn()
+    # Stages, each captured and replayed alone: the config-2 loop (10 Euler steps
+    # over the prefix cache just filled), and for e2e the SigLIP tower and the
+    # prefix LM.
+    den_fn = step_fn if not e2e_work else engine.capture_denoise(noise)
+    den_ms = ms if not e2e_work else max_over_ranks(_time_replays(den_fn, max(10, args.steps // 2), dev, stream))
+    denoise_us = den_ms * 1e3 / engine.config.num_steps
+    step_bytes = engine.denoise_step_bytes()
+    stages = {"denoise": {"us_per_step": denoise_us, "algorithmic_bytes": step_bytes,
+                          "hbm_gbs": step_bytes / (denoise_us * 1e-6) / 1e9,
+                          "frac_of_measured_hbm": step_bytes / (denoise_us * 1e-6) / 1e9 / hbm_peak}}
+    if e2e_work:
+        for name, flops in (("siglip", siglip_flops(views)), ("prefix", prefix_flops(p))):
+            fn = engine.capture_stage(name)
+            st_ms = max_over_ranks(_time_replays(fn, max(10, args.steps // 2), dev, stream))
+            tf = flops / (st_ms * 1e-3) / 1e12
+            stages[name] = {"ms": st_ms, "gflop": flops / 1e9, "tflops": tf, "frac_of_measured_bf16_burst": tf / bf16_peak,
+                            "frac_of_measured_bf16_sustained": tf / bf16_sus}
         torch.cuda.synchronize(dev)
-        e0.record(stream)
-        n_den = max(10, args.steps // 2)
-        for _ in range(n_den):
-            den_fn()
-        e1.record(stream)
-        torch.cuda.synchronize(dev)
-        den_ms = e0.elapsed_time(e1) / n_den
-        if pg is not None:
-            t = torch.tensor([den_ms], device=dev)
-            pg.all_reduce(t, op=pg.ReduceOp.MAX)
-            den_ms = float(t.item())
 
-    # End to end through the public API: host noise (pinned) in, host actions out.
+    # End to end through the public API: host images / ids / noise (pinned) in,
+    # host actions out.
     noise_host = synthetic.make_noise(2 + rank).pin_memory()
     for _ in range(2):  # warm-up through the same API (graph capture on first use)
-        if args.workload == "e2e":
+        if e2e_work:
             engine.sample_actions(obs, noise=noise_host)["actions"].cpu()
         else:
             engine.denoise(noise_host)["actions"].cpu()
@@ -342,16 +395,12 @@ def run_ours(args):
     e2e_n = max(10, args.steps // 4)
     t0 = time.perf_counter()
     for _ in range(e2e_n):
-        if args.workload == "e2e":
+        if e2e_work:
             out = engine.sample_actions(obs, noise=noise_host)["actions"].cpu()
         else:
             out = engine.denoise(noise_host)["actions"].cpu()
-    e2e_ms = (time.perf_counter() - t0) * 1e3 / e2e_n
-    if pg is not None:
-        t = torch.tensor([e2e_ms], device=dev)
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    h2d = noise_host.numel() * 4 + (engine.observation_host_bytes(obs) if args.workload == "e2e" else 0)
+    e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3 / e2e_n)
+    h2d = noise_host.numel() * 4 + (engine.observation_host_bytes(obs) if e2e_work else 0)
     d2h = out.numel() * out.element_size()
 
     # Dominant kernel (largest share of the step in the ncu launch list): the
@@ -360,18 +409,17 @@ def run_ours(args):
     roof = engine.time_down_kernel(reps=20)
     achieved = roof["bytes"] / (roof["us"] * 1e-6) / 1e9
     traffic = _traffic_from_profiles("skinny_gemm_gated_resid_down")
-    denoise_us = engine.last_denoise_step_us(den_ms)
 
     line = {
         "metric": METRIC, "value": ms, "unit": UNIT, "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded random-init weights, N(0,1) prefix embeddings and noise)",
+        "data": "synthetic (seeded random-init weights, U[-1,1] images, uniform token ids, N(0,1) noise)",
         "config": _config(args, ws),
         "throughput_obs_per_s": ws * 1000.0 / ms,
-        "denoise_step": {"us": denoise_us, "algorithmic_bytes": engine.denoise_step_bytes(),
-                         "hbm_gbs": engine.denoise_step_bytes() / (denoise_us * 1e-6) / 1e9 if denoise_us else None,
-                         "frac_of_measured_hbm": (engine.denoise_step_bytes() / (denoise_us * 1e-6) / 1e9 / hbm_peak)
-                         if denoise_us else None},
+        "stages": stages,
+        "denoise_step": {"us": denoise_us, "algorithmic_bytes": step_bytes,
+                         "hbm_gbs": stages["denoise"]["hbm_gbs"],
+                         "frac_of_measured_hbm": stages["denoise"]["frac_of_measured_hbm"]},
         "roofline": {"kernel": "skinny_gemm_kernel<GATED_RESID,64,3> (down_proj + gated residual, M=50, N=1024, "
                                "K=4096)",
                      "bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
@@ -381,18 +429,24 @@ def run_ours(args):
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(),
     }
+    engine.release_graphs()
+    del engine
+    torch.cuda.empty_cache()
     if ws == 1 and rank == 0 and not args.no_cpu_baseline:
-        cs = CpuSampler(args.workload)
-        for c in cs.components:
-            cs.run(c, record=False)
-        for _ in range(3):
-            for c in cs.components:
-                cs.run(c)
-        line["cpu_baseline"] = {"value": cs.estimate_ms(), "unit": UNIT, "cores": cs.torch.get_num_threads(),
-                                "kind": "port", "sample": cs.describe()}
+        rc = RefCpu(args.workload)
+        rc.run()
+        times = [rc.run()]
+        line["cpu_baseline"] = {"value": statistics.mean(times), "unit": UNIT, "cores": rc.torch.get_num_threads(),
+                                "kind": rc.kind, "sample": rc.describe() + "; one timed call after one warm-up call"}
+    if ws == 1 and rank == 0 and not args.no_duel:
+        import kernel_cases
+
+        try:
+            line["kernel_duel"] = kernel_cases.kernel_duel(reps=20)
+        except Exception as e:  # the reference's Triton path failing must not lose the bench line
+            line["kernel_duel"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
     if rank == 0:
         print(json.dumps(line), flush=True)
-    engine.release_graphs()
     if pg is not None:
         pg.barrier()
         pg.destroy_process_group()
@@ -405,8 +459,9 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["denoise", "e2e"], default="e2e")
+    ap.add_argument("--workload", choices=["e2e", "long", "denoise"], default="e2e")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-duel", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -42,7 +42,9 @@ const char* pi05_last_error(void);
 size_t pi05_workspace_bytes(int max_tokens, int max_kv);
 
 /* Synchronise `stream`, copy the workspace status word to *host_status and clear
- * it.  Returns PI05_ERR_DEVICE if the word was non-zero. */
+ * it.  Returns PI05_ERR_DEVICE if the word was non-zero; in that case the
+ * workspace's split-K counters are also reset, so that the next call starts from
+ * a clean state after a kernel gave up on a wait. */
 int pi05_read_device_status(void* workspace, int* host_status, void* stream);
 
 /* Number of kernel launches this library has issued in this process (a CUDA-graph
@@ -57,6 +59,16 @@ void pi05_debug_set_splits(int splits);
  * append per-CTA timestamp records to (word 0: record counter, word 1: capacity
  * in records; record i at words 8 + 8 i).  NULL disables.  Process-wide. */
 void pi05_debug_set_trace(unsigned long long* buf);
+
+/* Failure-path test hook -- no counterpart in the reference.  While armed
+ * (skip_split >= 0), the split-K GEMMs run their global-memory split-K path, in
+ * which split `skip_split` of the first output tile neither publishes its
+ * partial nor arrives at the tile's counter, and the arrival wait gives up after
+ * wait_ns nanoseconds (0 = the built-in 2 s limit).  The waiting CTAs then set
+ * PI05_DEV_TIMEOUT_EPILOGUE in the device status word, skip the tile's epilogue
+ * and exit normally, so the context stays usable.  skip_split < 0 disarms.
+ * Process-wide; for tests only. */
+void pi05_debug_set_fault(int skip_split, unsigned long long wait_ns);
 
 /* ---- fused denoise ops (swap-AB tcgen05 GEMM + fused epilogue) ---------- */
 
@@ -87,6 +99,14 @@ int pi05_qkv_rope_kv(const void* x, const void* w, const void* cos, const void* 
  * different host threads on one device) race and must be serialised by the caller. */
 int pi05_gate_up_geglu_noalloc(const void* x, const void* wg, const void* wu, void* out, int m, int n, int k,
                                void* stream);
+
+/* Status of pi05_gate_up_geglu_noalloc on the current device -- no counterpart in
+ * the reference.  Synchronises `stream`, copies the built-in scratch's status word
+ * (nonzero = a kernel wait timed out and its output is not valid) to *host_status,
+ * clears it, and returns PI05_ERR_DEVICE when it was nonzero.  The word is sticky:
+ * calls of the entry point do not clear it, so a timeout of any earlier call is
+ * reported by the next read.  Allocates nothing. */
+int pi05_gate_up_geglu_noalloc_status(int* host_status, void* stream);
 
 /* out[m, n] = bf16(resid[m, n] + bf16(x @ w^T) * bf16(gate[n])); gate NULL -> plain residual.
  * Replaces o_proj / down_proj + _gated_residual

@@ -72,6 +72,13 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // Buffer set by pi05_debug_set_trace (per-CTA GEMM timestamps), or nullptr.
 unsigned long long* debug_trace_buffer();
 
+// Failure-path test hook set by pi05_debug_set_fault (skip_split < 0 = off).
+struct DebugFault {
+  int skip_split = -1;
+  unsigned long long wait_ns = 0;
+};
+DebugFault debug_fault();
+
 // Count of kernel launches issued by this library (all threads, all devices).
 void count_launch();
 long long launch_count();

@@ -15,6 +15,11 @@
 // 4 KiB header (status word and barrier counters), held by every GPU that loads
 // the library until the process exits.  When a shape would need more partial
 // space, fewer K splits are used (down to one, which needs none).
+//
+// Device status: the kernel's bounded waits report a timeout into the status
+// word of the built-in header.  Each call clears the barrier counters but leaves
+// the status word alone, so a timeout stays visible until the caller reads (and
+// clears) it with pi05_gate_up_geglu_noalloc_status.
 #include <mutex>
 
 #include "../../include/pi05_b200.h"
@@ -89,9 +94,10 @@ extern "C" int pi05_gate_up_geglu_noalloc(const void* x, const void* wg, const v
   int rc = scratch_address(&base);
   if (rc) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  // The barrier counters and the status word must start at zero; a call that
-  // gave up on a wait could have left them otherwise.  The partials need no clearing.
-  cudaError_t e = cudaMemsetAsync(base, 0, kNoAllocHeaderBytes, st);
+  // The barrier counters must start at zero; a call that gave up on a wait could
+  // have left them otherwise.  The status word (bytes 0..63) is kept until read;
+  // the partials need no clearing.
+  cudaError_t e = cudaMemsetAsync(static_cast<char*>(base) + 64, 0, kNoAllocHeaderBytes - 64, st);
   if (e != cudaSuccess) {
     set_last_error("gate_up_geglu_noalloc: clearing the scratch header failed: %s", cudaGetErrorString(e));
     return PI05_ERR_LAUNCH;
@@ -117,4 +123,30 @@ extern "C" int pi05_gate_up_geglu_noalloc(const void* x, const void* wg, const v
   while (splits > 1 && (size_t)splits * per_split > kNoAllocPartialBytes) --splits;
   if (2 * p.n_tiles > kNoAllocCounters) splits = 1;
   return skinny_gemm_run(SK_EPI_GEGLU, p, wg, wu, n, n, x, k, splits, stream);
+}
+
+extern "C" int pi05_gate_up_geglu_noalloc_status(int* host_status, void* stream) {
+  if (host_status == nullptr) {
+    set_last_error("gate_up_geglu_noalloc_status: null pointer");
+    return PI05_ERR_INVALID_ARG;
+  }
+  void* base = nullptr;
+  int rc = scratch_address(&base);
+  if (rc) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int v = 0;
+  cudaError_t e = cudaMemcpyAsync(&v, base, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(base, 0, sizeof(int), st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) {
+    set_last_error("gate_up_geglu_noalloc_status: status read failed: %s", cudaGetErrorString(e));
+    return PI05_ERR_LAUNCH;
+  }
+  *host_status = v;
+  if (v != 0) {
+    set_last_error("gate_up_geglu_noalloc: device status word 0x%x (a kernel wait timed out)", v);
+    return PI05_ERR_DEVICE;
+  }
+  return PI05_OK;
 }

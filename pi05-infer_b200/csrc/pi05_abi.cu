@@ -13,6 +13,8 @@ namespace {
 
 std::atomic<int> g_split_override{0};
 std::atomic<unsigned long long*> g_trace{nullptr};
+std::atomic<int> g_fault_split{-1};
+std::atomic<unsigned long long> g_fault_wait_ns{0};
 
 inline bool nz(const void* p) { return p != nullptr; }
 
@@ -35,6 +37,12 @@ int ws_for_skinny(void* ws, size_t bytes, SkinnyParams* p) {
 
 namespace pi05 {
 unsigned long long* debug_trace_buffer() { return g_trace.load(); }
+DebugFault debug_fault() {
+  DebugFault f;
+  f.skip_split = g_fault_split.load();
+  f.wait_ns = g_fault_wait_ns.load();
+  return f;
+}
 }  // namespace pi05
 
 extern "C" {
@@ -72,7 +80,11 @@ int pi05_read_device_status(void* workspace, int* host_status, void* stream) {
   }
   *host_status = v;
   if (v != 0) {
-    set_last_error("device status word 0x%x (kernel wait timed out)", v);
+    // A kernel that gave up on a wait may have left split-K counters armed.
+    e = cudaMemsetAsync(static_cast<char*>(workspace) + kWsCounterOffset, 0, kWsMaxCounters * sizeof(int), st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    set_last_error("device status word 0x%x (kernel wait timed out)%s", v,
+                   e == cudaSuccess ? "" : "; resetting the split-K counters failed");
     return PI05_ERR_DEVICE;
   }
   return PI05_OK;
@@ -83,6 +95,11 @@ long long pi05_launch_count(void) { return launch_count(); }
 void pi05_debug_set_splits(int splits) { g_split_override.store(std::max(0, splits)); }
 
 void pi05_debug_set_trace(unsigned long long* buf) { g_trace.store(buf); }
+
+void pi05_debug_set_fault(int skip_split, unsigned long long wait_ns) {
+  g_fault_wait_ns.store(wait_ns);
+  g_fault_split.store(skip_split < 0 ? -1 : skip_split);
+}
 
 int pi05_gate_up_geglu(const void* x, const void* wg, const void* wu, void* out, int m, int n, int k,
                        void* workspace, size_t workspace_bytes, void* stream) {

@@ -384,21 +384,25 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 ? 2 : 1))
       const size_t tile_id = (size_t)blockIdx.y * p.n_tiles + tile;
       float* part = p.accum + tile_id * p.splits * TOK * kBM;
       float* mine = part + (size_t)split * TOK * kBM;
-      for (int idx = et * 4; idx < mt * kBM; idx += kEpiThreads * 4)
-        __stcg(reinterpret_cast<float4*>(mine + idx),
-               make_float4(stage_tile[idx], stage_tile[idx + 1], stage_tile[idx + 2], stage_tile[idx + 3]));
+      // Test hook: this split of tile 0 leaves its partial and arrival out.
+      const bool skip = p.fault_skip_split == split && tile_id == 0;
+      if (!skip)
+        for (int idx = et * 4; idx < mt * kBM; idx += kEpiThreads * 4)
+          __stcg(reinterpret_cast<float4*>(mine + idx),
+                 make_float4(stage_tile[idx], stage_tile[idx + 1], stage_tile[idx + 2], stage_tile[idx + 3]));
       __threadfence();
       named_bar_sync(1, kEpiThreads);
       if (p.trace != nullptr) t_pub = globaltimer_ns();
       int* arrive = p.counters + 2 * tile_id;
       int* depart = arrive + 1;
       if (et == 0) {
-        atomicAdd(arrive, 1);
+        if (!skip) atomicAdd(arrive, 1);
         int seen = ld_acquire(arrive);
         if (seen < p.splits) {
           const uint64_t t0 = globaltimer_ns();
+          const uint64_t limit = p.wait_ns != 0 ? p.wait_ns : kWaitTimeoutNs;
           while ((seen = ld_acquire(arrive)) < p.splits) {
-            if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+            if (globaltimer_ns() - t0 > limit) {
               report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
               break;
             }
@@ -765,7 +769,13 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
         break;
     }
   }
-  const bool use_cluster = p.allow_cluster != 0 && max_cl > 1 && !cluster_disabled();
+  // An armed failure hook (pi05_debug_set_fault) selects the global split-K path it acts on.
+  const DebugFault fault = debug_fault();
+  if (fault.skip_split >= 0) {
+    p.fault_skip_split = fault.skip_split;
+    p.wait_ns = fault.wait_ns;
+  }
+  const bool use_cluster = p.allow_cluster != 0 && max_cl > 1 && !cluster_disabled() && fault.skip_split < 0;
   if (splits_override > 0) {
     p.splits = std::min(splits_override, p.kb_total);
     p.cluster = (use_cluster && p.splits > 1 && p.splits <= max_cl) ? 1 : 0;

@@ -112,6 +112,11 @@ struct SkinnyParams {
   //  first weight TMA issued}.
   unsigned long long* trace = nullptr;
   int trace_tag = 0;
+  // Failure-path test hook (global split-K path only; set by the launcher from
+  // pi05_debug_set_fault): split fault_skip_split of tile 0 neither publishes nor
+  // arrives, and the arrival wait gives up after wait_ns (0 = kWaitTimeoutNs).
+  int fault_skip_split = -1;
+  unsigned long long wait_ns = 0;
   // workspace
   float* accum = nullptr;   // fp32 split-K accumulator (zero on entry, left zero on exit)
   size_t accum_bytes = 0;

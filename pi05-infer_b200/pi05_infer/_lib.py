@@ -38,9 +38,11 @@ SIGNATURES = {
     "pi05_read_device_status": (_I, [_P, ctypes.POINTER(_I), _P]),
     "pi05_debug_set_splits": (None, [_I]),
     "pi05_debug_set_trace": (None, [_P]),
+    "pi05_debug_set_fault": (None, [_I, ctypes.c_ulonglong]),
     "pi05_launch_count": (ctypes.c_longlong, []),
     "pi05_gate_up_geglu": (_I, [_P, _P, _P, _P, _I, _I, _I, _P, _Z, _P]),
     "pi05_gate_up_geglu_noalloc": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),
+    "pi05_gate_up_geglu_noalloc_status": (_I, [ctypes.POINTER(_I), _P]),
     "pi05_qkv_rope_kv": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _Z, _P]),
     "pi05_linear_gated_residual": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P, _Z, _P]),
     "pi05_linear": (_I, [_P, _P, _P, _I, _I, _I, _P, _Z, _P]),

@@ -22,28 +22,40 @@ SUPPORTED_CONFIGS = ("pi05_libero", "pi05_turtle", "pi05")
 
 
 def _load_state_dict(model_path: str) -> Dict[str, torch.Tensor]:
+    """The checkpoint's state dict, searched in the reference's order
+    (``builder.py:77-106``): an FSDP ``model_state_dict/full_weights.pt``, then
+    ``actor/model_state_dict/full_weights.pt``, then ``*.safetensors`` files; a path
+    to a single ``.pt`` / ``.safetensors`` file is also accepted."""
+    path = model_path
     if os.path.isdir(model_path):
-        files = sorted(glob.glob(os.path.join(model_path, "*.safetensors")))
-        if files:
+        for cand in (os.path.join(model_path, "model_state_dict", "full_weights.pt"),
+                     os.path.join(model_path, "actor", "model_state_dict", "full_weights.pt"),
+                     os.path.join(model_path, "full_weights.pt")):
+            if os.path.exists(cand):
+                path = cand
+                break
+        else:
+            files = sorted(glob.glob(os.path.join(model_path, "*.safetensors")))
+            if not files:
+                raise FileNotFoundError(f"no full_weights.pt or *.safetensors under {model_path}")
             from safetensors.torch import load_file
 
             sd: Dict[str, torch.Tensor] = {}
             for f in files:
                 sd.update(load_file(f))
             return sd
-        pt = os.path.join(model_path, "full_weights.pt")
-        if os.path.exists(pt):
-            model_path = pt
-        else:
-            raise FileNotFoundError(f"no *.safetensors or full_weights.pt under {model_path}")
-    obj = torch.load(model_path, map_location="cpu", weights_only=True)
+    if path.endswith(".safetensors"):
+        from safetensors.torch import load_file
+
+        return load_file(path)
+    obj = torch.load(path, map_location="cpu", weights_only=True)
     if isinstance(obj, dict) and "state_dict" in obj and isinstance(obj["state_dict"], dict):
         obj = obj["state_dict"]
-    # FSDP / wrapper prefixes (builder.py:88-101)
+    # FSDP / wrapper prefixes
     out = {}
     for k, v in obj.items():
-        for pre in ("module.", "model.", "_orig_mod."):
-            if k.startswith(pre) and not k.startswith("model.layers"):
+        for pre in ("module.", "_orig_mod."):
+            if k.startswith(pre):
                 k = k[len(pre):]
         out[k] = v
     return out
@@ -66,6 +78,12 @@ def build_model(model_path: str, config_name: str = "pi05_libero", *, data_kwarg
 
 
 def get_model(cfg: Any, torch_dtype=None) -> OpenPi0Inference:  # noqa: ARG001
-    """``get_model(cfg)`` (``builder.py:141-151``): ``cfg`` carries ``model_path`` / ``config_name``."""
-    get = cfg.get if isinstance(cfg, dict) else (lambda k, d=None: getattr(cfg, k, d))
-    return build_model(get("model_path"), get("config_name", "pi05_libero"))
+    """``get_model(cfg)`` (``builder.py:141-151``): ``cfg.model_path``, ``cfg.openpi``
+    (a mapping with ``config_name`` and config overrides) and ``cfg.openpi_data``;
+    attribute- or dict-style ``cfg`` alike."""
+    def get(k, d=None):
+        return cfg.get(k, d) if isinstance(cfg, dict) else getattr(cfg, k, d)
+
+    openpi_cfg = dict(get("openpi") or {})
+    config_name = openpi_cfg.pop("config_name", None) or get("config_name", "pi05_libero")
+    return build_model(get("model_path"), config_name, data_kwargs=get("openpi_data"), **openpi_cfg)

@@ -48,8 +48,16 @@ class Observation:
                    tokenized_prompt_mask=d["tokenized_prompt_mask"], state=d["state"])
 
 
+def _slice_observation(obs: Observation, i: int) -> Observation:
+    """Observation ``i`` of a batch, with its leading batch dimension kept (size 1)."""
+    sl = slice(i, i + 1)
+    return Observation({k: v[sl] for k, v in obs.images.items()}, {k: v[sl] for k, v in obs.image_masks.items()},
+                       obs.tokenized_prompt[sl], obs.tokenized_prompt_mask[sl],
+                       obs.state[sl] if obs.state is not None else None)
+
+
 class OpenPi0Inference:
-    """bs=1 pi0.5 inference engine (one observation per call; one engine per GPU for replicas)."""
+    """pi0.5 inference engine on one GPU (one engine per GPU for replicas)."""
 
     def __init__(self, config: Optional[EngineConfig] = None, state_dict: Optional[Dict[str, torch.Tensor]] = None,
                  device="cuda", prefix_len: int = 968, num_views: int = 3, prompt_len: int = 200):
@@ -76,14 +84,17 @@ class OpenPi0Inference:
         self._kv_pinned = None
         self._ids_pinned = None   # pinned int32 staging of the prompt ids
         self._ids_event = None
+        self._inputs_read = None  # event after the input copies of the last call
         if state_dict is not None:
             self.load_state_dict(state_dict)
 
     # ------------------------------------------------------------------ weights
     @classmethod
     def synthetic(cls, device="cuda", seed: int = 0, with_vision: bool = False, with_prefix: bool = True,
-                  config: Optional[EngineConfig] = None) -> "OpenPi0Inference":
-        """Random-init weights (N(0, 0.02)) drawn on the device (benchmarks, smoke tests)."""
+                  config: Optional[EngineConfig] = None, num_views: int = 3, prompt_len: int = 200
+                  ) -> "OpenPi0Inference":
+        """Random-init weights (N(0, 0.02)) drawn on the device (benchmarks, smoke tests);
+        the prefix holds ``num_views`` x 256 image tokens and ``prompt_len`` text tokens."""
         dev = torch.device(device)
         sd = {}
         sd.update(synthetic.make_expert_weights(seed, GEMMA_300M, device=dev))
@@ -91,7 +102,9 @@ class OpenPi0Inference:
             sd.update(synthetic.make_prefix_lm_weights(seed + 10, GEMMA_2B, device=dev, with_embedding=with_vision))
         if with_vision:
             sd.update(synthetic.make_siglip_weights(seed + 20, device=dev))
-        eng = cls(config, sd, device=dev)
+        npatch = (config or EngineConfig()).siglip.num_patches
+        eng = cls(config, sd, device=dev, prefix_len=num_views * npatch + prompt_len, num_views=num_views,
+                  prompt_len=prompt_len)
         return eng
 
     def load_state_dict(self, sd: Dict[str, torch.Tensor]) -> None:
@@ -234,11 +247,32 @@ class OpenPi0Inference:
     # ------------------------------------------------------------ public API
     @torch.no_grad()
     def sample_actions(self, observation: Observation, noise: Optional[torch.Tensor] = None) -> dict:
-        """Full inference: prefix cache + ``num_steps`` flow_ode Euler steps (engine.py:344-406)."""
-        prefix, den = self._runners()
+        """Full inference: prefix cache + ``num_steps`` flow_ode Euler steps (engine.py:344-406).
+
+        ``bsize = observation.state.shape[0]`` (``engine.py:350``); ``noise`` is
+        ``[bsize, action_horizon, action_dim]`` or None (drawn N(0, 1) on the device).
+        Observations of a batch are independent: each runs the captured pipeline
+        in turn on this engine's GPU.  Returns ``{"actions": [bsize, H, 32]}`` fp32 on
+        the device.  The caller's (pinned) input buffers have been read when this
+        returns, so they may be reused at once."""
+        bsize = int(observation.state.shape[0]) if observation.state is not None and observation.state.dim() > 1 \
+            else int(observation.tokenized_prompt.shape[0])
+        h, a = self.config.action_horizon, self.config.action_dim
         if noise is None:
-            noise = torch.randn((1, self.config.action_horizon, self.config.action_dim), dtype=torch.float32,
-                                device=self.device)
+            noise = torch.randn((bsize, h, a), dtype=torch.float32, device=self.device)
+        noise = noise.reshape(-1, h, a)
+        if noise.shape[0] != bsize:
+            raise ValueError(f"noise has batch {noise.shape[0]}, observation has {bsize}")
+        if bsize == 1:
+            return {"actions": self._sample_one(observation, noise[0])}
+        outs = [self._sample_one(_slice_observation(observation, i), noise[i]) for i in range(bsize)]
+        return {"actions": torch.cat(outs, 0)}
+
+    def _sample_one(self, observation: Observation, noise: torch.Tensor) -> torch.Tensor:
+        prefix, den = self._runners()
+        for n, img in observation.images.items():
+            if img.shape[0] != 1:
+                raise ValueError(f"image {n!r}: expected one observation, got batch {img.shape[0]}")
         if self.use_cuda_graph and self.vision is not None and self.embed_table is not None:
             # The whole pipeline (SigLIP, embeddings, prefix LM, Euler loop) replays as
             # one CUDA graph captured on the first call; each call only refreshes its
@@ -248,6 +282,7 @@ class OpenPi0Inference:
                 self._set_key_valid(self._prefix_valid(observation))
                 self.capture_full(observation, noise.to(self.device).float())
                 self._full_key = key
+            stream = torch.cuda.current_stream(self.device)
             # Images first: their copy (1.8 MB) overlaps the host work that follows.
             for i, n in enumerate(observation.images):
                 self._static_imgs[i: i + 1].copy_(observation.images[n], non_blocking=True)
@@ -265,16 +300,23 @@ class OpenPi0Inference:
                     self._ids_event.synchronize()
                 self._ids_pinned.copy_(ids)
                 self._ids.copy_(self._ids_pinned, non_blocking=True)
-                self._ids_event.record(torch.cuda.current_stream(self.device))
+                self._ids_event.record(stream)
             den.x_t.copy_(noise.reshape(den.horizon, den.action_dim), non_blocking=True)
+            if self._inputs_read is None:
+                self._inputs_read = torch.cuda.Event()
+            self._inputs_read.record(stream)
             self._graphs["full"].replay()
-            actions = den.x_t
+            actions = den.x_t.clone()
+            # The caller's buffers were copied by the work before the replay; wait for
+            # those copies only (the graph keeps running).
+            self._inputs_read.synchronize()
         else:
             valid = self._embed_prefix(observation)
             self._set_key_valid(valid)
             prefix.enqueue(abi.stream_of(self.device))
-            actions = den.run(noise.to(self.device, non_blocking=True).float(), use_graph=self.use_cuda_graph)
-        return {"actions": actions.clone().reshape(1, self.config.action_horizon, self.config.action_dim)}
+            actions = den.run(noise.to(self.device, non_blocking=True).float(), use_graph=self.use_cuda_graph).clone()
+            torch.cuda.current_stream(self.device).synchronize()
+        return actions.reshape(1, self.config.action_horizon, self.config.action_dim)
 
     @torch.no_grad()
     def denoise(self, noise: Optional[torch.Tensor] = None) -> dict:
@@ -366,6 +408,32 @@ class OpenPi0Inference:
             g.replay()
 
         return step
+
+    def capture_stage(self, stage: str):
+        """Capture one stage of the captured pipeline alone as a CUDA graph (after
+        ``capture_full``): "siglip" (the views -> image tokens of the prefix) or
+        "prefix" (the prefix LM over the current prefix embeddings, which are
+        restored before every replay).  Returns a zero-arg replay callable."""
+        prefix, den = self._runners()
+        st = torch.cuda.current_stream(self.device)
+        if stage == "siglip":
+            def enqueue(s):
+                self._siglip.enqueue(self._static_imgs, prefix.h, s)
+        elif stage == "prefix":
+            saved = prefix.h.clone()
+
+            def enqueue(s):
+                prefix.h.copy_(saved)
+                prefix.enqueue(s)
+        else:
+            raise ValueError(stage)
+        enqueue(st.cuda_stream)
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            enqueue(torch.cuda.current_stream(self.device).cuda_stream)
+        self._graphs[stage] = g
+        return g.replay
 
     def _time_per_layer(self, launch, reps: int) -> float:
         """Mean µs of ``launch(layer)`` over all expert layers, captured once in a

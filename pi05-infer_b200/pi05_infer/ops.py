@@ -7,15 +7,66 @@ the reference keep working; the dispatchers ``fused_gate_up_geglu`` /
 ``fused_qkv_rope_kv`` keep its contract of returning ``None`` when the fast path
 does not apply (``rlinf_fused_denoise.py:489-562``).  The implementation is the
 sm_100a library; there is no Triton and no eager fallback inside the ops.
+
+The module also exports the rest of the reference module's public names
+(``rlinf_fused_denoise.py:32-38``): ``HAVE_FUSED_DENOISE_OPS`` and the two
+``fuse_*_enabled`` switches, so that the reference's own callers can import this
+module in place of ``rlinf_fused_denoise`` (``modeling_gemma.py:54-60`` reads the
+flag and keeps the module only when it is true).
 """
 
 from __future__ import annotations
 
+import os
 from typing import Optional
 
 import torch
 
 from . import _lib
+
+__all__ = [
+    "HAVE_FUSED_DENOISE_OPS",
+    "fuse_geglu_enabled",
+    "fuse_qkv_rope_enabled",
+    "fused_gate_up_geglu",
+    "fused_qkv_rope_kv",
+]
+
+
+def _library_loads() -> bool:
+    try:
+        _lib.lib()
+        return True
+    except (RuntimeError, OSError):
+        return False
+
+
+# True when the sm_100a library is built and loads (the reference's flag is true
+# when Triton imports, rlinf_fused_denoise.py:72-82).  Per call, the dispatchers
+# still return None for CPU tensors, as the reference's do.
+HAVE_FUSED_DENOISE_OPS = _library_loads()
+
+
+def _env_int(name: str, default: int, legacy: Optional[str] = None) -> int:
+    raw = os.environ.get(name) or (os.environ.get(legacy) if legacy else None)
+    if not raw:
+        return default
+    try:
+        return int(raw)
+    except ValueError:
+        return default
+
+
+def fuse_geglu_enabled() -> bool:
+    """True when the fused gate/up+GeGLU op should be used (kill switch
+    ``RLINF_FUSE_GEGLU=0``, alias ``RLINF_FUSE_SWIGLU``; ``rlinf_fused_denoise.py:97-101``)."""
+    return HAVE_FUSED_DENOISE_OPS and _env_int("RLINF_FUSE_GEGLU", 1, legacy="RLINF_FUSE_SWIGLU") != 0
+
+
+def fuse_qkv_rope_enabled() -> bool:
+    """True when the fused QKV+RoPE op should be used (kill switch
+    ``RLINF_FUSE_QKV_ROPE=0``; ``rlinf_fused_denoise.py:104-106``)."""
+    return HAVE_FUSED_DENOISE_OPS and _env_int("RLINF_FUSE_QKV_ROPE", 1) != 0
 
 _WS = {}
 _WS_TOKENS = 512
@@ -169,7 +220,7 @@ def _needs_autograd(*ts: torch.Tensor) -> bool:
 
 def fused_gate_up_geglu(x: torch.Tensor, wg: torch.Tensor, wu: torch.Tensor) -> Optional[torch.Tensor]:
     """Dispatcher with the reference's guards (``rlinf_fused_denoise.py:489-517``): ``None`` = not applicable."""
-    if _needs_autograd(x, wg, wu):
+    if not fuse_geglu_enabled() or _needs_autograd(x, wg, wu):
         return None
     if (
         not x.is_cuda
@@ -192,7 +243,7 @@ def fused_qkv_rope_kv(
     v_cache: torch.Tensor, krow0: int, n_q_heads: int, n_kv_heads: int, head_dim: int,
 ) -> Optional[torch.Tensor]:
     """Dispatcher with the reference's guards (``rlinf_fused_denoise.py:520-562``)."""
-    if _needs_autograd(x, w):
+    if not fuse_qkv_rope_enabled() or _needs_autograd(x, w):
         return None
     if (
         not x.is_cuda

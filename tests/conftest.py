@@ -46,3 +46,16 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+def load_ref_loader():
+    """Import ``baseline/ref_loader.py`` (loads files of the reference installed under
+    ``baseline/_ref``); None when the reference is not installed there."""
+    name = "pi05_ref_loader"
+    if name not in sys.modules:
+        spec = importlib.util.spec_from_file_location(name, os.path.join(REPO, "baseline", "ref_loader.py"))
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules[name] = mod
+        spec.loader.exec_module(mod)
+    mod = sys.modules[name]
+    return mod if mod.available() else None

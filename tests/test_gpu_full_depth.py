@@ -1,0 +1,91 @@
+"""GPU parity of ``sample_actions`` at the shipped depth against the CPU oracle.
+
+Config 3 (3 views, 200 prompt tokens, P=968) and config 5 (5 views, P=1480) with
+the full model: SigLIP So400m (27 layers), the Gemma-2B prefix LM (18 layers,
+k/v-only last layer), the Gemma-300M action expert (18 layers) and 10 Euler
+steps, all through ``OpenPi0Inference.sample_actions`` (one captured CUDA graph).
+
+Checked against the oracle's bf16 policy on the same seeded weights and inputs:
+
+* prefix K/V of every layer (the valid prefix rows of the static cache), cosine
+  >= 0.9999 per layer;
+* the last Euler step's velocity, cosine >= 0.9999;
+* the final actions, max-abs <= 2e-2 (the north-star action tolerance).
+"""
+
+import pytest
+import torch
+
+from conftest import load_oracle
+
+from pi05_infer import ops, synthetic
+from pi05_infer.config import EngineConfig
+from pi05_infer.engine import Observation, OpenPi0Inference
+
+pytestmark = pytest.mark.gpu
+
+oracle = load_oracle()
+
+
+def _cos(a, b):
+    a = a.flatten().double()
+    b = b.flatten().double()
+    return float(a @ b / (a.norm() * b.norm()))
+
+
+@pytest.fixture(scope="module")
+def weights():
+    torch.set_num_threads(max(1, torch.get_num_threads()))
+    sd = {}
+    sd.update(synthetic.make_expert_weights(0))
+    sd.update(synthetic.make_prefix_lm_weights(10, with_embedding=True))
+    sd.update(synthetic.make_siglip_weights(20))
+    return sd
+
+
+def _observation(num_views, seed, n_pad):
+    g = torch.Generator().manual_seed(seed)
+    imgs = {f"cam{i}": torch.rand((1, 3, 224, 224), generator=g) * 2 - 1 for i in range(num_views)}
+    masks = {k: torch.ones(1, dtype=torch.bool) for k in imgs}
+    toks = torch.randint(0, synthetic.VOCAB_SIZE, (1, 200), generator=g)
+    tmask = torch.ones(1, 200, dtype=torch.bool)
+    if n_pad:
+        tmask[0, 200 - n_pad:] = False
+    return Observation(imgs, masks, toks, tmask, torch.zeros(1, 32))
+
+
+@pytest.mark.parametrize("num_views,n_pad", [(3, 23), (5, 0)], ids=["config3", "config5"])
+def test_sample_actions_full_depth(weights, num_views, n_pad):
+    sd = weights
+    prefix_len = num_views * 256 + 200
+    eng = OpenPi0Inference(EngineConfig(), sd, device="cuda", prefix_len=prefix_len, num_views=num_views)
+    obs = _observation(num_views, 100 + num_views, n_pad)
+    noise = synthetic.make_noise(2)
+    act = eng.sample_actions(obs, noise=noise)["actions"][0].cpu()
+    torch.cuda.synchronize()
+    assert ops.read_device_status() == 0
+    v_last = eng._denoise.v_t.float().cpu()
+    kc = [k[0, :prefix_len].float().cpu() for k in eng._denoise.k_cache]
+    vc = [v[0, :prefix_len].float().cpu() for v in eng._denoise.v_cache]
+    # a replay of the captured graph reproduces the call bit for bit
+    act2 = eng.sample_actions(obs, noise=noise)["actions"][0].cpu()
+    assert torch.equal(act, act2)
+    del eng
+    torch.cuda.empty_cache()
+
+    imgs = torch.cat([obs.images[k] for k in obs.images], 0)
+    feats = oracle.siglip_image_features(sd, imgs, 27, "bf16")
+    lang = oracle.embed_language(sd[synthetic.EMBED_KEY], obs.tokenized_prompt[0], "bf16")
+    embs = oracle.embed_prefix(feats, lang)
+    pad = torch.cat([torch.ones(num_views * 256, dtype=torch.bool), obs.tokenized_prompt_mask[0]])
+    kv = oracle.prefix_lm_kv(sd, embs, pad, 18, "bf16")
+    valid = pad.nonzero().flatten()
+    for i, (k, v) in enumerate(kv):
+        ck = _cos(kc[i][valid], k[valid])
+        cv = _cos(vc[i][valid], v[valid])
+        assert ck >= 0.9999 and cv >= 0.9999, (i, ck, cv)
+    vels = []
+    ref = oracle.denoise_loop(sd, noise[0], kv, pad, 18, 10, "bf16", velocities=vels)
+    assert _cos(v_last, vels[-1]) >= 0.9999, _cos(v_last, vels[-1])
+    err = (act - ref).abs().max().item()
+    assert err <= 2e-2, err
