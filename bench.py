@@ -31,6 +31,7 @@ workload, on all host threads.
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import os
 import statistics
@@ -200,7 +201,10 @@ class RefCpu:
         e2e = workload != "denoise"
         if self.kind == "reference":
             rp = _load_file("pi05_ref_pipeline", os.path.join(HERE, "baseline", "ref_pipeline.py"))
-            self.pipe = rp.RefCpuPipeline("e2e" if e2e else "denoise", num_views=views)
+            # transformers prints docstring checks of the reference's classes to
+            # stdout while they are defined; stdout carries only the JSON line
+            with contextlib.redirect_stdout(sys.stderr):
+                self.pipe = rp.RefCpuPipeline("e2e" if e2e else "denoise", num_views=views)
             if not e2e:
                 self.kv = [(k, v) for k, v in synthetic.make_prefix_kv(1, 18, p)]
         else:
@@ -215,7 +219,7 @@ class RefCpu:
     def run(self) -> float:
         """One full call; returns its wall time in ms."""
         t0 = time.perf_counter()
-        with self.torch.no_grad():
+        with self.torch.no_grad(), contextlib.redirect_stdout(sys.stderr):
             if self.kind == "reference":
                 self.pipe.sample_actions(self.images, self.tokens, self.pad, self.noise, kv=self.kv)
             else:
@@ -442,7 +446,8 @@ def run_ours(args):
         import kernel_cases
 
         try:
-            line["kernel_duel"] = kernel_cases.kernel_duel(reps=20)
+            with contextlib.redirect_stdout(sys.stderr):
+                line["kernel_duel"] = kernel_cases.kernel_duel(reps=20)
         except Exception as e:  # the reference's Triton path failing must not lose the bench line
             line["kernel_duel"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
     if rank == 0:
