@@ -220,8 +220,9 @@ typedef struct Pi05ExpertPlan {
   void* workspace;
   size_t workspace_bytes;
   int attn_splits;                /* <= 0: automatic */
-  unsigned long long* trace;      /* optional device buffer for the persistent kernel's phase timestamps
-                                     ([SMs][pi05_trace_slots()] ns), NULL = off */
+  unsigned long long* trace;      /* optional device buffer for per-CTA timestamp records of the
+                                     loop's GEMM and attention launches (layout of pi05_debug_set_trace),
+                                     NULL = off */
   const Pi05ExpertFold* fold;     /* host array [num_steps * depth] (step-major), or NULL.  When set
                                      (and tokens <= 64), pi05_denoise_step runs no norm kernel inside
                                      the layers: q|k|v and gate/up read the residual stream h with these
@@ -239,9 +240,6 @@ typedef struct Pi05ExpertPlan {
 int pi05_fold_adarms(const void* w, int rows, int k, const float* scale, const float* shift, void* w_out,
                      float* b_out, void* stream);
 
-/* Timestamp slots per CTA that pi05_denoise_loop_persistent writes when plan->trace is set. */
-int pi05_trace_slots(void);
-
 /* One Euler step `step` (0-based) of the denoise loop: action_in_proj, 18 expert
  * layers, final norm, action_out_proj, Euler update of plan->x_t.
  * Replaces one replay of the reference's captured step (engine.py:629-676, 908-1001). */
@@ -250,14 +248,6 @@ int pi05_denoise_step(const Pi05ExpertPlan* plan, int step, void* stream);
 /* All plan->num_steps steps (engine.py:390-405), one launch per kernel phase. */
 int pi05_denoise_loop(const Pi05ExpertPlan* plan, void* stream);
 
-/* All plan->num_steps steps in ONE persistent cooperative launch (one CTA per SM,
- * warp-specialised: weight TMA / MMA / activation TMA / worker warps, phases
- * ordered by completion counters).  Same math as pi05_denoise_loop.  Needs
- * width 1024, head_dim 256, one KV head, tokens <= 64, <= 18 layers, <= 16 steps
- * and at least 144 SMs; otherwise returns PI05_ERR_SHAPE.  Uses the workspace
- * scratch for a second normalised-activation buffer and the attention partials
- * (plan->xn is the first). */
-int pi05_denoise_loop_persistent(const Pi05ExpertPlan* plan, void* stream);
 
 
 /* ---- prefix (PaliGemma Gemma-2B over image + language tokens) ------------- */
@@ -390,6 +380,33 @@ typedef struct Pi05SiglipPlan {
  * PaliGemma get_image_features (gemma_pytorch.py:106-107) over cat(images)
  * (pi0_pytorch.py:203-217). */
 int pi05_siglip_forward(const Pi05SiglipPlan* plan, void* stream);
+
+/* ---- observation preprocessing and action output transform ---------------- */
+
+/* Camera images as the environment gives them, uint8 [n, h, w, 3] (layout 0) or
+ * [n, 3, h, w] (layout 1), to the model's fp32 [n, 3, size, size] in [-1, 1]:
+ * p / 255 * 2 - 1 after a bilinear resize (half-pixel centres) that keeps the
+ * aspect ratio and fits the longer side, the border filled with -1.  An image
+ * already size x size is copied pixel for pixel.  Replaces the image part of
+ * openpi's preprocess_observation_pytorch (called at pi0_pytorch.py:165-174) and of
+ * the input transforms that predict_action_batch runs (engine.py:321-342). */
+int pi05_preprocess_images(const uint8_t* images, int n, int h, int w, int layout, float* out, int size,
+                           void* stream);
+
+/* out[r, j] = normalised x[r, j] for j < din (statistics for j < nstat, the rest
+ * passed through), 0 for din <= j < dout.  mode 0: (x - a) / (b + 1e-6) with
+ * a = mean, b = std; mode 1: (x - a) / (b - a + 1e-6) * 2 - 1 with a = q01,
+ * b = q99.  Replaces openpi Normalize + PadStatesAndActions on the state
+ * (input transforms built at builder.py:120-128). */
+int pi05_normalize_rows(const float* x, int rows, int din, const float* a, const float* b, int nstat, int mode,
+                        float* out, int dout, void* stream);
+
+/* out[r, j] = un-normalised x[r, j] for j < dout <= din: mode 0: x * (b + 1e-6) + a;
+ * mode 1: (x + 1) / 2 * (b - a + 1e-6) + a; statistics for j < nstat.  Replaces
+ * openpi Unnormalize on the actions and the policy's output slice (builder.py:129-136,
+ * dataconfig/policies/turtle_policy.py:89-93, libero_policy.py LiberoOutputs). */
+int pi05_unnormalize_rows(const float* x, int rows, int din, const float* a, const float* b, int nstat, int mode,
+                          float* out, int dout, void* stream);
 
 #ifdef __cplusplus
 }

@@ -79,41 +79,13 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 
 __device__ __forceinline__ float bfr(float x) { return __bfloat162float(__float2bfloat16(x)); }
 
-// In-cluster merge of the split partials: one merge row is the unnormalised O
-// (256 fp32), the running max m and the sum l, padded to 16 bytes.
-constexpr int kMergeFloats = kD + 4;
-constexpr int kMergeRowBytes = kMergeFloats * 4;  // 1040
-
-// Shared memory of one CTA: Q rows, nbuf K and V chunk buffers, the chunk key
-// masks; with the in-cluster merge, receive slots for `splits` sources of this
-// CTA's merge rows and the receive barrier.
+// Shared memory of one CTA: Q rows, nbuf K and V chunk buffers, the chunk key masks.
 template <int WARPS>
-__host__ __device__ constexpr size_t attn_smem_base(int nbuf) {
+__host__ __device__ constexpr size_t attn_smem_bytes(int nbuf) {
   return (size_t)16 * WARPS * kRowBytes + (size_t)nbuf * 2 * kChunk * kRowBytes + (size_t)nbuf * kChunk;
 }
 
 template <int WARPS>
-__host__ __device__ constexpr size_t attn_recv_offset(int nbuf) {
-  return (attn_smem_base<WARPS>(nbuf) + 127) & ~size_t(127);
-}
-
-template <int WARPS>
-__host__ __device__ constexpr size_t attn_smem_bytes(int nbuf, int merge_splits) {
-  return merge_splits <= 1 ? attn_smem_base<WARPS>(nbuf)
-                           : attn_recv_offset<WARPS>(nbuf) +
-                                 (size_t)merge_splits * ((16 * WARPS + merge_splits - 1) / merge_splits) *
-                                     kMergeRowBytes +
-                                 16;
-}
-
-// MERGE: the p.splits CTAs of a row block form a cluster (cluster dims (1, splits))
-// and merge their partials through distributed shared memory instead of global
-// memory and a second kernel.  Rank r owns rows [r*R/splits, (r+1)*R/splits) of the
-// block (R = 16 x WARPS): every CTA stages its partial rows (O, m, l) in the
-// finished K/V buffers and sends each owner its rows with one bulk copy that
-// completes on the owner's receive barrier; each owner merges its rows over all
-// splits in split order and writes the normalised bf16 output.
-template <int WARPS, bool MERGE>
 __global__ void __launch_bounds__(WARPS * 32, 1)
     mqa_flash_kernel(const AttnParams p) {
   constexpr int kRows = 16 * WARPS;
@@ -127,35 +99,9 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int row0 = blockIdx.x * kRows;
   const int split = blockIdx.y;
-  // Merge state (MERGE only): this rank's merge rows, receive slots and barrier
-  // (recomputed where used, so nothing stays live across the key loop).
-  auto merge_rows = [&](int& r0, int& r1) {
-    r0 = (split * kRows) / p.splits;
-    r1 = ((split + 1) * kRows) / p.splits;
-  };
-  auto merge_recv = [&]() { return reinterpret_cast<float*>(smem + attn_recv_offset<WARPS>(p.nbuf)); };
-  auto merge_bar = [&]() {
-    return reinterpret_cast<uint64_t*>(merge_recv() +
-                                       (size_t)p.splits * ((kRows + p.splits - 1) / p.splits) * kMergeFloats);
-  };
-  if constexpr (MERGE) {
-    int mr0, mr1;
-    merge_rows(mr0, mr1);
-    const int n_split = p.splits, slot_floats = (mr1 - mr0) * kMergeFloats;
-    uint64_t* rbar = merge_bar();
-    if (tid == 0) {
-      mbar_init(rbar, 1);
-      fence_mbar_init();
-      mbar_arrive_expect_tx(rbar, (uint32_t)((n_split - 1) * slot_floats * 4));
-    }
-    // Every receive barrier of the cluster is initialised before any copy targets it.
-    __syncwarp();
-    cluster_arrive_release();
-    cluster_wait();
-  }
   const bool tr = p.trace != nullptr && tid == 0;
   const uint64_t t_entry = tr ? globaltimer_ns() : 0;
-  uint64_t t_wait = 0, t_data = 0, t_loop = 0, t_recv = 0, t_merged = 0;
+  uint64_t t_wait = 0, t_data = 0, t_loop = 0;
   const int n_chunks_total = (p.kv_len + kChunk - 1) / kChunk;
   const int c_begin = (split * n_chunks_total) / p.splits;
   const int c_end = ((split + 1) * n_chunks_total) / p.splits;
@@ -312,8 +258,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   cp_wait<0>();
   if (tr) t_loop = globaltimer_ns();
   // Trace record {tag << 32 | smid << 16 | cta, entry, grid-dependency wait done,
-  // first chunk ready, key loop done, output / partial written, merge rows received
-  // (in-cluster merge), merged rows written (in-cluster merge)}.
+  // first chunk ready, key loop done, output / partial written, 0, 0}.
   auto trace_out = [&]() {
     if (!tr) return;
     const unsigned long long slot = atomicAdd(p.trace, 1ull);
@@ -326,93 +271,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       w[3] = t_data;
       w[4] = t_loop;
       w[5] = globaltimer_ns();
-      w[6] = t_recv;
-      w[7] = t_merged;
+      w[6] = 0;
+      w[7] = 0;
     }
   };
-
-  if constexpr (MERGE) {
-    int mr0, mr1;
-    merge_rows(mr0, mr1);
-    const int n_split = p.splits, slot_floats = (mr1 - mr0) * kMergeFloats;
-    float* s_recv = merge_recv();
-    uint64_t* rbar = merge_bar();
-    // Stage this split's partial rows (O, m, l) in the finished K/V buffers.
-    float* stg = reinterpret_cast<float*>(sK);
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      float* dst = stg + (warp * 16 + g + h * 8) * kMergeFloats;
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        *reinterpret_cast<float2*>(dst + j * 8 + 2 * t4) = make_float2(o[j][2 * h], o[j][2 * h + 1]);
-      if (t4 == 0) *reinterpret_cast<float2*>(dst + kD) = make_float2(m_run[h], l_run[h]);
-    }
-    fence_proxy_async_smem();  // the bulk copies read the staging rows through the async proxy
-    __syncthreads();
-    if (tid < n_split && tid != split) {
-      const int d0 = (tid * kRows) / n_split, d1 = ((tid + 1) * kRows) / n_split;
-      const uint32_t bytes = (uint32_t)(d1 - d0) * kMergeRowBytes;
-      bulk_copy_to_peer(mapa_shared(smem_u32(s_recv) + (uint32_t)split * bytes, (uint32_t)tid),
-                        smem_u32(stg) + (uint32_t)d0 * kMergeRowBytes, bytes,
-                        mapa_shared(smem_u32(rbar), (uint32_t)tid));
-    }
-    const bool ok = mbar_wait_cluster(rbar, 0);
-    if (!ok && tid == 0) report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
-    if (tr) t_recv = globaltimer_ns();
-    // Everything this CTA receives has landed; its sources may leave once every
-    // owner has said so.
-    __syncwarp();
-    cluster_arrive_relaxed();
-    if (ok) {
-      // Merge rows mr0..mr1-1.  First each row's split weights w_s = exp(m_s - max)
-      // and 1 / sum_s l_s w_s (one warp per row, lane s = split s), into the free Q
-      // buffer; then every thread sums 4 columns of a row over the splits in order.
-      const int n_own = mr1 - mr0;
-      float* s_w = reinterpret_cast<float*>(sQ);  // [n_own][33]: w_0 .. w_31, 1 / l
-      auto src = [&](int i, int sp) -> const float* {
-        return sp == split ? stg + (mr0 + i) * kMergeFloats : s_recv + sp * slot_floats + i * kMergeFloats;
-      };
-      for (int i = warp; i < n_own; i += WARPS) {
-        const float ms = lane < n_split ? src(i, lane)[kD] : -INFINITY;
-        const float ls = lane < n_split ? src(i, lane)[kD + 1] : 0.f;
-        float mmax = ms;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffff, mmax, o));
-        const float w = ms != -INFINITY ? __expf(ms - mmax) : 0.f;
-        float l = ls * w;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffff, l, o);
-        s_w[i * 33 + lane] = w;
-        if (lane == 0) s_w[i * 33 + 32] = l > 0.f ? 1.f / l : 0.f;
-      }
-      __syncthreads();
-      for (int idx = tid; idx < n_own * (kD / 4); idx += WARPS * 32) {
-        const int i = idx / (kD / 4), c = (idx % (kD / 4)) * 4;
-        const int r = row0 + mr0 + i;
-        if (r >= p.rows) continue;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-        for (int sp = 0; sp < n_split; ++sp) {  // loads of four splits in flight, sums in split order
-          const float w = s_w[i * 33 + sp];
-          const float4 a = *reinterpret_cast<const float4*>(src(i, sp) + c);
-          acc[0] += a.x * w;
-          acc[1] += a.y * w;
-          acc[2] += a.z * w;
-          acc[3] += a.w * w;
-        }
-        const float inv = s_w[i * 33 + 32];
-        uint2 pk;
-        pk.x = pack_bf16(acc[0] * inv, acc[1] * inv);
-        pk.y = pack_bf16(acc[2] * inv, acc[3] * inv);
-        *reinterpret_cast<uint2*>(p.out + (size_t)r * p.out_stride + c) = pk;
-      }
-    }
-    if (tr) t_merged = globaltimer_ns();
-    __syncwarp();
-    cluster_wait();
-    trace_out();
-    return;
-  }
 
   // Output: rows (warp*16 + g) and (+8), columns j*8 + 2*t4 .. +1.
 #pragma unroll
@@ -535,59 +397,14 @@ int set_attn_smem() {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 16 && done[dev]) return PI05_OK;
-  cudaError_t e = cudaFuncSetAttribute(mqa_flash_kernel<W, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)attn_smem_bytes<W>(2, 1));
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(mqa_flash_kernel<W, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)attn_smem_bytes<W>(2, 16));
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(mqa_flash_kernel<W, true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaError_t e = cudaFuncSetAttribute(mqa_flash_kernel<W>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)attn_smem_bytes<W>(2));
   if (e != cudaSuccess) {
     set_last_error("attention smem attr: %s", cudaGetErrorString(e));
     return PI05_ERR_LAUNCH;
   }
   if (dev < 16) done[dev] = true;
   return PI05_OK;
-}
-
-// Whether clusters of `splits` merge CTAs (with `smem` bytes each) can be
-// scheduled on this device (queried once per device and split count).
-template <int W>
-bool merge_cluster_fits(int splits, size_t smem) {
-  static signed char cached[16][17] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (splits < 2 || splits > 16) return false;
-  if (dev < 16 && cached[dev][splits] != 0) return cached[dev][splits] > 0;
-  cudaLaunchConfig_t cfg;
-  std::memset(&cfg, 0, sizeof(cfg));
-  cfg.gridDim = dim3(1, splits);
-  cfg.blockDim = dim3(W * 32);
-  cfg.dynamicSmemBytes = smem;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = splits;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  int n = 0;
-  const bool ok = cudaOccupancyMaxActiveClusters(&n, mqa_flash_kernel<W, true>, &cfg) == cudaSuccess && n > 0;
-  if (!ok) cudaGetLastError();
-  if (dev < 16) cached[dev][splits] = ok ? 1 : -1;
-  return ok;
-}
-
-// PI05_ATTN_MERGE=1 in the environment merges the mma.sync path's split partials
-// inside a cluster instead of global partials and the combine kernel.  Off by
-// default: on B200 the key loop of the slowest split of a cluster bounds the
-// merge, which then costs as much as the combine kernel it removes.
-bool attn_merge_enabled() {
-  static int v = [] {
-    const char* e = getenv("PI05_ATTN_MERGE");
-    return (e != nullptr && e[0] == '1') ? 1 : 0;
-  }();
-  return v != 0;
 }
 
 }  // namespace
@@ -629,27 +446,9 @@ int mma_sync_attention(AttnParams p, float* part, size_t part_bytes, int splits,
   }
   splits = splits > n_chunks ? n_chunks : splits;
   splits = splits > 32 ? 32 : splits;
-  // In-cluster merge: up to 16 splits (one chunk each when the keys allow), two
-  // CTAs per SM.
-  int merge = 0;
-  if (attn_merge_enabled()) {
-    int ms = auto_splits ? std::min(16, n_chunks) : splits;
-    while (auto_splits && ms > 2 && (long)row_blocks * ms > 2L * sms) ms /= 2;
-    const int nb = (n_chunks + ms - 1) / ms > 1 ? 2 : 1;
-    if (ms >= 2 && ms <= 16 && set_attn_smem<W>() == PI05_OK &&
-        merge_cluster_fits<W>(ms, attn_smem_bytes<W>(nb, ms))) {
-      merge = ms;
-      splits = ms;
-    }
-  }
   p.splits = splits;
   p.nbuf = (n_chunks + splits - 1) / splits > 1 ? 2 : 1;
-  if (merge) {
-    const size_t smem = attn_smem_bytes<W>(p.nbuf, merge);
-    return launch_pdl_cluster(mqa_flash_kernel<W, true>, dim3(row_blocks, splits), dim3(W * 32), smem, st,
-                              pdl_enabled(), dim3(1, splits, 1), p);
-  }
-  const size_t smem = attn_smem_bytes<W>(p.nbuf, 1);
+  const size_t smem = attn_smem_bytes<W>(p.nbuf);
   if (splits > 1) {
     const size_t need_o = (size_t)splits * p.rows * kD * sizeof(float);
     const size_t need = need_o + (size_t)splits * p.rows * 2 * sizeof(float);
@@ -663,7 +462,7 @@ int mma_sync_attention(AttnParams p, float* part, size_t part_bytes, int splits,
   }
   int rc = set_attn_smem<W>();
   if (rc) return rc;
-  rc = launch_pdl(mqa_flash_kernel<W, false>, dim3(row_blocks, splits), dim3(W * 32), smem, st, pdl_enabled(), p);
+  rc = launch_pdl(mqa_flash_kernel<W>, dim3(row_blocks, splits), dim3(W * 32), smem, st, pdl_enabled(), p);
   if (rc || splits == 1) return rc;
   return launch_combine(p, st);
 }

@@ -1,9 +1,12 @@
 // C-ABI entry points for the norms, attention, glue and the whole denoise loop.
 //
 // pi05_denoise_step enqueues one Euler step of the action expert on a stream:
-//   action_in_proj -> 18 x [adaRMS, QKV+RoPE+KV-tail, MQA attention,
-//   o_proj+gated residual, adaRMS, gate/up+GeGLU, down+gated residual]
+//   action_in_proj -> 18 x [QKV+RoPE+KV-tail (input adaRMS folded in), MQA
+//   attention (+ split combine), o_proj+gated residual, gate/up+GeGLU
+//   (post-attention adaRMS folded in), down+gated residual]
 //   -> final adaRMS + action_out_proj + Euler update.
+// Without folded weights (or with more than 64 tokens) the two adaRMS norms of a
+// layer run as kernels of their own before the projections.
 // Every launch carries the PDL attribute, so each kernel's prologue and weight
 // prefetch overlap the previous kernel's tail.  The engine captures the whole
 // loop in one CUDA graph.
@@ -35,34 +38,6 @@ const int* debug_split_overrides() {
   }();
   (void)init;
   return v;
-}
-
-// PI05_FUSED_NORM=1 in the environment folds input_layernorm (after layer 0) into
-// the q|k|v GEMM: down_proj writes row statistics, q|k|v normalises h while
-// staging its X operand.  Off by default: on B200 the staging (L2 loads of h and
-// the statistics, then the normalisation, before the first MMA) costs q|k|v about
-// as much as the norm kernel it removes.
-bool fused_norm_enabled() {
-  static int v = [] {
-    const char* e = getenv("PI05_FUSED_NORM");
-    return (e != nullptr && e[0] == '1') ? 1 : 0;
-  }();
-  return v != 0;
-}
-
-// PI05_PRODUCER_NORM=1 runs the norms after layer 0's input_layernorm in the
-// epilogue of the GEMM that produces their input (o_proj for
-// post_attention_layernorm, down_proj for the next layer's input_layernorm): the
-// last owner of each token slice, elected by a ticket, normalises the slice's whole
-// rows.  Off by default: on B200 the ticket and the row loads are two L2 round
-// trips while the next GEMM's weight stream fills the memory system, which lengthens
-// the producer's tail by more than the norm kernel and its launch gap cost.
-bool producer_norm_enabled() {
-  static int v = [] {
-    const char* e = getenv("PI05_PRODUCER_NORM");
-    return (e != nullptr && e[0] == '1') ? 1 : 0;
-  }();
-  return v != 0;
 }
 
 // PI05_FOLD_NORM=0 in the environment keeps the norm kernels even when the plan
@@ -215,55 +190,25 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
   auto* act = static_cast<__nv_bfloat16*>(P->act);
   const int kv_len = P->prefix_len + T;
   const float scale = 1.0f / std::sqrt((float)D);
-  // Fused input_layernorm: down_proj writes per-(128-column tile, token) sums of
-  // squares of the new residual stream next to it, and the next layer's q|k|v GEMM
-  // normalises h from those sums while staging its X operand, so that norm needs
-  // no kernel of its own after layer 0.
-  const int n_parts = W / 128;
-  const bool fuse = fused_norm_enabled() && W <= kNormMaxK && T <= 64 && n_parts <= kNormMaxParts &&
-                    (size_t)n_parts * T * sizeof(float) <= kWsStatsBytes;
-  float* ssq_attn = ws.stats;  // input of input_layernorm (from down_proj)
-  const bool prod = !fuse && producer_norm_enabled() && T <= 64 && (size_t)n_parts * T * sizeof(float) <= kWsStatsBytes;
   // Folded norms (default when the plan carries folded weights): no norm kernel
   // inside the layers.  action_in (layer 0, one part) and down_proj write the row
   // statistics of input_layernorm's input to ssq_attn, o_proj those of
   // post_attention_layernorm's input to ssq_mlp; q|k|v and gate/up read h with the
   // step's folded weights and apply rstd and the folded bias to their accumulators.
-  const bool fold = P->fold != nullptr && !fuse && !prod && fold_norm_enabled() && T <= 64 &&
-                    n_parts <= kNormMaxParts && (size_t)2 * n_parts * T * sizeof(float) <= kWsStatsBytes;
+  const int n_parts = W / 128;
+  const bool fold = P->fold != nullptr && fold_norm_enabled() && T <= 64 && n_parts <= kNormMaxParts &&
+                    (size_t)2 * n_parts * T * sizeof(float) <= kWsStatsBytes;
+  float* ssq_attn = ws.stats;
   float* ssq_mlp = ws.stats + (size_t)n_parts * T;
   const Pi05ExpertFold* FS = fold ? P->fold + (size_t)step * P->depth : nullptr;
-  // Folded weights of the op after layer l's: layer l + 1 of this step, or layer 0
-  // of the next step (of step 0 after the last one).
-  auto fold_next = [&](int l) -> const Pi05ExpertFold& {
-    if (l + 1 < P->depth) return FS[l + 1];
-    const int ns = step + 1 < P->num_steps ? step + 1 : 0;
-    return P->fold[(size_t)ns * P->depth];
-  };
-  // Producer-side norm of the GEMM output `h` into xn with modulation `mod`.
-  auto producer_norm = [&](SkinnyParams& sp, const float* mod) {
-    sp.row_ssq = ws.stats;
-    sp.ssq_ld = T;
-    sp.norm_out = xn;
-    sp.norm_ldo = W;
-    sp.norm_mod = mod;
-    sp.norm_d = W;
-    sp.norm_eps = P->eps;
-    sp.norm_tickets = ws.counters + kWsNormTicketBase;
-  };
 
   int rc = action_in_run(P->x_t, P->w_in, P->b_in, h, T, P->action_dim, W, stream, fold ? ssq_attn : nullptr);
   for (int l = 0; l < P->depth && rc == PI05_OK; ++l) {
     const Pi05ExpertLayer& L = P->layers[l];
-    // The same op of the next layer (layer 0 again for the next Euler step) is
-    // prefetched into L2 by each GEMM while it runs.
-    const Pi05ExpertLayer& N = P->layers[(l + 1) % P->depth];
     const float* mod1 = mods + (size_t)(2 * l) * 3 * W;
     const float* mod2 = mods + (size_t)(2 * l + 1) * 3 * W;
-    // input_layernorm (adaRMS): after layer 0 fused into q|k|v, or produced by the
-    // previous down_proj
-    const bool fuse1 = fuse && l > 0;
-    if (!fold && !fuse1 && !(prod && l > 0)) {
+    // input_layernorm (adaRMS), unless folded into q|k|v
+    if (!fold) {
       rc = rms_norm_run(h, W, mod1, nullptr, xn, W, T, W, P->eps, stream);
       if (rc) break;
     }
@@ -289,17 +234,7 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.n_kv_heads = HKV;
       sp.head_dim = D;
       const int rows = (HQ + 2 * HKV) * D;
-      sp.pf0 = N.w_qkv;
-      sp.pf0_bytes = (size_t)rows * W * 2;
       sp.trace_tag = (step * P->depth + l) * 8 + 0;
-      if (fuse1) {
-        sp.norm_ssq = ssq_attn;
-        sp.norm_parts = n_parts;
-        sp.norm_ld = T;
-        sp.norm_mod = mod1;
-        sp.norm_d = W;
-        sp.norm_eps = P->eps;
-      }
       const void* wq = L.w_qkv;
       if (fold) {
         wq = FS[l].w_qkv;
@@ -310,9 +245,8 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
         sp.fold_eps = P->eps;
         sp.fold_bias0 = FS[l].b_qkv;
         sp.fold_bias1 = FS[l].b_qkv;
-        sp.pf0 = fold_next(l).w_qkv;
       }
-      rc = skinny_gemm_run(SK_EPI_QKV_ROPE, sp, wq, wq, rows, rows, (fuse1 || fold) ? h : xn, W, so[0], stream);
+      rc = skinny_gemm_run(SK_EPI_QKV_ROPE, sp, wq, wq, rows, rows, fold ? h : xn, W, so[0], stream);
       if (rc) break;
     }
     // attention over [prefix | suffix] keys
@@ -353,10 +287,7 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.resid = h;
       sp.ldr = W;
       sp.gate = mod1 + 2 * W;
-      sp.pf0 = N.w_o;
-      sp.pf0_bytes = (size_t)W * HQ * D * 2;
       sp.trace_tag = (step * P->depth + l) * 8 + 1;
-      if (prod) producer_norm(sp, mod2);  // post_attention_layernorm
       if (fold) {
         sp.row_ssq = ssq_mlp;
         sp.ssq_ld = T;
@@ -364,8 +295,8 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       rc = skinny_gemm_run(SK_EPI_GATED_RESID, sp, L.w_o, L.w_o, W, W, attn, HQ * D, so[1], stream);
       if (rc) break;
     }
-    // post_attention_layernorm (adaRMS)
-    if (!prod && !fold) {
+    // post_attention_layernorm (adaRMS), unless folded into gate/up
+    if (!fold) {
       rc = rms_norm_run(h, W, mod2, nullptr, xn, W, T, W, P->eps, stream);
       if (rc) break;
     }
@@ -382,10 +313,6 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.n_tiles = F / 64;
       sp.out = act;
       sp.ldo = F;
-      sp.pf0 = N.w_gate;
-      sp.pf0_bytes = (size_t)F * W * 2;
-      sp.pf1 = N.w_up;
-      sp.pf1_bytes = (size_t)F * W * 2;
       sp.trace_tag = (step * P->depth + l) * 8 + 2;
       const void* wg = L.w_gate;
       const void* wu = L.w_up;
@@ -399,8 +326,6 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
         sp.fold_eps = P->eps;
         sp.fold_bias0 = FS[l].b_gate;
         sp.fold_bias1 = FS[l].b_up;
-        sp.pf0 = fold_next(l).w_gate;
-        sp.pf1 = fold_next(l).w_up;
       }
       rc = skinny_gemm_run(SK_EPI_GEGLU, sp, wg, wu, F, F, fold ? h : xn, W, so[2], stream);
       if (rc) break;
@@ -421,13 +346,10 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.resid = h;
       sp.ldr = W;
       sp.gate = mod2 + 2 * W;
-      if ((fuse || fold) && l + 1 < P->depth) {
+      if (fold && l + 1 < P->depth) {
         sp.row_ssq = ssq_attn;
         sp.ssq_ld = T;
       }
-      if (prod && l + 1 < P->depth) producer_norm(sp, mods + (size_t)(2 * (l + 1)) * 3 * W);  // next input_layernorm
-      sp.pf0 = N.w_down;
-      sp.pf0_bytes = (size_t)W * F * 2;
       sp.trace_tag = (step * P->depth + l) * 8 + 3;
       rc = skinny_gemm_run(SK_EPI_GATED_RESID, sp, L.w_down, L.w_down, W, W, act, F, so[3], stream);
       if (rc) break;

@@ -433,80 +433,10 @@ __device__ __forceinline__ uint32_t push_recv_bytes(int splits, int mt, int rank
   return (uint32_t)((splits - 1) * (t1 - t0) * kBM * 4);
 }
 
-// Producer-side (ada)RMS norm of a finished token slice (GATED_RESID with
-// norm_out set, one token tile, norm_d <= 8 * 128): the owner of slice [t0, t1) of
-// each 128-column tile has stored its rows and their sums of squares; it takes the
-// slice's ticket, and the last of the n_tiles owners normalises the slice's whole
-// rows into norm_out with the arithmetic of the norm kernel
-// (modeling_gemma.py:82-116):
-//   rstd = rsqrt(sum_j ssq[j][t] / d + eps),  y = bf16(h * rstd * (1 + scale) + shift)
-// with the partials summed in tile order, and re-arms the ticket for the next
-// launch.  Thread et owns columns 8 et .. 8 et + 7; sc / sh are its scale and shift
-// (loaded before the receive wait).  Called by the 128 epilogue threads after the
-// unit loop, when the receive slots `scratch` are free (norm_scratch_bytes); `flag`
-// is a shared word.  The critical path is the ticket (it releases the CTA's stores,
-// ordered before it by the barrier) and one batch of L2 loads; the arithmetic runs
-// as a rolled loop over the slice's tokens, because in this once-per-launch code
-// instruction fetch, not arithmetic, is what the threads wait for.
-__host__ __device__ __forceinline__ int norm_scratch_bytes(int nt, int nparts, int d) {
-  return ((nt * nparts * 4 + 15) & ~15) + nt * d * 2;
-}
-
-__device__ __forceinline__ void push_norm_slice(const SkinnyParams& p, int tok0, int t0, int t1, int rank, int et,
-                                                float* scratch, int* flag, const float (&sc)[8],
-                                                const float (&sh)[8], unsigned long long* nstamps) {
-  const int nt = t1 - t0;
-  if (nt <= 0) return;  // an empty slice on every tile: no ticket taken
-  named_bar_sync(1, kEpiThreads);
-  if (et == 0) {
-    const int prev = atom_add_acq_rel_gpu(p.norm_tickets + rank, 1);
-    const int last = prev == p.n_tiles - 1;
-    if (last) atomicExch(p.norm_tickets + rank, 0);
-    *flag = last;
-    if (nstamps != nullptr) {  // trace: ticket taken (ns), last owner
-      nstamps[0] = globaltimer_ns();
-      nstamps[1] = (unsigned long long)last;
-    }
-  }
-  named_bar_sync(1, kEpiThreads);
-  if (*flag == 0) return;
-  if (nstamps != nullptr) nstamps[2] = globaltimer_ns();
-  const int d = p.norm_d, nparts = p.n_tiles, c = et * 8;
-  float* s_part = scratch;  // [nt][nparts]
-  __nv_bfloat16* s_rows = reinterpret_cast<__nv_bfloat16*>(
-      reinterpret_cast<uint8_t*>(scratch) + ((nt * nparts * 4 + 15) & ~15));  // [nt][d]
-  const __nv_bfloat16* rows = p.out + (size_t)(tok0 + t0) * p.ldo;
-  for (int i = et; i < nt * nparts; i += kEpiThreads)
-    s_part[i] = __ldcg(p.row_ssq + (size_t)(i % nparts) * p.ssq_ld + tok0 + t0 + i / nparts);
-  if (c < d) {
-#pragma unroll 1
-    for (int t = 0; t < nt; ++t) cp_async_16(s_rows + (size_t)t * d + c, rows + (size_t)t * p.ldo + c);
-    cp_async_wait_all();
-  }
-  named_bar_sync(1, kEpiThreads);  // the partials
-  if (nstamps != nullptr) nstamps[3] = globaltimer_ns();
-  if (c >= d) return;
-#pragma unroll 1
-  for (int t = 0; t < nt; ++t) {
-    float ss = 0.f;
-#pragma unroll 1
-    for (int j = 0; j < nparts; ++j) ss += s_part[t * nparts + j];
-    const float rstd = rsqrtf(ss / (float)d + p.norm_eps);
-    const uint4 u = *reinterpret_cast<const uint4*>(s_rows + (size_t)t * d + c);
-    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
-    __align__(16) __nv_bfloat16 o[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] = __float2bfloat16(__bfloat162float(h[j]) * rstd * (1.0f + sc[j]) + sh[j]);
-    if (nstamps != nullptr && t == 0) nstamps[4] = globaltimer_ns();
-    *reinterpret_cast<uint4*>(p.norm_out + (size_t)(tok0 + t0 + t) * p.norm_ldo + c) =
-        *reinterpret_cast<const uint4*>(o);
-  }
-}
-
 template <int EPI, int KIND, int U>
 __device__ __forceinline__ void cluster_push_body(const SkinnyParams& p, const float* st, const float* recv,
                                                   uint64_t* rbar, int tile, int tok0, int mt, int rank, int et,
-                                                  bool epi, unsigned long long* stamps, int* flag) {
+                                                  bool epi, unsigned long long* stamps) {
   constexpr int H = (KIND == CK_GEGLU || KIND == CK_ROT) ? 2 : 1;
   constexpr int UPT = H == 2 ? 16 : 32;  // units per token
   const int splits = p.splits;
@@ -516,9 +446,6 @@ __device__ __forceinline__ void cluster_push_body(const SkinnyParams& p, const f
   const bool stamp = stamps != nullptr && epi && et == 0;
   constexpr int kSU = H == 1 ? 4 : 2;  // splits whose loads are in flight together
   UnitOps ops0;  // operands of this thread's first unit, loaded before the receive wait
-  constexpr bool kNormOut = KIND == CK_ROWS && EPI == SK_EPI_GATED_RESID;
-  const bool pnorm = kNormOut && epi && p.norm_out != nullptr;
-  float nsc[8], nsh[8];  // producer-side norm: scale and shift of this thread's 8 columns
   if (stamp) stamps[0] = globaltimer_ns();
   bool ok = true;
   if (epi) {
@@ -533,12 +460,6 @@ __device__ __forceinline__ void cluster_push_body(const SkinnyParams& p, const f
     }
     if (stamp) stamps[1] = globaltimer_ns();
     if (unit_valid<EPI, KIND>(p, tile, u0 + et, u1)) unit_load_ops<EPI, KIND>(p, tile, tok0, u0 + et, ops0);
-    if (kNormOut && pnorm && et * 8 < p.norm_d) {
-      load4f(p.norm_mod + et * 8, nsc);
-      load4f(p.norm_mod + et * 8 + 4, nsc + 4);
-      load4f(p.norm_mod + p.norm_d + et * 8, nsh);
-      load4f(p.norm_mod + p.norm_d + et * 8 + 4, nsh + 4);
-    }
     ok = mbar_wait_cluster(rbar, 0);
     if (!ok) report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
   }
@@ -592,9 +513,6 @@ __device__ __forceinline__ void cluster_push_body(const SkinnyParams& p, const f
       }
     }
   }
-  if (kNormOut && pnorm && ok)
-    push_norm_slice(p, tok0, t0, t1, rank, et, const_cast<float*>(recv), flag, nsc, nsh,
-                    stamp ? stamps + 10 : nullptr);
   if (stamp) stamps[3] = globaltimer_ns();
   __syncwarp();
   cluster_wait();
@@ -604,40 +522,38 @@ __device__ __forceinline__ void cluster_push_body(const SkinnyParams& p, const f
 template <int EPI, int KIND>
 __device__ __forceinline__ void cluster_push_kind(const SkinnyParams& p, const float* st, const float* recv,
                                                   uint64_t* rbar, int tile, int tok0, int mt, int rank, int et,
-                                                  bool epi, unsigned long long* stamps, int* flag) {
+                                                  bool epi, unsigned long long* stamps) {
   constexpr int H = (KIND == CK_GEGLU || KIND == CK_ROT) ? 2 : 1;
   const int tmax = (mt + p.splits - 1) / p.splits;
   const int per_thread = (tmax * (H == 2 ? 16 : 32) + kEpiThreads - 1) / kEpiThreads;
   if (per_thread >= 4)
-    cluster_push_body<EPI, KIND, 4>(p, st, recv, rbar, tile, tok0, mt, rank, et, epi, stamps, flag);
+    cluster_push_body<EPI, KIND, 4>(p, st, recv, rbar, tile, tok0, mt, rank, et, epi, stamps);
   else if (per_thread >= 2)
-    cluster_push_body<EPI, KIND, 2>(p, st, recv, rbar, tile, tok0, mt, rank, et, epi, stamps, flag);
+    cluster_push_body<EPI, KIND, 2>(p, st, recv, rbar, tile, tok0, mt, rank, et, epi, stamps);
   else
-    cluster_push_body<EPI, KIND, 1>(p, st, recv, rbar, tile, tok0, mt, rank, et, epi, stamps, flag);
+    cluster_push_body<EPI, KIND, 1>(p, st, recv, rbar, tile, tok0, mt, rank, et, epi, stamps);
 }
 
 // Whole push-form cluster epilogue; every thread of the CTA calls it, the epilogue
 // threads after fencing the staging tile they wrote (fence.proxy.async) followed by
 // a barrier among themselves.  `recv` must hold splits * ceil(mt / splits) * 512
 // bytes; `rbar` was initialised with one arrival, armed with push_recv_bytes() and
-// published by a cluster barrier before the mainloop.  `flag` is a shared word for
-// the producer-side norm's ticket.  Trace stamps (optional): [0..4] the phases,
-// [10..14] the producer-side norm: ticket time, last-owner flag, and in the last
-// owner the flag barrier passed, the loads' barrier passed, the first row computed.
+// published by a cluster barrier before the mainloop.  Trace stamps (optional):
+// [0..4] the phases.
 template <int EPI>
 __device__ __forceinline__ void cluster_push_epilogue(const SkinnyParams& p, const float* st, const float* recv,
                                                       uint64_t* rbar, int tile, int tok0, int mt, int rank, int et,
-                                                      bool epi, unsigned long long* stamps, int* flag) {
+                                                      bool epi, unsigned long long* stamps) {
   if (EPI == SK_EPI_GEGLU) {
-    cluster_push_kind<EPI, CK_GEGLU>(p, st, recv, rbar, tile, tok0, mt, rank, et, epi, stamps, flag);
+    cluster_push_kind<EPI, CK_GEGLU>(p, st, recv, rbar, tile, tok0, mt, rank, et, epi, stamps);
   } else if (EPI == SK_EPI_QKV_ROPE) {
     const int n_rot_tiles = (p.n_q_heads + p.n_kv_heads) * (p.head_dim / 128);
     if (tile < n_rot_tiles)
-      cluster_push_kind<EPI, CK_ROT>(p, st, recv, rbar, tile, tok0, mt, rank, et, epi, stamps, flag);
+      cluster_push_kind<EPI, CK_ROT>(p, st, recv, rbar, tile, tok0, mt, rank, et, epi, stamps);
     else
-      cluster_push_kind<EPI, CK_V>(p, st, recv, rbar, tile, tok0, mt, rank, et, epi, stamps, flag);
+      cluster_push_kind<EPI, CK_V>(p, st, recv, rbar, tile, tok0, mt, rank, et, epi, stamps);
   } else {
-    cluster_push_kind<EPI, CK_ROWS>(p, st, recv, rbar, tile, tok0, mt, rank, et, epi, stamps, flag);
+    cluster_push_kind<EPI, CK_ROWS>(p, st, recv, rbar, tile, tok0, mt, rank, et, epi, stamps);
   }
 }
 

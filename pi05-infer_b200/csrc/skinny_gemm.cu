@@ -49,15 +49,14 @@ constexpr int recv_bytes() {
   return TOK == 64 ? 32768 : 0;
 }
 
-// Fused-norm area: rstd per token, scale and shift of the CTA's K range (at most
-// STAGES k-blocks).
-template <int TOK, int STAGES>
-constexpr int norm_bytes() {
-  return TOK * 4 + 2 * STAGES * 64 * 4;
+// Folded-norm area: rstd per token and the folded bias of the tile's rows.
+template <int TOK>
+constexpr int fold_bytes() {
+  return TOK * 4 + kBM * 4;
 }
 
-// Ring, barrier area (512 B), receive slots; the fused-norm area follows and is
-// only allocated for launches that normalise X.
+// Ring, barrier area (512 B), receive slots; the folded-norm area follows and is
+// only allocated for launches with a folded norm.
 template <int TOK, int STAGES>
 constexpr int smem_base_bytes() {
   return 1024 + STAGES * (kABytes + TOK * 128) + 512 + recv_bytes<TOK>();
@@ -65,7 +64,7 @@ constexpr int smem_base_bytes() {
 
 template <int TOK, int STAGES>
 constexpr int smem_bytes() {
-  return smem_base_bytes<TOK, STAGES>() + norm_bytes<TOK, STAGES>();
+  return smem_base_bytes<TOK, STAGES>() + fold_bytes<TOK>();
 }
 
 // Small-token variants are limited to 170 registers so that two CTAs fit per SM:
@@ -95,18 +94,13 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 ? 2 : 1))
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(accum + 2);
   int* s_flag = reinterpret_cast<int*>(s_tmem + 1);  // [0] abort, [1] ticket
   uint64_t* rbar = accum + 9;                         // push-form split-K: partial slices received
-  uint64_t* xrdy = accum + 10;                        // [STAGES] fused norm: X stage normalised
   float* recv = reinterpret_cast<float*>(smem + STAGES * kStageBytes + 512);     // push-form receive slots
-  float* s_rstd = recv + recv_bytes<TOK>() / 4;                                   // [TOK]
-  float* s_mod = s_rstd + TOK;                                                    // [2][STAGES * 64]
-  // Fused norm of X (q|k|v only; its K range is at most STAGES k-blocks).
-  constexpr bool kNormCapable = EPI == SK_EPI_QKV_ROPE && TOK == 64;
-  const bool norm = kNormCapable && p.norm_ssq != nullptr;
-  // Folded norm of X (gate/up, q|k|v; 64-token tile): rstd per token (s_rstd) and
-  // the bias of the tile's 128 rows (in the fused-norm area; the two exclude each other).
+  // Folded norm of X (gate/up, q|k|v; 64-token tile): rstd per token and the bias
+  // of the tile's 128 rows.
   constexpr bool kFoldCapable = TOK == 64 && (EPI == SK_EPI_GEGLU || EPI == SK_EPI_QKV_ROPE);
   const bool fold = kFoldCapable && p.fold_ssq != nullptr;
-  float* s_fbias = s_mod;  // [kBM]
+  float* s_rstd = recv + recv_bytes<TOK>() / 4;  // [TOK]
+  float* s_fbias = s_rstd + TOK;                 // [kBM]
   float* stage_tile = reinterpret_cast<float*>(smem);
   constexpr bool kPushFits = recv_bytes<TOK>() > 0;
   const bool push = kPushFits && p.cluster && p.push;
@@ -127,10 +121,8 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 ? 2 : 1))
     }
     mbar_init(accum, 1);
     mbar_init(rbar, 1);
-    for (int s = 0; s < STAGES; ++s) mbar_init(&xrdy[s], 4);
     s_flag[0] = 0;
     s_flag[1] = 0;
-    for (int i = 14; i < 19; ++i) accum[i] = 0;  // trace: producer-side norm stamps
     fence_mbar_init();
     // Push form: expect this rank's token slice from every other split.
     if (push) mbar_arrive_expect_tx(rbar, push_recv_bytes(p.splits, mt, (int)cluster_ctarank()));
@@ -156,7 +148,6 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 ? 2 : 1))
   const uint32_t tmem_acc = *s_tmem;
   const uint64_t t_start = (p.trace != nullptr) ? globaltimer_ns() : 0;
   uint64_t t_pdl = 0, t_acc = 0, t_pub = 0, t_red = 0;
-  uint64_t t_nload = 0, t_nx0 = 0, t_nxl = 0;  // fused norm: loads done, first / last X stage normalised
   // Let the next kernel in the stream start its prologue / weight prefetch.
   pdl_launch_dependents();
 
@@ -168,17 +159,14 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 ? 2 : 1))
       const int pre = min(STAGES, nk);
       // Weights do not depend on the previous kernel: issue them before the grid-dependency wait.
       if (p.trace != nullptr) s_stamp[0] = globaltimer_ns();
-      // With the fused norm the epilogue warps fill the X slots; stages carry W only.
-      const uint32_t stage_tx = norm ? kABytes : kStageBytes;
       for (int i = 0; i < pre; ++i) {
-        mbar_arrive_expect_tx(&full[i], stage_tx);
+        mbar_arrive_expect_tx(&full[i], kStageBytes);
         const int kx = (kb0 + i) * kBK;
         tma_load_2d(sA + i * kABytes, &tm_w0, &full[i], kx, tr.row0, pol_w);
         tma_load_2d(sA + i * kABytes + kABytes / 2, &tm_w1, &full[i], kx, tr.row1, pol_w);
       }
       pdl_wait();
-      if (!norm)
-        for (int i = 0; i < pre; ++i) tma_load_2d(sB + i * kBBytes, &tm_x, &full[i], (kb0 + i) * kBK, tok0, pol_x);
+      for (int i = 0; i < pre; ++i) tma_load_2d(sB + i * kBBytes, &tm_x, &full[i], (kb0 + i) * kBK, tok0, pol_x);
       for (int i = pre; i < nk; ++i) {
         const int s = i % STAGES;
         if (!mbar_wait(&empty[s], ((i / STAGES) & 1) ^ 1)) {
@@ -197,12 +185,6 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 ? 2 : 1))
     pdl_wait();
     if (lane == 0) {
       bool ok = true;
-      // Fused norm: the epilogue warps write the whole X operand once.
-      if (norm && !mbar_wait(&xrdy[0], 0)) {
-        report_status(p.status, PI05_DEV_TIMEOUT_MMA);
-        s_flag[0] = 1;
-        ok = false;
-      }
       for (int i = 0; i < nk && ok; ++i) {
         const int s = i % STAGES;
         if (!mbar_wait(&full[s], (i / STAGES) & 1)) {
@@ -224,22 +206,7 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 ? 2 : 1))
       if (ok) umma_commit(accum);
     }
   } else {
-    // Epilogue warps 2..5: TMEM lane quarter = warp % 4.  While the mainloop runs,
-    // one lane spreads this CTA's share of the L2 prefetch ranges.
-    if (warp == 2 && lane == 0) {
-      const int nct = gridDim.x * gridDim.y, id = blockIdx.y * gridDim.x + blockIdx.x;
-      const void* pfs[2] = {p.pf0, p.pf1};
-      const size_t pfb[2] = {p.pf0_bytes, p.pf1_bytes};
-      for (int r = 0; r < 2; ++r) {
-        if (pfs[r] == nullptr || pfb[r] == 0) continue;
-        const size_t share = ((pfb[r] / nct) + 255) & ~size_t(255);
-        const size_t b0 = (size_t)id * share;
-        for (size_t off = b0; off < pfb[r] && off < b0 + share; off += 65536) {
-          const size_t n = min(min(share - (off - b0), pfb[r] - off), (size_t)65536);
-          if (n >= 16) prefetch_l2_bulk(static_cast<const char*>(pfs[r]) + off, (uint32_t)(n & ~size_t(15)));
-        }
-      }
-    }
+    // Epilogue warps 2..5: TMEM lane quarter = warp % 4.
     if constexpr (kFoldCapable) {
       if (fold) {
         // The folded bias is a weight: staged before the grid-dependency wait.
@@ -268,86 +235,6 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 ? 2 : 1))
           s_rstd[et] = et < mt ? rsqrtf(ss / (float)p.fold_d + p.fold_eps) : 0.f;
         }
         named_bar_sync(1, kEpiThreads);  // s_rstd, s_fbias
-      }
-    }
-    if constexpr (kNormCapable) {
-      if (norm) {
-        // Fused (ada)RMS norm of X.  The CTA's K range holds at most STAGES
-        // k-blocks, so its whole X operand fits the ring's X slots: every X
-        // k-block is loaded straight from the residual stream h (L2), normalised in
-        // registers, x = bf16(h * rstd * (1 + scale) + shift), and written once in
-        // the 128B-swizzled operand layout; the producer streams only weights.  rstd
-        // comes from the producer's per-tile partial sums of squares (in order).
-        const int d = p.norm_d;
-        const int kbase = kb0 * kBK;
-        const int klen = min(nk * kBK, p.k - kbase);  // multiple of 8
-        // rstd of token et (threads < TOK), published through shared memory.
-        if (et < TOK) {
-          float ssv[kNormMaxParts];
-#pragma unroll
-          for (int j = 0; j < kNormMaxParts; ++j)
-            ssv[j] = (et < mt && j < p.norm_parts) ? p.norm_ssq[(size_t)j * p.norm_ld + tok0 + et] : 0.f;
-          float ss = 0.f;
-#pragma unroll
-          for (int j = 0; j < kNormMaxParts; ++j) ss += ssv[j];  // parts in order (zeros past the end)
-          s_rstd[et] = et < mt ? rsqrtf(ss / (float)d + p.norm_eps) : 0.f;
-        }
-        // Scale / shift of the CTA's K range into shared memory (float4 chunks).
-        for (int c = et; 4 * c < klen; c += kEpiThreads) {
-          reinterpret_cast<float4*>(s_mod)[c] = reinterpret_cast<const float4*>(p.norm_mod + kbase)[c];
-          reinterpret_cast<float4*>(s_mod + STAGES * kBK)[c] = reinterpret_cast<const float4*>(p.norm_mod + d + kbase)[c];
-        }
-        // This thread's chunk g (8 k values) of rows t = et/8 + 16 r, all k-blocks:
-        // every load issued before the first is used.
-        constexpr int kRPT = TOK / 16;
-        const int g = et & 7, t0r = et >> 3;
-        uint4 hx[STAGES][kRPT];
-#pragma unroll
-        for (int i = 0; i < STAGES; ++i) {
-          const int kc = i * kBK + g * 8;  // within the CTA's K range
-          const bool kin = i < nk && kc < klen;
-#pragma unroll
-          for (int r = 0; r < kRPT; ++r) {
-            const int t = t0r + 16 * r;
-            hx[i][r] = (kin && t < mt)
-                           ? *reinterpret_cast<const uint4*>(p.norm_x + (size_t)(tok0 + t) * p.norm_ldx + kbase + kc)
-                           : make_uint4(0u, 0u, 0u, 0u);
-          }
-        }
-        named_bar_sync(1, kEpiThreads);  // s_rstd, s_mod
-        if (p.trace != nullptr) t_nload = globaltimer_ns();
-#pragma unroll
-        for (int i = 0; i < STAGES; ++i) {
-          if (i >= nk) break;
-          const int kc = i * kBK + g * 8;
-          const bool kin = kc < klen;
-          float scv[8], shv[8];
-          if (kin) {
-            load8f(s_mod + kc, scv);
-            load8f(s_mod + STAGES * kBK + kc, shv);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) scv[j] = shv[j] = 0.f;
-          }
-          uint8_t* xs = sB + i * kBBytes;
-#pragma unroll
-          for (int r = 0; r < kRPT; ++r) {
-            const int t = t0r + 16 * r;
-            float x[8], o[8];
-            unpack8(hx[i][r], x);
-            const float rs = s_rstd[t];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float nv = x[j] * rs;
-              o[j] = t < mt ? nv * (1.0f + scv[j]) + shv[j] : 0.f;  // zero-padded k gives 0 * ... + 0
-            }
-            *reinterpret_cast<uint4*>(xs + t * 128 + ((g ^ (t & 7)) << 4)) = pack8(o);
-          }
-        }
-        fence_proxy_async_smem();  // generic-proxy writes -> the MMA's async-proxy reads
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&xrdy[0]);
-        if (p.trace != nullptr) t_nx0 = t_nxl = globaltimer_ns();
       }
     }
     const bool ok = mbar_wait(accum, 0);
@@ -439,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 ? 2 : 1))
     __syncwarp();
     if (push)
       cluster_push_epilogue<EPI>(p, stage_tile, recv, rbar, tile, tok0, mt, (int)cluster_ctarank(),
-                                 (int)threadIdx.x - 64, warp >= 2, p.trace != nullptr ? cl_stamps : nullptr, &s_flag[1]);
+                                 (int)threadIdx.x - 64, warp >= 2, p.trace != nullptr ? cl_stamps : nullptr);
     else
       cluster_epilogue<EPI>(p, smem_u32(stage_tile), tile, tok0, mt, (int)cluster_ctarank(), (int)threadIdx.x - 64,
                             warp >= 2, p.trace != nullptr ? cl_stamps : nullptr);
@@ -451,8 +338,7 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 ? 2 : 1))
 
   if (p.trace != nullptr && threadIdx.x == 64) {
     const unsigned long long cta = ((unsigned long long)smid() << 16) | (blockIdx.y * gridDim.x + blockIdx.x);
-    const unsigned long long slot =
-        atomicAdd(p.trace, (p.cluster ? 2ull : 1ull) + (norm ? 1ull : 0ull) + (p.cluster && p.norm_out ? 1ull : 0ull));
+    const unsigned long long slot = atomicAdd(p.trace, p.cluster ? 2ull : 1ull);
     const unsigned long long cap = p.trace[1];  // records the buffer holds
     if (slot < cap) {
       unsigned long long* w = p.trace + 8 + slot * 8;
@@ -467,34 +353,11 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 ? 2 : 1))
     }
     if (p.cluster && slot + 1 < cap) {
       // Cluster epilogue record (tag + 2^30): before / after the first cluster
-      // barrier, first DSMEM pass summed, last store issued, exit barrier passed,
-      // then (producer-side norm) the ticket time and whether this CTA was last.
+      // barrier (push form: epilogue start / copies issued), first DSMEM pass
+      // summed (push form: slices received), last store issued, exit barrier passed.
       unsigned long long* w = p.trace + 8 + (slot + 1) * 8;
       w[0] = ((unsigned long long)(p.trace_tag + (1 << 30)) << 32) | cta;
       for (int i = 0; i < 5; ++i) w[1 + i] = cl_stamps[i];
-      w[6] = cl_stamps[10];  // producer-side norm: ticket taken, last owner
-      w[7] = cl_stamps[11];
-    }
-    if (p.cluster && p.norm_out != nullptr && slot + 2 < cap) {
-      // Producer-side norm record (tag + 3 * 2^30): ticket, last flag, then in the
-      // last owner: flag barrier passed, loads' barrier passed, first row computed.
-      unsigned long long* w = p.trace + 8 + (slot + 2) * 8;
-      w[0] = ((unsigned long long)(p.trace_tag + (3u << 30)) << 32) | cta;
-      for (int i = 0; i < 5; ++i) w[1 + i] = cl_stamps[10 + i];
-      w[6] = 0;
-      w[7] = 0;
-    }
-    const unsigned long long ns = slot + (p.cluster ? 2 : 1) + (p.cluster && p.norm_out != nullptr ? 1 : 0);
-    if (norm && ns < cap) {
-      // Fused-norm record (tag + 2^31): grid-dependency wait done, rstd / scale
-      // loads done, first and last X stage normalised.
-      unsigned long long* w = p.trace + 8 + ns * 8;
-      w[0] = ((unsigned long long)(p.trace_tag + (2u << 30)) << 32) | cta;
-      w[1] = t_pdl;
-      w[2] = t_nload;
-      w[3] = t_nx0;
-      w[4] = t_nxl;
-      w[5] = t_acc;
       w[6] = 0;
       w[7] = 0;
     }
@@ -522,8 +385,8 @@ template <int EPI, int TOK, int STAGES>
 int launch_one(const SkinnyParams& p, const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x,
                int tok_tiles, cudaStream_t stream) {
   constexpr int kSmemMax = smem_bytes<TOK, STAGES>();
-  // Without the fused or folded norm their area is left out.
-  const int kSmem = (p.norm_ssq != nullptr || p.fold_ssq != nullptr) ? kSmemMax : smem_base_bytes<TOK, STAGES>();
+  // Without a folded norm its area is left out.
+  const int kSmem = p.fold_ssq != nullptr ? kSmemMax : smem_base_bytes<TOK, STAGES>();
   auto kern = skinny_gemm_kernel<EPI, TOK, STAGES>;
   static bool attr_done[16] = {false};
   int dev = 0;
@@ -652,57 +515,11 @@ int skinny_choose_splits_cluster(int n_tiles, int kb_total, int tok_tiles, int s
   return best;
 }
 
-// PI05_L2_PREFETCH=1 in the environment issues the next-layer L2 prefetch ranges
-// that callers pass (pf0 / pf1).  Off by default: the small-token GEMMs issue their
-// first ring of weight TMA loads before the grid-dependency wait, which already
-// covers most of a split's K range, and on B200 the extra prefetch stream made the
-// denoise step slower (760 -> 746 us/step without it).
-bool l2_prefetch_enabled() {
-  static int v = [] {
-    const char* e = getenv("PI05_L2_PREFETCH");
-    return (e != nullptr && e[0] == '1') ? 1 : 0;
-  }();
-  return v != 0;
-}
-
-bool push_enabled() {
-  static int v = [] {
-    const char* e = getenv("PI05_PUSH");
-    return (e != nullptr && e[0] == '0') ? 0 : 1;
-  }();
-  return v != 0;
-}
-
-bool cluster_disabled() {
-  static int v = [] {
-    const char* e = getenv("PI05_CLUSTER");
-    return (e != nullptr && e[0] == '0') ? 1 : 0;
-  }();
-  return v != 0;
-}
-
 int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int w_rows0, int w_rows1,
                     const void* x, int ldx, int splits_override, void* stream) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (p.m_tok <= 0 || p.k <= 0 || p.k % 8 != 0 || p.n_tiles <= 0 || (p.n_valid % 8) != 0) {
     set_last_error("skinny_gemm: bad shape m=%d k=%d tiles=%d", p.m_tok, p.k, p.n_tiles);
-    return PI05_ERR_SHAPE;
-  }
-  if (p.norm_ssq != nullptr &&
-      (epi != SK_EPI_QKV_ROPE || p.norm_d != p.k || p.k > kNormMaxK || p.norm_parts <= 0 ||
-       p.norm_parts > kNormMaxParts || p.norm_mod == nullptr || !aligned16(p.norm_mod) || p.norm_d % 8 != 0 ||
-       !aligned16(x) || ldx % 8 != 0 || p.m_tok > 64)) {
-    set_last_error("skinny_gemm: fused norm needs q|k|v, <= 64 tokens, norm_d == k <= %d, 1..%d parts, aligned "
-                   "operands", kNormMaxK, kNormMaxParts);
-    return PI05_ERR_SHAPE;
-  }
-  if (p.norm_out != nullptr &&
-      (epi != SK_EPI_GATED_RESID || p.row_ssq == nullptr || p.ssq_ld < p.m_tok || p.norm_tickets == nullptr ||
-       p.norm_mod == nullptr || !aligned16(p.norm_mod) || !aligned16(p.norm_out) || !aligned16(p.out) ||
-       p.norm_ldo % 8 != 0 || p.ldo % 8 != 0 || p.norm_d != p.n_tiles * kBM || p.n_valid != 0 ||
-       p.norm_ssq != nullptr || p.m_tok > 64)) {
-    set_last_error("skinny_gemm: producer-side norm needs gated residual, <= 64 tokens, row statistics, "
-                   "norm_d == output width, aligned operands");
     return PI05_ERR_SHAPE;
   }
   const bool wide_ok = p.m_tok >= kWideMinTokens && !wide_disabled();
@@ -718,7 +535,7 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
     // Small-token kernel: <= 64 tokens, rstd and the folded bias (denoise adaRMS);
     // many-token kernel: rstd only (the prefix LM's RMSNorm has no shift).
     bool bad = (epi != SK_EPI_GEGLU && epi != SK_EPI_QKV_ROPE) || p.fold_parts <= 0 || p.fold_d <= 0 ||
-               p.fold_ld < p.m_tok || p.norm_ssq != nullptr || p.ln_sum != nullptr;
+               p.fold_ld < p.m_tok || p.ln_sum != nullptr;
     if (wide_ok)
       bad = bad || p.fold_bias0 != nullptr || p.fold_bias1 != nullptr ||
             (epi == SK_EPI_QKV_ROPE && p.head_dim != 256);
@@ -726,17 +543,11 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
       bad = bad || p.m_tok > 64 || p.fold_parts > kNormMaxParts || p.fold_bias0 == nullptr || p.fold_bias1 == nullptr;
     if (bad) {
       set_last_error("skinny_gemm: folded norm needs gate/up or q|k|v; <= 64 tokens with 1..%d parts and both bias "
-                     "vectors, or >= %d tokens without bias; no fused norm", kNormMaxParts, kWideMinTokens);
+                     "vectors, or >= %d tokens without bias", kNormMaxParts, kWideMinTokens);
       return PI05_ERR_SHAPE;
     }
   }
-  if (p.norm_ssq != nullptr) {
-    p.norm_x = static_cast<const __nv_bfloat16*>(x);
-    p.norm_ldx = ldx;
-  }
-  // The fused and producer-side norms exist only in the small-token kernel.
-  const bool skinny_only = p.norm_ssq != nullptr || p.norm_out != nullptr;
-  if (wide_ok && !skinny_only) {
+  if (wide_ok) {
     int n_cols = 0;
     if (epi == SK_EPI_GEGLU)
       n_cols = p.n_tiles * 64;
@@ -775,7 +586,7 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
     p.fault_skip_split = fault.skip_split;
     p.wait_ns = fault.wait_ns;
   }
-  const bool use_cluster = p.allow_cluster != 0 && max_cl > 1 && !cluster_disabled() && fault.skip_split < 0;
+  const bool use_cluster = p.allow_cluster != 0 && max_cl > 1 && fault.skip_split < 0;
   if (splits_override > 0) {
     p.splits = std::min(splits_override, p.kb_total);
     p.cluster = (use_cluster && p.splits > 1 && p.splits <= max_cl) ? 1 : 0;
@@ -787,22 +598,6 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
   } else {
     p.splits = skinny_choose_splits(p.n_tiles, p.kb_total, tok_tiles, num_sms());
     p.cluster = 0;
-  }
-  if (p.norm_ssq != nullptr) {
-    // The whole X operand of a CTA must fit the ring's three X slots.
-    const int need = (p.kb_total + 2) / 3;
-    if (p.splits < need) {
-      if (need > 1 && use_cluster && need <= max_cl) {
-        p.splits = need;
-        p.cluster = 1;
-      } else if (need > 1 && (long)tok_tiles * p.n_tiles * need <= num_sms()) {
-        p.splits = need;
-        p.cluster = 0;
-      } else {
-        set_last_error("skinny_gemm: fused norm needs %d splits", need);
-        return PI05_ERR_SHAPE;
-      }
-    }
   }
   if (p.splits > 1 && !p.cluster) {
     const size_t need = (size_t)tok_tiles * p.n_tiles * p.splits * tok * kBM * sizeof(float);
@@ -816,26 +611,11 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
       return PI05_ERR_WORKSPACE;
     }
   }
-  if (!l2_prefetch_enabled()) {
-    p.pf0 = nullptr;
-    p.pf1 = nullptr;
-  }
   // Push-form split-K for the small-token tile (splits <= 16 fit its receive slots).
   {
     const int mt = std::min(p.m_tok, tok);
     const long need = (long)(p.splits - 1) * ((mt + p.splits - 1) / p.splits) * kBM * 4;
-    p.push = (p.cluster && tok == 64 && p.splits <= 16 && need <= 32768 && push_enabled()) ? 1 : 0;
-  }
-  // The producer-side norm runs in the push form's epilogue (one token tile, rows
-  // of at most 8 columns per epilogue thread, the slice's rows within the receive
-  // slots); any other schedule normalises with the norm kernel after the GEMM.
-  __nv_bfloat16* norm_after = nullptr;
-  const bool norm_in_epilogue =
-      p.push && tok_tiles == 1 && p.norm_d <= 8 * kEpiThreads &&
-      norm_scratch_bytes((std::min(p.m_tok, tok) + p.splits - 1) / p.splits, p.n_tiles, p.norm_d) <= recv_bytes<64>();
-  if (p.norm_out != nullptr && !norm_in_epilogue) {
-    norm_after = p.norm_out;
-    p.norm_out = nullptr;
+    p.push = (p.cluster && tok == 64 && p.splits <= 16 && need <= 32768) ? 1 : 0;
   }
   CUtensorMap tw0, tw1, tx;
   int rc = make_tmap_bf16_2d(&tw0, w0, w_rows0, p.k, p.k, 64, 64, true);
@@ -864,9 +644,6 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
       set_last_error("skinny_gemm: unknown epilogue %d", epi);
       return PI05_ERR_INVALID_ARG;
   }
-  if (rc == 0 && norm_after != nullptr)
-    rc = rms_norm_run(p.out, p.ldo, p.norm_mod, nullptr, norm_after, p.norm_ldo, p.m_tok, p.norm_d, p.norm_eps,
-                      stream);
   return rc;
 }
 

@@ -52,28 +52,6 @@ struct SkinnyParams {
   float* row_ssq = nullptr;
   int ssq_ld = 0;
   float* row_sum = nullptr;  // many-token kernel: the parts' plain sums, same layout (LayerNorm means)
-  // Normalised copy of the output for the next (ada)RMS norm (GATED_RESID, push-form
-  // cluster split-K, one token tile): when norm_out is set, the owner of each token
-  // slice of a tile writes the slice's sums of squares to row_ssq, and the last of
-  // the n_tiles owners of a slice (ticket norm_tickets[slice]) writes
-  // norm_out[t, k] = bf16(out[t, k] * rstd[t] * (1 + norm_mod[k]) + norm_mod[norm_d + k]),
-  // rstd as for the fused norm below (norm_parts = n_tiles, norm_ld = ssq_ld).
-  __nv_bfloat16* norm_out = nullptr;
-  int norm_ldo = 0;
-  int* norm_tickets = nullptr;  // [cluster size], zero on entry, left zero
-  // Fused (ada)RMS norm of the X operand (QKV_ROPE, <= 64 tokens): when norm_ssq is
-  // set, X holds the raw residual stream h, which the kernel normalises while
-  // staging it: x = bf16(h * rstd[t] * (1 + norm_mod[k]) + norm_mod[norm_d + k]),
-  // rstd[t] = rsqrt(sum_j norm_ssq[j * norm_ld + t] / norm_d + norm_eps) over
-  // norm_parts partial sums in order.  Needs k <= kNormMaxK.
-  const float* norm_ssq = nullptr;
-  const __nv_bfloat16* norm_x = nullptr;  // set by the launcher: X (= h) and its row stride
-  int norm_ldx = 0;
-  int norm_parts = 0;
-  int norm_ld = 0;
-  const float* norm_mod = nullptr;
-  int norm_d = 0;
-  float norm_eps = 0.f;
   // Folded (ada)RMS norm of the X operand (GEGLU / QKV_ROPE): X holds
   // the raw residual stream h and the weights carry the norm's (1 + scale) in their
   // columns (pi05_fold_adarms), so the norm reduces to a per-token factor and a
@@ -99,12 +77,6 @@ struct SkinnyParams {
   // mean = sum / fold_d, rstd = rsqrt(ssq / fold_d - mean^2 + fold_eps).
   const float* ln_sum = nullptr;
   const float* ln_colsum = nullptr;
-  // L2 prefetch issued by every CTA for its share of these ranges (e.g. the same
-  // op's weights of the next layer), so later launches read them from L2.
-  const void* pf0 = nullptr;
-  size_t pf0_bytes = 0;
-  const void* pf1 = nullptr;
-  size_t pf1_bytes = 0;
   // Optional timing trace: word 0 is a slot counter, word 1 the capacity in
   // records (records beyond it are dropped); each CTA appends 8 words at 8 + 8*slot
   // {tag << 32 | cta, entry, after prologue, after grid-dependency wait,
@@ -124,19 +96,13 @@ struct SkinnyParams {
   int* status = nullptr;    // device status word
 };
 
-constexpr int kNormMaxK = 1024;    // fused-norm X operands: K range staged in shared memory
-constexpr int kNormMaxParts = 16;  // fused-norm partial sums of squares per token
+constexpr int kNormMaxParts = 16;  // folded-norm partial sums of squares per token
 
 // Parts per token that a GATED_RESID / STORE launch of m_tok tokens and n_cols
 // output columns writes to row_ssq (the kernel it will run on decides).
 int row_ssq_parts(int m_tok, int n_cols);
 int skinny_choose_splits(int n_tiles, int kb_total, int tok_tiles, int sms);
 int skinny_choose_splits_cluster(int n_tiles, int kb_total, int tok_tiles, int sms, int max_cluster);
-// PI05_CLUSTER=0 in the environment selects the global-memory split-K path.
-bool cluster_disabled();
-// PI05_PUSH=0 in the environment selects the pull form of the cluster split-K.
-bool push_enabled();
-bool l2_prefetch_enabled();
 
 // w0/w1: weight matrices for the two 64-row boxes of each tile (the same matrix
 // except for GEGLU, where w0 = gate and w1 = up).  w_rows*: their row counts.

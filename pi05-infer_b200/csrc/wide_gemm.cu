@@ -94,64 +94,32 @@ constexpr int wide_smem_bytes() {
   return wide_smem_base<EPI, BN, STAGES, EW, PAIR>() + (wide_scol<EPI, BN, STAGES, EW, PAIR>() ? BN * 4 : 0);
 }
 
-constexpr int kMaxSegs = 4;  // stream-K: CTAs sharing one tile at most
-
 struct WideSched {
   int m_tiles;
   int n_tiles;
   int kb_total;
-  int splits;   // split-K (STORE / GATED_RESID only): splits, or partial slots per tile (stream-K)
-  int streamk;  // 1: every unit takes an equal contiguous range of the (tile, k-block) space
-  int grid;     // stream-K: the number of units (the launch grid)
+  int splits;   // split-K (STORE / GATED_RESID only)
 };
 
 // A unit's work item: tile (m, n), k-block range [kb0, kb1), and the segment s of
-// nseg that cut the tile's K range (split-K / stream-K; nseg = 1 for a whole tile).
+// nseg that cut the tile's K range (split-K; nseg = 1 for a whole tile).
 struct WideTile {
   int m, s, n, kb0, kb1, nseg;
 };
-
-// Stream-K: unit c owns units [start(c), start(c+1)) of the tile-major (tile, k-block)
-// space; the unit holding k-block u.
-__device__ __forceinline__ long sk_start(int c, long total_units, int n_units) {
-  return (long)c * total_units / n_units;
-}
-
-__device__ __forceinline__ int sk_owner(long u, long total_units, int n_units) {
-  int c = (int)((u * n_units) / total_units);
-  while (c + 1 < n_units && sk_start(c + 1, total_units, n_units) <= u) ++c;
-  while (c > 0 && sk_start(c, total_units, n_units) > u) --c;
-  return c;
-}
 
 // Item i of unit `unit` (false past its last).  Tiles are ordered m fastest, so
 // units running together share weight tiles.
 __device__ __forceinline__ bool wide_item(int unit, int i, int n_units, const WideSched& ws, WideTile& w) {
   const int tiles = ws.m_tiles * ws.n_tiles;
-  if (!ws.streamk) {
-    const int t = unit + i * n_units;
-    if (t >= tiles * ws.splits) return false;
-    w.m = t % ws.m_tiles;
-    const int r = t / ws.m_tiles;
-    w.s = r % ws.splits;
-    w.n = r / ws.splits;
-    w.kb0 = (w.s * ws.kb_total) / ws.splits;
-    w.kb1 = ((w.s + 1) * ws.kb_total) / ws.splits;
-    w.nseg = ws.splits;
-    return true;
-  }
-  const long kb = ws.kb_total, total = (long)tiles * kb;
-  const long u0 = sk_start(unit, total, n_units), u1 = sk_start(unit + 1, total, n_units);
-  const long tile = u0 / kb + i;
-  const long a = max(u0, tile * kb), b = min(u1, (tile + 1) * kb);
-  if (a >= b) return false;
-  w.m = (int)(tile % ws.m_tiles);
-  w.n = (int)(tile / ws.m_tiles);
-  w.kb0 = (int)(a - tile * kb);
-  w.kb1 = (int)(b - tile * kb);
-  const int first = sk_owner(tile * kb, total, n_units);
-  w.s = unit - first;
-  w.nseg = sk_owner((tile + 1) * kb - 1, total, n_units) - first + 1;
+  const int t = unit + i * n_units;
+  if (t >= tiles * ws.splits) return false;
+  w.m = t % ws.m_tiles;
+  const int r = t / ws.m_tiles;
+  w.s = r % ws.splits;
+  w.n = r / ws.splits;
+  w.kb0 = (w.s * ws.kb_total) / ws.splits;
+  w.kb1 = ((w.s + 1) * ws.kb_total) / ws.splits;
+  w.nseg = ws.splits;
   return true;
 }
 
@@ -990,24 +958,8 @@ int wide_launch(const SkinnyParams& p, const WideSched& ws, const WideMaps& mp, 
     return launch_pdl_cluster(kern, dim3(2 * pairs), dim3(wide_threads<EW>()), kSmem, stream, pdl_enabled(),
                               dim3(2, 1, 1), mp, p, ws);
   }
-  const int grid = ws.streamk ? ws.grid : std::min(total, wide_sms());
+  const int grid = std::min(total, wide_sms());
   return launch_pdl(kern, dim3(grid), dim3(wide_threads<EW>()), kSmem, stream, pdl_enabled(), mp, p, ws);
-}
-
-// Host copy of the stream-K schedule: the largest number of units sharing one tile
-// when `units` units split tiles x kb k-blocks evenly.
-int sk_max_segs(long tiles, long kb, int units) {
-  const long total = tiles * kb;
-  auto start = [&](int c) { return (long)c * total / units; };
-  auto owner = [&](long u) {
-    int c = (int)((u * units) / total);
-    while (c + 1 < units && start(c + 1) <= u) ++c;
-    while (c > 0 && start(c) > u) --c;
-    return c;
-  };
-  int best = 1;
-  for (long t = 0; t < tiles; ++t) best = std::max(best, owner((t + 1) * kb - 1) - owner(t * kb) + 1);
-  return best;
 }
 
 // Debug override read once: PI05_WIDE_BN (128 / 256) for STORE / GATED_RESID.
@@ -1019,20 +971,15 @@ int env_int(const char* name) {
 }  // namespace
 
 int wide_choose(int epi, int m_tiles, int n_cols, int kb_total, int sms, int* bn, int* splits, int* pair,
-                int* streamk, bool allow_pair) {
+                bool allow_pair) {
   static const int force_bn = env_int("PI05_WIDE_BN");
   static const int force_splits = env_int("PI05_WIDE_SPLITS");
   static const int force_pair = [] {
     const char* e = getenv("PI05_WIDE_PAIR");
     return e != nullptr ? atoi(e) : -1;
   }();
-  static const int force_sk = [] {
-    const char* e = getenv("PI05_WIDE_STREAMK");
-    return e != nullptr ? atoi(e) : -1;
-  }();
   *splits = 1;
   *pair = 0;
-  *streamk = 0;
   // CTA pairs pay a longer prologue and (with split-K) a slower epilogue; they win
   // on the long-running projections: gate/up at full token tiles and long-K ones
   // (the prefix down_proj).  PI05_WIDE_PAIR=0 / 1 disables / forces them.
@@ -1077,23 +1024,6 @@ int wide_choose(int epi, int m_tiles, int n_cols, int kb_total, int sms, int* bn
       }
     }
   }
-  // Stream-K (PI05_WIDE_STREAMK=1): every SM takes an equal share of the (tile,
-  // k-block) space, tiles cut across SMs finished by their last segment.
-  if (force_sk > 0) {
-    const int b = 128;
-    const long tiles = (long)m_tiles * ((n_cols + b - 1) / b);
-    int units = (int)std::min<long>(sms, tiles * kb_total);
-    while (units > 1 && sk_max_segs(tiles, kb_total, units) > kMaxSegs) --units;
-    const int segs = sk_max_segs(tiles, kb_total, units);
-    // Measured slower than the classic schedule on the prefix / SigLIP shapes (the
-    // partial round trips of 3-4 segments per tile): on request only.
-    if (force_sk > 0 && segs > 1) {
-      *bn = b;
-      *splits = segs;  // partial slots per tile
-      *streamk = units;
-      return 0;
-    }
-  }
   if (force_bn == 128 || force_bn == 256) *bn = force_bn;
   if (force_splits >= 1 && force_splits <= 2) *splits = force_splits;
   return 0;
@@ -1121,12 +1051,9 @@ int wide_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int w
   WideSched ws;
   const int cta_m_tiles = (p.m_tok + kWBM - 1) / kWBM;
   ws.kb_total = (p.k + kBK - 1) / kBK;
-  int bn = 256, splits = 1, pair = 0, sk_units = 0;
+  int bn = 256, splits = 1, pair = 0;
   // The folded LayerNorm runs on single CTAs (its column sums are staged per CTA).
-  wide_choose(epi, cta_m_tiles, n_cols, ws.kb_total, wide_sms(), &bn, &splits, &pair, &sk_units,
-              p.ln_colsum == nullptr);
-  ws.streamk = sk_units > 0 ? 1 : 0;
-  ws.grid = sk_units;
+  wide_choose(epi, cta_m_tiles, n_cols, ws.kb_total, wide_sms(), &bn, &splits, &pair, p.ln_colsum == nullptr);
   // Pairs schedule 256-token tiles; every CTA still owns 128 tokens of one.
   ws.m_tiles = pair ? (cta_m_tiles + 1) / 2 : cta_m_tiles;
   const int m_tiles_cta = pair ? 2 * ws.m_tiles : ws.m_tiles;
@@ -1141,8 +1068,6 @@ int wide_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int w
     if (p.accum == nullptr || p.counters == nullptr || need > p.accum_bytes ||
         (long)m_tiles_cta * ws.n_tiles > kWsNormTicketBase || splits > ws.kb_total) {
       splits = 1;
-      ws.streamk = 0;
-      ws.grid = 0;
     }
   }
   ws.splits = splits;

@@ -10,12 +10,11 @@ namespace pi05 {
 int wide_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int w_rows0, int w_rows1, int n_cols,
                   const void* x, int ldx, void* stream);
 
-// Tile width (128 / 256), split-K count, whether a CTA pair shares each tile
-// (cta_group::2, 256 x 256 tiles), and the stream-K unit count (0 = off; then
-// `splits` is the partial slots per tile) for an epilogue kind and shape; m_tiles
-// counts 128-token tiles.
+// Tile width (128 / 256), split-K count and whether a CTA pair shares each tile
+// (cta_group::2, 256 x 256 tiles) for an epilogue kind and shape; m_tiles counts
+// 128-token tiles.
 int wide_choose(int epi, int m_tiles, int n_cols, int kb_total, int sms, int* bn, int* splits, int* pair,
-                int* streamk, bool allow_pair = true);
+                bool allow_pair = true);
 
 // PI05_WIDE=0 in the environment keeps every projection on the small-token kernel.
 bool wide_disabled();

@@ -51,9 +51,10 @@ _EXTRA = {
     "pi05_adarms_table": (_I, [_P, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _Z, _P]),
     "pi05_denoise_step": (_I, [ctypes.POINTER(Pi05ExpertPlan), _I, _P]),
     "pi05_denoise_loop": (_I, [ctypes.POINTER(Pi05ExpertPlan), _P]),
-    "pi05_denoise_loop_persistent": (_I, [ctypes.POINTER(Pi05ExpertPlan), _P]),
-    "pi05_trace_slots": (_I, []),
     "pi05_fold_adarms": (_I, [_P, _I, _I, _P, _P, _P, _P, _P]),
+    "pi05_preprocess_images": (_I, [_P, _I, _I, _I, _I, _P, _I, _P]),
+    "pi05_normalize_rows": (_I, [_P, _I, _I, _P, _P, _I, _I, _P, _I, _P]),
+    "pi05_unnormalize_rows": (_I, [_P, _I, _I, _P, _P, _I, _I, _P, _I, _P]),
 }
 _lib.SIGNATURES.update(_EXTRA)
 
@@ -118,11 +119,6 @@ def fold_adarms(w, scale, shift, w_out, b_out, stream=None):
 def denoise_loop(plan: Pi05ExpertPlan, stream: int):
     _bind()
     _lib.call("pi05_denoise_loop", ctypes.byref(plan), stream)
-
-
-def denoise_loop_persistent(plan: Pi05ExpertPlan, stream: int):
-    _bind()
-    _lib.call("pi05_denoise_loop_persistent", ctypes.byref(plan), stream)
 
 
 def denoise_step(plan: Pi05ExpertPlan, step: int, stream: int):

@@ -1,9 +1,11 @@
 """``build_model`` / ``get_model`` with the reference's signatures (``builder.py:34-151``).
 
 Loads a pi0.5 checkpoint (``*.safetensors`` or an FSDP ``full_weights.pt``, as the
-reference's builder does, ``builder.py:77-106``) into an ``OpenPi0Inference``.
-openpi's data configs and input/output transforms are out of scope, so
-``config_name`` only selects the model family (pi0.5 variants) and
+reference's builder does, ``builder.py:77-106``) into an ``OpenPi0Inference``,
+with the checkpoint's ``norm_stats.json`` (``builder.py:112-136``) when present.
+``config_name`` selects the policy's input/output transform (``pi05_libero``: main
++ wrist camera, 7 action dims; ``pi05_turtle``: main + extra views, 6 action dims;
+``pi05``: none); openpi's other data-config options are out of scope, so
 ``data_kwargs`` is accepted and ignored.
 """
 
@@ -17,8 +19,10 @@ import torch
 
 from .config import EngineConfig
 from .engine import OpenPi0Inference
+from .transforms import load_norm_stats
 
 SUPPORTED_CONFIGS = ("pi05_libero", "pi05_turtle", "pi05")
+_POLICY = {"pi05_libero": "libero", "pi05_turtle": "turtle", "pi05": "none"}
 
 
 def _load_state_dict(model_path: str) -> Dict[str, torch.Tensor]:
@@ -67,14 +71,21 @@ def build_model(model_path: str, config_name: str = "pi05_libero", *, data_kwarg
     del data_kwargs
     if config_name not in SUPPORTED_CONFIGS:
         raise ValueError(f"config {config_name!r} not supported (pi0.5 variants only: {SUPPORTED_CONFIGS})")
-    cfg = EngineConfig()
+    cfg = EngineConfig(policy=_POLICY[config_name])
     device = overrides.pop("device", "cuda")
     for k, v in overrides.items():
         if not hasattr(cfg, k):
             raise TypeError(f"unknown override {k!r}")
         setattr(cfg, k, v)
     sd = _load_state_dict(model_path)
-    return OpenPi0Inference(cfg, sd, device=device)
+    engine = OpenPi0Inference(cfg, sd, device=device)
+    # norm statistics of the checkpoint (<asset_id>/norm_stats.json), when present
+    if os.path.isdir(model_path):
+        try:
+            engine.set_norm_stats(load_norm_stats(model_path))
+        except FileNotFoundError:
+            pass
+    return engine
 
 
 def get_model(cfg: Any, torch_dtype=None) -> OpenPi0Inference:  # noqa: ARG001

@@ -77,3 +77,13 @@ class EngineConfig:
     prefix_lm: GemmaShape = GEMMA_2B
     siglip: SiglipShape = SIGLIP_SO400M
     max_prefix_len: int = 1480
+    # Input / output transforms of predict_action_batch (openpi data config):
+    # "libero" (main + wrist camera, 7 action dims), "turtle" (main + up to two
+    # extra views, 6 action dims) or "none" (32 action dims, no camera mapping);
+    # quantile normalisation as openpi uses it for pi0.5.
+    policy: str = "libero"
+    use_quantile_norm: bool = True
+
+    @property
+    def env_action_dim(self) -> int:
+        return {"libero": 7, "turtle": 6}.get(self.policy, self.action_dim)

@@ -26,10 +26,11 @@ from typing import Any, Dict, Optional
 
 import torch
 
-from . import _lib, abi, ops, synthetic
+from . import _lib, abi, ops, synthetic, transforms
 from .config import ACTION_DIM, ACTION_HORIZON, GEMMA_2B, GEMMA_300M, SIGLIP_SO400M, EngineConfig
 from .expert import DenoiseRunner, ExpertWeights
 from .prefix import PrefixRunner, PrefixWeights, embed_tokens
+from .transforms import NormStats
 
 
 @dataclasses.dataclass
@@ -85,6 +86,7 @@ class OpenPi0Inference:
         self._ids_pinned = None   # pinned int32 staging of the prompt ids
         self._ids_event = None
         self._inputs_read = None  # event after the input copies of the last call
+        self.norm_stats: Optional[Dict[str, NormStats]] = None
         if state_dict is not None:
             self.load_state_dict(state_dict)
 
@@ -327,12 +329,77 @@ class OpenPi0Inference:
         actions = den.run(noise.to(self.device, non_blocking=True).float(), use_graph=self.use_cuda_graph)
         return {"actions": actions.clone().reshape(1, self.config.action_horizon, self.config.action_dim)}
 
-    def predict_action_batch(self, env_obs: Dict[str, Any]) -> torch.Tensor:
-        """``engine.py:321-342`` without openpi's input/output transforms: a dict with
-        openpi ``Observation`` keys in, ``[B, action_chunk, 32]`` actions out."""
-        obs = Observation.from_dict(env_obs)
-        out = self.sample_actions(obs)["actions"]
+    # ---------------------------------------------------- input / output transforms
+    def set_norm_stats(self, stats: Optional[Dict[str, "NormStats"]], use_quantiles: Optional[bool] = None) -> None:
+        """Statistics for the state normalisation and the action un-normalisation
+        (``norm_stats.json`` of the checkpoint, ``builder.py:112-136``)."""
+        self.norm_stats = stats
+        if use_quantiles is not None:
+            self.config.use_quantile_norm = use_quantiles
+
+    def obs_processor(self, env_obs: Dict[str, Any]) -> Observation:
+        """Environment observation -> model observation, on the GPU (``engine.py:287-303``
+        and the policy's input transform): ``main_images`` / ``wrist_images`` /
+        ``extra_view_images`` uint8 ``[B, H, W, 3]`` (extra views ``[B, n, H, W, 3]``) map
+        to the three camera slots and are resized / scaled to [-1, 1]
+        (``pi05_preprocess_images``); ``states`` ``[B, s]`` are normalised and padded
+        to the action dimension.  Prompt tokenisation stays with the caller:
+        ``tokenized_prompt`` / ``tokenized_prompt_mask`` ``[B, L]``."""
+        size = self.config.siglip.image_size
+
+        def prep(x):
+            x = torch.as_tensor(x)
+            return transforms.preprocess_images(x.to(self.device, non_blocking=True), size)
+
+        main = prep(env_obs["main_images"])
+        b = main.shape[0]
+        slots = [main]
+        wrist = env_obs.get("wrist_images")
+        extra = env_obs.get("extra_view_images")
+        if self.config.policy == "turtle":
+            views = []
+            if extra is not None:
+                extra = torch.as_tensor(extra)
+                views = [prep(extra[:, i]) for i in range(extra.shape[1])] if extra.dim() == 5 else [prep(extra)]
+            slots += views[:2]
+        else:
+            if wrist is not None:
+                slots.append(prep(wrist))
+            if extra is not None:
+                slots.append(prep(extra))
+        names = ["base_0_rgb", "left_wrist_0_rgb", "right_wrist_0_rgb"][: self.num_views]
+        images, masks = {}, {}
+        for i, n in enumerate(names):
+            present = i < len(slots)
+            images[n] = slots[i] if present else torch.full_like(main, -1.0)  # zero image = -1 after scaling
+            masks[n] = torch.full((b,), present, dtype=torch.bool)
+        stats = getattr(self, "norm_stats", None)
+        st = transforms.normalize_state(torch.as_tensor(env_obs["states"]).to(self.device),
+                                        None if stats is None else stats.get("state"),
+                                        self.config.use_quantile_norm, self.config.action_dim)
+        return Observation(images, masks, torch.as_tensor(env_obs["tokenized_prompt"]),
+                           torch.as_tensor(env_obs["tokenized_prompt_mask"]).bool(), st)
+
+    def output_transform(self, actions: torch.Tensor) -> torch.Tensor:
+        """Model actions ``[B, H, 32]`` -> environment actions ``[B, action_chunk,
+        env_action_dim]``: un-normalised with the action statistics and cut to the
+        robot's action dimension (``engine.py:270-284``, ``LiberoOutputs`` /
+        ``TurtleOutputs``)."""
+        stats = getattr(self, "norm_stats", None)
+        out = transforms.unnormalize_actions(actions, None if stats is None else stats.get("actions"),
+                                             self.config.use_quantile_norm, self.config.env_action_dim)
         return out[:, : self.config.action_chunk]
+
+    def predict_action_batch(self, env_obs: Dict[str, Any]) -> torch.Tensor:
+        """Environment observations -> environment actions (``engine.py:321-342``):
+        ``obs_processor`` (GPU preprocessing), ``sample_actions``, ``output_transform``.
+        A dict that already holds openpi ``Observation`` keys (``image``,
+        ``image_mask``, ``state``, ...) skips the input transform."""
+        if "image" in env_obs:
+            obs = Observation.from_dict(env_obs)
+        else:
+            obs = self.obs_processor(env_obs)
+        return self.output_transform(self.sample_actions(obs)["actions"])
 
     # ------------------------------------------------------------ bench hooks
     def synthetic_observation(self, seed: int = 100) -> Observation:

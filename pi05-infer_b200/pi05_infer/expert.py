@@ -106,7 +106,7 @@ class DenoiseRunner:
     """Static buffers + C plan for the ``num_steps`` Euler loop of one observation."""
 
     def __init__(self, weights: ExpertWeights, prefix_len: int, num_steps: int = 10, horizon: int = 50,
-                 action_dim: int = 32, attn_splits: int = 0, persistent: Optional[bool] = None):
+                 action_dim: int = 32, attn_splits: int = 0):
         self.w = weights
         s = weights.shape
         dev = weights.device
@@ -179,19 +179,6 @@ class DenoiseRunner:
                                                      ("w_qkv", "w_gate", "w_up", "b_qkv", "b_gate", "b_up")))
             self.plan.fold = ctypes.cast(self._fold, ctypes.POINTER(abi.Pi05ExpertFold))
         self.graph: Optional[torch.cuda.CUDAGraph] = None
-        # pi05_denoise_loop (one launch per kernel phase) by default;
-        # pi05_denoise_loop_persistent (one launch for the loop) on request or with
-        # PI05_PERSISTENT=1, when the GPU and shapes allow it.
-        if persistent is None:
-            persistent = os.environ.get("PI05_PERSISTENT", "0") == "1"
-        self.persistent = persistent and self._persistent_supported()
-
-    def _persistent_supported(self) -> bool:
-        s = self.w.shape
-        props = torch.cuda.get_device_properties(self.device)
-        return (s.width == 1024 and s.head_dim == 256 and s.num_kv_heads == 1 and s.depth <= 18
-                and self.horizon <= 64 and self.num_steps <= 16 and props.multi_processor_count >= 144
-                and self.action_dim <= 32)
 
     def build_table(self) -> None:
         """The adaRMS modulation table for every step, on device (engine.py:556-599)."""
@@ -233,10 +220,7 @@ class DenoiseRunner:
         s = self.w.shape
         abi.rope_table(self.key_valid, self.prefix_len, 1, self.horizon, self.inv_freq, s.head_dim, self.rope_cos,
                        self.rope_sin, stream)
-        if self.persistent:
-            abi.denoise_loop_persistent(self.plan, stream)
-        else:
-            abi.denoise_loop(self.plan, stream)
+        abi.denoise_loop(self.plan, stream)
 
     def run(self, noise: torch.Tensor, use_graph: bool = True) -> torch.Tensor:
         """Run the loop from ``noise`` [50, 32]; returns the actions (a view of the static buffer)."""
