@@ -228,6 +228,13 @@ typedef struct Pi05ExpertPlan {
                                      the layers: q|k|v and gate/up read the residual stream h with these
                                      folded weights and scale each token by its rstd from the row
                                      statistics that action_in / o_proj / down_proj write. */
+  int batch;                      /* independent observations denoised together (0 or 1: one).  With
+                                     batch = B > 1 every GEMM runs over B * tokens rows (observation b's
+                                     rows b * tokens ..); x_t, v_t, h, xn, q, attn, act, rope_cos and
+                                     rope_sin hold B * tokens rows; each layer's k_cache / v_cache hold
+                                     B caches [hkv, kv_rows, d] back to back and key_valid B masks of
+                                     kv_rows; kv_stage is needed. */
+  void* kv_stage;                 /* batch > 1: [2][B * tokens][d] bf16 staging of the new K / V rows */
 } Pi05ExpertPlan;
 
 /* Folds an adaRMS norm into the projection that consumes its output, for the

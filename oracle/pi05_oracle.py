@@ -418,3 +418,62 @@ def embed_language(embed_table: Tensor, tokens: Tensor, policy: str) -> Tensor:
 def embed_prefix(image_feats: Tensor, lang_emb: Tensor) -> Tensor:
     """Concatenate ``[views*patches + tokens, width]`` (``pi0_pytorch.py:190-253``)."""
     return torch.cat([image_feats.reshape(-1, image_feats.shape[-1]), lang_emb.reshape(-1, lang_emb.shape[-1])], dim=0)
+
+
+# ---------------------------------------------------------------------------
+# input / output transforms around sample_actions (predict_action_batch)
+# ---------------------------------------------------------------------------
+# The reference runs these through openpi (third-party, not in the reference
+# tree): its image preprocessing (preprocess_observation_pytorch, called at
+# pi0_pytorch.py:165-174, and the ResizeImages input transform) and its
+# Normalize / Unnormalize transforms built at builder.py:120-136.  openpi's
+# source is absent here, so the image resize is anchored on torch's
+# F.interpolate (bilinear, half-pixel centres, no antialiasing) with the
+# resize-with-pad geometry (aspect ratio kept, longer side fitted, centred, black
+# border); parity with openpi's own resize is unpinned.
+
+
+def preprocess_images(images: Tensor, size: int = 224) -> Tensor:
+    """uint8 ``[n, h, w, 3]`` (or ``[n, 3, h, w]``) -> fp32 ``[n, 3, size, size]`` in [-1, 1]."""
+    x = images
+    if not (x.shape[1] == 3 and x.shape[-1] != 3):
+        x = x.permute(0, 3, 1, 2)
+    x = x.float()
+    n, _, h, w = x.shape
+    ratio = max(w / size, h / size)
+    rh = min(max(int(h / ratio), 1), size)
+    rw = min(max(int(w / ratio), 1), size)
+    if (rh, rw) != (h, w):
+        x = torch.nn.functional.interpolate(x, size=(rh, rw), mode="bilinear", align_corners=False, antialias=False)
+    out = torch.full((n, 3, size, size), -1.0)
+    py, px = (size - rh) // 2, (size - rw) // 2
+    out[:, :, py: py + rh, px: px + rw] = x / 255.0 * 2.0 - 1.0
+    return out
+
+
+def normalize(x: Tensor, a: Tensor, b: Tensor, use_quantiles: bool, out_dim: int) -> Tensor:
+    """openpi Normalize (mean/std or q01/q99) on the first ``len(a)`` features, then
+    zero-padding to ``out_dim`` (PadStatesAndActions)."""
+    x = x.float().clone()
+    d = min(a.numel(), x.shape[-1])
+    a, b = a[:d].float(), b[:d].float()
+    if use_quantiles:
+        x[..., :d] = (x[..., :d] - a) / (b - a + 1e-6) * 2.0 - 1.0
+    else:
+        x[..., :d] = (x[..., :d] - a) / (b + 1e-6)
+    pad = out_dim - x.shape[-1]
+    return torch.nn.functional.pad(x, (0, pad)) if pad > 0 else x
+
+
+def unnormalize(x: Tensor, a: Tensor, b: Tensor, use_quantiles: bool, out_dim: int) -> Tensor:
+    """openpi Unnormalize on the first ``len(a)`` features, then the policy's output
+    slice ``[..., :out_dim]`` (LiberoOutputs, TurtleOutputs at
+    dataconfig/policies/turtle_policy.py:89-93)."""
+    x = x.float().clone()
+    d = min(a.numel(), x.shape[-1])
+    a, b = a[:d].float(), b[:d].float()
+    if use_quantiles:
+        x[..., :d] = (x[..., :d] + 1.0) / 2.0 * (b - a + 1e-6) + a
+    else:
+        x[..., :d] = x[..., :d] * (b + 1e-6) + a
+    return x[..., :out_dim]

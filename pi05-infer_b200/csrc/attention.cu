@@ -99,6 +99,11 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int row0 = blockIdx.x * kRows;
   const int split = blockIdx.y;
+  // This CTA's observation (blockIdx.z; 0 without a batch).
+  const size_t bz = blockIdx.z;
+  const __nv_bfloat16* kbase = p.k + bz * p.kv_batch;
+  const __nv_bfloat16* vbase = p.v + bz * p.kv_batch;
+  const uint8_t* valid_base = p.key_valid + bz * p.valid_batch;
   const bool tr = p.trace != nullptr && tid == 0;
   const uint64_t t_entry = tr ? globaltimer_ns() : 0;
   uint64_t t_wait = 0, t_data = 0, t_loop = 0;
@@ -115,12 +120,12 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       const int key = key0 + r;
       const bool ok = key < p.kv_len;
       const size_t off = (size_t)(ok ? key : 0) * p.kv_stride + c * 8;
-      cp_async16(kb + swz(r, c), p.k + off, ok);
-      cp_async16(vb + swz(r, c), p.v + off, ok);
+      cp_async16(kb + swz(r, c), kbase + off, ok);
+      cp_async16(vb + swz(r, c), vbase + off, ok);
     }
     for (int r = tid; r < kChunk; r += WARPS * 32) {
       const int key = key0 + r;
-      sValid[buf * kChunk + r] = (key < p.kv_len && p.key_valid[key]) ? 1 : 0;
+      sValid[buf * kChunk + r] = (key < p.kv_len && valid_base[key]) ? 1 : 0;
     }
   };
 
@@ -138,7 +143,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     const int gr = row0 + r;
     const bool ok = gr < p.rows;
     cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(sQ)) + swz(r, c),
-               p.q + (size_t)(ok ? gr : 0) * p.q_stride + c * 8, ok);
+               p.q + bz * p.q_batch + (size_t)(ok ? gr : 0) * p.q_stride + c * 8, ok);
   }
 
   float o[32][4];
@@ -283,20 +288,20 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     if (r >= p.rows) continue;
     if (p.splits == 1) {
       const float inv = l_run[h] > 0.f ? 1.f / l_run[h] : 0.f;
-      __nv_bfloat16* dst = p.out + (size_t)r * p.out_stride;
+      __nv_bfloat16* dst = p.out + bz * p.out_batch + (size_t)r * p.out_stride;
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         *reinterpret_cast<__nv_bfloat162*>(dst + j * 8 + 2 * t4) =
             __floats2bfloat162_rn(o[j][2 * h] * inv, o[j][2 * h + 1] * inv);
       }
     } else {
-      float* dst = p.part_o + ((size_t)split * p.part_rows + r) * kD;
+      float* dst = p.part_o + (((size_t)bz * p.splits + split) * p.part_rows + r) * kD;
 #pragma unroll
       for (int j = 0; j < 32; ++j)
         *reinterpret_cast<float2*>(dst + j * 8 + 2 * t4) = make_float2(o[j][2 * h], o[j][2 * h + 1]);
       if (t4 == 0) {
-        p.part_ml[((size_t)split * p.part_rows + r) * 2] = m_run[h];
-        p.part_ml[((size_t)split * p.part_rows + r) * 2 + 1] = l_run[h];
+        p.part_ml[(((size_t)bz * p.splits + split) * p.part_rows + r) * 2] = m_run[h];
+        p.part_ml[(((size_t)bz * p.splits + split) * p.part_rows + r) * 2 + 1] = l_run[h];
       }
     }
   }
@@ -329,10 +334,14 @@ __global__ void __launch_bounds__(64) mqa_combine_kernel(const AttnParams p) {
   }
   if (warp >= p.rows) return;
   const int r = warp;
+  // Observation blockIdx.y: its partials and output rows.
+  const size_t bz = blockIdx.y;
+  const float* part_o = p.part_o + bz * p.splits * p.part_rows * kD;
+  const float* part_ml = p.part_ml + bz * p.splits * p.part_rows * 2;
   float ms = -INFINITY, ls = 0.f;
   if (lane < p.splits) {
-    ms = p.part_ml[((size_t)lane * p.part_rows + r) * 2];
-    ls = p.part_ml[((size_t)lane * p.part_rows + r) * 2 + 1];
+    ms = part_ml[((size_t)lane * p.part_rows + r) * 2];
+    ls = part_ml[((size_t)lane * p.part_rows + r) * 2 + 1];
   }
   float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   if (p.splits <= kCombineMaxSplits) {
@@ -340,7 +349,7 @@ __global__ void __launch_bounds__(64) mqa_combine_kernel(const AttnParams p) {
 #pragma unroll
     for (int j = 0; j < kCombineMaxSplits; ++j) {
       if (j < p.splits) {
-        const float4* src = reinterpret_cast<const float4*>(p.part_o + ((size_t)j * p.part_rows + r) * kD + lane * 8);
+        const float4* src = reinterpret_cast<const float4*>(part_o + ((size_t)j * p.part_rows + r) * kD + lane * 8);
         a[j] = __ldcg(src);
         b[j] = __ldcg(src + 1);
       }
@@ -369,7 +378,7 @@ __global__ void __launch_bounds__(64) mqa_combine_kernel(const AttnParams p) {
     for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffff, l, o);
     for (int j = 0; j < p.splits; ++j) {
       const float wj = __shfl_sync(0xffffffff, w, j & 31);
-      const float4* src = reinterpret_cast<const float4*>(p.part_o + ((size_t)j * p.part_rows + r) * kD + lane * 8);
+      const float4* src = reinterpret_cast<const float4*>(part_o + ((size_t)j * p.part_rows + r) * kD + lane * 8);
       const float4 x = __ldcg(src), y = __ldcg(src + 1);
       acc[0] += x.x * wj; acc[1] += x.y * wj; acc[2] += x.z * wj; acc[3] += x.w * wj;
       acc[4] += y.x * wj; acc[5] += y.y * wj; acc[6] += y.z * wj; acc[7] += y.w * wj;
@@ -378,7 +387,7 @@ __global__ void __launch_bounds__(64) mqa_combine_kernel(const AttnParams p) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] *= inv;
   }
-  __nv_bfloat16* dst = p.out + (size_t)r * p.out_stride + lane * 8;
+  __nv_bfloat16* dst = p.out + bz * p.out_batch + (size_t)r * p.out_stride + lane * 8;
   uint4 pk;
   pk.x = pack_bf16(acc[0], acc[1]);
   pk.y = pack_bf16(acc[2], acc[3]);
@@ -421,7 +430,7 @@ int tc_min_rows() {
 
 // Two rows (warps) per CTA, so the partial reads spread over every SM.
 int launch_combine(const AttnParams& p, cudaStream_t st) {
-  return launch_pdl(mqa_combine_kernel, dim3((p.rows + 1) / 2), dim3(64), 0, st, pdl_enabled(), p);
+  return launch_pdl(mqa_combine_kernel, dim3((p.rows + 1) / 2, p.batch), dim3(64), 0, st, pdl_enabled(), p);
 }
 
 // mma.sync path: W warps of 16 query rows per CTA (default 2, which halves the
@@ -442,7 +451,7 @@ int mma_sync_attention(AttnParams p, float* part, size_t part_bytes, int splits,
     // Up to two CTAs per SM (a CTA's 2 warps use half of the SM's sub-partitions;
     // the key loop is bound by the mma.sync rate per sub-partition).
     splits = 1;
-    while (row_blocks * splits * 2 <= 2 * sms && splits * 2 <= n_chunks) splits *= 2;
+    while (row_blocks * p.batch * splits * 2 <= 2 * sms && splits * 2 <= n_chunks) splits *= 2;
   }
   splits = splits > n_chunks ? n_chunks : splits;
   splits = splits > 32 ? 32 : splits;
@@ -450,19 +459,19 @@ int mma_sync_attention(AttnParams p, float* part, size_t part_bytes, int splits,
   p.nbuf = (n_chunks + splits - 1) / splits > 1 ? 2 : 1;
   const size_t smem = attn_smem_bytes<W>(p.nbuf);
   if (splits > 1) {
-    const size_t need_o = (size_t)splits * p.rows * kD * sizeof(float);
-    const size_t need = need_o + (size_t)splits * p.rows * 2 * sizeof(float);
+    const size_t need_o = (size_t)p.batch * splits * p.rows * kD * sizeof(float);
+    const size_t need = need_o + (size_t)p.batch * splits * p.rows * 2 * sizeof(float);
     if (part == nullptr || need > part_bytes) {
       set_last_error("attention: workspace too small (%zu needed)", need);
       return PI05_ERR_WORKSPACE;
     }
     p.part_rows = p.rows;
     p.part_o = part;
-    p.part_ml = part + (size_t)splits * p.rows * kD;
+    p.part_ml = part + (size_t)p.batch * splits * p.rows * kD;
   }
   int rc = set_attn_smem<W>();
   if (rc) return rc;
-  rc = launch_pdl(mqa_flash_kernel<W>, dim3(row_blocks, splits), dim3(W * 32), smem, st, pdl_enabled(), p);
+  rc = launch_pdl(mqa_flash_kernel<W>, dim3(row_blocks, splits, p.batch), dim3(W * 32), smem, st, pdl_enabled(), p);
   if (rc || splits == 1) return rc;
   return launch_combine(p, st);
 }
@@ -473,13 +482,13 @@ int mqa_attention_run(AttnParams p, float* part, size_t part_bytes, int splits, 
     set_last_error("attention: head_dim %d unsupported (256 only)", p.head_dim);
     return PI05_ERR_SHAPE;
   }
-  if (p.rows <= 0 || p.kv_len <= 0) {
-    set_last_error("attention: empty rows/keys");
+  if (p.rows <= 0 || p.kv_len <= 0 || p.batch <= 0 || p.batch > 65535) {
+    set_last_error("attention: empty rows/keys or bad batch");
     return PI05_ERR_SHAPE;
   }
   // tcgen05 for many query rows (prefix LM: 968 x 8); the mma.sync kernel below is
   // faster for the denoise suffix (50 x 8 rows), where each CTA owns one key chunk.
-  if (tc_attention_enabled() && p.rows > tc_min_rows())
+  if (tc_attention_enabled() && p.rows > tc_min_rows() && p.batch == 1)
     return mqa_tc_attention_run(p, part, part_bytes, splits, st, launch_combine);
   static const int warps = [] {
     const char* e = getenv("PI05_ATTN_WARPS");

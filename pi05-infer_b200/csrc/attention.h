@@ -28,9 +28,17 @@ struct AttnParams {
   int* status = nullptr;               // device status word (bounded-wait timeouts)
   unsigned long long* trace = nullptr; // optional per-CTA timestamps (same format as the GEMMs)
   int trace_tag = 0;
-  float* part_o = nullptr;             // [splits, part_rows, head_dim]
-  float* part_ml = nullptr;            // [splits, part_rows, 2]
+  float* part_o = nullptr;             // [batch][splits, part_rows, head_dim]
+  float* part_ml = nullptr;            // [batch][splits, part_rows, 2]
   int part_rows = 0;                   // row pitch of one split's partials (>= rows)
+  // Independent observations (mma.sync kernel only): observation z uses q + z * q_batch,
+  // k / v + z * kv_batch, key_valid + z * valid_batch and out + z * out_batch
+  // (elements), with the same rows / kv_len each.
+  int batch = 1;
+  size_t q_batch = 0;
+  size_t kv_batch = 0;
+  size_t valid_batch = 0;
+  size_t out_batch = 0;
 };
 
 // splits <= 0 picks a split count that covers the SMs.  head_dim 256 runs on the

@@ -170,10 +170,17 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
     set_last_error("denoise_step: step %d out of range", step);
     return PI05_ERR_INVALID_ARG;
   }
-  const int T = P->tokens, W = P->width, F = P->mlp_dim, HQ = P->n_q_heads, HKV = P->n_kv_heads, D = P->head_dim;
-  if (HKV != 1 || D != 256 || W % 128 || F % 128 || P->kv_rows < P->prefix_len + T) {
+  // Tt: tokens of one observation; T: rows of every GEMM (B observations stacked).
+  const int Tt = P->tokens, W = P->width, F = P->mlp_dim, HQ = P->n_q_heads, HKV = P->n_kv_heads, D = P->head_dim;
+  const int B = P->batch > 1 ? P->batch : 1;
+  const int T = Tt * B;
+  if (HKV != 1 || D != 256 || W % 128 || F % 128 || P->kv_rows < P->prefix_len + Tt) {
     set_last_error("denoise_step: unsupported shape (hkv=%d d=%d width=%d mlp=%d)", HKV, D, W, F);
     return PI05_ERR_SHAPE;
+  }
+  if (B > 1 && (P->kv_stage == nullptr || !aligned16(P->kv_stage) || B > 1024)) {
+    set_last_error("denoise_step: batch %d needs a 16-byte aligned kv_stage (and at most 1024 observations)", B);
+    return PI05_ERR_INVALID_ARG;
   }
   Workspace ws;
   if (split_workspace(P->workspace, P->workspace_bytes, &ws)) {
@@ -188,7 +195,11 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
   auto* q = static_cast<__nv_bfloat16*>(P->q);
   auto* attn = static_cast<__nv_bfloat16*>(P->attn);
   auto* act = static_cast<__nv_bfloat16*>(P->act);
-  const int kv_len = P->prefix_len + T;
+  const int kv_len = P->prefix_len + Tt;
+  // Batched: the q|k|v GEMM writes the new K / V rows to the staging buffer and a
+  // scatter moves them to each observation's cache rows [prefix_len, prefix_len + Tt).
+  auto* stage_k = static_cast<__nv_bfloat16*>(P->kv_stage);
+  auto* stage_v = stage_k == nullptr ? nullptr : stage_k + (size_t)T * D;
   const float scale = 1.0f / std::sqrt((float)D);
   // Folded norms (default when the plan carries folded weights): no norm kernel
   // inside the layers.  action_in (layer 0, one part) and down_proj write the row
@@ -226,10 +237,17 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.cos = static_cast<const __nv_bfloat16*>(P->rope_cos);
       sp.sin = static_cast<const __nv_bfloat16*>(P->rope_sin);
       sp.q_out = q;
-      sp.k_cache = static_cast<__nv_bfloat16*>(L.k_cache);
-      sp.v_cache = static_cast<__nv_bfloat16*>(L.v_cache);
-      sp.kv_head_stride = (size_t)P->kv_rows * D;
-      sp.krow0 = P->prefix_len;
+      if (B > 1) {
+        sp.k_cache = stage_k;
+        sp.v_cache = stage_v;
+        sp.kv_head_stride = (size_t)T * D;
+        sp.krow0 = 0;
+      } else {
+        sp.k_cache = static_cast<__nv_bfloat16*>(L.k_cache);
+        sp.v_cache = static_cast<__nv_bfloat16*>(L.v_cache);
+        sp.kv_head_stride = (size_t)P->kv_rows * D;
+        sp.krow0 = P->prefix_len;
+      }
       sp.n_q_heads = HQ;
       sp.n_kv_heads = HKV;
       sp.head_dim = D;
@@ -248,6 +266,10 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       }
       rc = skinny_gemm_run(SK_EPI_QKV_ROPE, sp, wq, wq, rows, rows, fold ? h : xn, W, so[0], stream);
       if (rc) break;
+      if (B > 1) {
+        rc = kv_scatter_run(stage_k, stage_v, L.k_cache, L.v_cache, B, Tt, P->prefix_len, P->kv_rows, D, stream);
+        if (rc) break;
+      }
     }
     // attention over [prefix | suffix] keys
     {
@@ -260,8 +282,13 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       ap.key_valid = P->key_valid;
       ap.out = attn;
       ap.out_stride = D;
-      ap.rows = T * HQ;
+      ap.rows = Tt * HQ;
       ap.kv_len = kv_len;
+      ap.batch = B;
+      ap.q_batch = (size_t)Tt * HQ * D;
+      ap.kv_batch = (size_t)P->kv_rows * D;
+      ap.valid_batch = (size_t)P->kv_rows;
+      ap.out_batch = (size_t)Tt * HQ * D;
       ap.head_dim = D;
       ap.scale = scale;
       ap.status = ws.status;

@@ -3,6 +3,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <algorithm>
+
 #include "elementwise.h"
 #include "host_util.h"
 #include "ptx.cuh"
@@ -305,6 +307,29 @@ __global__ void __launch_bounds__(256) linear_f32_rows_kernel(const float* __res
   }
 }
 
+// Batched denoise: the q|k|v GEMM writes the new K / V rows of all observations to
+// a staging buffer [batch * tokens, d] (row b * tokens + t); this copies row
+// (b, t) to row krow0 + t of observation b's cache [kv_rows, d].  One thread moves
+// 16 bytes.
+__global__ void __launch_bounds__(256) kv_scatter_kernel(const __nv_bfloat16* __restrict__ stage_k,
+                                                         const __nv_bfloat16* __restrict__ stage_v,
+                                                         __nv_bfloat16* __restrict__ k_cache,
+                                                         __nv_bfloat16* __restrict__ v_cache, int tokens, int krow0,
+                                                         int kv_rows, int d, int total_rows) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int per_row = d / 8;
+  const long n = (long)total_rows * per_row;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const int row = (int)(i / per_row), c = (int)(i % per_row) * 8;
+    const int b = row / tokens, t = row % tokens;
+    const size_t dst = ((size_t)b * kv_rows + krow0 + t) * d + c;
+    const size_t src = (size_t)row * d + c;
+    *reinterpret_cast<uint4*>(k_cache + dst) = *reinterpret_cast<const uint4*>(stage_k + src);
+    *reinterpret_cast<uint4*>(v_cache + dst) = *reinterpret_cast<const uint4*>(stage_v + src);
+  }
+}
+
 }  // namespace
 
 int rms_norm_run(const void* x, int ldx, const float* mod, const float* w, void* out, int ldo, int rows, int d,
@@ -416,6 +441,21 @@ int linear_f32_rows_run(const float* in, int n_rows, int k, const float* w, cons
     return PI05_ERR_LAUNCH;
   }
   return PI05_OK;
+}
+
+int kv_scatter_run(const void* stage_k, const void* stage_v, void* k_cache, void* v_cache, int batch, int tokens,
+                   int krow0, int kv_rows, int d, void* stream) {
+  if (batch <= 0 || tokens <= 0 || d % 8 != 0 || krow0 < 0 || krow0 + tokens > kv_rows) {
+    set_last_error("kv_scatter: bad shape batch=%d tokens=%d krow0=%d kv_rows=%d d=%d", batch, tokens, krow0,
+                   kv_rows, d);
+    return PI05_ERR_SHAPE;
+  }
+  const long n = (long)batch * tokens * (d / 8);
+  const int grid = (int)std::min<long>((n + 255) / 256, 1184);
+  return launch_pdl(kv_scatter_kernel, dim3(grid), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
+                    pdl_enabled(), static_cast<const __nv_bfloat16*>(stage_k),
+                    static_cast<const __nv_bfloat16*>(stage_v), static_cast<__nv_bfloat16*>(k_cache),
+                    static_cast<__nv_bfloat16*>(v_cache), tokens, krow0, kv_rows, d, batch * tokens);
 }
 
 }  // namespace pi05

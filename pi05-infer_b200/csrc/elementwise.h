@@ -21,6 +21,10 @@ int final_euler_run(const void* h, const float* mod, const float* w, const float
 int rope_table_run(const uint8_t* valid, int n_prefix, int mode, int rows, const float* inv_freq, int d, void* cos,
                    void* sin, void* stream);
 int sinusoid_run(const float* ts, int n_t, int dim, double min_p, double max_p, float* out, void* stream);
+// Batched denoise: staging rows (b * tokens + t) of K and V -> row krow0 + t of
+// observation b's cache ([batch][kv_rows][d]).
+int kv_scatter_run(const void* stage_k, const void* stage_v, void* k_cache, void* v_cache, int batch, int tokens,
+                   int krow0, int kv_rows, int d, void* stream);
 int linear_f32_rows_run(const float* in, int n_rows, int k, const float* w, const float* b, float* out, int n,
                         int act, void* stream);
 

@@ -87,6 +87,8 @@ class OpenPi0Inference:
         self._ids_event = None
         self._inputs_read = None  # event after the input copies of the last call
         self.norm_stats: Optional[Dict[str, NormStats]] = None
+        self._batched: Dict[int, DenoiseRunner] = {}  # batch size -> batched denoise runner
+        self._bstatic: Dict[int, Dict[str, torch.Tensor]] = {}  # batch size -> static inputs
         if state_dict is not None:
             self.load_state_dict(state_dict)
 
@@ -141,8 +143,9 @@ class OpenPi0Inference:
         if self.state_dict is None:
             return
         self.load_state_dict(self.state_dict)
-        if self._denoise is not None:
-            self._denoise.build_table()
+        for den in [self._denoise, *self._batched.values()]:
+            if den is not None:
+                den.build_table()
 
     # ------------------------------------------------------------ compat knobs
     def enable_torch_compile(self, mode: str = "max-autotune") -> None:  # noqa: ARG002
@@ -267,8 +270,96 @@ class OpenPi0Inference:
             raise ValueError(f"noise has batch {noise.shape[0]}, observation has {bsize}")
         if bsize == 1:
             return {"actions": self._sample_one(observation, noise[0])}
+        if self.vision is not None and self.embed_table is not None:
+            return {"actions": self._sample_batched(observation, noise)}
         outs = [self._sample_one(_slice_observation(observation, i), noise[i]) for i in range(bsize)]
         return {"actions": torch.cat(outs, 0)}
+
+    # -------------------------------------------------------- batched observations
+    def _batched_runner(self, bsize: int) -> DenoiseRunner:
+        r = self._batched.get(bsize)
+        if r is None:
+            r = DenoiseRunner(self.expert, prefix_len=self.prefix_len, num_steps=self.config.num_steps,
+                              horizon=self.config.action_horizon, action_dim=self.config.action_dim, batch=bsize)
+            self._batched[bsize] = r
+        return r
+
+    def _host_batch_key_valid(self, obs: Observation, bsize: int, kv_rows: int) -> torch.Tensor:
+        """Key masks of a batch, uint8 ``[bsize, kv_rows]``: the views' patches, the
+        prompt mask, then the action tokens (always valid)."""
+        npatch = self.config.siglip.num_patches
+        parts = [obs.image_masks[n].reshape(bsize, 1).cpu().expand(bsize, npatch) for n in obs.images]
+        parts.append(obs.tokenized_prompt_mask.reshape(bsize, -1).cpu())
+        parts.append(torch.ones(bsize, kv_rows - self.prefix_len, dtype=torch.bool))
+        return torch.cat(parts, 1).to(torch.uint8)
+
+    def _enqueue_batched(self, den: DenoiseRunner, bsize: int, stream: int) -> None:
+        """SigLIP, embeddings and the prefix LM of each observation into its own cache
+        (the prefix runner re-targeted at observation b's cache views), then one
+        batched Euler loop over all of them."""
+        prefix, den1 = self._runners()
+        npatch = self.config.siglip.num_patches
+        nv = self.num_views
+        st = self._bstatic[bsize]
+        base = nv * npatch
+        depth = self.config.expert.depth
+        for b in range(bsize):
+            self._siglip.enqueue(st["imgs"][b * nv: (b + 1) * nv], prefix.h, stream)
+            embed_tokens(self.embed_table, st["ids"][b], prefix.h[base: base + self.prompt_len],
+                         math.sqrt(self.embed_table.shape[1]), ops.workspace(self.device), stream)
+            caches = [den.cache(i, b) for i in range(depth)]
+            prefix.target([c[0] for c in caches], [c[1] for c in caches], den.key_valid_of(b))
+            prefix.enqueue(stream)
+        prefix.target(den1.k_cache, den1.v_cache)
+        den._enqueue(stream)
+
+    def _sample_batched(self, observation: Observation, noise: torch.Tensor) -> torch.Tensor:
+        """``bsize`` observations through one batched pipeline: the denoise GEMMs run at
+        bsize x 50 token rows, so the expert weights stream once per step for the batch."""
+        from .vision import SiglipRunner
+
+        bsize = noise.shape[0]
+        self._runners()
+        den = self._batched_runner(bsize)
+        if not hasattr(self, "_siglip"):
+            self._siglip = SiglipRunner(self.vision, self.num_views)
+        names = list(observation.images.keys())
+        if len(names) != self.num_views:
+            raise ValueError(f"expected {self.num_views} camera views, got {len(names)}")
+        st = self._bstatic.get(bsize)
+        if st is None:
+            size = self.config.siglip.image_size
+            st = {"imgs": torch.zeros((bsize * self.num_views, 3, size, size), dtype=torch.float32,
+                                      device=self.device),
+                  "ids": torch.zeros((bsize, self.prompt_len), dtype=torch.int32, device=self.device)}
+            self._bstatic[bsize] = st
+        imgs = st["imgs"].view(bsize, self.num_views, *st["imgs"].shape[1:])
+        for i, n in enumerate(names):
+            imgs[:, i].copy_(observation.images[n], non_blocking=True)
+        st["ids"].copy_(observation.tokenized_prompt.reshape(bsize, -1).to(torch.int32), non_blocking=True)
+        den.key_valid.copy_(self._host_batch_key_valid(observation, bsize, den.kv_rows).reshape(-1),
+                            non_blocking=True)
+        den.x_t.copy_(noise.reshape(den.rows, den.action_dim), non_blocking=True)
+        stream = torch.cuda.current_stream(self.device)
+        inputs_read = torch.cuda.Event()
+        inputs_read.record(stream)
+        if self.use_cuda_graph:
+            g = self._graphs.get(("batch", bsize))
+            if g is None:
+                saved = den.x_t.clone()
+                self._enqueue_batched(den, bsize, stream.cuda_stream)  # warm-up outside the capture
+                torch.cuda.synchronize(self.device)
+                den.x_t.copy_(saved)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    self._enqueue_batched(den, bsize, torch.cuda.current_stream(self.device).cuda_stream)
+                self._graphs[("batch", bsize)] = g
+            g.replay()
+        else:
+            self._enqueue_batched(den, bsize, stream.cuda_stream)
+        out = den.x_t.clone().reshape(bsize, self.config.action_horizon, self.config.action_dim)
+        inputs_read.synchronize()  # the caller's input buffers have been read
+        return out
 
     def _sample_one(self, observation: Observation, noise: torch.Tensor) -> torch.Tensor:
         prefix, den = self._runners()
@@ -566,6 +657,8 @@ class OpenPi0Inference:
 
     def release_graphs(self) -> None:
         self._graphs.clear()
+        for den in self._batched.values():
+            den.graph = None
         if self._denoise is not None:
             self._denoise.graph = None
 

@@ -103,10 +103,15 @@ class ExpertWeights:
 
 
 class DenoiseRunner:
-    """Static buffers + C plan for the ``num_steps`` Euler loop of one observation."""
+    """Static buffers + C plan for the ``num_steps`` Euler loop of ``batch`` observations.
+
+    With ``batch`` B > 1 the observations are denoised together: every GEMM runs
+    over B x horizon token rows (the weights stream once per step for all of them),
+    attention runs per observation over its own KV cache, and the per-layer caches
+    hold B caches back to back (``cache(i, b)`` is observation b's view)."""
 
     def __init__(self, weights: ExpertWeights, prefix_len: int, num_steps: int = 10, horizon: int = 50,
-                 action_dim: int = 32, attn_splits: int = 0):
+                 action_dim: int = 32, attn_splits: int = 0, batch: int = 1):
         self.w = weights
         s = weights.shape
         dev = weights.device
@@ -115,22 +120,27 @@ class DenoiseRunner:
         self.num_steps = num_steps
         self.horizon = horizon
         self.action_dim = action_dim
+        self.batch = batch
         self.kv_rows = prefix_len + horizon
+        m = horizon * batch  # token rows of every GEMM
+        self.rows = m
         bf = dict(dtype=torch.bfloat16, device=dev)
         f32 = dict(dtype=torch.float32, device=dev)
-        self.k_cache = [torch.zeros((s.num_kv_heads, self.kv_rows, s.head_dim), **bf) for _ in range(s.depth)]
-        self.v_cache = [torch.zeros((s.num_kv_heads, self.kv_rows, s.head_dim), **bf) for _ in range(s.depth)]
-        self.key_valid = torch.ones(self.kv_rows, dtype=torch.uint8, device=dev)
+        # [batch * hkv, kv_rows, d] per layer (hkv = 1): observation b's cache is row block b
+        self.k_cache = [torch.zeros((batch * s.num_kv_heads, self.kv_rows, s.head_dim), **bf) for _ in range(s.depth)]
+        self.v_cache = [torch.zeros((batch * s.num_kv_heads, self.kv_rows, s.head_dim), **bf) for _ in range(s.depth)]
+        self.key_valid = torch.ones(batch * self.kv_rows, dtype=torch.uint8, device=dev)
         self.inv_freq = rope_inv_freq(s.head_dim, s.rope_base, dev)
-        self.rope_cos = torch.empty((horizon, s.head_dim), **bf)
-        self.rope_sin = torch.empty((horizon, s.head_dim), **bf)
-        self.h = torch.zeros((horizon, s.width), **bf)
-        self.xn = torch.zeros((horizon, s.width), **bf)
-        self.q = torch.zeros((horizon, s.num_heads, s.head_dim), **bf)
-        self.attn = torch.zeros((horizon, s.q_dim), **bf)
-        self.act = torch.zeros((horizon, s.mlp_dim), **bf)
-        self.x_t = torch.zeros((horizon, action_dim), **f32)
-        self.v_t = torch.zeros((horizon, action_dim), **f32)
+        self.rope_cos = torch.empty((m, s.head_dim), **bf)
+        self.rope_sin = torch.empty((m, s.head_dim), **bf)
+        self.h = torch.zeros((m, s.width), **bf)
+        self.xn = torch.zeros((m, s.width), **bf)
+        self.q = torch.zeros((m, s.num_heads, s.head_dim), **bf)
+        self.attn = torch.zeros((m, s.q_dim), **bf)
+        self.act = torch.zeros((m, s.mlp_dim), **bf)
+        self.x_t = torch.zeros((m, action_dim), **f32)
+        self.v_t = torch.zeros((m, action_dim), **f32)
+        self.kv_stage = torch.zeros((2, m, s.head_dim), **bf) if batch > 1 else None
         self.ws = ops.workspace(dev)
         self.ts = timesteps(num_steps)
         self._host_ts = (ctypes.c_float * (num_steps + 1))(*[float(v) for v in self.ts])
@@ -142,7 +152,7 @@ class DenoiseRunner:
         # weight stream keeps its size; the copies cost num_steps x 22 MB per layer
         # of HBM (4 GB for the 10-step Gemma-300M loop).
         self.fold = None
-        if horizon <= 64 and os.environ.get("PI05_FOLD_NORM", "1") != "0":
+        if m <= 64 and os.environ.get("PI05_FOLD_NORM", "1") != "0":
             n = num_steps * s.depth
             self.fold = {
                 "w_qkv": torch.empty((n, s.qkv_dim, s.width), **bf),
@@ -170,7 +180,8 @@ class DenoiseRunner:
             rope_sin=self.rope_sin.data_ptr(), key_valid=self.key_valid.data_ptr(), x_t=self.x_t.data_ptr(),
             v_t=self.v_t.data_ptr(), h=self.h.data_ptr(), xn=self.xn.data_ptr(), q=self.q.data_ptr(),
             attn=self.attn.data_ptr(), act=self.act.data_ptr(), workspace=self.ws.data_ptr(),
-            workspace_bytes=self.ws.numel(), attn_splits=attn_splits)
+            workspace_bytes=self.ws.numel(), attn_splits=attn_splits, batch=batch,
+            kv_stage=self.kv_stage.data_ptr() if self.kv_stage is not None else None)
         if self.fold is not None:
             fd = self.fold
             self._fold = (abi.Pi05ExpertFold * (num_steps * s.depth))()
@@ -206,25 +217,39 @@ class DenoiseRunner:
                 abi.fold_adarms(L["w_gate"], m2[0], m2[1], fd["w_gate"][i], fd["b_gate"][i])
                 abi.fold_adarms(L["w_up"], m2[0], m2[1], fd["w_up"][i], fd["b_up"][i])
 
-    def set_prefix(self, kv: Sequence[Tuple[torch.Tensor, torch.Tensor]], prefix_valid: torch.Tensor) -> None:
+    def cache(self, i: int, b: int = 0) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Layer i's (K, V) cache of observation b, ``[1, kv_rows, d]`` views."""
+        return self.k_cache[i][b: b + 1], self.v_cache[i][b: b + 1]
+
+    def key_valid_of(self, b: int = 0) -> torch.Tensor:
+        return self.key_valid[b * self.kv_rows: (b + 1) * self.kv_rows]
+
+    def set_prefix(self, kv: Sequence[Tuple[torch.Tensor, torch.Tensor]], prefix_valid: torch.Tensor,
+                   b: int = 0) -> None:
         """Fill the prefix rows of every layer's static KV buffer (``prime_kv_static``)
-        and the key mask; ``kv[i]`` = (K, V) ``[P, 256]`` (any leading 1-dims)."""
+        and the key mask of observation b; ``kv[i]`` = (K, V) ``[P, 256]`` (any
+        leading 1-dims)."""
         p = self.prefix_len
         for i, (k, v) in enumerate(kv):
-            self.k_cache[i][0, :p].copy_(k.reshape(p, -1))
-            self.v_cache[i][0, :p].copy_(v.reshape(p, -1))
-        self.key_valid[:p].copy_(prefix_valid.reshape(-1).to(torch.uint8))
-        self.key_valid[p:].fill_(1)
+            kc, vc = self.cache(i, b)
+            kc[0, :p].copy_(k.reshape(p, -1))
+            vc[0, :p].copy_(v.reshape(p, -1))
+        kvld = self.key_valid_of(b)
+        kvld[:p].copy_(prefix_valid.reshape(-1).to(torch.uint8))
+        kvld[p:].fill_(1)
 
     def _enqueue(self, stream: int) -> None:
         s = self.w.shape
-        abi.rope_table(self.key_valid, self.prefix_len, 1, self.horizon, self.inv_freq, s.head_dim, self.rope_cos,
-                       self.rope_sin, stream)
+        hz = self.horizon
+        for b in range(self.batch):
+            abi.rope_table(self.key_valid_of(b), self.prefix_len, 1, hz, self.inv_freq, s.head_dim,
+                           self.rope_cos[b * hz: (b + 1) * hz], self.rope_sin[b * hz: (b + 1) * hz], stream)
         abi.denoise_loop(self.plan, stream)
 
     def run(self, noise: torch.Tensor, use_graph: bool = True) -> torch.Tensor:
-        """Run the loop from ``noise`` [50, 32]; returns the actions (a view of the static buffer)."""
-        self.x_t.copy_(noise.reshape(self.horizon, self.action_dim))
+        """Run the loop from ``noise`` [batch * 50, 32] (any leading shape); returns the
+        actions (a view of the static buffer, [batch * 50, 32])."""
+        self.x_t.copy_(noise.reshape(self.rows, self.action_dim))
         if use_graph:
             if self.graph is None:
                 self.capture()

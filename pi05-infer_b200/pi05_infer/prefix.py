@@ -10,7 +10,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from typing import Dict, List, Sequence
+from typing import Dict, List, Optional, Sequence
 
 import torch
 
@@ -154,6 +154,18 @@ class PrefixRunner:
             act=self.act.data_ptr(), workspace=self.ws.data_ptr(), workspace_bytes=self.ws.numel(),
             kv_only_last_layer=1 if kv_only_last_layer else 0,
             row_stats=self.row_stats.data_ptr() if weights.fold else None)
+
+    def target(self, k_cache: Sequence[torch.Tensor], v_cache: Sequence[torch.Tensor],
+               key_valid: Optional[torch.Tensor] = None) -> None:
+        """Point the plan at other KV caches ``[hkv, kv_rows, d]`` per layer (e.g.
+        observation b's views of a batched denoise runner) and, optionally, another
+        key mask (its first ``tokens`` entries are read).  The C call reads the plan
+        when it is enqueued, so each enqueue (and a graph captured from it) keeps
+        the targets it was enqueued with."""
+        for i in range(len(self._layers)):
+            self._layers[i].k_cache = k_cache[i].data_ptr()
+            self._layers[i].v_cache = v_cache[i].data_ptr()
+        self.plan.key_valid = (self.key_valid if key_valid is None else key_valid).data_ptr()
 
     def enqueue(self, stream: int) -> None:
         _bind()

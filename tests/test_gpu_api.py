@@ -131,10 +131,11 @@ def test_batched_observations():
         ref = _oracle_actions(sd, obs, noise[i], i)
         err = (act[i] - ref).abs().max().item()
         assert err <= 2e-2, (i, err)
-    # predict_action_batch: the same dict observation in, [B, action_chunk, 32] out
+    # predict_action_batch: the same dict observation in; without norm statistics the
+    # output transform is the policy's slice (libero: 7 action dims)
     env = {"image": obs.images, "image_mask": obs.image_masks, "tokenized_prompt": obs.tokenized_prompt,
            "tokenized_prompt_mask": obs.tokenized_prompt_mask, "state": obs.state}
     out = eng.predict_action_batch(env)
-    assert out.shape == (3, 50, 32)
+    assert out.shape == (3, 50, 7)
     with pytest.raises(ValueError):
         eng.sample_actions(obs, noise=synthetic.make_noise(4, batch=2))

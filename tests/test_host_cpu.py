@@ -74,7 +74,8 @@ int main(void) {
   P(Pi05ExpertPlan, depth) P(Pi05ExpertPlan, eps) P(Pi05ExpertPlan, layers) P(Pi05ExpertPlan, num_steps)
   P(Pi05ExpertPlan, host_timesteps) P(Pi05ExpertPlan, mod_table) P(Pi05ExpertPlan, key_valid)
   P(Pi05ExpertPlan, x_t) P(Pi05ExpertPlan, act) P(Pi05ExpertPlan, workspace) P(Pi05ExpertPlan, workspace_bytes)
-  P(Pi05ExpertPlan, attn_splits) P(Pi05ExpertPlan, trace)
+  P(Pi05ExpertPlan, attn_splits) P(Pi05ExpertPlan, trace) P(Pi05ExpertPlan, fold) P(Pi05ExpertPlan, batch)
+  P(Pi05ExpertPlan, kv_stage)
   P(Pi05PrefixLayer, ln1_w) P(Pi05PrefixLayer, v_cache)
   P(Pi05PrefixPlan, tokens) P(Pi05PrefixPlan, eps) P(Pi05PrefixPlan, layers) P(Pi05PrefixPlan, key_valid)
   P(Pi05PrefixPlan, act) P(Pi05PrefixPlan, workspace_bytes) P(Pi05PrefixPlan, kv_only_last_layer)

@@ -114,3 +114,24 @@ def test_masks():
     assert (m[:, 2] < -1e38).all() and (m[:, [0, 1, 3, 4, 5, 6]] == 0).all()
     pm = oracle.prefix_mask(pad)
     assert pm[0, 2] < -1e38 and pm[2, 0] < -1e38 and pm[0, 3] == 0
+
+
+def test_oracle_transforms_known_answers():
+    """Image scaling and resize-with-pad geometry, and Normalize / Unnormalize as
+    inverse pairs (oracle of the preprocessing kernels)."""
+    img = torch.tensor([0, 255, 51, 204], dtype=torch.uint8).repeat(224 * 56).reshape(1, 224, 224, 1).expand(
+        1, 224, 224, 3).contiguous()
+    out = oracle.preprocess_images(img, 224)
+    assert torch.allclose(out[0, 0, 0, :4], torch.tensor([-1.0, 1.0, -0.6, 0.6]), atol=1e-6)
+    wide = torch.full((1, 480, 640, 3), 255, dtype=torch.uint8)
+    out = oracle.preprocess_images(wide, 224)
+    # 480 x 640 -> 168 x 224, centred: rows 28 .. 195 white, the border black
+    assert torch.all(out[:, :, 28:196] == 1.0) and torch.all(out[:, :, :28] == -1.0) and torch.all(out[:, :, 196:] == -1.0)
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(4, 8, generator=g)
+    a = torch.randn(8, generator=g)
+    b = a + 2.0
+    for quant in (False, True):
+        y = oracle.normalize(x, a, b, quant, 32)
+        assert y.shape == (4, 32) and torch.all(y[:, 8:] == 0)
+        assert torch.allclose(oracle.unnormalize(y, a, b, quant, 8), x, atol=1e-5)
