@@ -386,6 +386,30 @@ def run_ours(args):
                             "frac_of_measured_bf16_sustained": tf / bf16_sus}
         torch.cuda.synchronize(dev)
 
+    # Config 4 on one GPU: B independent observations denoised together (the expert
+    # GEMMs at B x 50 token rows); each observation's cache is a copy of the one
+    # filled above.
+    from pi05_infer.expert import DenoiseRunner
+
+    batched = {}
+    for bsz in (8,):
+        _, den1 = engine._runners()
+        rb = DenoiseRunner(engine.expert, prefix_len=engine.prefix_len, num_steps=engine.config.num_steps,
+                           horizon=engine.config.action_horizon, action_dim=engine.config.action_dim, batch=bsz,
+                           fold_source=den1)
+        for b in range(bsz):
+            rb.set_prefix([(k[0, : engine.prefix_len], v[0, : engine.prefix_len])
+                           for k, v in zip(den1.k_cache, den1.v_cache)], den1.key_valid[: engine.prefix_len], b)
+        bnoise = synthetic.make_noise(7, batch=bsz).to(dev)
+        rb.run(bnoise, use_graph=True)
+        loop_ms = max_over_ranks(_time_replays(lambda: rb.graph.replay(), max(5, args.steps // 4), dev, stream))
+        batched[f"b{bsz}"] = {"loop_ms": loop_ms, "us_per_step": loop_ms * 1e3 / engine.config.num_steps,
+                              "obs_per_s_denoise": ws * bsz * 1000.0 / loop_ms,
+                              "speedup_vs_b1_loop": bsz * (denoise_us * engine.config.num_steps / 1e3) / loop_ms}
+        rb.graph = None
+        del rb
+    stages["batched_denoise"] = batched
+
     # End to end through the public API: host images / ids / noise (pinned) in,
     # host actions out.
     noise_host = synthetic.make_noise(2 + rank).pin_memory()

@@ -223,8 +223,8 @@ typedef struct Pi05ExpertPlan {
   unsigned long long* trace;      /* optional device buffer for per-CTA timestamp records of the
                                      loop's GEMM and attention launches (layout of pi05_debug_set_trace),
                                      NULL = off */
-  const Pi05ExpertFold* fold;     /* host array [num_steps * depth] (step-major), or NULL.  When set
-                                     (and tokens <= 64), pi05_denoise_step runs no norm kernel inside
+  const Pi05ExpertFold* fold;     /* host array [num_steps * depth] (step-major), or NULL.  When set,
+                                     pi05_denoise_step runs no norm kernel inside
                                      the layers: q|k|v and gate/up read the residual stream h with these
                                      folded weights and scale each token by its rstd from the row
                                      statistics that action_in / o_proj / down_proj write. */

@@ -207,7 +207,7 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
   // post_attention_layernorm's input to ssq_mlp; q|k|v and gate/up read h with the
   // step's folded weights and apply rstd and the folded bias to their accumulators.
   const int n_parts = W / 128;
-  const bool fold = P->fold != nullptr && fold_norm_enabled() && T <= 64 && n_parts <= kNormMaxParts &&
+  const bool fold = P->fold != nullptr && fold_norm_enabled() && n_parts <= kNormMaxParts &&
                     (size_t)2 * n_parts * T * sizeof(float) <= kWsStatsBytes;
   float* ssq_attn = ws.stats;
   float* ssq_mlp = ws.stats + (size_t)n_parts * T;
@@ -232,6 +232,8 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.accum = ws.accum;
       sp.accum_bytes = ws.accum_bytes;
       sp.m_tok = T;
+      sp.allow_wide = 0;  // batched rows: 64-token tiles on blockIdx.y
+      sp.max_tok = 64;
       sp.k = W;
       sp.n_tiles = (HQ + HKV) * (D / 128) + HKV * D / 128;
       sp.cos = static_cast<const __nv_bfloat16*>(P->rope_cos);
@@ -307,6 +309,8 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.accum = ws.accum;
       sp.accum_bytes = ws.accum_bytes;
       sp.m_tok = T;
+      sp.allow_wide = 0;  // batched rows: 64-token tiles on blockIdx.y
+      sp.max_tok = 64;
       sp.k = HQ * D;
       sp.n_tiles = W / 128;
       sp.out = h;
@@ -336,6 +340,8 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.accum = ws.accum;
       sp.accum_bytes = ws.accum_bytes;
       sp.m_tok = T;
+      sp.allow_wide = 0;  // batched rows: 64-token tiles on blockIdx.y
+      sp.max_tok = 64;
       sp.k = W;
       sp.n_tiles = F / 64;
       sp.out = act;
@@ -366,6 +372,8 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       sp.accum = ws.accum;
       sp.accum_bytes = ws.accum_bytes;
       sp.m_tok = T;
+      sp.allow_wide = 0;  // batched rows: 64-token tiles on blockIdx.y
+      sp.max_tok = 64;
       sp.k = F;
       sp.n_tiles = W / 128;
       sp.out = h;

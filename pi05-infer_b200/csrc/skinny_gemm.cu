@@ -522,7 +522,7 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
     set_last_error("skinny_gemm: bad shape m=%d k=%d tiles=%d", p.m_tok, p.k, p.n_tiles);
     return PI05_ERR_SHAPE;
   }
-  const bool wide_ok = p.m_tok >= kWideMinTokens && !wide_disabled();
+  const bool wide_ok = p.m_tok >= kWideMinTokens && p.allow_wide != 0 && !wide_disabled();
   if (p.fold_ssq != nullptr && epi == SK_EPI_STORE) {
     // Folded LayerNorm: many-token kernel only, sums, sums of squares and column sums.
     if (!wide_ok || p.ln_sum == nullptr || p.ln_colsum == nullptr || p.fold_parts <= 0 || p.fold_d <= 0 ||
@@ -540,9 +540,10 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
       bad = bad || p.fold_bias0 != nullptr || p.fold_bias1 != nullptr ||
             (epi == SK_EPI_QKV_ROPE && p.head_dim != 256);
     else
-      bad = bad || p.m_tok > 64 || p.fold_parts > kNormMaxParts || p.fold_bias0 == nullptr || p.fold_bias1 == nullptr;
+      bad = bad || (p.m_tok > 64 && p.max_tok != 64) || p.fold_parts > kNormMaxParts || p.fold_bias0 == nullptr ||
+            p.fold_bias1 == nullptr;
     if (bad) {
-      set_last_error("skinny_gemm: folded norm needs gate/up or q|k|v; <= 64 tokens with 1..%d parts and both bias "
+      set_last_error("skinny_gemm: folded norm needs gate/up or q|k|v; 64-token tiles with 1..%d parts and both bias "
                      "vectors, or >= %d tokens without bias", kNormMaxParts, kWideMinTokens);
       return PI05_ERR_SHAPE;
     }
@@ -558,7 +559,7 @@ int skinny_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int
     if (epi != SK_EPI_QKV_ROPE || p.head_dim == 256)
       return wide_gemm_run(epi, p, w0, w1, w_rows0, w_rows1, n_cols, x, ldx, stream);
   }
-  const int tok = p.m_tok <= 64 ? 64 : (p.m_tok <= 128 ? 128 : 256);
+  const int tok = (p.m_tok <= 64 || p.max_tok == 64) ? 64 : (p.m_tok <= 128 ? 128 : 256);
   const int tok_tiles = (p.m_tok + tok - 1) / tok;
   p.kb_total = (p.k + kBK - 1) / kBK;
   int max_cl = 1;

@@ -21,6 +21,8 @@ struct SkinnyParams {
   int splits = 1;    // set by the launcher
   int cluster = 0;   // set by the launcher: 1 = the splits of a tile form a cluster and reduce through DSMEM
   int allow_cluster = 1;  // 0 = split-K only through the global accumulator
+  int allow_wide = 1;     // 0 = stay on this kernel for more than 128 tokens (token tiles on blockIdx.y)
+  int max_tok = 0;        // 64 = 64-token tiles whatever the token count (0 = 64 / 128 / 256 by count)
   int push = 0;      // set by the launcher: cluster split-K pushes partial slices to their owners (TOK 64)
   // STORE / GATED_RESID / GEGLU
   __nv_bfloat16* out = nullptr;

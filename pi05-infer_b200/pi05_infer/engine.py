@@ -279,8 +279,10 @@ class OpenPi0Inference:
     def _batched_runner(self, bsize: int) -> DenoiseRunner:
         r = self._batched.get(bsize)
         if r is None:
+            _, den1 = self._runners()
             r = DenoiseRunner(self.expert, prefix_len=self.prefix_len, num_steps=self.config.num_steps,
-                              horizon=self.config.action_horizon, action_dim=self.config.action_dim, batch=bsize)
+                              horizon=self.config.action_horizon, action_dim=self.config.action_dim, batch=bsize,
+                              fold_source=den1)
             self._batched[bsize] = r
         return r
 

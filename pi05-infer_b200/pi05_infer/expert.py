@@ -111,7 +111,8 @@ class DenoiseRunner:
     hold B caches back to back (``cache(i, b)`` is observation b's view)."""
 
     def __init__(self, weights: ExpertWeights, prefix_len: int, num_steps: int = 10, horizon: int = 50,
-                 action_dim: int = 32, attn_splits: int = 0, batch: int = 1):
+                 action_dim: int = 32, attn_splits: int = 0, batch: int = 1,
+                 fold_source: Optional["DenoiseRunner"] = None):
         self.w = weights
         s = weights.shape
         dev = weights.device
@@ -145,14 +146,18 @@ class DenoiseRunner:
         self.ts = timesteps(num_steps)
         self._host_ts = (ctypes.c_float * (num_steps + 1))(*[float(v) for v in self.ts])
         self.table = torch.empty((num_steps, weights.n_norm * 3 * s.width), **f32)
-        # Folded norms (default for <= 64 tokens, PI05_FOLD_NORM=0 to keep the norm
+        # Folded norms (default for <= 64 tokens per observation, PI05_FOLD_NORM=0 to keep the norm
         # kernels): per step and layer, q|k|v and gate/up with that step's
         # input_layernorm / post_attention_layernorm (1 + scale) folded into their
         # columns, plus the biases W . shift (pi05_fold_adarms).  The step's
         # weight stream keeps its size; the copies cost num_steps x 22 MB per layer
         # of HBM (4 GB for the 10-step Gemma-300M loop).
         self.fold = None
-        if m <= 64 and os.environ.get("PI05_FOLD_NORM", "1") != "0":
+        self._fold_owner = fold_source is None
+        if fold_source is not None:
+            # the folded copies depend on the weights and timesteps only: share them
+            self.fold = fold_source.fold
+        elif horizon <= 64 and os.environ.get("PI05_FOLD_NORM", "1") != "0":
             n = num_steps * s.depth
             self.fold = {
                 "w_qkv": torch.empty((n, s.qkv_dim, s.width), **bf),
@@ -202,8 +207,9 @@ class DenoiseRunner:
 
     def build_fold(self) -> None:
         """Fold every step's layer norms into the q|k|v and gate/up copies, in place
-        (after the table; a captured graph keeps its addresses)."""
-        if self.fold is None:
+        (after the table; a captured graph keeps its addresses).  A runner that shares
+        another's copies leaves them to their owner."""
+        if self.fold is None or not self._fold_owner:
             return
         s = self.w.shape
         W = s.width
