@@ -235,6 +235,12 @@ typedef struct Pi05ExpertPlan {
                                      B caches [hkv, kv_rows, d] back to back and key_valid B masks of
                                      kv_rows; kv_stage is needed. */
   void* kv_stage;                 /* batch > 1: [2][B * tokens][d] bf16 staging of the new K / V rows */
+  const float* host_step_coefs;   /* host [num_steps][3] or NULL (flow_ode): the sampler's update
+                                     x <- (x - v t) * c0 + (x + v (1 - t)) * c1 + c2 * noise, as
+                                     sample_mean_var_val computes mean and std for flow_sde / flow_cps
+                                     (_extract_src/openpi_action_model.py:984-1006) */
+  const float* step_noise;        /* [num_steps][B * tokens][action_dim] fp32 N(0, 1), read where
+                                     c2 != 0 */
 } Pi05ExpertPlan;
 
 /* Folds an adaRMS norm into the projection that consumes its output, for the

@@ -272,6 +272,31 @@ def euler(x_t: Tensor, v_t: Tensor, t: float, delta: float) -> Tensor:
     return x0 * (1 - (t - delta)) + x1 * (t - delta)
 
 
+def sampler_step(x_t: Tensor, v_t: Tensor, idx: int, num_steps: int, method: str, noise_level: float,
+                 step_noise: Optional[Tensor]) -> Tensor:
+    """``x_t_mean + noise * x_t_std`` of ``sample_mean_var_val`` for flow_sde / flow_cps
+    (``_extract_src/openpi_action_model.py:984-1006``), fp32."""
+    ts = timesteps(num_steps)
+    t = ts[idx]
+    delta = ts[idx] - ts[idx + 1]
+    nl = torch.tensor(noise_level, dtype=torch.float32)
+    x0 = x_t - v_t * t
+    x1 = x_t + v_t * (1 - t)
+    if method == "flow_sde":
+        denom = torch.where(ts == 1, ts[1], ts)
+        sigma = (nl * torch.sqrt(ts / (1 - denom))[:-1])[idx]
+        w0 = 1 - (t - delta)
+        w1 = t - delta - sigma ** 2 * delta / (2 * t)
+        std = torch.sqrt(delta) * sigma
+    elif method == "flow_cps":
+        w0 = 1 - (t - delta)
+        w1 = (t - delta) * torch.cos(torch.pi * nl / 2)
+        std = (t - delta) * torch.sin(torch.pi * nl / 2)
+    else:
+        raise ValueError(method)
+    return x0 * w0 + x1 * w1 + step_noise * std
+
+
 def denoise_loop(
     w: Dict[str, Tensor],
     noise: Tensor,
@@ -283,8 +308,12 @@ def denoise_loop(
     table: Optional[Tensor] = None,
     prefix: str = "paligemma_with_expert.gemma_expert.model.",
     velocities: Optional[list] = None,
+    method: str = "flow_ode",
+    noise_level: float = 0.0,
+    step_noise: Optional[Tensor] = None,
 ) -> Tensor:
-    """The ``num_steps`` Euler loop of ``sample_actions`` (``engine.py:390-405``)."""
+    """The ``num_steps`` Euler loop of ``sample_actions`` (``engine.py:390-405``); a
+    stochastic ``method`` adds ``step_noise[s]`` per step (``sampler_step``)."""
     if table is None:
         table = adarms_table(w, depth, num_steps, prefix)
     ts = timesteps(num_steps)
@@ -293,7 +322,10 @@ def denoise_loop(
         v = velocity(w, x, kv_prefix, table[s], prefix_pad, depth, policy)
         if velocities is not None:
             velocities.append(v.clone())
-        x = euler(x, v, float(ts[s]), float(ts[s] - ts[s + 1]))
+        if method == "flow_ode":
+            x = euler(x, v, float(ts[s]), float(ts[s] - ts[s + 1]))
+        else:
+            x = sampler_step(x, v, s, num_steps, method, noise_level, step_noise[s])
     return x
 
 

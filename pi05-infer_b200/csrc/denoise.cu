@@ -393,8 +393,10 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
   if (rc) return rc;
   const float t = P->host_timesteps[step];
   const float delta = P->host_timesteps[step] - P->host_timesteps[step + 1];
+  const float* coefs = P->host_step_coefs != nullptr ? P->host_step_coefs + 3 * step : nullptr;
+  const float* noise = P->step_noise != nullptr ? P->step_noise + (size_t)step * T * P->action_dim : nullptr;
   return final_euler_run(h, mods + (size_t)(2 * P->depth) * 3 * W, P->w_out, P->b_out, P->x_t, P->v_t, T, W,
-                         P->action_dim, P->eps, t, delta, stream);
+                         P->action_dim, P->eps, t, delta, stream, coefs, noise);
 }
 
 int pi05_denoise_loop(const Pi05ExpertPlan* plan, void* stream) {

@@ -153,7 +153,8 @@ __global__ void __launch_bounds__(256) final_euler_kernel(const __nv_bfloat16* _
                                                           const float* __restrict__ w,
                                                           const float* __restrict__ b, float* __restrict__ x_t,
                                                           float* __restrict__ v_out, int d, int dout, float eps,
-                                                          float t, float delta) {
+                                                          float t, float wa, float wb, float sd,
+                                                          const float* __restrict__ noise) {
   extern __shared__ float hn[];  // [d]
   __shared__ float red[32];
   __shared__ float vs[64];
@@ -187,7 +188,9 @@ __global__ void __launch_bounds__(256) final_euler_kernel(const __nv_bfloat16* _
     const float x = x_t[(size_t)row * dout + j];
     const float x0 = x - v * t;
     const float x1 = x + v * (1.0f - t);
-    x_t[(size_t)row * dout + j] = x0 * (1.0f - (t - delta)) + x1 * (t - delta);
+    float xn = x0 * wa + x1 * wb;
+    if (noise != nullptr) xn += noise[(size_t)row * dout + j] * sd;  // stochastic samplers
+    x_t[(size_t)row * dout + j] = xn;
     if (v_out != nullptr) v_out[(size_t)row * dout + j] = v;
   }
 }
@@ -387,14 +390,23 @@ int fold_adarms_run(const void* w, int rows, int k, const float* scale, const fl
 }
 
 int final_euler_run(const void* h, const float* mod, const float* w, const float* b, float* x_t, float* v_out,
-                    int rows, int d, int dout, float eps, float t, float delta, void* stream) {
+                    int rows, int d, int dout, float eps, float t, float delta, void* stream, const float* coefs,
+                    const float* noise) {
   if (dout > 64) {
     set_last_error("final_euler: action dim > 64 unsupported");
     return PI05_ERR_SHAPE;
   }
+  // flow_ode unless the sampler's weights are given: x0 * (1 - (t - delta)) + x1 * (t - delta)
+  const float wa = coefs != nullptr ? coefs[0] : 1.0f - (t - delta);
+  const float wb = coefs != nullptr ? coefs[1] : t - delta;
+  const float sd = coefs != nullptr ? coefs[2] : 0.0f;
+  if (sd != 0.0f && noise == nullptr) {
+    set_last_error("final_euler: a stochastic sampler step needs its noise");
+    return PI05_ERR_INVALID_ARG;
+  }
   return launch_pdl(final_euler_kernel, dim3(rows), dim3(256), d * sizeof(float),
                     reinterpret_cast<cudaStream_t>(stream), pdl_enabled(), static_cast<const __nv_bfloat16*>(h), mod,
-                    w, b, x_t, v_out, d, dout, eps, t, delta);
+                    w, b, x_t, v_out, d, dout, eps, t, wa, wb, sd, sd != 0.0f ? noise : nullptr);
 }
 
 int rope_table_run(const uint8_t* valid, int n_prefix, int mode, int rows, const float* inv_freq, int d, void* cos,

@@ -16,8 +16,11 @@ int row_ssq_run(const void* x, int ldx, int rows, int d, int part_cols, float* s
 // w_out = bf16(w * (1 + scale)) column-wise, b_out = w . shift (fp32); w [rows, k], k % 8 == 0.
 int fold_adarms_run(const void* w, int rows, int k, const float* scale, const float* shift, void* w_out,
                     float* b_out, void* stream);
+// Final adaRMS + action_out_proj + the sampler update of x_t.  coefs (host, or null =
+// flow_ode): {x0 weight, x1 weight, std}; noise [rows, dout] is added times std.
 int final_euler_run(const void* h, const float* mod, const float* w, const float* b, float* x_t, float* v_out,
-                    int rows, int d, int dout, float eps, float t, float delta, void* stream);
+                    int rows, int d, int dout, float eps, float t, float delta, void* stream,
+                    const float* coefs = nullptr, const float* noise = nullptr);
 int rope_table_run(const uint8_t* valid, int n_prefix, int mode, int rows, const float* inv_freq, int d, void* cos,
                    void* sin, void* stream);
 int sinusoid_run(const float* ts, int n_t, int dim, double min_p, double max_p, float* out, void* stream);

@@ -39,7 +39,7 @@ class Pi05ExpertPlan(ctypes.Structure):
         ("x_t", _P), ("v_t", _P), ("h", _P), ("xn", _P), ("q", _P), ("attn", _P), ("act", _P),
         ("workspace", _P), ("workspace_bytes", _Z), ("attn_splits", _I), ("trace", _P),
         ("fold", ctypes.POINTER(Pi05ExpertFold)),
-        ("batch", _I), ("kv_stage", _P),
+        ("batch", _I), ("kv_stage", _P), ("host_step_coefs", ctypes.POINTER(_F)), ("step_noise", _P),
     ]
 
 

@@ -71,6 +71,8 @@ class EngineConfig:
     action_horizon: int = ACTION_HORIZON
     action_dim: int = ACTION_DIM
     action_chunk: int = ACTION_HORIZON
+    # Sampler of the Euler loop: "flow_ode" (deterministic, the reference engine's) or
+    # the stochastic "flow_sde" / "flow_cps" with this noise level.
     noise_level: float = 0.0
     noise_method: str = "flow_ode"
     expert: GemmaShape = GEMMA_300M

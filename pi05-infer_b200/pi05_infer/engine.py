@@ -162,7 +162,9 @@ class OpenPi0Inference:
     def _runners(self):
         if self._denoise is None:
             self._denoise = DenoiseRunner(self.expert, prefix_len=self.prefix_len, num_steps=self.config.num_steps,
-                                          horizon=self.config.action_horizon, action_dim=self.config.action_dim)
+                                          horizon=self.config.action_horizon, action_dim=self.config.action_dim,
+                                          noise_method=self.config.noise_method,
+                                          noise_level=self.config.noise_level)
         if self._prefix is None and self.prefix_w is not None:
             self._prefix = PrefixRunner(self.prefix_w, self.prefix_len, self._denoise.k_cache, self._denoise.v_cache)
         return self._prefix, self._denoise
@@ -282,7 +284,8 @@ class OpenPi0Inference:
             _, den1 = self._runners()
             r = DenoiseRunner(self.expert, prefix_len=self.prefix_len, num_steps=self.config.num_steps,
                               horizon=self.config.action_horizon, action_dim=self.config.action_dim, batch=bsize,
-                              fold_source=den1)
+                              fold_source=den1, noise_method=self.config.noise_method,
+                              noise_level=self.config.noise_level)
             self._batched[bsize] = r
         return r
 
@@ -345,6 +348,7 @@ class OpenPi0Inference:
         stream = torch.cuda.current_stream(self.device)
         inputs_read = torch.cuda.Event()
         inputs_read.record(stream)
+        den.draw_step_noise()
         if self.use_cuda_graph:
             g = self._graphs.get(("batch", bsize))
             if g is None:
@@ -400,6 +404,7 @@ class OpenPi0Inference:
             if self._inputs_read is None:
                 self._inputs_read = torch.cuda.Event()
             self._inputs_read.record(stream)
+            den.draw_step_noise()  # stochastic samplers: fresh per-step noise
             self._graphs["full"].replay()
             actions = den.x_t.clone()
             # The caller's buffers were copied by the work before the replay; wait for

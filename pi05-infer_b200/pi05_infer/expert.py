@@ -41,6 +41,38 @@ def timesteps(num_steps: int) -> torch.Tensor:
     return torch.cat([ts, torch.zeros(1)])
 
 
+SAMPLERS = ("flow_ode", "flow_sde", "flow_cps")
+
+
+def sampler_coefs(num_steps: int, method: str, noise_level: float) -> torch.Tensor:
+    """Per-step sampler update ``x <- x0 * c0 + x1 * c1 + c2 * noise`` with
+    ``x0 = x - v t``, ``x1 = x + v (1 - t)``: fp32 ``[num_steps, 3]``, computed as
+    ``sample_mean_var_val`` computes the mean weights and the std
+    (``_extract_src/openpi_action_model.py:984-1006``; the inference engine keeps only
+    flow_ode, ``engine.py:629-676``)."""
+    if method not in SAMPLERS:
+        raise ValueError(f"noise_method {method!r} not supported ({SAMPLERS})")
+    ts = timesteps(num_steps)
+    t = ts[:-1]
+    delta = ts[:-1] - ts[1:]
+    nl = torch.tensor(noise_level, dtype=torch.float32)
+    if method == "flow_ode":
+        c0, c1, sd = 1 - (t - delta), t - delta, torch.zeros_like(t)
+    elif method == "flow_sde":
+        denom = torch.where(ts == 1, ts[1], ts)
+        sigmas = nl * torch.sqrt(ts / (1 - denom))[:-1]
+        c0 = torch.ones_like(t) - (t - delta)
+        c1 = t - delta - sigmas ** 2 * delta / (2 * t)
+        sd = torch.sqrt(delta) * sigmas
+    else:  # flow_cps
+        cos_term = torch.cos(torch.pi * nl / 2)
+        sin_term = torch.sin(torch.pi * nl / 2)
+        c0 = torch.ones_like(t) - (t - delta)
+        c1 = (t - delta) * cos_term
+        sd = (t - delta) * sin_term
+    return torch.stack([c0, c1, sd], 1).to(torch.float32).contiguous()
+
+
 class ExpertWeights:
     """Device copies of the action expert and its glue, packed for the kernels."""
 
@@ -112,7 +144,8 @@ class DenoiseRunner:
 
     def __init__(self, weights: ExpertWeights, prefix_len: int, num_steps: int = 10, horizon: int = 50,
                  action_dim: int = 32, attn_splits: int = 0, batch: int = 1,
-                 fold_source: Optional["DenoiseRunner"] = None):
+                 fold_source: Optional["DenoiseRunner"] = None, noise_method: str = "flow_ode",
+                 noise_level: float = 0.0):
         self.w = weights
         s = weights.shape
         dev = weights.device
@@ -142,6 +175,12 @@ class DenoiseRunner:
         self.x_t = torch.zeros((m, action_dim), **f32)
         self.v_t = torch.zeros((m, action_dim), **f32)
         self.kv_stage = torch.zeros((2, m, s.head_dim), **bf) if batch > 1 else None
+        # Sampler: flow_ode (the reference engine's) or a stochastic one, whose per-step
+        # N(0, 1) noise lives in step_noise (redrawn by draw_step_noise before a call).
+        self.noise_method = noise_method
+        self.coefs = sampler_coefs(num_steps, noise_method, noise_level)
+        self.stochastic = noise_method != "flow_ode"
+        self.step_noise = torch.zeros((num_steps, m, action_dim), **f32) if self.stochastic else None
         self.ws = ops.workspace(dev)
         self.ts = timesteps(num_steps)
         self._host_ts = (ctypes.c_float * (num_steps + 1))(*[float(v) for v in self.ts])
@@ -186,7 +225,11 @@ class DenoiseRunner:
             v_t=self.v_t.data_ptr(), h=self.h.data_ptr(), xn=self.xn.data_ptr(), q=self.q.data_ptr(),
             attn=self.attn.data_ptr(), act=self.act.data_ptr(), workspace=self.ws.data_ptr(),
             workspace_bytes=self.ws.numel(), attn_splits=attn_splits, batch=batch,
-            kv_stage=self.kv_stage.data_ptr() if self.kv_stage is not None else None)
+            kv_stage=self.kv_stage.data_ptr() if self.kv_stage is not None else None,
+            step_noise=self.step_noise.data_ptr() if self.step_noise is not None else None)
+        if self.stochastic:
+            self._host_coefs = (ctypes.c_float * self.coefs.numel())(*[float(v) for v in self.coefs.flatten()])
+            self.plan.host_step_coefs = ctypes.cast(self._host_coefs, ctypes.POINTER(ctypes.c_float))
         if self.fold is not None:
             fd = self.fold
             self._fold = (abi.Pi05ExpertFold * (num_steps * s.depth))()
@@ -252,10 +295,23 @@ class DenoiseRunner:
                            self.rope_cos[b * hz: (b + 1) * hz], self.rope_sin[b * hz: (b + 1) * hz], stream)
         abi.denoise_loop(self.plan, stream)
 
-    def run(self, noise: torch.Tensor, use_graph: bool = True) -> torch.Tensor:
+    def draw_step_noise(self, generator: Optional[torch.Generator] = None) -> None:
+        """Fresh N(0, 1) noise for every step of a stochastic sampler (the reference
+        draws ``sample_noise(x_t.shape)`` once per step, ``engine.py:395-402``)."""
+        if self.step_noise is not None:
+            self.step_noise.normal_(generator=generator)
+
+    def run(self, noise: torch.Tensor, use_graph: bool = True,
+            step_noise: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Run the loop from ``noise`` [batch * 50, 32] (any leading shape); returns the
-        actions (a view of the static buffer, [batch * 50, 32])."""
+        actions (a view of the static buffer, [batch * 50, 32]).  A stochastic sampler
+        uses ``step_noise`` [num_steps, batch * 50, 32] when given, else fresh noise."""
         self.x_t.copy_(noise.reshape(self.rows, self.action_dim))
+        if self.step_noise is not None:
+            if step_noise is not None:
+                self.step_noise.copy_(step_noise.reshape(self.step_noise.shape))
+            else:
+                self.draw_step_noise()
         if use_graph:
             if self.graph is None:
                 self.capture()

@@ -59,3 +59,33 @@ def test_batched_denoise_parity(batch, depth, p, steps):
     # a second replay of the captured graph is bit-identical
     again = r.run(noise.cuda(), use_graph=True).clone().cpu().reshape(batch, 50, 32)
     assert torch.equal(again, got)
+
+
+@pytest.mark.parametrize("method", ["flow_sde", "flow_cps"])
+def test_stochastic_samplers(method):
+    """flow_sde / flow_cps (``_extract_src/openpi_action_model.py:984-1006``) with a
+    given per-step noise, single and batched, against the oracle."""
+    depth, p, steps, batch = 2, 64, 3, 2
+    shape = GemmaShape(width=1024, depth=depth, mlp_dim=4096, num_heads=8, num_kv_heads=1, head_dim=256)
+    sd = synthetic.make_expert_weights(0, shape)
+    w = ExpertWeights(sd, shape, "cuda")
+    kv = [(k[0, 0].bfloat16().float(), v[0, 0].bfloat16().float()) for k, v in synthetic.make_prefix_kv(1, depth, p)]
+    pad = torch.ones(p, dtype=torch.bool)
+    g = torch.Generator().manual_seed(9)
+    noise = synthetic.make_noise(2, batch=batch)
+    step_noise = torch.randn(steps, batch * 50, 32, generator=g)
+    r = DenoiseRunner(w, prefix_len=p, num_steps=steps, batch=batch, noise_method=method, noise_level=0.5)
+    for b in range(batch):
+        r.set_prefix([(k.cuda(), v.cuda()) for k, v in kv], pad.cuda(), b)
+    got = r.run(noise.cuda(), use_graph=True, step_noise=step_noise.cuda()).clone().cpu().reshape(batch, 50, 32)
+    assert ops.read_device_status() == 0
+    sn = step_noise.reshape(steps, batch, 50, 32)
+    for b in range(batch):
+        ref = oracle.denoise_loop(sd, noise[b], kv, pad, depth, steps, "bf16", method=method, noise_level=0.5,
+                                  step_noise=sn[:, b])
+        err = (got[b] - ref).abs().max().item()
+        assert err <= 2e-2, (b, err)
+    # without given noise every call draws fresh noise: two calls differ
+    a1 = r.run(noise.cuda(), use_graph=True).clone()
+    a2 = r.run(noise.cuda(), use_graph=True).clone()
+    assert (a1 - a2).abs().max().item() > 1e-3

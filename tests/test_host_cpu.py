@@ -75,7 +75,7 @@ int main(void) {
   P(Pi05ExpertPlan, host_timesteps) P(Pi05ExpertPlan, mod_table) P(Pi05ExpertPlan, key_valid)
   P(Pi05ExpertPlan, x_t) P(Pi05ExpertPlan, act) P(Pi05ExpertPlan, workspace) P(Pi05ExpertPlan, workspace_bytes)
   P(Pi05ExpertPlan, attn_splits) P(Pi05ExpertPlan, trace) P(Pi05ExpertPlan, fold) P(Pi05ExpertPlan, batch)
-  P(Pi05ExpertPlan, kv_stage)
+  P(Pi05ExpertPlan, kv_stage) P(Pi05ExpertPlan, host_step_coefs) P(Pi05ExpertPlan, step_noise)
   P(Pi05PrefixLayer, ln1_w) P(Pi05PrefixLayer, v_cache)
   P(Pi05PrefixPlan, tokens) P(Pi05PrefixPlan, eps) P(Pi05PrefixPlan, layers) P(Pi05PrefixPlan, key_valid)
   P(Pi05PrefixPlan, act) P(Pi05PrefixPlan, workspace_bytes) P(Pi05PrefixPlan, kv_only_last_layer)
@@ -198,3 +198,27 @@ def test_replica_failure_detected_gloo():
     assert res[1][0] == "RuntimeError"  # the failing replica saw its own error
     assert res[0][0] != "completed"  # the survivor did not return a partial result
     assert res[0][1] < 60.0  # and learned of the failure within the bound
+
+
+def test_sampler_coefficients_match_oracle():
+    """The host-side per-step sampler weights (what the final Euler kernel applies)
+    reproduce the oracle's flow_sde / flow_cps step and the flow_ode Euler update."""
+    from conftest import load_oracle
+    from pi05_infer.expert import sampler_coefs
+
+    oracle = load_oracle()
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(50, 32, generator=g)
+    v = torch.randn(50, 32, generator=g)
+    n = torch.randn(50, 32, generator=g)
+    ts = oracle.timesteps(10)
+    for method in ("flow_ode", "flow_sde", "flow_cps"):
+        c = sampler_coefs(10, method, 0.5)
+        for s in range(10):
+            t = float(ts[s])
+            got = (x - v * t) * c[s, 0] + (x + v * (1 - t)) * c[s, 1] + n * c[s, 2]
+            if method == "flow_ode":
+                ref = oracle.euler(x, v, t, float(ts[s] - ts[s + 1]))
+            else:
+                ref = oracle.sampler_step(x, v, s, 10, method, 0.5, n)
+            assert torch.allclose(got, ref, atol=1e-5), (method, s)
