@@ -320,7 +320,7 @@ def run_ours(args):
         pg = dist
 
     from pi05_infer import _lib, synthetic
-    from pi05_infer.engine import OpenPi0Inference
+    from pi05_infer.engine import Observation, OpenPi0Inference
 
     hbm_peak, bf16_peak, bf16_sus, peak_src = _peaks()
     views, p = _workload_shape(args.workload)
@@ -409,6 +409,27 @@ def run_ours(args):
         rb.graph = None
         del rb
     stages["batched_denoise"] = batched
+    if e2e_work:
+        # The same batch end to end through the public API: 8 observations in one
+        # sample_actions call (SigLIP over all 24 views in one pass, 8 prefix LMs,
+        # one batched denoise loop), host inputs in, host actions out.
+        bsz = 8
+        g = torch.Generator().manual_seed(300 + rank)
+        bimgs = {f"cam{i}": (torch.rand((bsz, 3, 224, 224), generator=g) * 2 - 1).pin_memory() for i in range(views)}
+        bobs = Observation(bimgs, {k: torch.ones(bsz, dtype=torch.bool) for k in bimgs},
+                           torch.randint(0, synthetic.VOCAB_SIZE, (bsz, 200), generator=g),
+                           torch.ones(bsz, 200, dtype=torch.bool), torch.zeros(bsz, 32))
+        bnoise_h = synthetic.make_noise(8, batch=bsz).pin_memory()
+        for _ in range(2):
+            engine.sample_actions(bobs, noise=bnoise_h)["actions"].cpu()
+        torch.cuda.synchronize(dev)
+        nb = max(3, args.steps // 10)
+        t0 = time.perf_counter()
+        for _ in range(nb):
+            engine.sample_actions(bobs, noise=bnoise_h)["actions"].cpu()
+        bms = max_over_ranks((time.perf_counter() - t0) * 1e3 / nb)
+        stages["batched_e2e"] = {"batch": bsz, "ms_per_call": bms, "obs_per_s": ws * bsz * 1000.0 / bms,
+                                 "speedup_vs_bs1_e2e": bsz * ms / bms}
 
     # End to end through the public API: host images / ids / noise (pinned) in,
     # host actions out.

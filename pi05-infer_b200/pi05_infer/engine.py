@@ -89,6 +89,7 @@ class OpenPi0Inference:
         self.norm_stats: Optional[Dict[str, NormStats]] = None
         self._batched: Dict[int, DenoiseRunner] = {}  # batch size -> batched denoise runner
         self._bstatic: Dict[int, Dict[str, torch.Tensor]] = {}  # batch size -> static inputs
+        self._bsiglip: Dict[int, Any] = {}  # batch size -> SiglipRunner over all its views
         if state_dict is not None:
             self.load_state_dict(state_dict)
 
@@ -299,17 +300,19 @@ class OpenPi0Inference:
         return torch.cat(parts, 1).to(torch.uint8)
 
     def _enqueue_batched(self, den: DenoiseRunner, bsize: int, stream: int) -> None:
-        """SigLIP, embeddings and the prefix LM of each observation into its own cache
-        (the prefix runner re-targeted at observation b's cache views), then one
-        batched Euler loop over all of them."""
+        """SigLIP over every view of the batch in one pass, then the embeddings and the
+        prefix LM of each observation into its own cache (the prefix runner
+        re-targeted at observation b's cache views), then one batched Euler loop over
+        all of them."""
         prefix, den1 = self._runners()
         npatch = self.config.siglip.num_patches
         nv = self.num_views
         st = self._bstatic[bsize]
         base = nv * npatch
         depth = self.config.expert.depth
+        self._bsiglip[bsize].enqueue(st["imgs"], st["feats"], stream)
         for b in range(bsize):
-            self._siglip.enqueue(st["imgs"][b * nv: (b + 1) * nv], prefix.h, stream)
+            prefix.h[:base].copy_(st["feats"][b * base: (b + 1) * base])
             embed_tokens(self.embed_table, st["ids"][b], prefix.h[base: base + self.prompt_len],
                          math.sqrt(self.embed_table.shape[1]), ops.workspace(self.device), stream)
             caches = [den.cache(i, b) for i in range(depth)]
@@ -326,17 +329,19 @@ class OpenPi0Inference:
         bsize = noise.shape[0]
         self._runners()
         den = self._batched_runner(bsize)
-        if not hasattr(self, "_siglip"):
-            self._siglip = SiglipRunner(self.vision, self.num_views)
         names = list(observation.images.keys())
         if len(names) != self.num_views:
             raise ValueError(f"expected {self.num_views} camera views, got {len(names)}")
         st = self._bstatic.get(bsize)
         if st is None:
-            size = self.config.siglip.image_size
-            st = {"imgs": torch.zeros((bsize * self.num_views, 3, size, size), dtype=torch.float32,
-                                      device=self.device),
-                  "ids": torch.zeros((bsize, self.prompt_len), dtype=torch.int32, device=self.device)}
+            nrows = bsize * self.num_views * self.config.siglip.num_patches
+            # the tower over all bsize x views images at once (its GEMMs then fill the
+            # GPU); the batch's images are written straight into its input buffer
+            self._bsiglip[bsize] = SiglipRunner(self.vision, bsize * self.num_views)
+            st = {"imgs": self._bsiglip[bsize].images,
+                  "ids": torch.zeros((bsize, self.prompt_len), dtype=torch.int32, device=self.device),
+                  "feats": torch.zeros((nrows, self.config.prefix_lm.width), dtype=torch.bfloat16,
+                                       device=self.device)}
             self._bstatic[bsize] = st
         imgs = st["imgs"].view(bsize, self.num_views, *st["imgs"].shape[1:])
         for i, n in enumerate(names):
