@@ -148,6 +148,7 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 ? 2 : 1))
   const uint32_t tmem_acc = *s_tmem;
   const uint64_t t_start = (p.trace != nullptr) ? globaltimer_ns() : 0;
   uint64_t t_pdl = 0, t_acc = 0, t_pub = 0, t_red = 0;
+  uint64_t t_staged = 0, t_bar = 0;  // accumulator staged in shared memory; epilogue barrier passed
   // Let the next kernel in the stream start its prologue / weight prefetch.
   pdl_launch_dependents();
 
@@ -257,8 +258,10 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 ? 2 : 1))
         for (int j = 0; j < 32; ++j) stage_tile[(c * 32 + j) * kBM + row] = v[j];
       }
     }
+    if (p.trace != nullptr) t_staged = globaltimer_ns();
     if (push) fence_proxy_async_smem();  // the bulk copies read the staging tile
     named_bar_sync(1, kEpiThreads);
+    if (p.trace != nullptr) t_bar = globaltimer_ns();
     const int items = epi_items<EPI>(p, tile, mt);
     if (ok && p.splits == 1) {
       TileSrc src{stage_tile, nullptr, 1, TOK * kBM};
@@ -354,12 +357,13 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 ? 2 : 1))
     if (p.cluster && slot + 1 < cap) {
       // Cluster epilogue record (tag + 2^30): before / after the first cluster
       // barrier (push form: epilogue start / copies issued), first DSMEM pass
-      // summed (push form: slices received), last store issued, exit barrier passed.
+      // summed (push form: slices received), last store issued, exit barrier passed,
+      // then the accumulator staged in shared memory and the epilogue barrier passed.
       unsigned long long* w = p.trace + 8 + (slot + 1) * 8;
       w[0] = ((unsigned long long)(p.trace_tag + (1 << 30)) << 32) | cta;
       for (int i = 0; i < 5; ++i) w[1 + i] = cl_stamps[i];
-      w[6] = 0;
-      w[7] = 0;
+      w[6] = t_staged;
+      w[7] = t_bar;
     }
   }
 
