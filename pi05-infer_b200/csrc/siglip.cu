@@ -261,6 +261,30 @@ __global__ void __launch_bounds__(128) mha72_kernel(const __nv_bfloat16* __restr
 
 inline bool nz(const void* p) { return p != nullptr; }
 
+int siglip_attention_run(const void* qkv, int views, int seq, int width, int heads, int head_dim, void* out,
+                         void* stream) {
+  if (!nz(qkv) || !nz(out)) {
+    set_last_error("siglip_attention: null pointer");
+    return PI05_ERR_INVALID_ARG;
+  }
+  if (head_dim != kHd || seq != 256 || heads * head_dim != width || views <= 0 || !aligned16(qkv) ||
+      !aligned16(out)) {
+    set_last_error("siglip_attention: supports head_dim 72, 256 tokens per view, 16-byte aligned buffers");
+    return PI05_ERR_SHAPE;
+  }
+  const size_t smem = (size_t)(64 + 2 * 256) * kRowB;
+  static bool attr_done[16] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 16 && !attr_done[dev]) {
+    cudaFuncSetAttribute(mha72_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr_done[dev] = true;
+  }
+  return launch_pdl(mha72_kernel<256>, dim3(views * heads, seq / 64), dim3(128), smem,
+                    reinterpret_cast<cudaStream_t>(stream), pdl_enabled(), static_cast<const __nv_bfloat16*>(qkv),
+                    width, heads, 1.0f / std::sqrt((float)head_dim), static_cast<__nv_bfloat16*>(out));
+}
+
 // PI05_FOLD_NORM=0 in the environment keeps the LayerNorm kernels.
 bool siglip_fold_enabled() {
   static int v = [] {
@@ -301,25 +325,7 @@ int pi05_layer_norm(const void* x, const float* w, const float* b, void* out, in
 
 int pi05_siglip_attention(const void* qkv, int views, int seq, int width, int heads, int head_dim, void* out,
                           void* stream) {
-  if (!nz(qkv) || !nz(out)) {
-    set_last_error("siglip_attention: null pointer");
-    return PI05_ERR_INVALID_ARG;
-  }
-  if (head_dim != kHd || seq != 256 || heads * head_dim != width || views <= 0) {
-    set_last_error("siglip_attention: supports head_dim 72, 256 tokens per view");
-    return PI05_ERR_SHAPE;
-  }
-  const size_t smem = (size_t)(64 + 2 * 256) * kRowB;
-  static bool attr_done[16] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 16 && !attr_done[dev]) {
-    cudaFuncSetAttribute(mha72_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr_done[dev] = true;
-  }
-  return launch_pdl(mha72_kernel<256>, dim3(views * heads, seq / 64), dim3(128), smem,
-                    reinterpret_cast<cudaStream_t>(stream), pdl_enabled(), static_cast<const __nv_bfloat16*>(qkv),
-                    width, heads, 1.0f / std::sqrt((float)head_dim), static_cast<__nv_bfloat16*>(out));
+  return siglip_attention_run(qkv, views, seq, width, heads, head_dim, out, stream);
 }
 
 int pi05_siglip_forward(const Pi05SiglipPlan* P, void* stream) {
@@ -411,7 +417,7 @@ int pi05_siglip_forward(const Pi05SiglipPlan* P, void* stream) {
       rc = skinny_gemm_run(SK_EPI_STORE, sp, wq, wq, 3 * W, 3 * W, fold ? h : xn, W, 0, stream);
       if (rc) return rc;
     }
-    rc = pi05_siglip_attention(qkv, V, S, W, P->n_heads, P->head_dim, attn, stream);
+    rc = siglip_attention_run(qkv, V, S, W, P->n_heads, P->head_dim, attn, stream);
     if (rc) return rc;
     {
       SkinnyParams sp = base_params(ws);
