@@ -139,13 +139,14 @@ int pi05_attention(const void* q, const void* k, const void* v, const uint8_t* k
                    void* stream);
 
 /* h[rows, dout] = bf16(x @ w^T + b), fp32 math.  Replaces action_in_proj
- * (pi05_infer/openpi_patched/pi0_pytorch.py:303-323). */
+ * (pi05_infer/openpi_patched/pi0_pytorch.py:303-323).  din <= 64. */
 int pi05_action_in(const float* x, const float* w, const float* b, void* h, int rows, int din, int dout,
                    void* stream);
 
 /* Final adaRMSNorm -> fp32 -> action_out_proj -> flow_ode Euler update of x_t in
  * place (modeling_gemma.py:782-783; engine.py:664-675, 754-767).  v_out (may be
- * NULL) receives the velocity.  dout <= 64. */
+ * NULL) receives the velocity.  d a multiple of 256 up to 2048, h / w / mod
+ * 16-byte aligned, dout <= 64. */
 int pi05_final_euler(const void* h, const float* mod, const float* w, const float* b, float* x_t, float* v_out,
                      int rows, int d, int dout, float eps, float t, float delta, void* stream);
 

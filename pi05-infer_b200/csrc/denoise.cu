@@ -202,7 +202,7 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
   auto* stage_v = stage_k == nullptr ? nullptr : stage_k + (size_t)T * D;
   const float scale = 1.0f / std::sqrt((float)D);
   // Folded norms (default when the plan carries folded weights): no norm kernel
-  // inside the layers.  action_in (layer 0, one part) and down_proj write the row
+  // inside the layers.  action_in (layer 0) and down_proj write the row
   // statistics of input_layernorm's input to ssq_attn, o_proj those of
   // post_attention_layernorm's input to ssq_mlp; q|k|v and gate/up read h with the
   // step's folded weights and apply rstd and the folded bias to their accumulators.
@@ -213,7 +213,7 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
   float* ssq_mlp = ws.stats + (size_t)n_parts * T;
   const Pi05ExpertFold* FS = fold ? P->fold + (size_t)step * P->depth : nullptr;
 
-  int rc = action_in_run(P->x_t, P->w_in, P->b_in, h, T, P->action_dim, W, stream, fold ? ssq_attn : nullptr);
+  int rc = action_in_run(P->x_t, P->w_in, P->b_in, h, T, P->action_dim, W, stream, fold ? ssq_attn : nullptr, T);
   for (int l = 0; l < P->depth && rc == PI05_OK; ++l) {
     const Pi05ExpertLayer& L = P->layers[l];
     const float* mod1 = mods + (size_t)(2 * l) * 3 * W;
@@ -259,7 +259,7 @@ int pi05_denoise_step(const Pi05ExpertPlan* P, int step, void* stream) {
       if (fold) {
         wq = FS[l].w_qkv;
         sp.fold_ssq = ssq_attn;
-        sp.fold_parts = l == 0 ? 1 : n_parts;
+        sp.fold_parts = n_parts;
         sp.fold_ld = T;
         sp.fold_d = W;
         sp.fold_eps = P->eps;

@@ -12,6 +12,19 @@
 namespace pi05 {
 namespace {
 
+// 8 consecutive fp32 / bf16 values (16-byte aligned) into registers.
+__device__ __forceinline__ void ew_load8f(const float* src, float* f) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(src));
+  const float4 c = __ldg(reinterpret_cast<const float4*>(src + 4));
+  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = c.x; f[5] = c.y; f[6] = c.z; f[7] = c.w;
+}
+
+__device__ __forceinline__ void ew_unpack8(const uint4& u, float* f) {
+  const __nv_bfloat16* v = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) f[j] = __bfloat162float(v[j]);
+}
+
 __device__ __forceinline__ float block_sum(float v, float* red) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffff, v, o);
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
@@ -66,29 +79,75 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const __nv_bfloat16* __re
 // action_in_proj (pi0_pytorch.py:303-323): h[t, n] = bf16(sum_k x[t, k] w[n, k] + b[n]), fp32 math.
 // ssq (optional): ssq[t] = sum_n bf16(h[t, n])^2, the row statistics of the first
 // input_layernorm for the folded-norm q|k|v GEMM.
-__global__ void __launch_bounds__(256) action_in_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                                                        const float* __restrict__ b, __nv_bfloat16* __restrict__ h,
-                                                        float* __restrict__ ssq, int din, int dout) {
-  extern __shared__ float xs[];
+// action_in_proj on (token, 128-column part) CTAs of 128 threads, one output per
+// thread: h[t, n] = bf16(b[n] + sum_k x[t, k] * w[n, k]) with the sum taken in k
+// order (fp32).  The part's weight rows are staged in shared memory (row pitch
+// din + 1 floats: thread n reads row n with no bank conflict) before the
+// grid-dependency wait, since they do not depend on the previous kernel; only the
+// token's x row does.  ssq (optional) receives the sum of squares of the part's
+// bf16 outputs at ssq[part * ssq_ld + t], the folded input norm's row statistics.
+constexpr int kActionInCols = 128;
+constexpr int kActionInMaxDin = 64;
+
+__global__ void __launch_bounds__(kActionInCols) action_in_kernel(const float* __restrict__ x,
+                                                                  const float* __restrict__ w,
+                                                                  const float* __restrict__ b,
+                                                                  __nv_bfloat16* __restrict__ h,
+                                                                  float* __restrict__ ssq, int ssq_ld, int din,
+                                                                  int dout, int vec) {
+  __shared__ float ws[kActionInCols * (kActionInMaxDin + 1)];
+  __shared__ float xs[kActionInMaxDin];
   __shared__ float red[32];
+  const int t = blockIdx.x, n0 = blockIdx.y * kActionInCols;
+  const int rows = min(kActionInCols, dout - n0), pitch = din + 1;
+  if (vec) {  // din % 4 == 0, w 16-byte aligned
+    // All of the thread's float4 loads in flight before the first store.
+    constexpr int kPer = kActionInCols * kActionInMaxDin / 4 / kActionInCols;
+    const int n4 = rows * din / 4;
+    const float4* w4 = reinterpret_cast<const float4*>(w + (size_t)n0 * din);
+    float4 v[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int i = threadIdx.x + j * kActionInCols;
+      if (i < n4) v[j] = __ldg(w4 + i);
+    }
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int i = threadIdx.x + j * kActionInCols;
+      if (i < n4) {
+        const int r = (4 * i) / din, k = 4 * i - r * din;
+        float* dst = ws + r * pitch + k;
+        dst[0] = v[j].x;
+        dst[1] = v[j].y;
+        dst[2] = v[j].z;
+        dst[3] = v[j].w;
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < rows * din; i += blockDim.x) {
+      const int r = i / din, k = i - r * din;
+      ws[r * pitch + k] = __ldg(w + (size_t)(n0 + r) * din + k);
+    }
+  }
+  const int n = n0 + threadIdx.x;
+  const float bias = threadIdx.x < rows ? __ldg(b + n) : 0.f;
   pdl_wait();
   pdl_launch_dependents();  // let the next kernel's CTAs start their prologue / weight prefetch
-  const int t = blockIdx.x;
   for (int k = threadIdx.x; k < din; k += blockDim.x) xs[k] = x[(size_t)t * din + k];
   __syncthreads();
   float ss = 0.f;
-  for (int n = threadIdx.x; n < dout; n += blockDim.x) {
-    float acc = b[n];
-    const float* wr = w + (size_t)n * din;
+  if (threadIdx.x < rows) {
+    float acc = bias;
+    const float* wr = ws + threadIdx.x * pitch;
     for (int k = 0; k < din; ++k) acc = fmaf(xs[k], wr[k], acc);
     const __nv_bfloat16 o = __float2bfloat16(acc);
     h[(size_t)t * dout + n] = o;
     const float f = __bfloat162float(o);
-    ss = fmaf(f, f, ss);
+    ss = f * f;
   }
   if (ssq != nullptr) {
     const float total = block_sum(ss, red);
-    if (threadIdx.x == 0) ssq[t] = total;
+    if (threadIdx.x == 0) ssq[(size_t)blockIdx.y * ssq_ld + t] = total;
   }
 }
 
@@ -146,45 +205,70 @@ __global__ void __launch_bounds__(256) fold_adarms_kernel(const __nv_bfloat16* _
   if (lane == 0) b_out[r] = acc;
 }
 
-// Final adaRMS norm -> fp32 -> action_out_proj -> flow_ode Euler step
-// (modeling_gemma.py:782-783, engine.py:754-767, engine.py:664-675).
-__global__ void __launch_bounds__(256) final_euler_kernel(const __nv_bfloat16* __restrict__ h,
-                                                          const float* __restrict__ mod,
-                                                          const float* __restrict__ w,
-                                                          const float* __restrict__ b, float* __restrict__ x_t,
-                                                          float* __restrict__ v_out, int d, int dout, float eps,
-                                                          float t, float wa, float wb, float sd,
-                                                          const float* __restrict__ noise) {
-  extern __shared__ float hn[];  // [d]
+// Final adaRMS norm -> fp32 -> action_out_proj -> Euler / sampler step
+// (modeling_gemma.py:782-783, engine.py:754-767, engine.py:664-675), on (token, 8-output)
+// CTAs of d / 8 threads holding 8 columns each (d a multiple of 256, at most 2048):
+//   hn[i] = bf16(h[i] * rstd * (1 + scale[i]) + shift[i]),  rstd over the whole row
+//   v[j]  = b[j] + sum_i hn[i] * w[j, i]                      (fp32)
+//   x_t[j] = (x - v t) wa + (x + v (1 - t)) wb (+ noise[j] sd)
+// The weights and the modulation, which do not depend on the previous kernel, are
+// read into registers before the grid-dependency wait.
+constexpr int kEulerOuts = 8;
+constexpr int kEulerMaxThreads = 256;
+
+__global__ void __launch_bounds__(kEulerMaxThreads) final_euler_kernel(const __nv_bfloat16* __restrict__ h,
+                                                                    const float* __restrict__ mod,
+                                                                    const float* __restrict__ w,
+                                                                    const float* __restrict__ b,
+                                                                    float* __restrict__ x_t, float* __restrict__ v_out,
+                                                                    int d, int dout, float eps, float t, float wa,
+                                                                    float wb, float sd,
+                                                                    const float* __restrict__ noise) {
   __shared__ float red[32];
-  __shared__ float vs[64];
+  __shared__ float part[kEulerMaxThreads / 32][kEulerOuts];
+  const int row = blockIdx.x, j0 = blockIdx.y * kEulerOuts, c = threadIdx.x * 8;
+  const int nj = min(kEulerOuts, dout - j0);
+  float wr[kEulerOuts][8], sc[8], sh[8];
+#pragma unroll
+  for (int j = 0; j < kEulerOuts; ++j) {
+    if (j < nj) {
+      ew_load8f(w + (size_t)(j0 + j) * d + c, wr[j]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) wr[j][i] = 0.f;
+    }
+  }
+  ew_load8f(mod + c, sc);
+  ew_load8f(mod + d + c, sh);
   pdl_wait();
   pdl_launch_dependents();  // let the next kernel's CTAs start their prologue / weight prefetch
-  const int row = blockIdx.x;
-  const __nv_bfloat16* hr = h + (size_t)row * d;
+  float hv[8];
+  ew_unpack8(*reinterpret_cast<const uint4*>(h + (size_t)row * d + c), hv);
   float ss = 0.f;
-  for (int i = threadIdx.x; i < d; i += blockDim.x) {
-    const float f = __bfloat162float(hr[i]);
-    ss += f * f;
-  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss += hv[i] * hv[i];
   const float rstd = rsqrtf(block_sum(ss, red) / (float)d + eps);
-  for (int i = threadIdx.x; i < d; i += blockDim.x) {
-    const float n = __bfloat162float(hr[i]) * rstd;
-    hn[i] = bf16_round(n * (1.0f + mod[i]) + mod[d + i]);
+  float acc[kEulerOuts];
+#pragma unroll
+  for (int j = 0; j < kEulerOuts; ++j) acc[j] = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float hn = bf16_round(hv[i] * rstd * (1.0f + sc[i]) + sh[i]);
+#pragma unroll
+    for (int j = 0; j < kEulerOuts; ++j) acc[j] = fmaf(hn, wr[j][i], acc[j]);
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < kEulerOuts; ++j) {
+    float v = acc[j];
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) part[warp][j] = v;
   }
   __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  for (int j = warp; j < dout; j += nw) {
-    const float* wr = w + (size_t)j * d;
-    float acc = 0.f;
-    for (int i = lane; i < d; i += 32) acc = fmaf(hn[i], wr[i], acc);
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffff, acc, o);
-    if (lane == 0) vs[j] = acc + b[j];
-  }
-  __syncthreads();
-  if (threadIdx.x < dout) {
-    const int j = threadIdx.x;
-    const float v = vs[j];
+  if (threadIdx.x < nj) {
+    const int j = j0 + threadIdx.x;
+    float v = b[j];
+    for (int q = 0; q < (int)(blockDim.x >> 5); ++q) v += part[q][threadIdx.x];
     const float x = x_t[(size_t)row * dout + j];
     const float x0 = x - v * t;
     const float x1 = x + v * (1.0f - t);
@@ -351,10 +435,15 @@ int rms_norm_run(const void* x, int ldx, const float* mod, const float* w, void*
 }
 
 int action_in_run(const float* x, const float* w, const float* b, void* h, int rows, int din, int dout,
-                  void* stream, float* ssq) {
-  return launch_pdl(action_in_kernel, dim3(rows), dim3(256), din * sizeof(float),
-                    reinterpret_cast<cudaStream_t>(stream), pdl_enabled(), x, w, b, static_cast<__nv_bfloat16*>(h),
-                    ssq, din, dout);
+                  void* stream, float* ssq, int ssq_ld) {
+  if (rows <= 0 || din <= 0 || din > kActionInMaxDin || dout <= 0 || (ssq != nullptr && ssq_ld < rows)) {
+    set_last_error("action_in: bad shape rows=%d din=%d (<= %d) dout=%d", rows, din, kActionInMaxDin, dout);
+    return PI05_ERR_SHAPE;
+  }
+  const dim3 grid(rows, (dout + kActionInCols - 1) / kActionInCols);
+  return launch_pdl(action_in_kernel, grid, dim3(kActionInCols), 0, reinterpret_cast<cudaStream_t>(stream),
+                    pdl_enabled(), x, w, b, static_cast<__nv_bfloat16*>(h), ssq, ssq_ld, din, dout,
+                    (din % 4 == 0 && aligned16(w)) ? 1 : 0);
 }
 
 int row_ssq_run(const void* x, int ldx, int rows, int d, int part_cols, float* ssq, int ld, void* stream) {
@@ -404,9 +493,16 @@ int final_euler_run(const void* h, const float* mod, const float* w, const float
     set_last_error("final_euler: a stochastic sampler step needs its noise");
     return PI05_ERR_INVALID_ARG;
   }
-  return launch_pdl(final_euler_kernel, dim3(rows), dim3(256), d * sizeof(float),
-                    reinterpret_cast<cudaStream_t>(stream), pdl_enabled(), static_cast<const __nv_bfloat16*>(h), mod,
-                    w, b, x_t, v_out, d, dout, eps, t, wa, wb, sd, sd != 0.0f ? noise : nullptr);
+  if (rows <= 0 || dout <= 0 || d % 256 != 0 || d > 8 * kEulerMaxThreads || !aligned16(h) || !aligned16(w) ||
+      !aligned16(mod)) {
+    set_last_error("final_euler: width %d must be a multiple of 256 up to %d, h / w / mod 16-byte aligned", d,
+                   8 * kEulerMaxThreads);
+    return PI05_ERR_SHAPE;
+  }
+  const dim3 grid(rows, (dout + kEulerOuts - 1) / kEulerOuts);
+  return launch_pdl(final_euler_kernel, grid, dim3(d / 8), 0, reinterpret_cast<cudaStream_t>(stream),
+                    pdl_enabled(), static_cast<const __nv_bfloat16*>(h), mod, w, b, x_t, v_out, d, dout, eps, t, wa,
+                    wb, sd, sd != 0.0f ? noise : nullptr);
 }
 
 int rope_table_run(const uint8_t* valid, int n_prefix, int mode, int rows, const float* inv_freq, int d, void* cos,

@@ -8,15 +8,16 @@ namespace pi05 {
 // mod != null: adaRMS with mod = [scale | shift | gate] (fp32, 3*d); else plain RMSNorm with weight w (fp32, d).
 int rms_norm_run(const void* x, int ldx, const float* mod, const float* w, void* out, int ldo, int rows, int d,
                  float eps, void* stream);
-// ssq (optional): per-token sum of squares of the bf16 outputs, ssq[t].
+// ssq (optional): sum of squares of the bf16 outputs per token and 128-column
+// part, ssq[part * ssq_ld + t] (parts = ceil(dout / 128)).  din <= 64.
 int action_in_run(const float* x, const float* w, const float* b, void* h, int rows, int din, int dout,
-                  void* stream, float* ssq = nullptr);
+                  void* stream, float* ssq = nullptr, int ssq_ld = 0);
 // ssq[part * ld + row] = sum of x^2 over each part_cols-column part of a row (d <= 2048).
 int row_ssq_run(const void* x, int ldx, int rows, int d, int part_cols, float* ssq, int ld, void* stream);
 // w_out = bf16(w * (1 + scale)) column-wise, b_out = w . shift (fp32); w [rows, k], k % 8 == 0.
 int fold_adarms_run(const void* w, int rows, int k, const float* scale, const float* shift, void* w_out,
                     float* b_out, void* stream);
-// Final adaRMS + action_out_proj + the sampler update of x_t.  coefs (host, or null =
+// Final adaRMS + action_out_proj + the sampler update of x_t (d == 1024).  coefs (host, or null =
 // flow_ode): {x0 weight, x1 weight, std}; noise [rows, dout] is added times std.
 int final_euler_run(const void* h, const float* mod, const float* w, const float* b, float* x_t, float* v_out,
                     int rows, int d, int dout, float eps, float t, float delta, void* stream,

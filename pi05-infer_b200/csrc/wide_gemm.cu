@@ -123,21 +123,6 @@ __device__ __forceinline__ bool wide_item(int unit, int i, int n_units, const Wi
   return true;
 }
 
-// Split-K partials of one output tile: [slot][128 rows][BN] fp32, row-major, so a
-// thread (one row) moves whole 128-byte lines.
-struct WideSplit {
-  const float* part;  // this tile's partials; nullptr without split-K
-  int nseg, own, row;
-};
-
-// Accumulator columns [col, col + 32) of this thread's row (TMEM; a split tile's
-// finishing segment has already summed every segment into it).
-template <int BN>
-__device__ __forceinline__ void wide_acc32(uint32_t taddr, int col, const WideSplit& sp, float* v) {
-  (void)sp;
-  tmem_ld32(taddr + col, v);
-}
-
 // Tensor maps of one launch.  out: STORE / GATED_RESID / GEGLU output, or q_out
 // for QKV_ROPE.  in0 / in1: residual (GATED_RESID) or cos / sin (QKV_ROPE).
 // kc / vc: the K and V cache rows [0, krow0 + m_tok) (QKV_ROPE).  All epilogue
@@ -233,12 +218,50 @@ __device__ __forceinline__ void slab_store(const EpiWarp& e, const CUtensorMap* 
   }
 }
 
-// STORE / GATED_RESID (same arithmetic as apply_epilogue).
-template <int EPI, int BN>
-__device__ __forceinline__ bool wide_epi_rows(const SkinnyParams& p, const WideMaps& mp, EpiWarp& e, uint32_t taddr,
-                                              int n_tile, int m0, const WideSplit& sp, const float* sbias,
-                                              const float* scol = nullptr, float ln_rs = 1.f, float ln_rm = 0.f) {
+// STORE / GATED_RESID epilogue features of a launch, fixed per launch (bit mask).
+// Each combination the pipelines use is compiled as its own body, so that a
+// feature a launch does not have costs no instruction per element: the epilogue
+// of a one-tile-per-CTA launch is not overlapped with any mainloop, and the
+// per-element work of 4 or 8 epilogue warps over a 128 x BN tile is on its
+// critical path.  kEpAny decides every feature at run time (other combinations).
+enum : int {
+  kEpBias = 1,   // + bias[n] (staged per tile)
+  kEpLn = 2,     // folded LayerNorm: rstd * acc - rstd * mean * colsum[n]   (STORE)
+  kEpGelu = 4,   // GELU-tanh of the bf16-rounded value                      (STORE)
+  kEpPos = 8,    // + pos[token % pos_rows, n]                               (STORE)
+  kEpGate = 16,  // residual + y * bf16(gate[n])                             (GATED_RESID)
+  kEpSsq = 32,   // row sums of squares of the stored values per 64-column slab
+  kEpSum = 64,   // ... and row sums (with kEpSsq)
+  kEpAny = 128,
+};
+
+template <int EPI>
+__device__ __forceinline__ int wide_epi_mask(const SkinnyParams& p) {
+  int m = 0;
+  if (p.bias != nullptr) m |= kEpBias;
+  if (EPI == SK_EPI_STORE && p.ln_colsum != nullptr) m |= kEpLn;
+  if (EPI == SK_EPI_STORE && p.act == 1) m |= kEpGelu;
+  if (EPI == SK_EPI_STORE && p.pos != nullptr) m |= kEpPos;
+  if (EPI == SK_EPI_GATED_RESID && p.gate != nullptr) m |= kEpGate;
+  if (p.row_ssq != nullptr) m |= kEpSsq | (p.row_sum != nullptr ? kEpSum : 0);
+  return m;
+}
+
+// STORE / GATED_RESID (same arithmetic as apply_epilogue), features F.
+template <int EPI, int BN, int F>
+__device__ __forceinline__ bool wide_epi_rows_f(const SkinnyParams& p, const WideMaps& mp, EpiWarp& e, uint32_t taddr,
+                                                int n_tile, int m0, const float* sbias, const float* scol, float ln_rs,
+                                                float ln_rm) {
   constexpr int NS = BN / 64;
+  constexpr bool kAny = (F & kEpAny) != 0;
+  const int fm = kAny ? wide_epi_mask<EPI>(p) : F;
+  const bool f_bias = (fm & kEpBias) != 0;
+  const bool f_ln = EPI == SK_EPI_STORE && (fm & kEpLn) != 0;
+  const bool f_gelu = EPI == SK_EPI_STORE && (fm & kEpGelu) != 0;
+  const bool f_pos = EPI == SK_EPI_STORE && (fm & kEpPos) != 0;
+  const bool f_gate = EPI == SK_EPI_GATED_RESID && (fm & kEpGate) != 0;
+  const bool f_ssq = (fm & kEpSsq) != 0;
+  const bool f_sum = (fm & kEpSum) != 0;
   const int r = e.lane;
   const int tok = m0 + e.q * 32 + r;
   const int n_valid = p.n_valid > 0 ? p.n_valid : 1 << 30;
@@ -262,61 +285,107 @@ __device__ __forceinline__ bool wide_epi_rows(const SkinnyParams& p, const WideM
 #pragma unroll 1
     for (int h = 0; h < 2; ++h) {
       float v[32];
-      wide_acc32<BN>(taddr, j * 64 + h * 32, sp, v);
-      if (EPI == SK_EPI_STORE && p.ln_colsum != nullptr) {
-        // Folded LayerNorm: rstd * (acc - mean * colsum), column sums staged per tile
-        // (zero past n_valid) or read from global memory.
-        const int c0 = n_tile * BN + j * 64 + h * 32;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float cs = scol != nullptr ? scol[j * 64 + h * 32 + i] : (c0 + i < n_valid ? p.ln_colsum[c0 + i] : 0.f);
-          v[i] = v[i] * ln_rs - ln_rm * cs;
-        }
-      }
+      tmem_ld32(taddr + j * 64 + h * 32, v);
       if (EPI == SK_EPI_GATED_RESID && h == 0) ok = slab_wait(e, b, p.status) && ok;
 #pragma unroll
       for (int g4 = 0; g4 < 4; ++g4) {
         const int g = h * 4 + g4;
-        const int n = n_tile * BN + j * 64 + g * 8;
+        const int c = j * 64 + g * 8;  // column within the tile
+        const int n = n_tile * BN + c;
         const bool in = n < n_valid;
-        float bi[8], ps[8], gt[8], rs[8];
-        if (p.bias != nullptr) load8f(sbias + j * 64 + g * 8, bi);  // staged per tile, zero past n_valid
-        if (EPI == SK_EPI_STORE && p.pos != nullptr && in) load8f(p.pos + (size_t)(tok % p.pos_rows) * p.ldo + n, ps);
-        if (EPI == SK_EPI_GATED_RESID) {
-          unpack8(lds16(slab, r, g), rs);
-          if (p.gate != nullptr && in) load8f(p.gate + n, gt);
-        }
-        float o[8];
+        float* a = v + g4 * 8;
+        if (f_ln) {
+          // Folded LayerNorm: column sums staged per tile (zero past n_valid) or read
+          // from global memory.
+          float cs[8];
+          if (scol != nullptr) {
+            load8f(scol + c, cs);
+          } else {
 #pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
-          float y = v[g4 * 8 + jj];
-          if (p.bias != nullptr) y += bi[jj];
-          if (EPI == SK_EPI_STORE && p.pos != nullptr && in) y += ps[jj];
-          y = bf16_round(y);
-          if (EPI == SK_EPI_STORE && p.act == 1) y = gelu_tanh_fast(y);
-          if (EPI == SK_EPI_GATED_RESID) y = (p.gate != nullptr && in) ? rs[jj] + y * bf16_round(gt[jj]) : rs[jj] + y;
-          o[jj] = y;
+            for (int q = 0; q < 8; ++q) cs[q] = n + q < n_valid ? p.ln_colsum[n + q] : 0.f;
+          }
+#pragma unroll
+          for (int q = 0; q < 8; ++q) a[q] = a[q] * ln_rs - ln_rm * cs[q];
         }
-        const uint4 pk = pack8(o);
-        if (p.row_ssq != nullptr && in) {  // the stored (bf16) values
+        if (f_bias) {
+          float bi[8];
+          load8f(sbias + c, bi);  // staged per tile, zero past n_valid
+#pragma unroll
+          for (int q = 0; q < 8; ++q) a[q] += bi[q];
+        }
+        if (f_pos && in) {
+          float ps[8];
+          load8f(p.pos + (size_t)(tok % p.pos_rows) * p.ldo + n, ps);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) a[q] += ps[q];
+        }
+        if (f_gelu) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) a[q] = gelu_tanh_fast(bf16_round(a[q]));
+        }
+        if (EPI == SK_EPI_GATED_RESID) {
+          float rs[8];
+          unpack8(lds16(slab, r, g), rs);
+          if (f_gate && in) {
+            float gt[8];
+            load8f(p.gate + n, gt);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) a[q] = rs[q] + bf16_round(a[q]) * bf16_round(gt[q]);
+          } else {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) a[q] = rs[q] + bf16_round(a[q]);
+          }
+        }
+        const uint4 pk = pack8(a);
+        if (f_ssq && in) {  // the stored (bf16) values
           float q8[8];
           unpack8(pk, q8);
 #pragma unroll
-          for (int jj = 0; jj < 8; ++jj) {
-            ss = fmaf(q8[jj], q8[jj], ss);
-            sx += q8[jj];
+          for (int q = 0; q < 8; ++q) {
+            ss = fmaf(q8[q], q8[q], ss);
+            if (f_sum) sx += q8[q];
           }
         }
         sts16(slab, r, g, pk);
       }
     }
-    if (p.row_ssq != nullptr && tok < p.m_tok && n_tile * BN + j * 64 < n_valid) {
+    if (f_ssq && tok < p.m_tok && n_tile * BN + j * 64 < n_valid) {
       p.row_ssq[(size_t)(n_tile * (BN / 64) + j) * p.ssq_ld + tok] = ss;
-      if (p.row_sum != nullptr) p.row_sum[(size_t)(n_tile * (BN / 64) + j) * p.ssq_ld + tok] = sx;
+      if (f_sum) p.row_sum[(size_t)(n_tile * (BN / 64) + j) * p.ssq_ld + tok] = sx;
     }
     slab_store(e, &mp.out, slab, n_tile * BN + j * 64, m0 + e.q * 32);
   }
   return ok;
+}
+
+// The body for the launch's feature mask (the combinations the SigLIP encoder, the
+// prefix LM and the plain linear ops use; kEpAny otherwise).
+template <int EPI, int BN>
+__device__ __forceinline__ bool wide_epi_rows(const SkinnyParams& p, const WideMaps& mp, EpiWarp& e, uint32_t taddr,
+                                              int n_tile, int m0, const float* sbias, const float* scol, float ln_rs,
+                                              float ln_rm) {
+#define PI05_WIDE_EPI(F) wide_epi_rows_f<EPI, BN, (F)>(p, mp, e, taddr, n_tile, m0, sbias, scol, ln_rs, ln_rm)
+  const int m = wide_epi_mask<EPI>(p);
+  if (EPI == SK_EPI_STORE) {
+    switch (m) {
+      case 0: return PI05_WIDE_EPI(0);
+      case kEpBias: return PI05_WIDE_EPI(kEpBias);
+      case kEpBias | kEpLn: return PI05_WIDE_EPI(kEpBias | kEpLn);
+      case kEpBias | kEpLn | kEpGelu: return PI05_WIDE_EPI(kEpBias | kEpLn | kEpGelu);
+      case kEpBias | kEpGelu: return PI05_WIDE_EPI(kEpBias | kEpGelu);
+      case kEpBias | kEpPos | kEpSsq | kEpSum: return PI05_WIDE_EPI(kEpBias | kEpPos | kEpSsq | kEpSum);
+      default: return PI05_WIDE_EPI(kEpAny);
+    }
+  }
+  switch (m) {
+    case 0: return PI05_WIDE_EPI(0);
+    case kEpGate: return PI05_WIDE_EPI(kEpGate);
+    case kEpSsq: return PI05_WIDE_EPI(kEpSsq);
+    case kEpBias: return PI05_WIDE_EPI(kEpBias);
+    case kEpBias | kEpSsq | kEpSum: return PI05_WIDE_EPI(kEpBias | kEpSsq | kEpSum);
+    default: return PI05_WIDE_EPI(kEpAny);
+  }
+#undef PI05_WIDE_EPI
 }
 
 // GEGLU: TMEM columns [0, 128) are gate rows, [128, 256) the matching up rows.
@@ -737,7 +806,6 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
       else if (EPI == SK_EPI_QKV_ROPE)
         ok = wide_epi_qkv(p, mp, e, taddr, n, m * kWBM, rs);
       else {
-        WideSplit sp{nullptr, wt.nseg, wt.s, e.q * 32 + lane};
         bool finish = true;
         if (wt.nseg > 1) {
           // Publish this segment's partial, take a ticket; the segment taking the
@@ -826,8 +894,7 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
           }
         }
         if (finish) {
-          ok = wide_epi_rows<EPI, BN>(p, mp, e, taddr, n, m * kWBM, sp, sbias, kScol ? scol : nullptr, ln_rs,
-                                      ln_rm);
+          ok = wide_epi_rows<EPI, BN>(p, mp, e, taddr, n, m * kWBM, sbias, kScol ? scol : nullptr, ln_rs, ln_rm);
         } else if (EPI == SK_EPI_GATED_RESID && e.lane == 0) {
           // The residual slab prefetched for this tile is not consumed: retire its load.
           ok = slab_wait(e, 0, p.status);
