@@ -428,6 +428,10 @@ __device__ __forceinline__ void cluster_epilogue(const SkinnyParams& p, uint32_t
 // barrier, arrived once a CTA has received everything, keeps every source's
 // staging tile alive until all copies out of it have landed.
 // Bytes this rank receives in the push form (its token slice from every other rank).
+// Receive slot of source split `src` at owner `owner` (src != owner): the owner
+// keeps no slot for itself, so splits - 1 slots of its slice cover every source.
+__device__ __forceinline__ int recv_slot(int src, int owner) { return src < owner ? src : src - 1; }
+
 __device__ __forceinline__ uint32_t push_recv_bytes(int splits, int mt, int rank) {
   const int t0 = (rank * mt) / splits, t1 = ((rank + 1) * mt) / splits;
   return (uint32_t)((splits - 1) * (t1 - t0) * kBM * 4);
@@ -455,7 +459,7 @@ __device__ __forceinline__ void cluster_push_body(const SkinnyParams& p, const f
       const int d0 = (et * mt) / splits, d1 = ((et + 1) * mt) / splits;
       const uint32_t bytes = (uint32_t)(d1 - d0) * kBM * 4u;
       if (bytes > 0)
-        bulk_copy_to_peer(mapa_shared(smem_u32(recv) + (uint32_t)rank * bytes, (uint32_t)et),
+        bulk_copy_to_peer(mapa_shared(smem_u32(recv) + (uint32_t)recv_slot(rank, et) * bytes, (uint32_t)et),
                           smem_u32(st) + (uint32_t)d0 * kBM * 4u, bytes, mapa_shared(smem_u32(rbar), (uint32_t)et));
     }
     if (stamp) stamps[1] = globaltimer_ns();
@@ -493,7 +497,7 @@ __device__ __forceinline__ void cluster_push_body(const SkinnyParams& p, const f
             for (int j = 0; j < 4; ++j) y[h][j] = 0.f;
 #pragma unroll kSU
           for (int s = 0; s < splits; ++s) {  // loads of kSU splits in flight, sums in split order
-            const float* src = s == rank ? own : rcv + s * slot;
+            const float* src = s == rank ? own : rcv + recv_slot(s, rank) * slot;
 #pragma unroll
             for (int h = 0; h < H; ++h) {
               const float4 v = *reinterpret_cast<const float4*>(src + h * 64);
@@ -536,8 +540,8 @@ __device__ __forceinline__ void cluster_push_kind(const SkinnyParams& p, const f
 
 // Whole push-form cluster epilogue; every thread of the CTA calls it, the epilogue
 // threads after fencing the staging tile they wrote (fence.proxy.async) followed by
-// a barrier among themselves.  `recv` must hold splits * ceil(mt / splits) * 512
-// bytes; `rbar` was initialised with one arrival, armed with push_recv_bytes() and
+// a barrier among themselves.  `recv` must hold (splits - 1) * ceil(mt / splits) *
+// 512 bytes (slot recv_slot(s, rank) for source s); `rbar` was initialised with one arrival, armed with push_recv_bytes() and
 // published by a cluster barrier before the mainloop.  Trace stamps (optional):
 // [0..4] the phases.
 template <int EPI>

@@ -4,7 +4,7 @@
 //   Y[t, n] = sum_k X[t, k] * W[n, k]
 //
 // Tokens fill the UMMA M dimension (128 rows per tile) and BN weight rows the N
-// dimension (BN = 128 or 256), so TMEM lane r holds token r's BN outputs.
+// dimension (BN = 128, 192 or 256), so TMEM lane r holds token r's BN outputs.
 //
 // One CTA per SM loops over output tiles (m fastest, so the CTAs resident at a
 // time share weight tiles in L2):
@@ -525,14 +525,14 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
     wide_gemm_kernel(const __grid_constant__ WideMaps mp, const SkinnyParams p, const WideSched ws) {
   constexpr int kBBytes = wide_b_bytes<BN, PAIR>();
   constexpr int kStageBytes = kABytes + kBBytes;
-  constexpr uint32_t kTmemCols = 2 * BN;
+  constexpr uint32_t kTmemCols = BN == 192 ? 512 : 2 * BN;  // a power of two
   constexpr uint32_t kIdesc = umma_idesc_bf16(PAIR ? 2 * kWBM : kWBM, BN);
   static_assert(!PAIR || BN == 256, "CTA pairs use 256-wide tiles");
   constexpr int kSlabs = epi_slabs<EPI>();
   constexpr int kEW = EW;
   static_assert(EW == 4 || ((EPI == SK_EPI_STORE || EPI == SK_EPI_GATED_RESID) && EW == 8), "epilogue warps");
   constexpr int kET = kEW * 32;  // epilogue threads
-  static_assert(BN == 128 || BN == 256, "tile width");
+  static_assert(BN == 128 || BN == 192 || BN == 256, "tile width");
   static_assert((EPI != SK_EPI_GEGLU && EPI != SK_EPI_QKV_ROPE) || BN == 256, "paired epilogues use BN = 256");
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -1074,7 +1074,7 @@ int wide_choose(int epi, int m_tiles, int n_cols, int kb_total, int sms, int* bn
   // tile) + the partial round trip of a split.  A k-block moves 48 KB (256-wide) or
   // 32 KB (128-wide) of operands, at about 100 GB/s per SM.
   double best_cost = 1e30;
-  for (int b : {256, 128}) {
+  for (int b : {256, 192, 128}) {
     const int nt = (n_cols + b - 1) / b;
     for (int s = 1; s <= 2 && s * 8 <= kb_total; ++s) {
       const long tiles = (long)m_tiles * nt * s;
@@ -1083,7 +1083,8 @@ int wide_choose(int epi, int m_tiles, int n_cols, int kb_total, int sms, int* bn
       // A split adds the partial write + ticket and one L2 round trip per 32
       // columns when the finishing split reads the other partial.
       const double reduce = s > 1 ? 1.0 + 0.9 * (b / 32) : 0.0;
-      const double cost = (double)waves * (kb_per * (b == 256 ? 0.44 : 0.34) + 3.0) + reduce;
+      const double per_kb = b == 256 ? 0.44 : (b == 192 ? 0.39 : 0.34);
+      const double cost = (double)waves * (kb_per * per_kb + 3.0) + reduce;
       if (cost < best_cost - 1e-9) {
         best_cost = cost;
         *bn = b;
@@ -1091,7 +1092,7 @@ int wide_choose(int epi, int m_tiles, int n_cols, int kb_total, int sms, int* bn
       }
     }
   }
-  if (force_bn == 128 || force_bn == 256) *bn = force_bn;
+  if (force_bn == 128 || force_bn == 192 || force_bn == 256) *bn = force_bn;
   if (force_splits >= 1 && force_splits <= 2) *splits = force_splits;
   return 0;
 }
@@ -1183,15 +1184,19 @@ int wide_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int w
   }
   switch (epi) {
     case SK_EPI_STORE:
-      if (wide8) return bn == 256 ? wide_launch<SK_EPI_STORE, 256, 3, 8>(p, ws, mp, st)
-                                  : wide_launch<SK_EPI_STORE, 128, 5, 8>(p, ws, mp, st);
-      return bn == 256 ? wide_launch<SK_EPI_STORE, 256, 4, 4>(p, ws, mp, st)
-                       : wide_launch<SK_EPI_STORE, 128, 6, 4>(p, ws, mp, st);
+      if (wide8) return bn == 256   ? wide_launch<SK_EPI_STORE, 256, 3, 8>(p, ws, mp, st)
+                        : bn == 192 ? wide_launch<SK_EPI_STORE, 192, 3, 8>(p, ws, mp, st)
+                                    : wide_launch<SK_EPI_STORE, 128, 5, 8>(p, ws, mp, st);
+      return bn == 256   ? wide_launch<SK_EPI_STORE, 256, 4, 4>(p, ws, mp, st)
+             : bn == 192 ? wide_launch<SK_EPI_STORE, 192, 4, 4>(p, ws, mp, st)
+                         : wide_launch<SK_EPI_STORE, 128, 6, 4>(p, ws, mp, st);
     case SK_EPI_GATED_RESID:
-      if (wide8) return bn == 256 ? wide_launch<SK_EPI_GATED_RESID, 256, 3, 8>(p, ws, mp, st)
-                                  : wide_launch<SK_EPI_GATED_RESID, 128, 5, 8>(p, ws, mp, st);
-      return bn == 256 ? wide_launch<SK_EPI_GATED_RESID, 256, 4, 4>(p, ws, mp, st)
-                       : wide_launch<SK_EPI_GATED_RESID, 128, 6, 4>(p, ws, mp, st);
+      if (wide8) return bn == 256   ? wide_launch<SK_EPI_GATED_RESID, 256, 3, 8>(p, ws, mp, st)
+                        : bn == 192 ? wide_launch<SK_EPI_GATED_RESID, 192, 3, 8>(p, ws, mp, st)
+                                    : wide_launch<SK_EPI_GATED_RESID, 128, 5, 8>(p, ws, mp, st);
+      return bn == 256   ? wide_launch<SK_EPI_GATED_RESID, 256, 4, 4>(p, ws, mp, st)
+             : bn == 192 ? wide_launch<SK_EPI_GATED_RESID, 192, 4, 4>(p, ws, mp, st)
+                         : wide_launch<SK_EPI_GATED_RESID, 128, 6, 4>(p, ws, mp, st);
     case SK_EPI_GEGLU:
       return wide_launch<SK_EPI_GEGLU, 256, 4, 4>(p, ws, mp, st);
     case SK_EPI_QKV_ROPE:
