@@ -15,7 +15,8 @@
 //   O   += P_j . V_j          tcgen05.mma M=128 N=256 K=64, V read MN-major straight
 //                             from the cache layout [key][256]
 //
-// Warp roles: warp 0 TMA (Q once, K/V chunks through a 1- or 2-stage ring),
+// Warp roles: warp 0 TMA (Q once, K and V chunks through 1- or 2-stage rings, a
+// K slot released after its S, a V slot after its P.V),
 // warp 1 TMEM owner + MMA issuer (S_{j+1} is issued before P_j is ready, so the
 // tensor core works on the next scores while the softmax runs), warps 2-9
 // softmax and the output (two per TMEM lane quarter, so every SM sub-partition
@@ -65,7 +66,7 @@ struct TcMaps {
 constexpr int kMaxChunks = 64;  // key chunks per CTA whose mask bytes are staged (4096 keys)
 // Ring, barriers, the row-max / row-sum exchange [6][128], the staged key mask.
 size_t tc_smem_bytes(int nst) {
-  return 1024 + kQBytes + (size_t)nst * 2 * kKVBytes + kPBytes + 28 * 8 + 6 * kBR * 4 + kMaxChunks * kBC;
+  return 1024 + kQBytes + (size_t)nst * 2 * kKVBytes + kPBytes + 32 * 8 + 6 * kBR * 4 + kMaxChunks * kBC;
 }
 
 __device__ __forceinline__ uint32_t p_off(int r, int g) { return (uint32_t)(r * 128 + ((g ^ (r & 7)) << 4)); }
@@ -92,21 +93,23 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
   uint8_t* sP = sV + nst * kKVBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kPBytes);
   uint64_t* q_full = bars;        // Q landed
-  uint64_t* kv_full = bars + 1;   // [2] K/V chunk landed
-  uint64_t* kv_empty = bars + 3;  // [2] P.V of the chunk done
+  uint64_t* k_full = bars + 1;    // [2] K chunk landed
+  uint64_t* k_empty = bars + 3;   // [2] S of the chunk done (its K slot is free)
   uint64_t* s_full = bars + 5;    // [2] S buffer written
   uint64_t* s_empty = bars + 7;   // [2] S buffer read (128 arrivals)
   uint64_t* p_full = bars + 9;    // P written, O rescaled (128 arrivals)
   uint64_t* p_empty = bars + 10;  // P.V done (P free, O stable)
   uint64_t* mdone = bars + 11;    // every MMA of the CTA complete
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 12);
-  int* s_flag = reinterpret_cast<int*>(s_tmem + 1);  // [0] abort, [1] K/V chunks armed
-  // Row-max exchange of the two warps of each TMEM lane quarter: [quarter][S parity]
-  // (64 arrivals), then the final row-sum exchange [quarter].
-  uint64_t* xbar = bars + 14;
+  int* s_flag = reinterpret_cast<int*>(s_tmem + 1);  // [0] abort, [1] K chunks armed, [2] V chunks armed
+  // Per S parity, half and TMEM lane quarter: whether the warp's waits all succeeded
+  // (read by the quarter's other warp after their named barrier).
+  int* s_pair_ok = reinterpret_cast<int*>(bars + 14);  // [2][2][4]
   uint64_t* lbar = bars + 22;  // [4] row sums, [4] mask staged
+  uint64_t* v_full = bars + 28;   // [2] V chunk landed
+  uint64_t* v_empty = bars + 30;  // [2] P.V of the chunk done (its V slot is free)
   // Row max of each half for the two S parities [2][2][128], then the row sums [2][128].
-  float* s_red = reinterpret_cast<float*>(bars + 28);
+  float* s_red = reinterpret_cast<float*>(bars + 32);
   uint8_t* s_mask = reinterpret_cast<uint8_t*>(s_red + 6 * kBR);  // [nc * 64] key-mask bytes of this CTA
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -123,8 +126,10 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], kSoftThreads);
     }
@@ -132,10 +137,10 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
     mbar_init(p_empty, 1);
     mbar_init(mdone, 1);
     mbar_init(&lbar[4], kSoftThreads);  // mask bytes staged
-    for (int i = 0; i < 8; ++i) mbar_init(&xbar[i], 64);
     for (int i = 0; i < 4; ++i) mbar_init(&lbar[i], 64);
     s_flag[0] = 0;
     s_flag[1] = 0;
+    s_flag[2] = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -156,23 +161,27 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
   if (warp == 0) {
     if (lane == 0) {
       const uint64_t pol_kv = l2_policy_evict_last();
-      int armed = 0;
-      auto load_kv = [&](int j) -> bool {
+      int armed_k = 0, armed_v = 0;
+      // K and V of a chunk use separate slots: chunk j's K slot is free once S_j is
+      // done, its V slot once P_j.V_j is, so K_{j+nst} streams in while the
+      // softmax of chunk j still runs.
+      auto load_half = [&](int j, bool is_v) -> bool {
         const int st = j % nst;
-        if (j >= nst && !mbar_wait(&kv_empty[st], ((j / nst) - 1) & 1)) {
+        uint64_t* full = is_v ? v_full : k_full;
+        uint64_t* empty = is_v ? v_empty : k_empty;
+        if (j >= nst && !mbar_wait(&empty[st], ((j / nst) - 1) & 1)) {
           report_status(p.status, PI05_DEV_TIMEOUT_PRODUCER);
           s_flag[0] = 1;
           return false;
         }
-        mbar_arrive_expect_tx(&kv_full[st], 2 * kKVBytes);
+        mbar_arrive_expect_tx(&full[st], kKVBytes);
         const int key0 = (c_begin + j) * kBC;
-        for (int b = 0; b < 4; ++b) {
-          tma_load_2d(sK + st * kKVBytes + b * 8192, &mp.k, &kv_full[st], b * 64, key0, pol_kv);
-          tma_load_2d(sV + st * kKVBytes + b * 8192, &mp.v, &kv_full[st], b * 64, key0, pol_kv);
-        }
-        ++armed;
+        uint8_t* dst = (is_v ? sV : sK) + st * kKVBytes;
+        for (int b = 0; b < 4; ++b) tma_load_2d(dst + b * 8192, is_v ? &mp.v : &mp.k, &full[st], b * 64, key0, pol_kv);
+        ++(is_v ? armed_v : armed_k);
         return true;
       };
+      auto load_kv = [&](int j) -> bool { return load_half(j, false) && load_half(j, true); };
       // Chunk 0 from the static rows does not depend on the previous kernel.
       const bool first_static = nc > 0 && (c_begin + 1) * kBC <= p.static_rows;
       if (first_static) load_kv(0);
@@ -182,14 +191,15 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
       bool ok = true;
       if (!first_static && nc > 0) ok = load_kv(0);
       for (int j = 1; j < nc && ok; ++j) ok = load_kv(j);
-      s_flag[1] = armed;
+      s_flag[1] = armed_k;
+      s_flag[2] = armed_v;
     }
   } else if (warp == 1) {
     if (lane == 0) {
       bool ok = mbar_wait(q_full, 0);
       auto issue_s = [&](int j) -> bool {
         const int st = j % nst, sb = j & 1;
-        if (!mbar_wait(&kv_full[st], (j / nst) & 1)) return false;
+        if (!mbar_wait(&k_full[st], (j / nst) & 1)) return false;
         if (j >= 2 && !mbar_wait(&s_empty[sb], ((j >> 1) - 1) & 1)) return false;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(sb * kBC);
@@ -201,24 +211,25 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
             umma_bf16(d, umma_sdesc_sw128(a0 + b * 16384 + kk * 32), umma_sdesc_sw128(b0 + b * 8192 + kk * 32),
                       kIdescS, (b | kk) ? 1u : 0u);
         umma_commit(&s_full[sb]);
+        umma_commit(&k_empty[st]);
         return true;
       };
       if (ok && nc > 0) ok = issue_s(0);
       for (int j = 0; j < nc && ok; ++j) {
         if (j + 1 < nc) ok = issue_s(j + 1);
-        if (!ok || !mbar_wait(p_full, j & 1)) {
+        const int st = j % nst;
+        if (!ok || !mbar_wait(p_full, j & 1) || !mbar_wait(&v_full[st], (j / nst) & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const int st = j % nst;
         const uint32_t a0 = smem_u32(sP), b0 = smem_u32(sV + st * kKVBytes);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
           umma_bf16(tmem + kColO, umma_sdesc_sw128(a0 + kk * 32), umma_sdesc_mn_sw128(b0 + kk * 2048, 8192, 1024),
                     kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
         umma_commit(p_empty);
-        umma_commit(&kv_empty[st]);
+        umma_commit(&v_empty[st]);
       }
       if (!ok) {
         report_status(p.status, PI05_DEV_TIMEOUT_MMA);
@@ -272,10 +283,9 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
       bool all_valid = true;
 #pragma unroll
       for (int wd = 0; wd < 8; ++wd) all_valid = all_valid && !has_zero_byte(mask_word(vk, wd));
-      if (!mbar_wait(&s_full[sb], (j >> 1) & 1)) {
-        ok = false;
-        break;
-      }
+      // A failed wait does not leave the loop before the pair's exchange below:
+      // both warps of the quarter leave together there (a named barrier).
+      if (ok && !mbar_wait(&s_full[sb], (j >> 1) & 1)) ok = false;
       tc_fence_after();
       if (tr && j == 0) t_data = globaltimer_ns();
       float s[32];
@@ -283,21 +293,39 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
       tc_fence_before();
       mbar_arrive(&s_empty[sb]);
       // Scores: bf16(bf16(q.k) * scale); a power-of-two scale needs no second
-      // rounding (the product is exact).
-      float mx4[4];
+      // rounding (the product is exact).  The common case (power-of-two scale, no
+      // masked key in the half, both warp-uniform) keeps the raw scores: rounding
+      // and scaling are monotonic, so the half's max is bf16(max) * scale, and the
+      // exponent below takes bf16(s) * (scale * log2e), the same exact product.
+      const bool fast = scale_pow2 && all_valid;
+      float mxh;
+      if (fast) {
+        float mx4[4] = {s[0], s[1], s[2], s[3]};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) mx4[i] = -INFINITY;
+        for (int i = 4; i < 32; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], s[i]);
+        mxh = bf16_round(fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]))) * p.scale;
+      } else {
+        float mx4[4];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        float v = bf16_round(s[i]) * p.scale;
-        if (!scale_pow2) v = bf16_round(v);
-        if (!all_valid) v = key_ok(vk, i) ? v : -INFINITY;
-        s[i] = v;
-        mx4[i & 3] = fmaxf(mx4[i & 3], v);
+        for (int i = 0; i < 4; ++i) mx4[i] = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float v = bf16_round(s[i]) * p.scale;
+          if (!scale_pow2) v = bf16_round(v);
+          if (!all_valid) v = key_ok(vk, i) ? v : -INFINITY;
+          s[i] = v;
+          mx4[i & 3] = fmaxf(mx4[i & 3], v);
+        }
+        mxh = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       }
-      s_red[(sb * 2 + hh) * kBR + r] = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-      mbar_arrive(&xbar[q * 2 + sb]);
-      if (!mbar_wait(&xbar[q * 2 + sb], (j >> 1) & 1)) {
+      s_red[(sb * 2 + hh) * kBR + r] = mxh;
+      const bool warp_ok = __all_sync(0xffffffffu, ok);
+      if (lane == 0) s_pair_ok[(sb * 2 + hh) * 4 + q] = warp_ok ? 1 : 0;
+      // The quarter's two warps (one SM sub-partition): a hardware barrier, cheaper
+      // than an mbarrier round trip; the row max of each half is double-buffered
+      // by S parity, so neither warp can overwrite a value the other still reads.
+      named_bar_sync(4 + q, 64);
+      if (s_pair_ok[(sb * 2) * 4 + q] == 0 || s_pair_ok[(sb * 2 + 1) * 4 + q] == 0) {
         ok = false;
         break;
       }
@@ -318,20 +346,29 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
       float ls4[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) ls4[i] = 0.f;
+      if (fast) {
+        const float c = p.scale * kLog2e;  // exact: scale is a power of two
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float pv = ex2_approx(fmaf(s[i], kLog2e, -mb));  // exp(s - m); masked keys give 0
-        s[i] = pv;
-        ls4[i & 3] += pv;
+        for (int i = 0; i < 32; i += 2) bf16_round2(s[i], s[i + 1]);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float pv = ex2_approx(fmaf(s[i], c, -mb));  // exp(s - m)
+          s[i] = pv;
+          ls4[i & 3] += pv;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float pv = ex2_approx(fmaf(s[i], kLog2e, -mb));  // exp(s - m); masked keys give 0
+          s[i] = pv;
+          ls4[i & 3] += pv;
+        }
       }
       l = l * corr + ((ls4[0] + ls4[1]) + (ls4[2] + ls4[3]));
       if (j > 0) {
         // P.V of the previous chunk must be done: P is single-buffered and O may
-        // need rescaling.
-        if (!mbar_wait(p_empty, (j - 1) & 1)) {
-          ok = false;
-          break;
-        }
+        // need rescaling.  (A failure is acted on at the next exchange.)
+        if (ok && !mbar_wait(p_empty, (j - 1) & 1)) ok = false;
         tc_fence_after();
         // tcgen05.ld/st are warp-collective: rescale when any row of the warp moved
         // (rows whose base did not move multiply by 1).
@@ -427,7 +464,9 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
           p.part_ml[((size_t)split * p.part_rows + grow) * 2 + 1] = lt;
         }
       }
-      if (lane == 0) bulk_wait_group<0>();
+      // The stores have read the staging slabs before the CTA leaves; their global
+      // writes are complete when the grid is, before any dependent grid reads them.
+      if (lane == 0) bulk_wait_group_read<0>();
       __syncwarp();
       // Trace record {tag << 32 | cta, entry, grid-dependency wait done, first S
       // ready, last P.V done, output stored, 0, 0} (same layout as attention.cu).
@@ -453,10 +492,13 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
   // Teardown: if the producer stopped early, wait (bounded) for the copies it armed.
   __syncthreads();
   if (s_flag[0] != 0 && warp == 0 && lane == 0) {
-    const int armed = s_flag[1];
-    for (int st = 0; st < nst && st < armed; ++st) {
-      const int uses = (armed - st + nst - 1) / nst;
-      if (!mbar_wait(&kv_full[st], (uses - 1) & 1)) report_status(p.status, PI05_DEV_TIMEOUT_DRAIN);
+    for (int h = 0; h < 2; ++h) {
+      const int armed = s_flag[1 + h];
+      uint64_t* full = h == 0 ? k_full : v_full;
+      for (int st = 0; st < nst && st < armed; ++st) {
+        const int uses = (armed - st + nst - 1) / nst;
+        if (!mbar_wait(&full[st], (uses - 1) & 1)) report_status(p.status, PI05_DEV_TIMEOUT_DRAIN);
+      }
     }
   }
   tc_fence_before();

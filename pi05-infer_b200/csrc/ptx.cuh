@@ -435,6 +435,15 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16(x)); }
 
+// Two values rounded to bf16 (round to nearest even) and back: one paired
+// conversion instruction instead of two.
+__device__ __forceinline__ void bf16_round2(float& a, float& b) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  const uint32_t u = *reinterpret_cast<const uint32_t*>(&v);
+  a = __uint_as_float(u << 16);
+  b = __uint_as_float(u & 0xffff0000u);
+}
+
 // 2^x on the special-function unit (PTX ex2.approx.ftz.f32: -inf -> +0).
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
