@@ -141,12 +141,15 @@ __device__ __forceinline__ void load4f(const float* src, float* f) {
   f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
 }
 
+// Two fp32 values -> packed bf16 pair (round to nearest even), low half first: one
+// paired conversion instruction.
+__device__ __forceinline__ uint32_t pack2bf(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
 __device__ __forceinline__ uint2 pack4(const float* f) {
-  uint2 u;
-  __nv_bfloat16* b = reinterpret_cast<__nv_bfloat16*>(&u);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) b[j] = __float2bfloat16(f[j]);
-  return u;
+  return make_uint2(pack2bf(f[0], f[1]), pack2bf(f[2], f[3]));
 }
 
 // Unit geometry: token t and first tile row r of unit idx (tile-relative).
@@ -586,11 +589,7 @@ __device__ __forceinline__ void load8f(const float* src, float* f) {
 }
 
 __device__ __forceinline__ uint4 pack8(const float* f) {
-  uint4 u;
-  __nv_bfloat16* b = reinterpret_cast<__nv_bfloat16*>(&u);
-#pragma unroll
-  for (int j = 0; j < 8; ++j) b[j] = __float2bfloat16(f[j]);
-  return u;
+  return make_uint4(pack2bf(f[0], f[1]), pack2bf(f[2], f[3]), pack2bf(f[4], f[5]), pack2bf(f[6], f[7]));
 }
 
 // Apply the epilogue to item groups [i0, i1).  Each thread handles kBatch

@@ -321,19 +321,25 @@ __device__ __forceinline__ bool wide_epi_rows_f(const SkinnyParams& p, const Wid
         }
         if (f_gelu) {
 #pragma unroll
-          for (int q = 0; q < 8; ++q) a[q] = gelu_tanh_fast(bf16_round(a[q]));
+          for (int q = 0; q < 8; q += 2) bf16_round2(a[q], a[q + 1]);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) a[q] = gelu_tanh_fast(a[q]);
         }
         if (EPI == SK_EPI_GATED_RESID) {
           float rs[8];
           unpack8(lds16(slab, r, g), rs);
+#pragma unroll
+          for (int q = 0; q < 8; q += 2) bf16_round2(a[q], a[q + 1]);
           if (f_gate && in) {
             float gt[8];
             load8f(p.gate + n, gt);
 #pragma unroll
-            for (int q = 0; q < 8; ++q) a[q] = rs[q] + bf16_round(a[q]) * bf16_round(gt[q]);
+            for (int q = 0; q < 8; q += 2) bf16_round2(gt[q], gt[q + 1]);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) a[q] = rs[q] + a[q] * gt[q];
           } else {
 #pragma unroll
-            for (int q = 0; q < 8; ++q) a[q] = rs[q] + bf16_round(a[q]);
+            for (int q = 0; q < 8; ++q) a[q] = rs[q] + a[q];
           }
         }
         const uint4 pk = pack8(a);
