@@ -166,6 +166,13 @@ __global__ void __launch_bounds__(kThreads, (TOK <= 128 ? 2 : 1))
         tma_load_2d(sA + i * kABytes, &tm_w0, &full[i], kx, tr.row0, pol_w);
         tma_load_2d(sA + i * kABytes + kABytes / 2, &tm_w1, &full[i], kx, tr.row1, pol_w);
       }
+      // The k-blocks past the ring are loaded only once MMAs free a stage: bring
+      // their weights into L2 now, so those loads do not wait on HBM.
+      for (int i = pre; i < nk && i < pre + 8; ++i) {
+        const int kx = (kb0 + i) * kBK;
+        tma_prefetch_2d(&tm_w0, kx, tr.row0);
+        tma_prefetch_2d(&tm_w1, kx, tr.row1);
+      }
       pdl_wait();
       for (int i = 0; i < pre; ++i) tma_load_2d(sB + i * kBBytes, &tm_x, &full[i], (kb0 + i) * kBK, tok0, pol_x);
       for (int i = pre; i < nk; ++i) {
