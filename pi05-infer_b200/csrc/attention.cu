@@ -446,6 +446,11 @@ int mma_sync_attention(AttnParams p, float* part, size_t part_bytes, int splits,
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   }
+  static const int force_splits = [] {
+    const char* e = getenv("PI05_ATTN_SPLITS");
+    return e != nullptr ? atoi(e) : 0;
+  }();
+  if (splits <= 0 && force_splits > 0) splits = force_splits;  // tuning
   const bool auto_splits = splits <= 0;
   if (auto_splits) {
     // Up to two CTAs per SM (a CTA's 2 warps use half of the SM's sub-partitions;

@@ -1054,10 +1054,12 @@ int wide_choose(int epi, int m_tiles, int n_cols, int kb_total, int sms, int* bn
   *splits = 1;
   *pair = 0;
   // CTA pairs pay a longer prologue and (with split-K) a slower epilogue; they win
-  // on the long-running projections: gate/up at full token tiles and long-K ones
-  // (the prefix down_proj).  PI05_WIDE_PAIR=0 / 1 disables / forces them.
-  const bool pair_auto = m_tiles >= 4 && ((epi == SK_EPI_GEGLU && kb_total >= 16) ||
-                                          ((epi == SK_EPI_STORE || epi == SK_EPI_GATED_RESID) && kb_total >= 128));
+  // on the long-running projections: gate/up and q|k|v + RoPE at full token tiles
+  // (prefix q|k|v 21.1 -> 18.4 us) and long-K ones (the prefix down_proj).
+  // PI05_WIDE_PAIR=0 / 1 disables / forces them.
+  const bool pair_auto =
+      m_tiles >= 4 && (((epi == SK_EPI_GEGLU || epi == SK_EPI_QKV_ROPE) && kb_total >= 16) ||
+                       ((epi == SK_EPI_STORE || epi == SK_EPI_GATED_RESID) && kb_total >= 128));
   if (allow_pair && (force_pair > 0 || (force_pair < 0 && pair_auto))) {
     // CTA pairs: 256 x 256 tiles; split-K (STORE / GATED_RESID) until the pairs
     // cover the SMs.
