@@ -118,3 +118,21 @@ def test_reference_custom_ops_names():
     out = torch.ops.pi05_infer.gate_up_geglu(x, wg, wu)
     assert out.shape == (1, 50, 4096)
     assert ops.fused_gate_up_geglu(x.cpu(), wg.cpu(), wu.cpu()) is None  # CPU tensors: not applicable
+
+
+@pytest.mark.parametrize("m,n,k", [(768, 1152, 1152), (768, 1152, 4352), (768, 3456, 1152), (968, 2048, 2048)],
+                         ids=["siglip_o", "siglip_fc2", "siglip_qkv", "prefix_o"])
+def test_wide_gemm_ops(m, n, k):
+    """Many-token (wide) kernel at the SigLIP / prefix shapes: 128- and 192-column tiles,
+    split-K 2 on the long-K shape; plain, gated and in-place residual epilogues."""
+    g = torch.Generator(device=DEV).manual_seed(11)
+    x = _bf(torch.randn(m, k, device=DEV, generator=g))
+    w = _bf(torch.randn(n, k, device=DEV, generator=g) * 0.02)
+    y = (x.float() @ w.float().t()).bfloat16().float()
+    _close(ops.linear(x, w), x.float() @ w.float().t())
+    resid = _bf(torch.randn(m, n, device=DEV, generator=g))
+    gate = torch.randn(n, device=DEV, generator=g)
+    _close(ops.linear_gated_residual(x, w, resid, gate), resid.float() + y * gate.bfloat16().float(), atol=2e-2)
+    r2 = resid.clone()
+    ops.linear_gated_residual(x, w, r2, None, out=r2)
+    _close(r2, resid.float() + y, atol=2e-2)
