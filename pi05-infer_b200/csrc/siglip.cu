@@ -139,28 +139,28 @@ __global__ void __launch_bounds__(128) mha72_kernel(const __nv_bfloat16* __restr
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const size_t ld = (size_t)3 * width;
   const __nv_bfloat16* base = qkv + (size_t)view * SEQ * ld + h * kHd;
-  // 9 chunks of 16 B per 72-element row, copied asynchronously (all in flight at
-  // once); chunk 9 (columns 72..79) is zero-filled.
-  for (int i = tid; i < (64 + 2 * SEQ) * 10; i += 128) {
-    const int row = i / 10, c = i % 10;
-    __nv_bfloat16* dst;
-    const __nv_bfloat16* srcp;
-    if (row < 64) {
-      dst = sQ + row * kRowE;
-      srcp = base + (size_t)(q0 + row) * ld;
-    } else if (row < 64 + SEQ) {
-      dst = sK + (row - 64) * kRowE;
-      srcp = base + (size_t)(row - 64) * ld + width;
-    } else {
-      dst = sV + (row - 64 - SEQ) * kRowE;
-      srcp = base + (size_t)(row - 64 - SEQ) * ld + 2 * width;
+  // 9 chunks of 16 B per 72-element row, copied asynchronously; chunk 9 (columns
+  // 72..79) is zero-filled.  Four commit groups: Q with keys 0..63, then keys
+  // 64c..64c+63 (K and V rows), so the key loop starts on the first 64 keys while
+  // the others are still arriving.
+  auto copy_rows = [&](__nv_bfloat16* dst0, const __nv_bfloat16* src0, int rows) {
+    for (int i = tid; i < rows * 10; i += 128) {
+      const int row = i / 10, c = i % 10;
+      const int n = c < 9 ? 16 : 0;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst0 + row * kRowE + c * 8)),
+                   "l"(src0 + (size_t)row * ld + (c < 9 ? c * 8 : 0)), "r"(n)
+                   : "memory");
     }
-    const int n = c < 9 ? 16 : 0;
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst + c * 8)),
-                 "l"(srcp + (c < 9 ? c * 8 : 0)), "r"(n)
-                 : "memory");
+  };
+  copy_rows(sQ, base + (size_t)q0 * ld, 64);
+#pragma unroll
+  for (int c = 0; c < SEQ / 64; ++c) {
+    copy_rows(sK + c * 64 * kRowE, base + (size_t)(c * 64) * ld + width, 64);
+    copy_rows(sV + c * 64 * kRowE, base + (size_t)(c * 64) * ld + 2 * width, 64);
+    asm volatile("cp.async.commit_group;" ::: "memory");
   }
-  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+  static_assert(SEQ == 256, "four key groups");
+  asm volatile("cp.async.wait_group 3;" ::: "memory");
   __syncthreads();
   const uint32_t aQ = static_cast<uint32_t>(__cvta_generic_to_shared(sQ));
   const uint32_t aK = static_cast<uint32_t>(__cvta_generic_to_shared(sK));
@@ -179,6 +179,15 @@ __global__ void __launch_bounds__(128) mha72_kernel(const __nv_bfloat16* __restr
   for (int j = 0; j < 10; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
   for (int kc = 0; kc < SEQ; kc += 64) {
+    if (kc > 0) {  // keys kc .. kc+63 (groups still in flight after this one: 3 - kc / 64)
+      if (kc == 64)
+        asm volatile("cp.async.wait_group 2;" ::: "memory");
+      else if (kc == 128)
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+      else
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+      __syncthreads();
+    }
     float s[8][4];
 #pragma unroll
     for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
