@@ -204,13 +204,17 @@ __global__ void __launch_bounds__(128) mha72_kernel(const __nv_bfloat16* __restr
     }
     float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < 8; ++j) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float v = bf16_round(bf16_round(s[j][e]) * scale);
-        s[j][e] = v;
-        mx[e >> 1] = fmaxf(mx[e >> 1], v);
+      for (int e = 0; e < 4; e += 2) {  // bf16(bf16(q.k) * scale), two values per conversion
+        bf16_round2(s[j][e], s[j][e + 1]);
+        s[j][e] *= scale;
+        s[j][e + 1] *= scale;
+        bf16_round2(s[j][e], s[j][e + 1]);
       }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) mx[e >> 1] = fmaxf(mx[e >> 1], s[j][e]);
+    }
     float corr[2];
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
