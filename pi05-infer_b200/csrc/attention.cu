@@ -158,6 +158,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   const uint32_t sQa = static_cast<uint32_t>(__cvta_generic_to_shared(sQ));
   const int g = lane >> 2, t4 = lane & 3;
   const float scale = p.scale;
+  int scale_exp;
+  const bool scale_pow2 = frexpf(scale, &scale_exp) == 0.5f;
 
   for (int ci = c_begin; ci < c_end; ++ci) {
     const int buf = (ci - c_begin) % nbuf;
@@ -198,11 +200,20 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
+      // bf16(bf16(q.k) * scale) two values per conversion (the second rounding is
+      // exact, so skipped, for a power-of-two scale); keys j*8 + 2*t4 (+1) of both
+      // rows share one 2-byte mask read.
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        bf16_round2(s[j][e], s[j][e + 1]);
+        s[j][e] *= scale;
+        s[j][e + 1] *= scale;
+        if (!scale_pow2) bf16_round2(s[j][e], s[j][e + 1]);
+      }
+      const uint32_t vk = *reinterpret_cast<const uint16_t*>(valid + j * 8 + 2 * t4);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int key = j * 8 + 2 * t4 + (e & 1);
-        float v = bfr(bfr(s[j][e]) * scale);
-        v = valid[key] ? v : -INFINITY;
+        const float v = ((vk >> ((e & 1) * 8)) & 0xffu) ? s[j][e] : -INFINITY;
         s[j][e] = v;
         mx[e >> 1] = fmaxf(mx[e >> 1], v);
       }
