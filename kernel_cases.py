@@ -12,6 +12,7 @@ launches of interest on a small device footprint:
   prefix_down    many-token GEMM + residual, M=968, N=2048, K=16384
   prefix_qkv     many-token GEMM + RoPE into the KV cache, M=968, N=10x256, K=2048
   siglip_fc1     many-token GEMM + bias + GELU, M=768, N=4304, K=1152
+  siglip_out     many-token GEMM + residual, M=768, N=1152, K=1152 (SigLIP out-proj)
   mqa_attention  denoise attention: 50 x 8 query rows over a 1018-key cache, d=256
   prefix_attention  prefix-LM attention: 968 x 8 query rows over 968 keys, d=256
                  (tcgen05 kernel, split-KV partials + combine)
@@ -35,7 +36,7 @@ sys.path.insert(0, os.path.join(HERE, "pi05-infer_b200"))
 
 from pi05_infer import abi, ops  # noqa: E402
 
-CASES = ("denoise_geglu", "denoise_down", "prefix_geglu", "prefix_down", "prefix_qkv", "siglip_fc1",
+CASES = ("denoise_geglu", "denoise_down", "prefix_geglu", "prefix_down", "prefix_qkv", "siglip_fc1", "siglip_out",
          "mqa_attention", "prefix_attention")
 
 
@@ -99,6 +100,16 @@ def build(case: str, dev="cuda"):
         w = rnd(4352, 1152, s=0.02)
         out = torch.empty(768, 4352, dtype=torch.bfloat16, device=dev)
         return (lambda: ops.linear(x, w, out=out)), None, 2 * 768 * 4352 * 1152
+    if case == "siglip_out":
+        x = rnd(768, 1152)
+        ws = [rnd(1152, 1152, s=0.02) for _ in range(27)]
+        h = rnd(768, 1152)
+        it = iter(range(1 << 60))
+
+        def f():
+            ops.linear_gated_residual(x, ws[next(it) % 27], h, None, out=h)
+
+        return f, None, 2 * 768 * 1152 * 1152
     if case == "prefix_attention":
         p, d = 968, 256
         q = rnd(p, 8, d)
