@@ -1194,16 +1194,14 @@ int wide_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int w
   }
   switch (epi) {
     case SK_EPI_STORE:
-      if (wide8) return bn == 256   ? wide_launch<SK_EPI_STORE, 256, 3, 8>(p, ws, mp, st)
-                        : bn == 192 ? wide_launch<SK_EPI_STORE, 192, 3, 8>(p, ws, mp, st)
-                                    : wide_launch<SK_EPI_STORE, 128, 5, 8>(p, ws, mp, st);
+      if (wide8) return bn == 256 ? wide_launch<SK_EPI_STORE, 256, 3, 8>(p, ws, mp, st)
+                                  : wide_launch<SK_EPI_STORE, 128, 5, 8>(p, ws, mp, st);
       return bn == 256   ? wide_launch<SK_EPI_STORE, 256, 4, 4>(p, ws, mp, st)
              : bn == 192 ? wide_launch<SK_EPI_STORE, 192, 4, 4>(p, ws, mp, st)
                          : wide_launch<SK_EPI_STORE, 128, 6, 4>(p, ws, mp, st);
     case SK_EPI_GATED_RESID:
-      if (wide8) return bn == 256   ? wide_launch<SK_EPI_GATED_RESID, 256, 3, 8>(p, ws, mp, st)
-                        : bn == 192 ? wide_launch<SK_EPI_GATED_RESID, 192, 3, 8>(p, ws, mp, st)
-                                    : wide_launch<SK_EPI_GATED_RESID, 128, 5, 8>(p, ws, mp, st);
+      if (wide8) return bn == 256 ? wide_launch<SK_EPI_GATED_RESID, 256, 3, 8>(p, ws, mp, st)
+                                  : wide_launch<SK_EPI_GATED_RESID, 128, 5, 8>(p, ws, mp, st);
       return bn == 256   ? wide_launch<SK_EPI_GATED_RESID, 256, 4, 4>(p, ws, mp, st)
              : bn == 192 ? wide_launch<SK_EPI_GATED_RESID, 192, 4, 4>(p, ws, mp, st)
                          : wide_launch<SK_EPI_GATED_RESID, 128, 6, 4>(p, ws, mp, st);
