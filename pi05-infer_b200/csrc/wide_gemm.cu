@@ -123,6 +123,27 @@ __device__ __forceinline__ bool wide_item(int unit, int i, int n_units, const Wi
   return true;
 }
 
+// Cluster split-K (CSPLIT): the two CTAs of a 2-CTA cluster take K halves of the
+// cluster's tile; CTA `rank` takes half `rank`.  One tile per cluster.
+__device__ __forceinline__ bool wide_item_cs(int unit, int i, int n_units, const WideSched& ws, int rank,
+                                             WideTile& w) {
+  const int t = unit + i * n_units;
+  if (t >= ws.m_tiles * ws.n_tiles) return false;
+  w.m = t % ws.m_tiles;
+  w.n = t / ws.m_tiles;
+  w.s = rank;
+  w.kb0 = (rank * ws.kb_total) / 2;
+  w.kb1 = ((rank + 1) * ws.kb_total) / 2;
+  w.nseg = 2;
+  return true;
+}
+
+// Receive buffers of the cluster split-K: per TMEM lane quarter, the peer's fp32
+// partial of the 64-column slab this CTA finishes ([32 rows][64], 16-byte chunks
+// XOR-swizzled by row so a thread's row reads hit distinct banks).
+constexpr int kCsRecvBytes = 4 * 32 * 64 * 4;
+__device__ __forceinline__ int cs_off(int r, int c4) { return r * 64 + ((c4 ^ (r & 15)) << 2); }
+
 // Tensor maps of one launch.  out: STORE / GATED_RESID / GEGLU output, or q_out
 // for QKV_ROPE.  in0 / in1: residual (GATED_RESID) or cos / sin (QKV_ROPE).
 // kc / vc: the K and V cache rows [0, krow0 + m_tok) (QKV_ROPE).  All epilogue
@@ -251,7 +272,7 @@ __device__ __forceinline__ int wide_epi_mask(const SkinnyParams& p) {
 template <int EPI, int BN, int F>
 __device__ __forceinline__ bool wide_epi_rows_f(const SkinnyParams& p, const WideMaps& mp, EpiWarp& e, uint32_t taddr,
                                                 int n_tile, int m0, const float* sbias, const float* scol, float ln_rs,
-                                                float ln_rm) {
+                                                float ln_rm, const float* add) {
   constexpr int NS = BN / 64;
   constexpr bool kAny = (F & kEpAny) != 0;
   const int fm = kAny ? wide_epi_mask<EPI>(p) : F;
@@ -286,6 +307,16 @@ __device__ __forceinline__ bool wide_epi_rows_f(const SkinnyParams& p, const Wid
     for (int h = 0; h < 2; ++h) {
       float v[32];
       tmem_ld32(taddr + j * 64 + h * 32, v);
+      if (add != nullptr) {  // the other K half of the tile (cluster split-K)
+#pragma unroll
+        for (int c4 = 0; c4 < 8; ++c4) {
+          const float4 t = *reinterpret_cast<const float4*>(add + cs_off(r, h * 8 + c4));
+          v[4 * c4] += t.x;
+          v[4 * c4 + 1] += t.y;
+          v[4 * c4 + 2] += t.z;
+          v[4 * c4 + 3] += t.w;
+        }
+      }
       if (EPI == SK_EPI_GATED_RESID && h == 0) ok = slab_wait(e, b, p.status) && ok;
 #pragma unroll
       for (int g4 = 0; g4 < 4; ++g4) {
@@ -369,8 +400,8 @@ __device__ __forceinline__ bool wide_epi_rows_f(const SkinnyParams& p, const Wid
 template <int EPI, int BN>
 __device__ __forceinline__ bool wide_epi_rows(const SkinnyParams& p, const WideMaps& mp, EpiWarp& e, uint32_t taddr,
                                               int n_tile, int m0, const float* sbias, const float* scol, float ln_rs,
-                                              float ln_rm) {
-#define PI05_WIDE_EPI(F) wide_epi_rows_f<EPI, BN, (F)>(p, mp, e, taddr, n_tile, m0, sbias, scol, ln_rs, ln_rm)
+                                              float ln_rm, const float* add = nullptr) {
+#define PI05_WIDE_EPI(F) wide_epi_rows_f<EPI, BN, (F)>(p, mp, e, taddr, n_tile, m0, sbias, scol, ln_rs, ln_rm, add)
   const int m = wide_epi_mask<EPI>(p);
   if (EPI == SK_EPI_STORE) {
     switch (m) {
@@ -526,7 +557,7 @@ __device__ __forceinline__ bool wide_epi_qkv(const SkinnyParams& p, const WideMa
 // barrier, which the leader arms for both; the leader's commits arrive on both
 // CTAs' barriers (one commit with a two-CTA mask); the epilogues are per CTA, the odd CTA's
 // warps signalling "accumulator drained" to the leader remotely.
-template <int EPI, int BN, int STAGES, int EW, bool PAIR>
+template <int EPI, int BN, int STAGES, int EW, bool PAIR, bool CSPLIT = false>
 __global__ void __launch_bounds__(wide_threads<EW>(), 1)
     wide_gemm_kernel(const __grid_constant__ WideMaps mp, const SkinnyParams p, const WideSched ws) {
   constexpr int kBBytes = wide_b_bytes<BN, PAIR>();
@@ -539,6 +570,8 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
   static_assert(EW == 4 || ((EPI == SK_EPI_STORE || EPI == SK_EPI_GATED_RESID) && EW == 8), "epilogue warps");
   constexpr int kET = kEW * 32;  // epilogue threads
   static_assert(BN == 128 || BN == 192 || BN == 256, "tile width");
+  static_assert(!CSPLIT || (!PAIR && BN == 128 && EW == 8 && (EPI == SK_EPI_STORE || EPI == SK_EPI_GATED_RESID)),
+                "cluster split-K: one 64-column slab per epilogue warp");
   static_assert((EPI != SK_EPI_GEGLU && EPI != SK_EPI_QKV_ROPE) || BN == 256, "paired epilogues use BN = 256");
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -546,7 +579,8 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * kABytes;
   uint8_t* sEpi = smem + STAGES * kStageBytes;  // kEW warps x kSlabs slabs, 1024-aligned
-  float* sbias = reinterpret_cast<float*>(sEpi + kEW * kSlabs * kSlabBytes);  // [BN] this tile's bias
+  uint8_t* sRecv = sEpi + kEW * kSlabs * kSlabBytes;  // CSPLIT: kCsRecvBytes of peer partials
+  float* sbias = reinterpret_cast<float*>(sRecv + (CSPLIT ? kCsRecvBytes : 0));  // [BN] this tile's bias
   constexpr bool kScol = wide_scol<EPI, BN, STAGES, EW, PAIR>();
   float* scol = sbias + BN;  // [BN] folded LayerNorm column sums (kScol)
   uint64_t* full = reinterpret_cast<uint64_t*>(sbias + (kScol ? 2 : 1) * BN);
@@ -555,7 +589,8 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
   uint64_t* acce = accf + 2;        // [2] accumulator drained (128 epilogue arrivals)
   uint64_t* mdone = acce + 2;       // all MMAs of this CTA complete
   uint64_t* sbar = mdone + 1;       // [kEW warps][2] epilogue slab loads
-  unsigned long long* s_stamp = reinterpret_cast<unsigned long long*>(sbar + 2 * kEW);  // [2] trace
+  uint64_t* rbar = sbar + 2 * kEW;  // CSPLIT: [4] peer partial of a lane quarter received
+  unsigned long long* s_stamp = reinterpret_cast<unsigned long long*>(rbar + (CSPLIT ? 4 : 0));  // [2] trace
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(s_stamp + 2);
   int* s_flag = reinterpret_cast<int*>(s_tmem + 1);  // [0] abort, [2] k-blocks armed
 
@@ -563,10 +598,13 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
   uint64_t t_setup = 0, t_acc = 0, t_epi = 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // Work units: CTAs, or CTA pairs (ws.m_tiles then counts 256-token pair tiles).
-  const int rank = PAIR ? (int)cluster_ctarank() : 0;
+  const int rank = (PAIR || CSPLIT) ? (int)cluster_ctarank() : 0;
   const bool leader = rank == 0;
-  const int unit0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
-  const int n_units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const int unit0 = (PAIR || CSPLIT) ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int n_units = (PAIR || CSPLIT) ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  auto next_item = [&](int item, WideTile& w) -> bool {
+    return CSPLIT ? wide_item_cs(unit0, item, n_units, ws, rank, w) : wide_item(unit0, item, n_units, ws, w);
+  };
   const int cta_m_tiles = PAIR ? 2 * ws.m_tiles : ws.m_tiles;  // 128-token tiles
 
   if (threadIdx.x == 0) {
@@ -580,6 +618,12 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
     }
     mbar_init(mdone, 1);
     for (int i = 0; i < 2 * kEW; ++i) mbar_init(&sbar[i], 1);
+    if (CSPLIT) {
+      for (int i = 0; i < 4; ++i) {
+        mbar_init(&rbar[i], 1);
+        mbar_arrive_expect_tx(&rbar[i], 32 * 64 * 4);  // one use per launch: one tile per cluster
+      }
+    }
     s_flag[0] = 0;
     s_flag[2] = 0;
     s_stamp[0] = 0;
@@ -611,7 +655,7 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (PAIR) {
+  if (PAIR || CSPLIT) {
     // Both CTAs' barriers are initialised before either signals the other.
     cluster_arrive_release();
     cluster_wait();
@@ -648,7 +692,7 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
         if (!PAIR || !leader) load(sB + st * kBBytes + (PAIR ? 0 : kBBytes / 2), &mp.w1, st, kb * kBK, row1, pol_w);
       };
       WideTile wt;
-      for (int item = 0; wide_item(unit0, item, n_units, ws, wt); ++item) {
+      for (int item = 0; next_item(item, wt); ++item) {
         const int m = PAIR ? 2 * wt.m + rank : wt.m;  // this CTA's 128-token tile
         int row0, row1;
         wide_rows<EPI, BN>(wt.n, row0, row1);
@@ -691,7 +735,7 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
       int it = 0, lt = 0;
       bool ok = true;
       WideTile wt;
-      for (int item = 0; ok && wide_item(unit0, item, n_units, ws, wt); ++item, ++lt) {
+      for (int item = 0; ok && next_item(item, wt); ++item, ++lt) {
         const int buf = lt & 1;
         if (!mbar_wait(&acce[buf], ((lt >> 1) & 1) ^ 1)) {
           report_status(p.status, PI05_DEV_TIMEOUT_MMA);
@@ -753,10 +797,11 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
     e.phase = 0;
     int lt = 0;
     WideTile wt;
-    for (int item = 0; wide_item(unit0, item, n_units, ws, wt); ++item, ++lt) {
+    for (int item = 0; next_item(item, wt); ++item, ++lt) {
       const int m = PAIR ? 2 * wt.m + rank : wt.m, n = wt.n;  // this CTA's 128-token tile
       const int buf = lt & 1;
-      wide_epi_prefetch<EPI, BN>(p, mp, e, n, m * kWBM);
+      // CSPLIT: a warp whose slab the peer finishes loads no residual.
+      if (!CSPLIT || e.half == rank) wide_epi_prefetch<EPI, BN>(p, mp, e, n, m * kWBM);
       if ((EPI == SK_EPI_STORE || EPI == SK_EPI_GATED_RESID) && (p.bias != nullptr || p.ln_colsum != nullptr)) {
         // Stage the tile's bias (and folded LayerNorm column sums) once; the
         // epilogue reads them as shared-memory broadcasts.
@@ -813,7 +858,41 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
         ok = wide_epi_qkv(p, mp, e, taddr, n, m * kWBM, rs);
       else {
         bool finish = true;
-        if (wt.nseg > 1) {
+        const float* add = nullptr;
+        if (CSPLIT) {
+          // The tile's two K halves: this CTA finishes slab `rank` (64 columns), the
+          // peer slab rank ^ 1.  A warp of the other slab sends its 32 rows of it,
+          // fp32, straight into the peer's receive buffer of its lane quarter (one
+          // 8 KB SM-to-SM copy completing on the peer's barrier); a warp of this
+          // CTA's slab waits for the peer's rows and adds them to its accumulator.
+          // a + b == b + a, so both CTAs' sums are the same whichever sent which.
+          const int peer = rank ^ 1;
+          if (e.half != rank) {
+            uint8_t* stg = slab_at(e, 0);  // the warp's two slabs: 8 KB
+            float* stgf = reinterpret_cast<float*>(stg);
+#pragma unroll 1
+            for (int h = 0; h < 2; ++h) {
+              float v[32];
+              tmem_ld32(taddr + e.half * 64 + h * 32, v);
+#pragma unroll
+              for (int c4 = 0; c4 < 8; ++c4)
+                *reinterpret_cast<float4*>(stgf + cs_off(lane, h * 8 + c4)) =
+                    make_float4(v[4 * c4], v[4 * c4 + 1], v[4 * c4 + 2], v[4 * c4 + 3]);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0)
+              bulk_copy_to_peer(mapa_shared(smem_u32(sRecv) + (uint32_t)(e.q * 8192), (uint32_t)peer), smem_u32(stg),
+                                8192u, mapa_shared(smem_u32(&rbar[e.q]), (uint32_t)peer));
+            finish = false;
+          } else {
+            if (!mbar_wait_cluster(&rbar[e.q], 0)) {
+              report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
+              ok = false;
+            }
+            add = reinterpret_cast<const float*>(sRecv + e.q * 8192);
+          }
+        } else if (wt.nseg > 1) {
           // Publish this segment's partial, take a ticket; the segment taking the
           // last ticket sums every segment's partial in segment order into its
           // TMEM accumulator and runs the epilogue.  No CTA waits for another.
@@ -900,7 +979,11 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
           }
         }
         if (finish) {
-          ok = wide_epi_rows<EPI, BN>(p, mp, e, taddr, n, m * kWBM, sbias, kScol ? scol : nullptr, ln_rs, ln_rm);
+          ok = wide_epi_rows<EPI, BN>(p, mp, e, taddr, n, m * kWBM, sbias, kScol ? scol : nullptr, ln_rs, ln_rm,
+                                      add) &&
+               ok;
+        } else if (CSPLIT) {
+          // Sender: no residual was prefetched.
         } else if (EPI == SK_EPI_GATED_RESID && e.lane == 0) {
           // The residual slab prefetched for this tile is not consumed: retire its load.
           ok = slab_wait(e, 0, p.status);
@@ -942,10 +1025,11 @@ __global__ void __launch_bounds__(wide_threads<EW>(), 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (PAIR) {
+  if (PAIR || CSPLIT) {
     // Neither CTA leaves (releasing shared memory the leader's MMAs read, or the
-    // barriers the other signals) before both are done; the leader's MMAs have
-    // all completed (mdone) before it arrives.
+    // barriers the other signals, or a partial the other still copies out) before
+    // both are done; the leader's MMAs have all completed (mdone) before it arrives,
+    // and a CSPLIT CTA's epilogue has received the peer's partial.
     cluster_arrive_release();
     cluster_wait();
   }
@@ -986,11 +1070,11 @@ int wide_sms() {
   return n;
 }
 
-template <int EPI, int BN, int STAGES, int EW, bool PAIR = false>
+template <int EPI, int BN, int STAGES, int EW, bool PAIR = false, bool CSPLIT = false>
 int wide_launch(const SkinnyParams& p, const WideSched& ws, const WideMaps& mp, cudaStream_t stream) {
-  constexpr int kSmem = wide_smem_bytes<EPI, BN, STAGES, EW, PAIR>();
+  constexpr int kSmem = wide_smem_bytes<EPI, BN, STAGES, EW, PAIR>() + (CSPLIT ? kCsRecvBytes : 0);
   static_assert(kSmem <= 232448, "shared memory per block");
-  auto kern = wide_gemm_kernel<EPI, BN, STAGES, EW, PAIR>;
+  auto kern = wide_gemm_kernel<EPI, BN, STAGES, EW, PAIR, CSPLIT>;
   static bool attr_done[16] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1031,6 +1115,9 @@ int wide_launch(const SkinnyParams& p, const WideSched& ws, const WideMaps& mp, 
     return launch_pdl_cluster(kern, dim3(2 * pairs), dim3(wide_threads<EW>()), kSmem, stream, pdl_enabled(),
                               dim3(2, 1, 1), mp, p, ws);
   }
+  if (CSPLIT)  // one tile per 2-CTA cluster (the launcher checks that they fit one wave)
+    return launch_pdl_cluster(kern, dim3(2 * ws.m_tiles * ws.n_tiles), dim3(wide_threads<EW>()), kSmem, stream,
+                              pdl_enabled(), dim3(2, 1, 1), mp, p, ws);
   const int grid = std::min(total, wide_sms());
   return launch_pdl(kern, dim3(grid), dim3(wide_threads<EW>()), kSmem, stream, pdl_enabled(), mp, p, ws);
 }
@@ -1102,6 +1189,27 @@ int wide_choose(int epi, int m_tiles, int n_cols, int kb_total, int sms, int* bn
   }
   if (force_bn == 128 || force_bn == 192 || force_bn == 256) *bn = force_bn;
   if (force_splits >= 1 && force_splits <= 2) *splits = force_splits;
+  // Cluster split-K (*pair = 2): the two K halves of a 128-column tile on the two
+  // CTAs of a cluster, which exchange half of their fp32 partials SM to SM and each
+  // finish one 64-column slab: no partial round trip through L2, and half the
+  // epilogue per CTA.  One tile per cluster, so every tile's pair must fit one wave.
+  // PI05_WIDE_CSPLIT=0 disables it.
+  static const int force_cs = [] {
+    const char* e = getenv("PI05_WIDE_CSPLIT");
+    return e != nullptr ? atoi(e) : -1;
+  }();
+  if (force_cs != 0 && force_bn <= 0 && force_splits <= 0 && (epi == SK_EPI_STORE || epi == SK_EPI_GATED_RESID) &&
+      kb_total >= 4 && (kb_total + 1) / 2 <= 40) {
+    const long tiles = (long)m_tiles * ((n_cols + 127) / 128);
+    if (2 * tiles <= sms) {
+      const double cost = (double)((kb_total + 1) / 2) * 0.34 + 3.0 + 1.0;
+      if (cost < best_cost - 1e-9) {
+        *bn = 128;
+        *splits = 2;
+        *pair = 2;
+      }
+    }
+  }
   return 0;
 }
 
@@ -1131,6 +1239,8 @@ int wide_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int w
   // The folded LayerNorm runs on single CTAs (its column sums are staged per CTA).
   wide_choose(epi, cta_m_tiles, n_cols, ws.kb_total, wide_sms(), &bn, &splits, &pair, p.ln_colsum == nullptr);
   // Pairs schedule 256-token tiles; every CTA still owns 128 tokens of one.
+  const bool csplit = pair == 2;
+  if (csplit) pair = 0;
   ws.m_tiles = pair ? (cta_m_tiles + 1) / 2 : cta_m_tiles;
   const int m_tiles_cta = pair ? 2 * ws.m_tiles : ws.m_tiles;
   if (epi == SK_EPI_GEGLU)
@@ -1139,7 +1249,7 @@ int wide_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int w
     ws.n_tiles = p.n_q_heads + 2 * p.n_kv_heads;
   else
     ws.n_tiles = (n_cols + bn - 1) / bn;
-  if (splits > 1) {
+  if (splits > 1 && !csplit) {
     const size_t need = (size_t)m_tiles_cta * ws.n_tiles * splits * kWBM * bn * sizeof(float);
     if (p.accum == nullptr || p.counters == nullptr || need > p.accum_bytes ||
         (long)m_tiles_cta * ws.n_tiles > kWsNormTicketBase || splits > ws.kb_total) {
@@ -1175,6 +1285,12 @@ int wide_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int w
   // which 8 warps split unevenly) keep 4 warps and a fourth stage (SigLIP 1.837 ->
   // 1.820 ms).
   const bool wide8 = bn != 192 && (ws.kb_total + ws.splits - 1) / ws.splits <= 40;
+  if (csplit) {
+    if (epi == SK_EPI_STORE) return wide_launch<SK_EPI_STORE, 128, 3, 8, false, true>(p, ws, mp, st);
+    if (epi == SK_EPI_GATED_RESID) return wide_launch<SK_EPI_GATED_RESID, 128, 3, 8, false, true>(p, ws, mp, st);
+    set_last_error("wide_gemm: cluster split-K for the row epilogues only");
+    return PI05_ERR_INVALID_ARG;
+  }
   if (pair) {
     switch (epi) {
       case SK_EPI_STORE:

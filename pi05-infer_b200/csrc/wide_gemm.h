@@ -10,9 +10,10 @@ namespace pi05 {
 int wide_gemm_run(int epi, SkinnyParams p, const void* w0, const void* w1, int w_rows0, int w_rows1, int n_cols,
                   const void* x, int ldx, void* stream);
 
-// Tile width (128 / 256), split-K count and whether a CTA pair shares each tile
-// (cta_group::2, 256 x 256 tiles) for an epilogue kind and shape; m_tiles counts
-// 128-token tiles.
+// Tile width (128 / 192 / 256), split-K count and the CTA grouping for an epilogue
+// kind and shape: *pair = 0 single CTAs, 1 a CTA pair shares each tile (cta_group::2,
+// 256 x 256 tiles), 2 cluster split-K (two CTAs take the K halves of a 128-column
+// tile and exchange partials SM to SM); m_tiles counts 128-token tiles.
 int wide_choose(int epi, int m_tiles, int n_cols, int kb_total, int sms, int* bn, int* splits, int* pair,
                 bool allow_pair = true);
 
