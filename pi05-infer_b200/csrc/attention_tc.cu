@@ -30,7 +30,9 @@
 // excluded, softmax in fp32 with a running max, probabilities enter P.V as bf16,
 // fp32 accumulation.  The exponent base is the running max held back by up to 8
 // (lazy rescaling), which changes no normalised value.  Split-KV partials use the
-// mma.sync kernel's layout and combine.
+// mma.sync kernel's layout; two splits merge inside this kernel (the second of a row
+// block's CTAs to finish merges the first's published partial), more go through the
+// combine kernel.
 #include <cuda_bf16.h>
 #include <stdint.h>
 
@@ -66,7 +68,7 @@ struct TcMaps {
 constexpr int kMaxChunks = 64;  // key chunks per CTA whose mask bytes are staged (4096 keys)
 // Ring, barriers, the row-max / row-sum exchange [6][128], the staged key mask.
 size_t tc_smem_bytes(int nst) {
-  return 1024 + kQBytes + (size_t)nst * 2 * kKVBytes + kPBytes + 32 * 8 + 6 * kBR * 4 + kMaxChunks * kBC;
+  return 1024 + kQBytes + (size_t)nst * 2 * kKVBytes + kPBytes + 44 * 8 + 6 * kBR * 4 + kMaxChunks * kBC;
 }
 
 __device__ __forceinline__ uint32_t p_off(int r, int g) { return (uint32_t)(r * 128 + ((g ^ (r & 7)) << 4)); }
@@ -108,8 +110,11 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
   uint64_t* lbar = bars + 22;  // [4] row sums, [4] mask staged
   uint64_t* v_full = bars + 28;   // [2] V chunk landed
   uint64_t* v_empty = bars + 30;  // [2] P.V of the chunk done (its V slot is free)
+  uint64_t* mrg = bars + 32;     // [2] split merge: ticket taken (256), partial published / seen (256)
+  uint64_t* mwb = bars + 34;     // [8] split merge: a warp's rows of the other split's partial landed
+  int* s_role = reinterpret_cast<int*>(bars + 42);  // split merge: ticket number of this CTA
   // Row max of each half for the two S parities [2][2][128], then the row sums [2][128].
-  float* s_red = reinterpret_cast<float*>(bars + 32);
+  float* s_red = reinterpret_cast<float*>(bars + 44);
   uint8_t* s_mask = reinterpret_cast<uint8_t*>(s_red + 6 * kBR);  // [nc * 64] key-mask bytes of this CTA
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -137,6 +142,10 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
     mbar_init(p_empty, 1);
     mbar_init(mdone, 1);
     mbar_init(&lbar[4], kSoftThreads);  // mask bytes staged
+    mbar_init(&mrg[0], kSoftThreads);
+    mbar_init(&mrg[1], kSoftThreads);
+    for (int i = 0; i < 8; ++i) mbar_init(&mwb[i], 1);
+    *s_role = 0;
     for (int i = 0; i < 4; ++i) mbar_init(&lbar[i], 64);
     s_flag[0] = 0;
     s_flag[1] = 0;
@@ -148,6 +157,7 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
     prefetch_tmap(&mp.k);
     prefetch_tmap(&mp.v);
     prefetch_tmap(p.splits == 1 ? &mp.out : &mp.po);
+    if (p.splits > 1 && p.counters != nullptr) prefetch_tmap(&mp.out);
   }
   if (warp == 1) {
     tmem_alloc(s_tmem, kTmemCols);
@@ -440,6 +450,127 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
             tma_store_2d(&mp.out, slab0 + jb * 4096, hh * 128 + jb * 64, row0 + q * 32);
           bulk_commit_group();
         }
+      } else if (p.counters != nullptr) {
+        // Two key splits merged here, not by the combine kernel: the CTA that takes
+        // the row block's first ticket publishes its partial (as below) and a flag;
+        // the one that takes the second waits (bounded) for that flag -- its peer is
+        // already running and waits on nothing -- loads the peer's partial by TMA,
+        // merges it with its own O (TMEM) in split order with the combine kernel's
+        // arithmetic, and writes the bf16 rows.  Its own partial never leaves the SM.
+        int* cnt = p.counters + 2 * blockIdx.x;  // [ticket, published]
+        if (threadIdx.x == 64) *s_role = atomicAdd(cnt, 1);
+        mbar_arrive(&mrg[0]);
+        bool mok = mbar_wait(&mrg[0], 0);
+        const int role = *s_role;
+        if (role == 0) {
+          const int y = split * p.part_rows + row0 + q * 32;
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint8_t* slab = slab0 + c * 4096;
+            float o[32];
+            tmem_ld32(tmem + lane_base + kColO + hh * 128 + c * 32, o);
+#pragma unroll
+            for (int g = 0; g < 8; ++g)
+              *reinterpret_cast<float4*>(slab + p_off(lane, g)) =
+                  make_float4(o[g * 4], o[g * 4 + 1], o[g * 4 + 2], o[g * 4 + 3]);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            for (int c = 0; c < 4; ++c) tma_store_2d(&mp.po, slab0 + c * 4096, hh * 128 + c * 32, y);
+            bulk_commit_group();
+            bulk_wait_group<0>();  // the writes themselves are done
+            fence_proxy_async_global();
+          }
+          if (hh == 0) {
+            p.part_ml[((size_t)split * p.part_rows + grow) * 2] = m;
+            p.part_ml[((size_t)split * p.part_rows + grow) * 2 + 1] = lt;
+          }
+          __syncwarp();
+          __threadfence();
+          mbar_arrive(&mrg[1]);
+          mok = mbar_wait(&mrg[1], 0) && mok;
+          if (threadIdx.x == 64) {
+            __threadfence();
+            st_release_gpu(cnt + 1, 1);
+          }
+        } else {
+          if (threadIdx.x == 64) {
+            // The peer took the first ticket, so it is running; bounded wait.
+            const uint64_t t0 = globaltimer_ns();
+            while (ld_acquire_gpu(cnt + 1) == 0) {
+              if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+                report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
+                break;
+              }
+            }
+            __threadfence();
+            fence_proxy_async_global();
+            cnt[0] = 0;  // re-armed for the next launch (the peer is done with both)
+            cnt[1] = 0;
+          }
+          mbar_arrive(&mrg[1]);
+          mok = mbar_wait(&mrg[1], 0) && mok;
+          const int other = split ^ 1;
+          uint64_t* wb = &mwb[warp - 2];
+          if (lane == 0) {
+            fence_proxy_async_global();
+            mbar_arrive_expect_tx(wb, 4 * 4096);
+            for (int c = 0; c < 4; ++c)
+              tma_load_2d(slab0 + c * 4096, &mp.po, wb, hh * 128 + c * 32, other * p.part_rows + row0 + q * 32,
+                          l2_policy_evict_first());
+          }
+          const float mo = __ldcg(p.part_ml + ((size_t)other * p.part_rows + grow) * 2);
+          const float lo = __ldcg(p.part_ml + ((size_t)other * p.part_rows + grow) * 2 + 1);
+          mok = mbar_wait(wb, 0) && mok;
+          if (!mok) report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
+          // Split order: split 0's (m, l, O) first.
+          const float m0 = split == 0 ? m : mo, l0 = split == 0 ? lt : lo;
+          const float m1 = split == 0 ? mo : m, l1 = split == 0 ? lo : lt;
+          const float mmax = fmaxf(m0, m1);
+          const float w0 = m0 != -INFINITY ? __expf(m0 - mmax) : 0.f;
+          const float w1 = m1 != -INFINITY ? __expf(m1 - mmax) : 0.f;
+          const float lsum = __fadd_rn(__fmul_rn(l0, w0), __fmul_rn(l1, w1));
+          const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+          // bf16 staging, 2 slabs per warp, in the V ring (two slots: the launcher's rule)
+          uint8_t* ob = smem + kQBytes + 2 * kKVBytes + (warp - 2) * 8192;
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            float own[32], oth[32];
+            tmem_ld32(tmem + lane_base + kColO + hh * 128 + c * 32, own);
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+              const float4 t = *reinterpret_cast<const float4*>(slab0 + c * 4096 + p_off(lane, g));
+              oth[4 * g] = t.x;
+              oth[4 * g + 1] = t.y;
+              oth[4 * g + 2] = t.z;
+              oth[4 * g + 3] = t.w;
+            }
+            float o[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float a0 = split == 0 ? own[i] : oth[i], a1 = split == 0 ? oth[i] : own[i];
+              o[i] = fmaf(a1, w1, __fmul_rn(a0, w0)) * inv;
+            }
+            uint8_t* slab = ob + (c >> 1) * 4096;
+#pragma unroll
+            for (int g4 = 0; g4 < 4; ++g4) {
+              uint4 u;
+              u.x = pack_bf16x2(o[g4 * 8 + 0], o[g4 * 8 + 1]);
+              u.y = pack_bf16x2(o[g4 * 8 + 2], o[g4 * 8 + 3]);
+              u.z = pack_bf16x2(o[g4 * 8 + 4], o[g4 * 8 + 5]);
+              u.w = pack_bf16x2(o[g4 * 8 + 6], o[g4 * 8 + 7]);
+              *reinterpret_cast<uint4*>(slab + p_off(lane, (c & 1) * 4 + g4)) = u;
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            for (int jb = 0; jb < 2; ++jb)
+              tma_store_2d(&mp.out, ob + jb * 4096, hh * 128 + jb * 64, row0 + q * 32);
+            bulk_commit_group();
+          }
+        }
       } else {
         const int y = split * p.part_rows + row0 + q * 32;
 #pragma unroll 1
@@ -565,7 +696,13 @@ int mqa_tc_attention_run(AttnParams p, float* part, size_t part_bytes, int split
   int rc = make_tmap_bf16_2d(&mp.q, p.q, p.rows, kD, p.q_stride, kBR, 64, true);
   if (!rc) rc = make_tmap_bf16_2d(&mp.k, p.k, p.kv_len, kD, p.kv_stride, kBC, 64, true);
   if (!rc) rc = make_tmap_bf16_2d(&mp.v, p.v, p.kv_len, kD, p.kv_stride, kBC, 64, true);
-  if (!rc && splits == 1) rc = make_tmap_bf16_2d(&mp.out, p.out, p.rows, kD, p.out_stride, 32, 64, true);
+  // Two splits merge inside the kernel (per-row-block ticket and flag in the
+  // workspace counters); more go through the combine kernel.
+  // (The merge stages its bf16 rows in the second V slot, so it needs two.)
+  const bool merge = splits == 2 && p.nbuf == 2 && p.counters != nullptr && 2 * row_blocks <= kWsNormTicketBase;
+  if (!merge) p.counters = nullptr;
+  if (!rc && (splits == 1 || merge))
+    rc = make_tmap_bf16_2d(&mp.out, p.out, p.rows, kD, p.out_stride, 32, 64, true);
   if (!rc && splits > 1) rc = make_tmap_f32_2d(&mp.po, p.part_o, (uint64_t)splits * p.part_rows, kD, kD, 32, 32, true);
   if (rc) return rc;
   const size_t smem = tc_smem_bytes(p.nbuf);
@@ -582,7 +719,7 @@ int mqa_tc_attention_run(AttnParams p, float* part, size_t part_bytes, int split
     attr_done[dev] = true;
   }
   rc = launch_pdl(mqa_tc_kernel, dim3(row_blocks, splits), dim3(kThreads), smem, stream, pdl_enabled(), mp, p);
-  if (rc || splits == 1) return rc;
+  if (rc || splits == 1 || merge) return rc;
   return combine(p, stream);
 }
 

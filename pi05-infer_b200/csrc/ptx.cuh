@@ -131,6 +131,24 @@ __device__ __forceinline__ void bulk_wait_group() {
 }
 
 // Make this thread's generic-proxy shared-memory writes visible to TMA.
+// Orders this thread's completed bulk (async-proxy) global writes with its later
+// generic-proxy operations (a flag that publishes them), and a generic acquire
+// with later async-proxy (TMA) reads of what it made visible.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// GPU-scope acquire load / release store of a flag in global memory.
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -83,10 +83,11 @@ def test_adarms_table(setup):
 @pytest.mark.parametrize("t,s", [(50, 1018), (50, 1530), (50, 100), (200, 968), (130, 300)],
                          ids=["p968", "p1480", "short", "prefix_tc", "ragged_tc"])
 def test_attention_op(t, s):
-    """Split counts 1, 4 and automatic.  50 tokens x 8 heads run the mma.sync kernel
+    """Split counts 1, 2, 4 and automatic.  50 tokens x 8 heads run the mma.sync kernel
     (16 splits at 1018 keys: one chunk per split, single buffered; 2 chunks per
     split at 1530 keys: double buffered); more than 1024 query rows run the
-    tcgen05 kernel (TMEM S/O, online softmax with O rescaling, MN-major V)."""
+    tcgen05 kernel (TMEM S/O, online softmax with O rescaling, MN-major V), whose two
+    key splits merge inside the kernel."""
     g = torch.Generator(device="cuda").manual_seed(5)
     h, d = 8, 256
     q = (torch.randn(t * h, d, device="cuda", generator=g) * 0.6).bfloat16()
@@ -95,7 +96,7 @@ def test_attention_op(t, s):
     valid = torch.ones(s, dtype=torch.uint8, device="cuda")
     valid[s * 7 // 8: s * 19 // 20] = 0
     ws = ops.workspace(q.device)
-    for splits in (1, 4, 0):
+    for splits in (1, 2, 4, 0):
         out = torch.empty_like(q)
         abi.attention(q, k, v, valid, out, 1 / 16, splits, ws)
         mask = torch.where(valid.bool().cpu(), 0.0, oracle.MASK_NEG)[None].expand(t, s)
