@@ -4,7 +4,7 @@
 //
 // All query heads share the single KV head, so the query rows (token, head) are
 // one [R, D] matrix and every CTA of a key range reads its K/V chunk once for 16 x
-// WARPS query rows.  The key mask depends only on the key (suffix tokens see every
+// W query rows.  The key mask depends only on the key (suffix tokens see every
 // valid prefix key and all suffix keys; valid prefix tokens see every valid prefix
 // key), so it is a byte per key.
 //
@@ -17,7 +17,8 @@
 // memory, cp.async K/V chunks of 64 keys (double-buffered when a split owns more
 // than one chunk).  Chunks of the static part of the cache (the prefix rows, written
 // long before) are fetched before the grid-dependency wait, so their latency hides
-// behind the previous kernel.
+// behind the previous kernel.  By default two warps share each 16 query rows, one
+// taking half the chunk's keys for S and half the head dims for P.V.
 //
 // Split-KV partials (unnormalised O, running max, sum) go through global memory
 // and a second kernel merges them in split order.
@@ -79,24 +80,49 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 
 __device__ __forceinline__ float bfr(float x) { return __bfloat162float(__float2bfloat16(x)); }
 
-// Shared memory of one CTA: Q rows, nbuf K and V chunk buffers, the chunk key masks.
-template <int WARPS>
-__host__ __device__ constexpr size_t attn_smem_bytes(int nbuf) {
-  return (size_t)16 * WARPS * kRowBytes + (size_t)nbuf * 2 * kChunk * kRowBytes + (size_t)nbuf * kChunk;
+// Exchange area of the warp pairs (H = 2), per row group: both warps' row maxima
+// [2][16] floats, their P fragments [2][2 k-steps][4][32 lanes] words, their row
+// sums [2][16] floats.
+template <int W, int H>
+__host__ __device__ constexpr size_t attn_xchg_bytes() {
+  return H == 1 ? 0 : (size_t)W * (2 * 16 * 4 + 2 * 2 * 4 * 32 * 4 + 2 * 16 * 4);
 }
 
-template <int WARPS>
-__global__ void __launch_bounds__(WARPS * 32, 1)
+// Shared memory of one CTA: Q rows, nbuf K and V chunk buffers, the pair exchange
+// area, the chunk key masks.
+template <int W, int H>
+__host__ __device__ constexpr size_t attn_smem_bytes(int nbuf) {
+  return (size_t)16 * W * kRowBytes + (size_t)nbuf * 2 * kChunk * kRowBytes + attn_xchg_bytes<W, H>() +
+         (size_t)nbuf * kChunk;
+}
+
+// W row groups of 16 query rows per CTA, H warps per row group.  With H = 2 the two
+// warps of a row group split each chunk: keys [32 hf, 32 hf + 32) for S = Q.K^T and
+// head dims [128 hf, 128 hf + 128) for O += P.V.  They agree on the chunk's row max
+// and hand each other their P fragments through shared memory (a named barrier of
+// the pair for each), and add their row sums at the end.  Each warp then issues half
+// the MMAs of a chunk, and an SM runs twice as many warps.
+template <int W, int H>
+__global__ void __launch_bounds__(W * H * 32, 1)
     mqa_flash_kernel(const AttnParams p) {
-  constexpr int kRows = 16 * WARPS;
+  static_assert(H == 1 || H == 2, "one or two warps per row group");
+  constexpr int kRows = 16 * W;
+  constexpr int kThreads = W * H * 32;
+  constexpr int NT = 8 / H;   // 8-key n-tiles of S per warp
+  constexpr int DT = 32 / H;  // 8-dim n-tiles of O per warp
   extern __shared__ __align__(128) uint8_t smem[];
   const int nbuf = p.nbuf;
   uint8_t* sQ = smem;                                     // kRows x 512 B
   uint8_t* sK = smem + kRows * kRowBytes;                 // nbuf x 64 x 512 B
   uint8_t* sV = sK + nbuf * kChunk * kRowBytes;           // nbuf x 64 x 512 B
-  uint8_t* sValid = sV + nbuf * kChunk * kRowBytes;       // nbuf x 64 bytes
+  uint8_t* sX = sV + nbuf * kChunk * kRowBytes;           // pair exchange (H = 2)
+  uint8_t* sValid = sX + attn_xchg_bytes<W, H>();         // nbuf x 64 bytes
+  float* sMax = reinterpret_cast<float*>(sX);                              // [W][2][16]
+  uint32_t* sP = reinterpret_cast<uint32_t*>(sX + W * 2 * 16 * 4);         // [W][2][2][4][32]
+  float* sL = reinterpret_cast<float*>(sX + W * (2 * 16 * 4 + 2 * 2 * 4 * 32 * 4));  // [W][2][16]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int rg = warp / H, hf = warp % H;
   const int row0 = blockIdx.x * kRows;
   const int split = blockIdx.y;
   // This CTA's observation (blockIdx.z; 0 without a batch).
@@ -115,7 +141,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     const int key0 = ci * kChunk;
     const uint32_t kb = static_cast<uint32_t>(__cvta_generic_to_shared(sK + buf * kChunk * kRowBytes));
     const uint32_t vb = static_cast<uint32_t>(__cvta_generic_to_shared(sV + buf * kChunk * kRowBytes));
-    for (int i = tid; i < kChunk * 32; i += WARPS * 32) {
+    for (int i = tid; i < kChunk * 32; i += kThreads) {
       const int r = i >> 5, c = i & 31;
       const int key = key0 + r;
       const bool ok = key < p.kv_len;
@@ -123,7 +149,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       cp_async16(kb + swz(r, c), kbase + off, ok);
       cp_async16(vb + swz(r, c), vbase + off, ok);
     }
-    for (int r = tid; r < kChunk; r += WARPS * 32) {
+    for (int r = tid; r < kChunk; r += kThreads) {
       const int key = key0 + r;
       sValid[buf * kChunk + r] = (key < p.kv_len && valid_base[key]) ? 1 : 0;
     }
@@ -138,7 +164,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   if (tr) t_wait = globaltimer_ns();
 
   // Q rows (zero-fill beyond R).
-  for (int i = tid; i < kRows * 32; i += WARPS * 32) {
+  for (int i = tid; i < kRows * 32; i += kThreads) {
     const int r = i >> 5, c = i & 31;
     const int gr = row0 + r;
     const bool ok = gr < p.rows;
@@ -146,9 +172,9 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
                p.q + bz * p.q_batch + (size_t)(ok ? gr : 0) * p.q_stride + c * 8, ok);
   }
 
-  float o[32][4];
+  float o[DT][4];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  for (int j = 0; j < DT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
   float m_run[2] = {-INFINITY, -INFINITY};
   float l_run[2] = {0.f, 0.f};
 
@@ -172,34 +198,35 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     const uint32_t sKa = static_cast<uint32_t>(__cvta_generic_to_shared(sK + buf * kChunk * kRowBytes));
     const uint32_t sVa = static_cast<uint32_t>(__cvta_generic_to_shared(sV + buf * kChunk * kRowBytes));
 
-    // S = Q_w (16 x 256) . K_chunk^T (256 x 64)
-    float s[8][4];
+    // S = Q_rg (16 x 256) . K_chunk^T (256 x 64 / H): keys kKeys * hf + j * 8
+    constexpr int kKeys = kChunk / H;
+    float s[NT][4];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+    for (int j = 0; j < NT; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < kD / 16; ++kk) {
       uint32_t a0, a1, a2, a3;
       {
-        const int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int r = rg * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
         const int c = kk * 2 + (lane >> 4);
         ldsm_x4(sQa + swz(r, c), a0, a1, a2, a3);
       }
 #pragma unroll
-      for (int jj = 0; jj < 4; ++jj) {  // two n-tiles of 8 keys per ldmatrix.x4
+      for (int jj = 0; jj < NT / 2; ++jj) {  // two n-tiles of 8 keys per ldmatrix.x4
         uint32_t b0, b1, b2, b3;
         const int mi = lane >> 3;
-        const int r = jj * 16 + (mi >> 1) * 8 + (lane & 7);
+        const int r = hf * kKeys + jj * 16 + (mi >> 1) * 8 + (lane & 7);
         const int c = kk * 2 + (mi & 1);
         ldsm_x4(sKa + swz(r, c), b0, b1, b2, b3);
         mma_bf16(s[2 * jj], a0, a1, a2, a3, b0, b1);
         mma_bf16(s[2 * jj + 1], a0, a1, a2, a3, b2, b3);
       }
     }
-    // scale, mask, online softmax (rows g and g+8 of this warp's 16)
-    const uint8_t* valid = sValid + buf * kChunk;
+    // scale, mask, online softmax (rows g and g+8 of this row group's 16)
+    const uint8_t* valid = sValid + buf * kChunk + hf * kKeys;
     float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < NT; ++j) {
       // bf16(bf16(q.k) * scale) two values per conversion (the second rounding is
       // exact, so skipped, for a power-of-two scale); keys j*8 + 2*t4 (+1) of both
       // rows share one 2-byte mask read.
@@ -218,18 +245,33 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
         mx[e >> 1] = fmaxf(mx[e >> 1], v);
       }
     }
-    float corr[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffff, mx[h], 1));
       mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffff, mx[h], 2));
+    }
+    if constexpr (H == 2) {
+      // The pair's chunk max: both warps take max(own, partner's) of the same two values.
+      float* mine = sMax + (rg * 2 + hf) * 16;
+      const float* other = sMax + (rg * 2 + (hf ^ 1)) * 16;
+      if (t4 == 0) {
+        mine[g] = mx[0];
+        mine[g + 8] = mx[1];
+      }
+      named_bar_sync(1 + rg, 64);
+      mx[0] = fmaxf(mx[0], other[g]);
+      mx[1] = fmaxf(mx[1], other[g + 8]);
+    }
+    float corr[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
       const float m_new = fmaxf(m_run[h], mx[h]);
       corr[h] = (m_new == -INFINITY) ? 1.f : __expf(m_run[h] - m_new);
       m_run[h] = m_new;
     }
     float ls[2] = {0.f, 0.f};
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < NT; ++j) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int h = e >> 1;
@@ -245,28 +287,57 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       l_run[h] = l_run[h] * corr[h] + ls[h];
     }
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
+    for (int j = 0; j < DT; ++j) {
       o[j][0] *= corr[0];
       o[j][1] *= corr[0];
       o[j][2] *= corr[1];
       o[j][3] *= corr[1];
     }
-    // O += P (16 x 64, bf16) . V_chunk (64 x 256)
+    // P (16 x 64, bf16) as mma A fragments: k-step kk covers keys 16 kk .. 16 kk + 15
+    // (H = 1: packed from s as the P.V loop reaches them).
+    uint32_t pa[4][4];
+    if constexpr (H == 2) {
+      // Each warp holds k-steps 2 hf, 2 hf + 1; the partner's two come through shared
+      // memory (lane-contiguous words).  The next chunk's max barrier orders the
+      // partner's reads before this warp overwrites its slots.
+      uint32_t* mine = sP + (rg * 2 + hf) * (2 * 4 * 32);
+      const uint32_t* other = sP + (rg * 2 + (hf ^ 1)) * (2 * 4 * 32);
+#pragma unroll
+      for (int kl = 0; kl < 2; ++kl) {
+        uint32_t w[4];
+        w[0] = pack_bf16(s[2 * kl][0], s[2 * kl][1]);
+        w[1] = pack_bf16(s[2 * kl][2], s[2 * kl][3]);
+        w[2] = pack_bf16(s[2 * kl + 1][0], s[2 * kl + 1][1]);
+        w[3] = pack_bf16(s[2 * kl + 1][2], s[2 * kl + 1][3]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) mine[(kl * 4 + i) * 32 + lane] = w[i];
+      }
+      named_bar_sync(1 + rg, 64);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint32_t* src = ((kk >> 1) == hf ? mine : other) + ((kk & 1) * 4) * 32 + lane;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) pa[kk][i] = src[i * 32];
+      }
+    }
+    // O[:, 256 hf / H ...] += P . V_chunk (64 x 256 / H)
 #pragma unroll
     for (int kk = 0; kk < kChunk / 16; ++kk) {
-      const uint32_t a0 = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
-      const uint32_t a1 = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
-      const uint32_t a2 = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-      const uint32_t a3 = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+      if constexpr (H == 1) {
+        pa[kk][0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
+        pa[kk][1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
+        pa[kk][2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+        pa[kk][3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+      }
 #pragma unroll
-      for (int jj = 0; jj < 16; ++jj) {  // two 8-wide d tiles per ldmatrix.x4.trans
+      for (int jj = 0; jj < DT / 2; ++jj) {  // two 8-wide d tiles per ldmatrix.x4.trans
         uint32_t b0, b1, b2, b3;
         const int mi = lane >> 3;
         const int r = kk * 16 + (mi & 1) * 8 + (lane & 7);
-        const int c = jj * 2 + (mi >> 1);
+        const int c = hf * DT + jj * 2 + (mi >> 1);
         ldsm_x4_t(sVa + swz(r, c), b0, b1, b2, b3);
-        mma_bf16(o[2 * jj], a0, a1, a2, a3, b0, b1);
-        mma_bf16(o[2 * jj + 1], a0, a1, a2, a3, b2, b3);
+        mma_bf16(o[2 * jj], pa[kk][0], pa[kk][1], pa[kk][2], pa[kk][3], b0, b1);
+        mma_bf16(o[2 * jj + 1], pa[kk][0], pa[kk][1], pa[kk][2], pa[kk][3], b2, b3);
       }
     }
     __syncthreads();
@@ -292,25 +363,38 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     }
   };
 
-  // Output: rows (warp*16 + g) and (+8), columns j*8 + 2*t4 .. +1.
+  if constexpr (H == 2) {
+    // Row sums of the pair, added in key order (warp 0's keys first).
+    float* mine = sL + (rg * 2 + hf) * 16;
+    if (t4 == 0) {
+      mine[g] = l_run[0];
+      mine[g + 8] = l_run[1];
+    }
+    named_bar_sync(1 + rg, 64);
+    const float* l0 = sL + rg * 2 * 16;
+    l_run[0] = l0[g] + l0[16 + g];
+    l_run[1] = l0[g + 8] + l0[16 + g + 8];
+  }
+  // Output: rows (rg*16 + g) and (+8), columns hf*256/H + j*8 + 2*t4 .. +1.
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
-    const int r = row0 + warp * 16 + g + h * 8;
+    const int r = row0 + rg * 16 + g + h * 8;
     if (r >= p.rows) continue;
+    const int col0 = hf * (kD / H);
     if (p.splits == 1) {
       const float inv = l_run[h] > 0.f ? 1.f / l_run[h] : 0.f;
-      __nv_bfloat16* dst = p.out + bz * p.out_batch + (size_t)r * p.out_stride;
+      __nv_bfloat16* dst = p.out + bz * p.out_batch + (size_t)r * p.out_stride + col0;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
+      for (int j = 0; j < DT; ++j) {
         *reinterpret_cast<__nv_bfloat162*>(dst + j * 8 + 2 * t4) =
             __floats2bfloat162_rn(o[j][2 * h] * inv, o[j][2 * h + 1] * inv);
       }
     } else {
-      float* dst = p.part_o + (((size_t)bz * p.splits + split) * p.part_rows + r) * kD;
+      float* dst = p.part_o + (((size_t)bz * p.splits + split) * p.part_rows + r) * kD + col0;
 #pragma unroll
-      for (int j = 0; j < 32; ++j)
+      for (int j = 0; j < DT; ++j)
         *reinterpret_cast<float2*>(dst + j * 8 + 2 * t4) = make_float2(o[j][2 * h], o[j][2 * h + 1]);
-      if (t4 == 0) {
+      if (t4 == 0 && hf == 0) {
         p.part_ml[(((size_t)bz * p.splits + split) * p.part_rows + r) * 2] = m_run[h];
         p.part_ml[(((size_t)bz * p.splits + split) * p.part_rows + r) * 2 + 1] = l_run[h];
       }
@@ -411,14 +495,14 @@ __global__ void __launch_bounds__(64) mqa_combine_kernel(const AttnParams p) {
 
 namespace {
 
-template <int W>
+template <int W, int H>
 int set_attn_smem() {
   static bool done[16] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 16 && done[dev]) return PI05_OK;
-  cudaError_t e = cudaFuncSetAttribute(mqa_flash_kernel<W>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)attn_smem_bytes<W>(2));
+  cudaError_t e = cudaFuncSetAttribute(mqa_flash_kernel<W, H>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)attn_smem_bytes<W, H>(2));
   if (e != cudaSuccess) {
     set_last_error("attention smem attr: %s", cudaGetErrorString(e));
     return PI05_ERR_LAUNCH;
@@ -444,9 +528,10 @@ int launch_combine(const AttnParams& p, cudaStream_t st) {
   return launch_pdl(mqa_combine_kernel, dim3((p.rows + 1) / 2, p.batch), dim3(64), 0, st, pdl_enabled(), p);
 }
 
-// mma.sync path: W warps of 16 query rows per CTA (default 2, which halves the
-// per-CTA tensor work of a chunk; PI05_ATTN_WARPS=4 selects 4, for tuning).
-template <int W>
+// mma.sync path: W row groups of 16 query rows per CTA, H warps per row group
+// (default W = 2, H = 2; PI05_ATTN_WARPS=4 selects W = 4, PI05_ATTN_PAIR=0 H = 1,
+// for tuning).
+template <int W, int H>
 int mma_sync_attention(AttnParams p, float* part, size_t part_bytes, int splits, cudaStream_t st) {
   constexpr int kRows = 16 * W;
   const int row_blocks = (p.rows + kRows - 1) / kRows;
@@ -473,7 +558,7 @@ int mma_sync_attention(AttnParams p, float* part, size_t part_bytes, int splits,
   splits = splits > 32 ? 32 : splits;
   p.splits = splits;
   p.nbuf = (n_chunks + splits - 1) / splits > 1 ? 2 : 1;
-  const size_t smem = attn_smem_bytes<W>(p.nbuf);
+  const size_t smem = attn_smem_bytes<W, H>(p.nbuf);
   if (splits > 1) {
     const size_t need_o = (size_t)p.batch * splits * p.rows * kD * sizeof(float);
     const size_t need = need_o + (size_t)p.batch * splits * p.rows * 2 * sizeof(float);
@@ -485,9 +570,10 @@ int mma_sync_attention(AttnParams p, float* part, size_t part_bytes, int splits,
     p.part_o = part;
     p.part_ml = part + (size_t)p.batch * splits * p.rows * kD;
   }
-  int rc = set_attn_smem<W>();
+  int rc = set_attn_smem<W, H>();
   if (rc) return rc;
-  rc = launch_pdl(mqa_flash_kernel<W>, dim3(row_blocks, splits, p.batch), dim3(W * 32), smem, st, pdl_enabled(), p);
+  rc = launch_pdl(mqa_flash_kernel<W, H>, dim3(row_blocks, splits, p.batch), dim3(W * H * 32), smem, st,
+                  pdl_enabled(), p);
   if (rc || splits == 1) return rc;
   return launch_combine(p, st);
 }
@@ -510,8 +596,14 @@ int mqa_attention_run(AttnParams p, float* part, size_t part_bytes, int splits, 
     const char* e = getenv("PI05_ATTN_WARPS");
     return (e != nullptr && atoi(e) == 4) ? 4 : 2;
   }();
-  return warps == 2 ? mma_sync_attention<2>(p, part, part_bytes, splits, st)
-                    : mma_sync_attention<4>(p, part, part_bytes, splits, st);
+  static const bool pair = [] {
+    const char* e = getenv("PI05_ATTN_PAIR");
+    return e == nullptr || atoi(e) != 0;
+  }();
+  if (warps == 4) return pair ? mma_sync_attention<4, 2>(p, part, part_bytes, splits, st)
+                              : mma_sync_attention<4, 1>(p, part, part_bytes, splits, st);
+  return pair ? mma_sync_attention<2, 2>(p, part, part_bytes, splits, st)
+              : mma_sync_attention<2, 1>(p, part, part_bytes, splits, st);
 }
 
 }  // namespace pi05

@@ -9,7 +9,9 @@ cosine >= 0.9999):
   PI05_FOLD_NORM=0    explicit adaRMS norm kernels instead of the default folded
                       norms (norm modulation folded into per-step q|k|v and
                       gate/up weights, rstd and bias applied to the accumulators)
-  PI05_ATTN_WARPS=4   4-warp (64-row) attention CTAs instead of 2-warp ones
+  PI05_ATTN_WARPS=4   64-row attention CTAs instead of 32-row ones
+  PI05_ATTN_PAIR=0    one warp per 16 query rows instead of a warp pair that splits
+                      each key chunk (keys for S, head dims for P.V)
   PI05_PDL=0          launches without programmatic dependent launch
 """
 
@@ -49,7 +51,7 @@ torch.save(out, sys.argv[2])
 
 def _run(env_extra, path):
     env = dict(os.environ)
-    for k in ("PI05_FOLD_NORM", "PI05_ATTN_WARPS", "PI05_PDL"):
+    for k in ("PI05_FOLD_NORM", "PI05_ATTN_WARPS", "PI05_ATTN_PAIR", "PI05_PDL"):
         env.pop(k, None)
     env.update(env_extra)
     subprocess.run([sys.executable, "-c", _SCRIPT, PKG_ROOT, path], env=env, check=True, timeout=600)
@@ -63,8 +65,8 @@ def default_actions(tmp_path_factory):
 
 @pytest.mark.parametrize(
     "switch",
-    [{"PI05_FOLD_NORM": "0"}, {"PI05_ATTN_WARPS": "4"}, {"PI05_PDL": "0"}],
-    ids=["norm_kernels", "attn_4warps", "no_pdl"],
+    [{"PI05_FOLD_NORM": "0"}, {"PI05_ATTN_WARPS": "4"}, {"PI05_ATTN_PAIR": "0"}, {"PI05_PDL": "0"}],
+    ids=["norm_kernels", "attn_4warps", "attn_single_warps", "no_pdl"],
 )
 def test_switch_matches_default(default_actions, switch, tmp_path):
     got = _run(switch, str(tmp_path / "variant.pt"))
