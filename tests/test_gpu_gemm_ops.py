@@ -120,11 +120,13 @@ def test_reference_custom_ops_names():
     assert ops.fused_gate_up_geglu(x.cpu(), wg.cpu(), wu.cpu()) is None  # CPU tensors: not applicable
 
 
-@pytest.mark.parametrize("m,n,k", [(768, 1152, 1152), (768, 1152, 4352), (768, 3456, 1152), (968, 2048, 2048)],
-                         ids=["siglip_o", "siglip_fc2", "siglip_qkv", "prefix_o"])
+@pytest.mark.parametrize("m,n,k", [(768, 1152, 1152), (768, 1152, 4352), (768, 3456, 1152), (968, 2048, 2048),
+                                   (600, 2048, 2048)],
+                         ids=["siglip_o", "siglip_fc2", "siglip_qkv", "prefix_o", "prefix_o_odd_pairs"])
 def test_wide_gemm_ops(m, n, k):
     """Many-token (wide) kernel at the SigLIP / prefix shapes: 128- and 192-column tiles,
-    split-K 2 on the long-K shape; plain, gated and in-place residual epilogues."""
+    cluster split-K on the SigLIP row epilogues, a ragged last token tile (600 tokens);
+    plain, gated and in-place residual epilogues."""
     g = torch.Generator(device=DEV).manual_seed(11)
     x = _bf(torch.randn(m, k, device=DEV, generator=g))
     w = _bf(torch.randn(n, k, device=DEV, generator=g) * 0.02)
