@@ -416,18 +416,24 @@ __global__ void __launch_bounds__(64) mqa_combine_kernel(const AttnParams p) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const uint64_t t_wait = tr ? globaltimer_ns() : 0;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (tr) {
-    // Trace record {(tag + 1) << 32 | cta, entry, grid-dependency wait done, 0, 0, 0, 0, 0}.
+  // Trace record {(tag + 1) << 32 | cta, entry, grid-dependency wait done, this
+  // thread's row written, 0, 0, 0, 0}.
+  auto trace_out = [&]() {
+    if (!tr) return;
     const unsigned long long slot = atomicAdd(p.trace, 1ull);
     if (slot < p.trace[1]) {
       unsigned long long* w = p.trace + 8 + slot * 8;
       w[0] = ((unsigned long long)(p.trace_tag + 1) << 32) | blockIdx.x;
       w[1] = t_entry;
       w[2] = t_wait;
-      w[3] = w[4] = w[5] = w[6] = w[7] = 0;
+      w[3] = globaltimer_ns();
+      w[4] = w[5] = w[6] = w[7] = 0;
     }
+  };
+  if (warp >= p.rows) {
+    trace_out();
+    return;
   }
-  if (warp >= p.rows) return;
   const int r = warp;
   // Observation blockIdx.y: its partials and output rows.
   const size_t bz = blockIdx.y;
@@ -489,6 +495,7 @@ __global__ void __launch_bounds__(64) mqa_combine_kernel(const AttnParams p) {
   pk.z = pack_bf16(acc[4], acc[5]);
   pk.w = pack_bf16(acc[6], acc[7]);
   *reinterpret_cast<uint4*>(dst) = pk;
+  trace_out();
 }
 
 }  // namespace
@@ -549,10 +556,13 @@ int mma_sync_attention(AttnParams p, float* part, size_t part_bytes, int splits,
   if (splits <= 0 && force_splits > 0) splits = force_splits;  // tuning
   const bool auto_splits = splits <= 0;
   if (auto_splits) {
-    // Up to two CTAs per SM (a CTA's 2 warps use half of the SM's sub-partitions;
-    // the key loop is bound by the mma.sync rate per sub-partition).
+    // Single warps: up to two CTAs per SM (a CTA's 2 warps use half of the SM's
+    // sub-partitions; the key loop is bound by the mma.sync rate per sub-partition).
+    // Warp pairs: up to one CTA per SM, so a split of the denoise owns two chunks
+    // and loads the second during the first (682 vs 694 us/step with 16 splits).
+    const int per_sm = H == 2 ? 1 : 2;
     splits = 1;
-    while (row_blocks * p.batch * splits * 2 <= 2 * sms && splits * 2 <= n_chunks) splits *= 2;
+    while (row_blocks * p.batch * splits * 2 <= per_sm * sms && splits * 2 <= n_chunks) splits *= 2;
   }
   splits = splits > n_chunks ? n_chunks : splits;
   splits = splits > 32 ? 32 : splits;
