@@ -155,10 +155,14 @@ __global__ void __launch_bounds__(W * H * 32, 1)
     }
   };
 
-  // The first chunk's K, V and mask come from the static rows when the whole chunk
-  // lies below static_rows: fetch them before waiting on the previous kernel.
+  // The first chunks' K, V and mask come from the static rows when a whole chunk
+  // lies below static_rows: fetch them (one per buffer) before waiting on the
+  // previous kernel.
   const bool first_static = c_begin < c_end && (c_begin + 1) * kChunk <= p.static_rows;
+  const bool second_static =
+      first_static && nbuf == 2 && c_begin + 1 < c_end && (c_begin + 2) * kChunk <= p.static_rows;
   if (first_static) load_chunk(c_begin, 0);
+  if (second_static) load_chunk(c_begin + 1, 1);
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (tr) t_wait = globaltimer_ns();
@@ -189,7 +193,7 @@ __global__ void __launch_bounds__(W * H * 32, 1)
 
   for (int ci = c_begin; ci < c_end; ++ci) {
     const int buf = (ci - c_begin) % nbuf;
-    if (ci + 1 < c_end) load_chunk(ci + 1, (buf + 1) % nbuf);
+    if (ci + 1 < c_end && !(second_static && ci == c_begin)) load_chunk(ci + 1, (buf + 1) % nbuf);
     cp_commit();
     cp_wait<1>();
     __syncthreads();
