@@ -121,12 +121,13 @@ def test_reference_custom_ops_names():
 
 
 @pytest.mark.parametrize("m,n,k", [(768, 1152, 1152), (768, 1152, 4352), (768, 3456, 1152), (968, 2048, 2048),
-                                   (600, 2048, 2048)],
-                         ids=["siglip_o", "siglip_fc2", "siglip_qkv", "prefix_o", "prefix_o_odd_pairs"])
+                                   (600, 2048, 2048), (968, 2048, 16384)],
+                         ids=["siglip_o", "siglip_fc2", "siglip_qkv", "prefix_o", "prefix_o_ragged", "prefix_down"])
 def test_wide_gemm_ops(m, n, k):
     """Many-token (wide) kernel at the SigLIP / prefix shapes: 128- and 192-column tiles,
-    cluster split-K on the SigLIP row epilogues, a ragged last token tile (600 tokens);
-    plain, gated and in-place residual epilogues."""
+    cluster split-K on the SigLIP row epilogues, a ragged last token tile (600 tokens),
+    CTA pairs with split-K 2 through the ticketed partials on the long-K prefix
+    down_proj; plain, gated and in-place residual epilogues."""
     g = torch.Generator(device=DEV).manual_seed(11)
     x = _bf(torch.randn(m, k, device=DEV, generator=g))
     w = _bf(torch.randn(n, k, device=DEV, generator=g) * 0.02)
