@@ -15,7 +15,9 @@ launches of interest on a small device footprint:
   siglip_out     many-token GEMM + residual, M=768, N=1152, K=1152 (SigLIP out-proj)
   mqa_attention  denoise attention: 50 x 8 query rows over a 1018-key cache, d=256
   prefix_attention  prefix-LM attention: 968 x 8 query rows over 968 keys, d=256
-                 (tcgen05 kernel, split-KV partials + combine)
+                 (tcgen05 kernel, two key splits merged in-kernel)
+  siglip_attention  SigLIP attention: 3 views x 16 heads, 256 x 256, head_dim 72,
+                 one launch per layer over 27 layers of q|k|v (143 MB > L2)
 
 ``python kernel_cases.py duel`` runs the same-box comparison with the reference's
 own Triton kernels (``_geglu_mm_kernel`` and ``_qkv_rope_kernel`` of
@@ -37,7 +39,7 @@ sys.path.insert(0, os.path.join(HERE, "pi05-infer_b200"))
 from pi05_infer import abi, ops  # noqa: E402
 
 CASES = ("denoise_geglu", "denoise_down", "prefix_geglu", "prefix_down", "prefix_qkv", "siglip_fc1", "siglip_out",
-         "mqa_attention", "prefix_attention")
+         "mqa_attention", "prefix_attention", "siglip_attention")
 
 
 def _bf(t):
@@ -136,6 +138,24 @@ def build(case: str, dev="cuda"):
             abi.attention(q, k, v, valid, out, 1.0 / math.sqrt(d), 0, wsp)
 
         return f, (p + s) * d * 2 * 2 + 2 * s * 8 * d * 2, 4 * s * 8 * (p + s) * d
+    if case == "siglip_attention":
+        import ctypes
+
+        from pi05_infer import vision
+
+        views, seq, width, heads, hd = 3, 256, 1152, 16, 72
+        qkvs = [rnd(views * seq, 3 * width) for _ in range(27)]
+        out = torch.empty(views * seq, width, dtype=torch.bfloat16, device=dev)
+        fn = vision._bind().pi05_siglip_attention
+        it = iter(range(1 << 60))
+
+        def f():
+            rc = fn(ctypes.c_void_p(qkvs[next(it) % 27].data_ptr()), views, seq, width, heads, hd,
+                    ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+            if rc != 0:
+                raise RuntimeError(f"pi05_siglip_attention: {rc}")
+
+        return f, views * seq * 4 * width * 2, 4 * views * heads * seq * seq * hd
     raise ValueError(case)
 
 
