@@ -39,8 +39,7 @@ struct AttnParams {
   size_t kv_batch = 0;
   size_t valid_batch = 0;
   size_t out_batch = 0;
-  int* counters = nullptr;  // tcgen05 kernel, two key splits: per row block [ticket, published]
-                            // (zero between launches); with them the splits merge in-kernel
+  int cluster_merge = 0;  // set by the launcher: the tcgen05 kernel's two key splits merge on 2-CTA clusters
 };
 
 // splits <= 0 picks a split count that covers the SMs.  head_dim 256 runs on the

@@ -30,9 +30,9 @@
 // excluded, softmax in fp32 with a running max, probabilities enter P.V as bf16,
 // fp32 accumulation.  The exponent base is the running max held back by up to 8
 // (lazy rescaling), which changes no normalised value.  Split-KV partials use the
-// mma.sync kernel's layout; two splits merge inside this kernel (the second of a row
-// block's CTAs to finish merges the first's published partial), more go through the
-// combine kernel.
+// mma.sync kernel's layout; two splits merge inside this kernel (the row block's two
+// split CTAs form a cluster and exchange halves of O through distributed shared
+// memory), more go through the combine kernel.
 #include <cuda_bf16.h>
 #include <stdint.h>
 
@@ -66,6 +66,8 @@ struct TcMaps {
 };
 
 constexpr int kMaxChunks = 64;  // key chunks per CTA whose mask bytes are staged (4096 keys)
+constexpr uint32_t kMrgRowBytes = 32 * 128 * 4;  // split merge: a lane quarter's rows of one O half (fp32)
+constexpr uint32_t kMrgMlBytes = 32 * 2 * 4;     // and their (m, l) pairs
 // Ring, barriers, the row-max / row-sum exchange [6][128], the staged key mask.
 size_t tc_smem_bytes(int nst) {
   return 1024 + kQBytes + (size_t)nst * 2 * kKVBytes + kPBytes + 44 * 8 + 6 * kBR * 4 + kMaxChunks * kBC;
@@ -110,9 +112,8 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
   uint64_t* lbar = bars + 22;  // [4] row sums, [4] mask staged
   uint64_t* v_full = bars + 28;   // [2] V chunk landed
   uint64_t* v_empty = bars + 30;  // [2] P.V of the chunk done (its V slot is free)
-  uint64_t* mrg = bars + 32;     // [2] split merge: ticket taken (256), partial published / seen (256)
-  uint64_t* mwb = bars + 34;     // [8] split merge: a warp's rows of the other split's partial landed
-  int* s_role = reinterpret_cast<int*>(bars + 42);  // split merge: ticket number of this CTA
+  uint64_t* rfree = bars + 32;   // split merge: the peer CTA's rings are free (one remote arrival)
+  uint64_t* rrecv = bars + 34;   // [4] split merge: the peer's rows of a lane quarter landed
   // Row max of each half for the two S parities [2][2][128], then the row sums [2][128].
   float* s_red = reinterpret_cast<float*>(bars + 44);
   uint8_t* s_mask = reinterpret_cast<uint8_t*>(s_red + 6 * kBR);  // [nc * 64] key-mask bytes of this CTA
@@ -142,22 +143,24 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
     mbar_init(p_empty, 1);
     mbar_init(mdone, 1);
     mbar_init(&lbar[4], kSoftThreads);  // mask bytes staged
-    mbar_init(&mrg[0], kSoftThreads);
-    mbar_init(&mrg[1], kSoftThreads);
-    for (int i = 0; i < 8; ++i) mbar_init(&mwb[i], 1);
-    *s_role = 0;
+    mbar_init(rfree, 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&rrecv[i], 1);
     for (int i = 0; i < 4; ++i) mbar_init(&lbar[i], 64);
     s_flag[0] = 0;
     s_flag[1] = 0;
     s_flag[2] = 0;
     fence_mbar_init();
+    // Split merge: each lane quarter receives the peer's 32 rows x 128 fp32 columns
+    // and their (m, l) pairs.
+    if (p.cluster_merge)
+      for (int i = 0; i < 4; ++i) mbar_arrive_expect_tx(&rrecv[i], kMrgRowBytes + kMrgMlBytes);
   }
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&mp.q);
     prefetch_tmap(&mp.k);
     prefetch_tmap(&mp.v);
     prefetch_tmap(p.splits == 1 ? &mp.out : &mp.po);
-    if (p.splits > 1 && p.counters != nullptr) prefetch_tmap(&mp.out);
+    if (p.cluster_merge) prefetch_tmap(&mp.out);
   }
   if (warp == 1) {
     tmem_alloc(s_tmem, kTmemCols);
@@ -165,6 +168,12 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
   }
   tc_fence_before();
   __syncthreads();
+  // Split merge: both CTAs' barriers are initialised and armed before either
+  // signals or copies into the other.
+  if (p.cluster_merge) {
+    cluster_arrive_release();
+    cluster_wait();
+  }
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
 
@@ -450,80 +459,51 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
             tma_store_2d(&mp.out, slab0 + jb * 4096, hh * 128 + jb * 64, row0 + q * 32);
           bulk_commit_group();
         }
-      } else if (p.counters != nullptr) {
-        // Two key splits merged here, not by the combine kernel: the CTA that takes
-        // the row block's first ticket publishes its partial (as below) and a flag;
-        // the one that takes the second waits (bounded) for that flag -- its peer is
-        // already running and waits on nothing -- loads the peer's partial by TMA,
-        // merges it with its own O (TMEM) in split order with the combine kernel's
-        // arithmetic, and writes the bf16 rows.  Its own partial never leaves the SM.
-        int* cnt = p.counters + 2 * blockIdx.x;  // [ticket, published]
-        if (threadIdx.x == 64) *s_role = atomicAdd(cnt, 1);
-        mbar_arrive(&mrg[0]);
-        bool mok = mbar_wait(&mrg[0], 0);
-        const int role = *s_role;
-        if (role == 0) {
-          const int y = split * p.part_rows + row0 + q * 32;
+      } else if (p.cluster_merge) {
+        // Two key splits merged here, not by the combine kernel: the row block's two
+        // split CTAs form a cluster (rank = split).  Each finishes the O half hh ==
+        // rank of its rows.  Once a CTA's MMAs are done its Q, K and P buffers are
+        // free, and it tells the peer so; the warps of the other half then push their
+        // 32 rows of that half (fp32) and the rows' (m, l) into the peer's K ring and
+        // P buffer (one SM-to-SM bulk copy each, completing on the peer's barrier of
+        // the lane quarter), and the warps of this CTA's half wait for the peer's
+        // rows and merge them with their own O from TMEM in split order with the
+        // combine kernel's arithmetic.  No partial goes through global memory.
+        const int rank = split;
+        const uint32_t peer = (uint32_t)(rank ^ 1);
+        if (threadIdx.x == 64) mbar_arrive_cluster(mapa_shared(smem_u32(rfree), peer));
+        if (hh != rank) {
+          bool sok = true;
+          if (lane == 0) sok = mbar_wait_cluster(rfree, 0);
+          sok = __shfl_sync(0xffffffffu, sok ? 1 : 0, 0) != 0;
+          if (!sok) report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
+          uint8_t* stg = sQ + q * kMrgRowBytes;
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
-            uint8_t* slab = slab0 + c * 4096;
             float o[32];
             tmem_ld32(tmem + lane_base + kColO + hh * 128 + c * 32, o);
 #pragma unroll
             for (int g = 0; g < 8; ++g)
-              *reinterpret_cast<float4*>(slab + p_off(lane, g)) =
+              *reinterpret_cast<float4*>(stg + c * 4096 + p_off(lane, g)) =
                   make_float4(o[g * 4], o[g * 4 + 1], o[g * 4 + 2], o[g * 4 + 3]);
           }
+          float* mls = reinterpret_cast<float*>(sP + q * kMrgMlBytes);
+          mls[2 * lane] = m;
+          mls[2 * lane + 1] = lt;
           fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0) {
-            for (int c = 0; c < 4; ++c) tma_store_2d(&mp.po, slab0 + c * 4096, hh * 128 + c * 32, y);
-            bulk_commit_group();
-            bulk_wait_group<0>();  // the writes themselves are done
-            fence_proxy_async_global();
-          }
-          if (hh == 0) {
-            p.part_ml[((size_t)split * p.part_rows + grow) * 2] = m;
-            p.part_ml[((size_t)split * p.part_rows + grow) * 2 + 1] = lt;
-          }
-          __syncwarp();
-          __threadfence();
-          mbar_arrive(&mrg[1]);
-          mok = mbar_wait(&mrg[1], 0) && mok;
-          if (threadIdx.x == 64) {
-            __threadfence();
-            st_release_gpu(cnt + 1, 1);
+          if (lane == 0 && sok) {
+            const uint32_t pb = mapa_shared(smem_u32(&rrecv[q]), peer);
+            bulk_copy_to_peer(mapa_shared(smem_u32(sK + q * kMrgRowBytes), peer), smem_u32(stg), kMrgRowBytes, pb);
+            bulk_copy_to_peer(mapa_shared(smem_u32(sP + 4096 + q * kMrgMlBytes), peer), smem_u32(mls), kMrgMlBytes,
+                              pb);
           }
         } else {
-          if (threadIdx.x == 64) {
-            // The peer took the first ticket, so it is running; bounded wait.
-            const uint64_t t0 = globaltimer_ns();
-            while (ld_acquire_gpu(cnt + 1) == 0) {
-              if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
-                report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
-                break;
-              }
-            }
-            __threadfence();
-            fence_proxy_async_global();
-            cnt[0] = 0;  // re-armed for the next launch (the peer is done with both)
-            cnt[1] = 0;
-          }
-          mbar_arrive(&mrg[1]);
-          mok = mbar_wait(&mrg[1], 0) && mok;
-          const int other = split ^ 1;
-          uint64_t* wb = &mwb[warp - 2];
-          if (lane == 0) {
-            fence_proxy_async_global();
-            mbar_arrive_expect_tx(wb, 4 * 4096);
-            for (int c = 0; c < 4; ++c)
-              tma_load_2d(slab0 + c * 4096, &mp.po, wb, hh * 128 + c * 32, other * p.part_rows + row0 + q * 32,
-                          l2_policy_evict_first());
-          }
-          const float mo = __ldcg(p.part_ml + ((size_t)other * p.part_rows + grow) * 2);
-          const float lo = __ldcg(p.part_ml + ((size_t)other * p.part_rows + grow) * 2 + 1);
-          mok = mbar_wait(wb, 0) && mok;
-          if (!mok) report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
+          // Every lane waits: the phase makes the peer's bulk writes visible to it.
+          if (!mbar_wait_cluster(&rrecv[q], 0)) report_status(p.status, PI05_DEV_TIMEOUT_EPILOGUE);
+          const uint8_t* rcv = sK + q * kMrgRowBytes;
+          const float* mlr = reinterpret_cast<const float*>(sP + 4096 + q * kMrgMlBytes);
+          const float mo = mlr[2 * lane], lo = mlr[2 * lane + 1];
           // Split order: split 0's (m, l, O) first.
           const float m0 = split == 0 ? m : mo, l0 = split == 0 ? lt : lo;
           const float m1 = split == 0 ? mo : m, l1 = split == 0 ? lo : lt;
@@ -540,7 +520,7 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
             tmem_ld32(tmem + lane_base + kColO + hh * 128 + c * 32, own);
 #pragma unroll
             for (int g = 0; g < 8; ++g) {
-              const float4 t = *reinterpret_cast<const float4*>(slab0 + c * 4096 + p_off(lane, g));
+              const float4 t = *reinterpret_cast<const float4*>(rcv + c * 4096 + p_off(lane, g));
               oth[4 * g] = t.x;
               oth[4 * g + 1] = t.y;
               oth[4 * g + 2] = t.z;
@@ -634,6 +614,12 @@ __global__ void __launch_bounds__(kThreads, 1) mqa_tc_kernel(const __grid_consta
   }
   tc_fence_before();
   __syncthreads();
+  // Split merge: neither CTA leaves while the other may still signal or copy into
+  // its shared memory.
+  if (p.cluster_merge) {
+    cluster_arrive_release();
+    cluster_wait();
+  }
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
@@ -696,11 +682,11 @@ int mqa_tc_attention_run(AttnParams p, float* part, size_t part_bytes, int split
   int rc = make_tmap_bf16_2d(&mp.q, p.q, p.rows, kD, p.q_stride, kBR, 64, true);
   if (!rc) rc = make_tmap_bf16_2d(&mp.k, p.k, p.kv_len, kD, p.kv_stride, kBC, 64, true);
   if (!rc) rc = make_tmap_bf16_2d(&mp.v, p.v, p.kv_len, kD, p.kv_stride, kBC, 64, true);
-  // Two splits merge inside the kernel (per-row-block ticket and flag in the
-  // workspace counters); more go through the combine kernel.
-  // (The merge stages its bf16 rows in the second V slot, so it needs two.)
-  const bool merge = splits == 2 && p.nbuf == 2 && p.counters != nullptr && 2 * row_blocks <= kWsNormTicketBase;
-  if (!merge) p.counters = nullptr;
+  // Two splits merge inside the kernel on 2-CTA clusters; more go through the
+  // combine kernel.  (The merge receives into the K ring and stages its bf16 rows in
+  // the V ring, so it needs two slots of each.)
+  const bool merge = splits == 2 && p.nbuf == 2;
+  p.cluster_merge = merge ? 1 : 0;
   if (!rc && (splits == 1 || merge))
     rc = make_tmap_bf16_2d(&mp.out, p.out, p.rows, kD, p.out_stride, 32, 64, true);
   if (!rc && splits > 1) rc = make_tmap_f32_2d(&mp.po, p.part_o, (uint64_t)splits * p.part_rows, kD, kD, 32, 32, true);
@@ -718,7 +704,11 @@ int mqa_tc_attention_run(AttnParams p, float* part, size_t part_bytes, int split
     }
     attr_done[dev] = true;
   }
-  rc = launch_pdl(mqa_tc_kernel, dim3(row_blocks, splits), dim3(kThreads), smem, stream, pdl_enabled(), mp, p);
+  if (merge)
+    rc = launch_pdl_cluster(mqa_tc_kernel, dim3(row_blocks, splits), dim3(kThreads), smem, stream, pdl_enabled(),
+                            dim3(1, 2, 1), mp, p);
+  else
+    rc = launch_pdl(mqa_tc_kernel, dim3(row_blocks, splits), dim3(kThreads), smem, stream, pdl_enabled(), mp, p);
   if (rc || splits == 1 || merge) return rc;
   return combine(p, stream);
 }

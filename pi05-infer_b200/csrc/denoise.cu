@@ -101,7 +101,6 @@ int pi05_attention(const void* q, const void* k, const void* v, const uint8_t* k
   p.kv_len = kv_len;
   p.head_dim = head_dim;
   p.status = w.status;
-  p.counters = w.counters;
   p.scale = scale;
   p.trace = debug_trace_buffer();
   return mqa_attention_run(p, w.scratch, w.scratch_bytes, splits, stream);

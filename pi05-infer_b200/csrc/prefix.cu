@@ -176,7 +176,6 @@ int pi05_prefix_forward(const Pi05PrefixPlan* P, void* stream) {
       ap.kv_len = T;
       ap.head_dim = D;
       ap.status = ws.status;
-      ap.counters = ws.counters;
       ap.scale = scale;
       rc = mqa_attention_run(ap, ws.scratch, ws.scratch_bytes, 0, stream);
       if (rc) break;
