@@ -9,8 +9,8 @@
 //   out   = LN_post(h) @ Wproj^T + b                written into the prefix buffer
 //
 // The GEMMs use the swap-AB tcgen05 kernel (bias / GELU / residual epilogues).
-// Attention here is per-head (16 heads x 72 dims, 256 tokens per view, no mask):
-// mma.sync flash kernel, head dim zero-padded to 80.
+// Attention is per head (16 heads x 72 dims, 256 tokens per view, no mask), a
+// tcgen05 kernel over whole rows (siglip_attn_tc.cu).
 #include <cmath>
 #include <cstdlib>
 
@@ -93,189 +93,22 @@ __global__ void __launch_bounds__(256) im2col_kernel(const float* __restrict__ i
   }
 }
 
-// ---- per-head flash attention, head dim 72 (padded to 80), mma.sync --------
-constexpr int kHd = 72;
-constexpr int kHdPad = 80;
-constexpr int kRowE = 88;              // smem row pitch in elements (176 B: conflict-free ldmatrix)
-constexpr int kRowB = kRowE * 2;
-
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& a, uint32_t& b, uint32_t& c, uint32_t& d) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(a), "=r"(b), "=r"(c), "=r"(d)
-               : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& a, uint32_t& b) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(a), "=r"(b) : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x2_t(uint32_t addr, uint32_t& a, uint32_t& b) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];" : "=r"(a), "=r"(b) : "r"(addr));
-}
-__device__ __forceinline__ void mma_bf16(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                         uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&v);
-}
-
-// Grid (views * heads, seq / 64); 4 warps x 16 query rows; all `seq` keys in smem.
-// qkv [views*seq, 3*width] (q | k | v, head h at columns h*72), out [views*seq, width].
-template <int SEQ>
-__global__ void __launch_bounds__(128) mha72_kernel(const __nv_bfloat16* __restrict__ qkv, int width, int heads,
-                                                    float scale, __nv_bfloat16* __restrict__ out) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(smem);  // 64 x 88
-  __nv_bfloat16* sK = sQ + 64 * kRowE;                          // SEQ x 88
-  __nv_bfloat16* sV = sK + SEQ * kRowE;                         // SEQ x 88
-  pdl_wait();
-  pdl_launch_dependents();  // let the next kernel's CTAs start their prologue / weight prefetch
-  const int vh = blockIdx.x, view = vh / heads, h = vh % heads;
-  const int q0 = blockIdx.y * 64;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const size_t ld = (size_t)3 * width;
-  const __nv_bfloat16* base = qkv + (size_t)view * SEQ * ld + h * kHd;
-  // 9 chunks of 16 B per 72-element row, copied asynchronously; chunk 9 (columns
-  // 72..79) is zero-filled.  Four commit groups: Q with keys 0..63, then keys
-  // 64c..64c+63 (K and V rows), so the key loop starts on the first 64 keys while
-  // the others are still arriving.
-  auto copy_rows = [&](__nv_bfloat16* dst0, const __nv_bfloat16* src0, int rows) {
-    for (int i = tid; i < rows * 10; i += 128) {
-      const int row = i / 10, c = i % 10;
-      const int n = c < 9 ? 16 : 0;
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst0 + row * kRowE + c * 8)),
-                   "l"(src0 + (size_t)row * ld + (c < 9 ? c * 8 : 0)), "r"(n)
-                   : "memory");
-    }
-  };
-  copy_rows(sQ, base + (size_t)q0 * ld, 64);
-#pragma unroll
-  for (int c = 0; c < SEQ / 64; ++c) {
-    copy_rows(sK + c * 64 * kRowE, base + (size_t)(c * 64) * ld + width, 64);
-    copy_rows(sV + c * 64 * kRowE, base + (size_t)(c * 64) * ld + 2 * width, 64);
-    asm volatile("cp.async.commit_group;" ::: "memory");
-  }
-  static_assert(SEQ == 256, "four key groups");
-  asm volatile("cp.async.wait_group 3;" ::: "memory");
-  __syncthreads();
-  const uint32_t aQ = static_cast<uint32_t>(__cvta_generic_to_shared(sQ));
-  const uint32_t aK = static_cast<uint32_t>(__cvta_generic_to_shared(sK));
-  const uint32_t aV = static_cast<uint32_t>(__cvta_generic_to_shared(sV));
-  const int g = lane >> 2, t4 = lane & 3;
-  // Q fragments for this warp's 16 rows, 5 k-steps of 16 dims.
-  uint32_t qa[5][4];
-#pragma unroll
-  for (int kk = 0; kk < 5; ++kk) {
-    const int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-    const int c = kk * 16 + (lane >> 4) * 8;
-    ldsm_x4(aQ + (r * kRowE + c) * 2, qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
-  }
-  float o[10][4];
-#pragma unroll
-  for (int j = 0; j < 10; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
-  for (int kc = 0; kc < SEQ; kc += 64) {
-    if (kc > 0) {  // keys kc .. kc+63 (groups still in flight after this one: 3 - kc / 64)
-      if (kc == 64)
-        asm volatile("cp.async.wait_group 2;" ::: "memory");
-      else if (kc == 128)
-        asm volatile("cp.async.wait_group 1;" ::: "memory");
-      else
-        asm volatile("cp.async.wait_group 0;" ::: "memory");
-      __syncthreads();
-    }
-    float s[8][4];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
-#pragma unroll
-    for (int kk = 0; kk < 5; ++kk) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        uint32_t b0, b1;
-        const int r = kc + j * 8 + (lane & 7);
-        const int c = kk * 16 + ((lane >> 3) & 1) * 8;
-        ldsm_x2(aK + (r * kRowE + c) * 2, b0, b1);
-        mma_bf16(s[j], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b0, b1);
-      }
-    }
-    float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-#pragma unroll
-      for (int e = 0; e < 4; e += 2) {  // bf16(bf16(q.k) * scale), two values per conversion
-        bf16_round2(s[j][e], s[j][e + 1]);
-        s[j][e] *= scale;
-        s[j][e + 1] *= scale;
-        bf16_round2(s[j][e], s[j][e + 1]);
-      }
-#pragma unroll
-      for (int e = 0; e < 4; ++e) mx[e >> 1] = fmaxf(mx[e >> 1], s[j][e]);
-    }
-    float corr[2];
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      mx[hh] = fmaxf(mx[hh], __shfl_xor_sync(0xffffffff, mx[hh], 1));
-      mx[hh] = fmaxf(mx[hh], __shfl_xor_sync(0xffffffff, mx[hh], 2));
-      const float mn = fmaxf(m_run[hh], mx[hh]);
-      corr[hh] = __expf(m_run[hh] - mn);
-      m_run[hh] = mn;
-    }
-    float ls[2] = {0.f, 0.f};
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float pv = __expf(s[j][e] - m_run[e >> 1]);
-        s[j][e] = pv;
-        ls[e >> 1] += pv;
-      }
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      ls[hh] += __shfl_xor_sync(0xffffffff, ls[hh], 1);
-      ls[hh] += __shfl_xor_sync(0xffffffff, ls[hh], 2);
-      l_run[hh] = l_run[hh] * corr[hh] + ls[hh];
-    }
-#pragma unroll
-    for (int j = 0; j < 10; ++j) {
-      o[j][0] *= corr[0];
-      o[j][1] *= corr[0];
-      o[j][2] *= corr[1];
-      o[j][3] *= corr[1];
-    }
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      const uint32_t a0 = pack2(s[2 * kk][0], s[2 * kk][1]);
-      const uint32_t a1 = pack2(s[2 * kk][2], s[2 * kk][3]);
-      const uint32_t a2 = pack2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-      const uint32_t a3 = pack2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
-#pragma unroll
-      for (int j = 0; j < 10; ++j) {
-        uint32_t b0, b1;
-        const int r = kc + kk * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
-        ldsm_x2_t(aV + (r * kRowE + j * 8) * 2, b0, b1);
-        mma_bf16(o[j], a0, a1, a2, a3, b0, b1);
-      }
-    }
-  }
-#pragma unroll
-  for (int hh = 0; hh < 2; ++hh) {
-    const float inv = 1.f / l_run[hh];
-    const int row = q0 + warp * 16 + g + hh * 8;
-    __nv_bfloat16* dst = out + ((size_t)view * SEQ + row) * width + h * kHd;
-#pragma unroll
-    for (int j = 0; j < 9; ++j)
-      *reinterpret_cast<uint32_t*>(dst + j * 8 + 2 * t4) = pack2(o[j][2 * hh] * inv, o[j][2 * hh + 1] * inv);
-  }
-}
+constexpr int kHd = 72;  // SigLIP head dim
 
 inline bool nz(const void* p) { return p != nullptr; }
 
+}  // namespace
+
+namespace pi05 {
+// The attention kernel (tcgen05, siglip_attn_tc.cu).
+int siglip_attention_tc_run(const void* qkv, int views, int width, int heads, void* out, int* status,
+                            cudaStream_t stream);
+}  // namespace pi05
+
+namespace {
+
 int siglip_attention_run(const void* qkv, int views, int seq, int width, int heads, int head_dim, void* out,
-                         void* stream) {
+                         void* stream, int* status = nullptr) {
   if (!nz(qkv) || !nz(out)) {
     set_last_error("siglip_attention: null pointer");
     return PI05_ERR_INVALID_ARG;
@@ -285,17 +118,7 @@ int siglip_attention_run(const void* qkv, int views, int seq, int width, int hea
     set_last_error("siglip_attention: supports head_dim 72, 256 tokens per view, 16-byte aligned buffers");
     return PI05_ERR_SHAPE;
   }
-  const size_t smem = (size_t)(64 + 2 * 256) * kRowB;
-  static bool attr_done[16] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 16 && !attr_done[dev]) {
-    cudaFuncSetAttribute(mha72_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr_done[dev] = true;
-  }
-  return launch_pdl(mha72_kernel<256>, dim3(views * heads, seq / 64), dim3(128), smem,
-                    reinterpret_cast<cudaStream_t>(stream), pdl_enabled(), static_cast<const __nv_bfloat16*>(qkv),
-                    width, heads, 1.0f / std::sqrt((float)head_dim), static_cast<__nv_bfloat16*>(out));
+  return siglip_attention_tc_run(qkv, views, width, heads, out, status, reinterpret_cast<cudaStream_t>(stream));
 }
 
 // PI05_FOLD_NORM=0 in the environment keeps the LayerNorm kernels.
@@ -430,7 +253,7 @@ int pi05_siglip_forward(const Pi05SiglipPlan* P, void* stream) {
       rc = skinny_gemm_run(SK_EPI_STORE, sp, wq, wq, 3 * W, 3 * W, fold ? h : xn, W, 0, stream);
       if (rc) return rc;
     }
-    rc = siglip_attention_run(qkv, V, S, W, P->n_heads, P->head_dim, attn, stream);
+    rc = siglip_attention_run(qkv, V, S, W, P->n_heads, P->head_dim, attn, stream, ws.status);
     if (rc) return rc;
     {
       SkinnyParams sp = base_params(ws);
