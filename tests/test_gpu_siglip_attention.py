@@ -3,8 +3,8 @@ dims, 256 tokens per view, no mask) against the oracle's numerics on the same bf
 q|k|v: s = bf16(bf16(q.k) * 72^-0.5), p = bf16(softmax(s)), o = bf16(p.v), as
 transformers' eager SiglipAttention computes it in bf16.  Tolerance: cosine
 >= 0.9999 per (view, head) and max-abs <= 4e-2 on outputs of magnitude ~1 (the
-kernel rounds the unnormalised probabilities exp(s - m) to bf16 and divides by the
-row sum at the end, flash-style, where the reference rounds normalised ones).
+tcgen05 kernel sees whole rows and rounds the normalised probabilities to bf16 as
+the reference does; the bound leaves room for the order of the fp32 sums).
 """
 
 import ctypes
